@@ -1,0 +1,320 @@
+"""Benchmark of the B200 MoE hot path; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill] [--impl reference]
+
+Workloads (synthetic data with the distributions BASELINE.json names):
+* ``decode``  (configs[1]): one decode step = 48 stacked config[0] MoE layers at batch b (default 1), Zipf(1.1)
+  routing, all 48 x 512 expert records resident in HBM, the step captured in one CUDA graph. Each layer reads
+  its own resident N(0,1) hidden state (the attention / hyper-connection segments between MoE layers, which
+  renormalise the residual stream in the real model, are not part of this path).
+* ``prefill`` (configs[2]/[3]): one step = one config[0] layer over a chunk of tokens per GPU.
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching stream with an
+L2 flush (256 MiB write) before it, barrier + synchronize on both sides, max over ranks. The JSON line carries
+``roofline`` (dominant launch vs MEASURED_PEAKS.json), ``cpu_baseline`` (oracle port on the host cores, rank 0,
+N=1), ``e2e`` (host buffers through the public API), ``gpu_launches`` and ``clocks``.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "slotstream-spark_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "MoE-layer tokens/s (decode b=1 HBM GB/s; prefill TFLOPS) at 1/2/4/8 B200"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.samples = []
+        self.proc = None
+        self.t_on = self.t_off = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        threading.Thread(target=self._read, daemon=True).start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.monotonic(), [v.strip() for v in line.split(",")]))
+
+    def mark_on(self):
+        self.t_on = time.monotonic()
+
+    def mark_off(self):
+        self.t_off = time.monotonic()
+
+    def stop(self):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        inside = [s for t, s in self.samples if self.t_on is not None and self.t_on <= t <= (self.t_off or t)]
+        use = inside if inside else [s for _, s in self.samples]
+        sm = [float(s[1]) for s in use if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in use if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in use for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(use), "samples_in_timed_region": len(inside)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed_steps(run, k, flush_buf, world, clocks=None):
+    """Per-step CUDA-event times (ms) on the current stream, L2 flushed before every step."""
+    st = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+    barrier(world)
+    if clocks:
+        clocks.mark_on()
+    for a, b in evs:
+        flush_buf.zero_()
+        a.record(st)
+        run()
+        b.record(st)
+    barrier(world)
+    if clocks:
+        clocks.mark_off()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+# ------------------------------------------------------------------ decode workload
+def bench_decode(args, world, rank):
+    from slotstream_b200 import synth
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    from slotstream_b200.records import BASELINE_LAYOUT as LAY, MAP_LAYERS
+    NL, E, K, b = 48, 512, 10, args.batch
+    dev = torch.device("cuda")
+    rb = LAY.record_bytes
+    seed = 1000 + rank
+    recs = torch.empty((NL * E, rb), dtype=torch.uint8, device=dev)
+    synth.fill_records_device(LAY, recs, seed)
+    shared = torch.empty((NL, rb), dtype=torch.uint8, device=dev)
+    synth.fill_records_device(LAY, shared, seed + 7)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    router_w = (torch.randn(NL, E, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    sh_gate_w = (torch.randn(NL, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.from_numpy(synth.zipf_bias(E)).to(dev)
+    map_t = torch.full((MAP_LAYERS * E,), -1, dtype=torch.int32, device=dev)
+    map_t[:NL * E] = torch.arange(NL * E, dtype=torch.int32, device=dev)
+    slot_ptr = recs.data_ptr() + torch.arange(NL * E, dtype=torch.int64, device=dev) * rb
+    x = torch.randn(NL, b, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
+    bufs = [DecodeLayerBuffers(b, K, LAY.hidden, LAY.inter, E, dev) for _ in range(NL)]
+
+    def step():
+        for l in range(NL):
+            moe_layer_decode(x[l], router_w[l], l, map_t, slot_ptr, shared[l], sh_gate_w[l], K, bufs[l], bias=bias)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    torch.cuda.synchronize()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    times = timed_steps(graph.replay, args.steps, flush, world, clocks)
+    clocks.stop()
+    ms = max_over_ranks(sum(times) / len(times), world)
+
+    # bytes per step from the routing the step actually produced (unique experts per layer)
+    uniq = [int(torch.unique(bf.ids).numel()) for bf in bufs]
+    per_layer_fixed = rb + E * LAY.hidden * 2 + LAY.hidden * 2 + b * LAY.hidden * 2 * 2
+    step_bytes = sum(u * rb for u in uniq) + NL * per_layer_fixed
+    errs = sum(int(bf.err.item()) for bf in bufs)
+
+    # dominant launch: the gate_up + down pair of moe_decode_layer, timed per layer outside the graph
+    lt = []
+    from slotstream_b200 import _lib
+    st = torch.cuda.current_stream()
+    for l in range(NL):
+        flush.zero_()
+        from slotstream_b200.kernels.router import router_topk
+        router_topk(x[l], router_w[l], K, bufs[l].ids, bufs[l].w, bias=bias, sh_gate_w=sh_gate_w[l],
+                    out_sh_gate=bufs[l].sh_gate, ws=bufs[l].ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        rc = _lib.lib().ssb_moe_decode_layer(
+            _lib.ptr(x[l]), _lib.ptr(bufs[l].ids), _lib.ptr(bufs[l].w), b, K, LAY.hidden, LAY.inter, l,
+            _lib.ptr(map_t), map_t.numel(), _lib.ptr(slot_ptr), slot_ptr.numel(), shared[l].data_ptr(),
+            _lib.ptr(bufs[l].sh_gate), _lib.ptr(bufs[l].h), _lib.ptr(bufs[l].o), _lib.ptr(bufs[l].out),
+            _lib.ptr(bufs[l].y), 0, _lib.ptr(bufs[l].err), _lib.stream())
+        _lib.check(rc, "moe_decode_layer")
+        e1.record(st)
+        torch.cuda.synchronize()
+        lt.append(e0.elapsed_time(e1))
+    launch_ms = sum(lt) / len(lt)
+    launch_bytes = (sum(u * rb for u in uniq) + NL * (rb + b * LAY.hidden * 2 * 2)) / NL
+    pk = peaks()
+    achieved = launch_bytes / (launch_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "moe_decode_layer (gate_up + down)", "achieved": round(achieved, 1),
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                "peak_source": pk["source"], "traffic": None,
+                "bytes_per_launch": int(launch_bytes), "launch_us": round(launch_ms * 1e3, 2)}
+
+    # e2e: host inputs (pinned) -> device, graph step, outputs -> host, all inside the timed region
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((NL, b, LAY.hidden), dtype=torch.bfloat16).pin_memory()
+    y_dev = torch.stack([bf.y for bf in bufs])
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        graph.replay()
+        y_host.copy_(torch.stack([bf.y for bf in bufs]), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_times = timed_steps(e2e_step, args.steps, flush, world)
+    e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
+    del y_dev
+
+    value = world * b / (ms * 1e-3)
+    res = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decode_step_48layer_b{b}", "layers": NL, "batch": b, "hidden": LAY.hidden,
+                   "inter": LAY.inter, "experts": E, "topk": K, "shared_experts": 1, "routing": "zipf_s1.1",
+                   "weights": "affine4_gs64 resident in HBM (48x512 records)", "cuda_graph": True,
+                   "l2": "flushed before every step (256 MiB write)", "parallelism": f"replicas{world}"},
+        "hbm_gbs_per_step": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+        "bytes_per_step": int(step_bytes), "unique_experts_per_layer_mean": round(sum(uniq) / NL, 2),
+        "roofline": roofline,
+        "e2e": {"value": round(world * b / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y_host.numel() * 2)},
+        "gpu_launches": 4 * NL * args.steps,
+        "clocks": clocks.summary(),
+        "device_errors": errs,
+    }
+    return res
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=["decode"], default="decode")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        # the reference's path is CPU-only: rank 0 alone runs it, other ranks exit without work
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps(reference_arm(args, int(os.environ.get("WORLD_SIZE", "1")))), flush=True)
+        return
+    world, rank, _ = dist_setup()
+    res = bench_decode(args, world, rank)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.cpu_baseline import time_decode
+        from slotstream_b200.records import BASELINE_LAYOUT
+        res["cpu_baseline"] = time_decode(BASELINE_LAYOUT, seconds=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def reference_arm(args, world):
+    """The reference's own CPU path (oracle torch port of moe_ref / affine_ref) on all host cores, same
+    metric and config; each step is a bounded sample."""
+    sys.path.insert(0, str(ROOT))
+    from oracle.cpu_baseline import time_decode
+    from slotstream_b200.records import BASELINE_LAYOUT
+    per_step = max(1.0, min(10.0, 60.0 / max(args.steps, 1)))
+    vals = []
+    for _ in range(args.warmup):
+        time_decode(BASELINE_LAYOUT, seconds=0.5)
+    for _ in range(args.steps):
+        vals.append(time_decode(BASELINE_LAYOUT, seconds=per_step))
+    v = statistics.mean(r["value"] for r in vals)
+    cb = dict(vals[-1])
+    cb["value"] = v
+    b = args.batch
+    return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"decode_step_48layer_b{b}", "layers": 48, "batch": b, "hidden": 2048,
+                       "inter": 512, "experts": 512, "topk": 10, "routing": "zipf_s1.1"},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+
+
+if __name__ == "__main__":
+    main()

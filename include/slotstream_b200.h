@@ -1,0 +1,154 @@
+/*
+ * slotstream_b200.h -- C ABI of the B200-native (sm_100a) MoE hot path of slotstream-spark.
+ *
+ * Every entry point takes raw device pointers, element counts and a cudaStream_t passed as void*; none
+ * allocates device memory, none synchronises the host, and every launch goes to the given stream, so
+ * the calls can be captured in a CUDA graph. Each returns SSB_OK (0), a negative SSB_E* code for a bad
+ * argument (checked before any launch), or a positive cudaError_t from the launch.
+ *
+ * Conventions: bf16 tensors are passed as uint16_t* bit patterns; 4-bit affine weights follow MLX
+ * (element i of a row in bits [4*(i%8), 4*(i%8)+4) of int32 word i/8, w = q*s + b with bf16 s, b per
+ * group of gs elements). An expert record is the reference's nine-piece layout (gate/up/down x w/s/b)
+ * with offsets derived from (hidden, inter, gs).
+ *
+ * "Replaces" names the reference interface (file:line inside fortil/slotstream-spark) whose Python
+ * function dispatches to the entry point in this build.
+ */
+#ifndef SLOTSTREAM_B200_H
+#define SLOTSTREAM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes */
+#define SSB_OK 0
+#define SSB_EINVAL (-1)       /* null pointer, count or size out of range */
+#define SSB_EUNSUPPORTED (-2) /* a shape these kernels do not handle (see each entry point) */
+#define SSB_ENODEVICE (-3)    /* current device is not sm_100 */
+
+/* ---- bits of the device error word (int32, caller-owned, OR-ed by kernels; never cleared by them) */
+#define SSB_ERR_EXPERT_RANGE 1 /* an expert id outside [0, 512) */
+#define SSB_ERR_UNMAPPED 2     /* map[layer*512 + e] < 0: the expert is not in the pool */
+#define SSB_ERR_SLOT_RANGE 4   /* a slot index outside slot_ptr */
+#define SSB_ERR_MISALIGNED 8   /* a record base that is not 16-byte aligned */
+#define SSB_ERR_TIMEOUT 16     /* a bounded device-side wait gave up (the kernel skipped its work) */
+
+/* ---- dtype tags for activations */
+#define SSB_BF16 0
+#define SSB_F32 1
+
+/* Library version string. */
+const char* ssb_version(void);
+
+/* SSB_OK when the current device is an sm_100 part (B200), SSB_ENODEVICE otherwise. */
+int ssb_device_check(void);
+
+/* Static + dynamic shared memory (bytes) that the named kernel family last launched with; -1 if the
+ * name is unknown or the kernel has not launched. Backs the reference's SHARED_BYTES bookkeeping
+ * (slotstream_spark/kernels/gemv_affine.py:15-25). */
+int ssb_kernel_smem(const char* name);
+
+/* Stable top-k of each row of fp32 scores [rows, n] (n <= 65536, 1 <= k <= n): order-preserving uint32
+ * keys (NaN lowest), ties to the lower index; k <= 16 sorted by (value desc, index asc), larger k by
+ * index asc; rows with fewer than k valid entries pad with index -1 / value -inf. n_valid (int32 [rows])
+ * and out_val may be NULL.
+ * Replaces: slotstream_spark/kernels/topk_stable.py:85-113 (kernel :28-82). */
+int ssb_topk_stable(const float* scores, const int32_t* n_valid, int64_t rows, int32_t n, int32_t k,
+                    int32_t* out_idx, float* out_val, void* stream);
+
+/* Router logits: logits[t, j] = sum_h x[t, h] * w[j, h] for j < n_rows, fp32 accumulation of the exact
+ * bf16 products; when w_extra != NULL one more column (index n_rows) is sum_h x[t, h] * w_extra[h].
+ * x bf16 [tokens, hidden], w bf16 [n_rows, hidden] row-major, logits fp32 [tokens, ld]
+ * (ld >= n_rows + (w_extra != NULL)). hidden must be a multiple of 256 and <= 4096.
+ * Replaces: the router GEMV of model/layers.py:339 (lin -> kernels/gemv_affine.py:177-198). */
+int ssb_router_logits(const uint16_t* x, const uint16_t* w, const uint16_t* w_extra, int64_t tokens,
+                      int32_t hidden, int32_t n_rows, int32_t ld, float* logits, void* stream);
+
+/* Router selection, one warp per token: (optional bf16 rounding of the logits), + bias[e] (optional,
+ * fp32 [experts]), fp32 softmax over `experts` columns, stable top-k on the probabilities (same key rule
+ * as ssb_topk_stable), renormalised weights w = p / sum(p). experts <= 1024, k <= 32.
+ * out_probs (fp32 [tokens, experts]) may be NULL. With SSB_ROUTER_SHARED_GATE, column `experts` of the
+ * logits is the shared-expert gate logit and out_sh_gate[t] = sigmoid(it).
+ * Replaces: model/layers.py:340-347 (softmax, topk_stable, renormalise) and the shared-expert gate of
+ * model/layers.py:401. */
+#define SSB_ROUTER_ROUND_BF16 1
+#define SSB_ROUTER_SHARED_GATE 2
+int ssb_router_select(const float* logits, int32_t ld, int64_t tokens, int32_t experts, int32_t k,
+                      const float* bias, int32_t flags, int32_t* out_idx, float* out_w, float* out_probs,
+                      float* out_sh_gate, void* stream);
+
+/* Stable counting sort of rows by local expert, padded per expert to block_m with the sentinel `rows`.
+ * local = expert_map ? expert_map[row_expert[i]] (-1 when row_expert[i] is outside [0, map_len))
+ *                    : row_expert[i];
+ * rows with local outside [0, num_local) are dropped. Outputs: sorted_rows int32 [P], block_expert int32
+ * [P / block_m] (-1 past num_padded), num_padded int32 [1], P = padded_rows(rows, num_local, block_m).
+ * num_local <= 1280.
+ * Replaces: slotstream_spark/kernels/moe_align.py:17-48 and align_rows of
+ * slotstream_spark/kernels/fused_moe_affine.py:130-133. */
+int ssb_moe_align(const int32_t* row_expert, int64_t rows, const int32_t* expert_map, int32_t map_len,
+                  int32_t num_local, int32_t block_m, int32_t* sorted_rows, int32_t* block_expert,
+                  int32_t* num_padded, void* stream);
+
+/* Decode grouped GEMV over routed experts found through the slot tables:
+ *   base(r, j) = slot_ptr[map[layer*512 + ids[r, j]]]
+ *   h[r, j, :] = silu(G x_r) * (U x_r)                  (fp32, exact fp32 dequant algebra)
+ *   o[r, j, :] = w[r, j] * (D h[r, j, :])               (fp32)
+ *   out[r, :]  = o[r, 0] + o[r, 1] + ... in rank order  (sequential fp32)
+ * x bf16|fp32 [rows, hidden] (x_dtype SSB_BF16 / SSB_F32); h_buf fp32 [rows, topk, inter];
+ * o_buf fp32 [rows, topk, hidden]; out fp32 [rows, hidden]. hidden % 512 == 0, inter % 512 == 0 or
+ * inter % 16 == 0 with inter <= 8192, gs 64. err (int32, nullable) gets SSB_ERR_* bits; a bad expert
+ * contributes zero. Row-invariant and placement-invariant bit for bit.
+ * Replaces: slotstream_spark/kernels/moe_gemv_affine.py:113-147 (kernels :55-110). */
+int ssb_moe_decode(const void* x, int32_t x_dtype, const int32_t* expert_ids, const float* weights,
+                   int64_t rows, int32_t topk, int32_t hidden, int32_t inter, int32_t layer,
+                   const int32_t* map_t, int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots,
+                   float* h_buf, float* o_buf, float* out, int32_t* err, void* stream);
+
+/* Fused decode layer (additive): ssb_moe_decode plus the shared expert, whose record sits at
+ * shared_record, gated by sh_gate[r] (the sigmoid from ssb_router_select):
+ *   sh[r, :] = sh_gate[r] * (D_s (silu(G_s x_r) * (U_s x_r)))
+ *   y[r, :]  = bf16( bf16(out[r, :]) + bf16(sh[r, :]) )      (bf16 [rows, hidden])
+ * h_buf must hold rows * (topk + 1) * inter floats (the shared expert's h follows the routed ones).
+ * flags bit 0 (SSB_DECODE_PDL): launch with programmatic dependent launch.
+ * Replaces: the decode MoE call site of slotstream_spark/runtime/graphs.py:160-169 (moe_decode + shared
+ * expert + routed.to(bf16) + sh). */
+#define SSB_DECODE_PDL 1
+int ssb_moe_decode_layer(const uint16_t* x, const int32_t* expert_ids, const float* weights, int64_t rows,
+                         int32_t topk, int32_t hidden, int32_t inter, int32_t layer, const int32_t* map_t,
+                         int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots, const void* shared_record,
+                         const float* sh_gate, float* h_buf, float* o_buf, float* out, uint16_t* y,
+                         int32_t flags, int32_t* err, void* stream);
+
+/* Rank-order combine: out[t, :] = rows[t*k] + rows[t*k + 1] + ... sequentially in fp32.
+ * rows fp32 [tokens * k, hidden], out fp32 [tokens, hidden]; hidden % 4 == 0.
+ * Replaces: combine_rank_order, slotstream_spark/kernels/fused_moe_affine.py:164-172. */
+int ssb_combine_rank_order(const float* rows, int64_t tokens, int32_t k, int32_t hidden, float* out,
+                           void* stream);
+
+/* Layer combine (additive): the rank-order sum above, then y[t, :] = bf16(bf16(sum) + bf16(sh[t, :]))
+ * (sh fp32 [tokens, hidden], nullable = no shared expert); out (nullable) also receives the fp32 sum.
+ * Replaces: the combine_rank_order + routed.to(bf16) + sh sequence of model/moe_sweep.py:161 and
+ * engine/prefill.py:200-201. */
+int ssb_combine_layer(const float* rows, int64_t tokens, int32_t k, int32_t hidden, const float* sh, float* out,
+                      uint16_t* y, void* stream);
+
+/* Affine GEMV: out[r, i] = sum_j x[r, j] * (q[i, j] * s[i, j / gs] + b[i, j / gs]), fp32 accumulation,
+ * bits 4 or 8, gs 32 or 64, k % 512 == 0 (4-bit) or k % 256 == 0 (8-bit), k <= 16384.
+ * Row-invariant: each output row is the same op sequence whatever `rows` is.
+ * Replaces: gemv(x, AffineWeight) of slotstream_spark/kernels/gemv_affine.py:214-262. */
+int ssb_gemv_affine(const void* x, int32_t x_dtype, int64_t rows, const int32_t* q, const uint16_t* s,
+                    const uint16_t* b, int32_t n, int32_t k, int32_t bits, int32_t gs, float* out, void* stream);
+
+/* Dense bf16 GEMV: out[r, i] = sum_j x[r, j] * w[i, j], fp32 accumulation; k % 256 == 0, k <= 16384.
+ * Replaces: gemv(x, DenseWeight) of slotstream_spark/kernels/gemv_affine.py:214-262. */
+int ssb_gemv_dense(const void* x, int32_t x_dtype, int64_t rows, const uint16_t* w, int32_t n, int32_t k,
+                   float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLOTSTREAM_B200_H */

@@ -1,0 +1,134 @@
+// moe_align: deterministic stable counting sort of rows by local expert, each expert padded to block_m
+// with the sentinel R (slotstream_spark/kernels/moe_align.py:17-48), with align_rows' expert_map gather
+// (slotstream_spark/kernels/fused_moe_affine.py:130-133) fused in. No global atomics, no host sync.
+//
+// One CTA of 32 warps. Warp w owns the contiguous row range [w*chunk, (w+1)*chunk). Pass 1 counts rows per
+// (warp, expert) in shared memory; a column scan turns the counts into per-(warp, expert) destinations;
+// pass 2 re-reads the rows in order and ranks equal experts inside each 32-row batch with match_any, so
+// the order inside an expert is the row order -- exactly the stable sort of the reference.
+#include "common.cuh"
+#include "registry.h"
+
+namespace {
+
+constexpr int AL_WARPS = 32;
+constexpr int AL_THREADS = AL_WARPS * 32;
+constexpr int AL_MAX_LOCAL = 1280;
+
+SSB_DEV int local_of(const int32_t* __restrict__ row_expert, const int32_t* __restrict__ emap, int map_len,
+                     int64_t i) {
+  int v = row_expert[i];
+  if (emap) v = (v >= 0 && v < map_len) ? emap[v] : -1;
+  return v;
+}
+
+__global__ void __launch_bounds__(AL_THREADS) k_moe_align(const int32_t* __restrict__ row_expert, int64_t R,
+                                                           const int32_t* __restrict__ emap, int map_len, int NL,
+                                                           int bm, int64_t P, int32_t* __restrict__ sorted_rows,
+                                                           int32_t* __restrict__ block_expert,
+                                                           int32_t* __restrict__ num_padded) {
+  extern __shared__ int sm[];
+  int* cnt = sm;                       // [AL_WARPS][NL]: counts, then destinations
+  int* tot = cnt + AL_WARPS * NL;      // [NL]
+  int* pend = tot + NL;                // [NL] inclusive scan of padded counts
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  pdl_trigger();
+  for (int i = tid; i < AL_WARPS * NL; i += AL_THREADS) cnt[i] = 0;
+  __syncthreads();
+  const int64_t chunk = (R + AL_WARPS - 1) / AL_WARPS;
+  const int64_t lo0 = (int64_t)warp * chunk;
+  const int64_t lo = lo0 < R ? lo0 : R, hi = lo + chunk < R ? lo + chunk : R;
+  int* mycnt = cnt + warp * NL;
+  for (int64_t base = lo; base < hi; base += 32) {
+    int64_t i = base + lane;
+    int v = i < hi ? local_of(row_expert, emap, map_len, i) : -1;
+    if (v >= 0 && v < NL) atomicAdd(&mycnt[v], 1);
+  }
+  __syncthreads();
+  for (int e = tid; e < NL; e += AL_THREADS) {
+    int run = 0;
+    for (int w = 0; w < AL_WARPS; ++w) {
+      int c = cnt[w * NL + e];
+      cnt[w * NL + e] = run;
+      run += c;
+    }
+    tot[e] = run;
+  }
+  __syncthreads();
+  if (warp == 0) {  // inclusive scan of padded counts over experts, one contiguous segment per lane
+    const int seg = (NL + 31) / 32;
+    const int e0 = lane * seg, e1 = min(NL, e0 + seg);
+    int s = 0;
+    for (int e = e0; e < e1; ++e) s += (tot[e] + bm - 1) / bm * bm;
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int run = incl - s;
+    for (int e = e0; e < e1; ++e) {
+      run += (tot[e] + bm - 1) / bm * bm;
+      pend[e] = run;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < AL_WARPS * NL; i += AL_THREADS) {
+    int e = i % NL;
+    int padded = (tot[e] + bm - 1) / bm * bm;
+    cnt[i] += pend[e] - padded;
+  }
+  __syncthreads();
+  for (int64_t base = lo; base < hi; base += 32) {
+    int64_t i = base + lane;
+    int v = i < hi ? local_of(row_expert, emap, map_len, i) : -1;
+    bool valid = v >= 0 && v < NL;
+    int key = valid ? v : -1 - lane;  // invalid lanes never match anyone
+    unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
+    unsigned below = peers & lanemask_lt();
+    if (valid) sorted_rows[mycnt[v] + __popc(below)] = (int32_t)i;
+    __syncwarp();
+    if (valid && below == 0) mycnt[v] += __popc(peers);
+    __syncwarp();
+  }
+  // padding inside each expert's span, then the tail past num_padded
+  for (int e = tid; e < NL; e += AL_THREADS) {
+    int padded = (tot[e] + bm - 1) / bm * bm;
+    for (int p = pend[e] - padded + tot[e]; p < pend[e]; ++p) sorted_rows[p] = (int32_t)R;
+  }
+  const int total = pend[NL - 1];
+  for (int64_t p = total + tid; p < P; p += AL_THREADS) sorted_rows[p] = (int32_t)R;
+  const int64_t nb = P / bm;
+  for (int64_t b = tid; b < nb; b += AL_THREADS) {
+    const int64_t pos = b * bm;
+    int e;  // first expert whose padded span ends after pos (searchsorted right)
+    int l = 0, h = NL;
+    while (l < h) {
+      int mid = (l + h) >> 1;
+      if (pend[mid] <= pos) l = mid + 1; else h = mid;
+    }
+    e = l;
+    block_expert[b] = e < NL ? e : -1;
+  }
+  if (tid == 0) num_padded[0] = total;
+}
+
+}  // namespace
+
+extern "C" int ssb_moe_align(const int32_t* row_expert, int64_t rows, const int32_t* expert_map, int32_t map_len,
+                             int32_t num_local, int32_t block_m, int32_t* sorted_rows, int32_t* block_expert,
+                             int32_t* num_padded, void* stream) {
+  SSB_CHECK_ARG(sorted_rows && block_expert && num_padded && rows >= 0 && (rows == 0 || row_expert));
+  SSB_CHECK_ARG(num_local >= 1 && block_m >= 1 && rows < 2147483647LL);
+  SSB_CHECK_ARG(!expert_map || map_len >= 0);
+  if (num_local > AL_MAX_LOCAL) return SSB_EUNSUPPORTED;
+  int64_t n = rows + (int64_t)num_local * (block_m - 1);
+  int64_t P = (n + block_m - 1) / block_m * block_m;
+  SSB_CHECK_ARG(P < 2147483647LL);
+  size_t smem = (size_t)(AL_WARPS * num_local + 2 * num_local) * sizeof(int);
+  ssb_note_smem("moe_align", k_moe_align, smem);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_moe_align, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return ssb_launch(k_moe_align, dim3(1), dim3(AL_THREADS), smem, (cudaStream_t)stream, true, row_expert, rows,
+                    expert_map, map_len, num_local, block_m, P, sorted_rows, block_expert, num_padded);
+}

@@ -1,0 +1,407 @@
+// Decode grouped GEMV over routed experts addressed through the slot tables
+// (slotstream_spark/kernels/moe_gemv_affine.py:113-147), plus the fused shared expert of the decode layer.
+//
+// Two launches:
+//  * gate_up: CTA = (pair p = (row, rank) or the shared expert, 32 rows of inter). One thread copies the
+//    slice of gate/up codes, scales and biases into shared memory with six bulk async copies; eight warps
+//    then form h = silu(G x) * (U x) in fp32 with the activation held in registers.
+//  * down   : CTA = (row, 16 rows of hidden). It stages the down slices of all of the row's experts with bulk
+//    copies issued BEFORE waiting on the gate_up grid (the records are static and the expert ids were
+//    written two launches back), so under programmatic dependent launch the down weights stream in while
+//    gate_up runs. It then forms o_k = w_k * (D_k h_k) and sums the ranks in order (out = o_0 + o_1 + ...),
+//    fusing the reference's separate _rank_sum kernel.
+// Every (row, rank, output) value is the same op sequence whatever the row count or slot placement, so a
+// 3-row call equals three 1-row calls bit for bit.
+#include "affine.cuh"
+#include "registry.h"
+
+namespace {
+
+constexpr int GU_ROWS = 32;    // inter rows per gate_up CTA
+constexpr int GU_WARPS = 8;
+constexpr int DN_ROWS = 16;    // hidden rows per down CTA
+constexpr int DN_WARPS = 4;
+
+struct DecodeArgs {
+  const void* x;
+  int x_f32;
+  const int32_t* ids;
+  const float* wts;
+  int64_t R;
+  int topk;
+  int H, I, gs;
+  int layer;
+  const int32_t* map;
+  int64_t map_len;
+  const int64_t* slot_ptr;
+  int64_t n_slots;
+  const uint8_t* shared_rec;
+  const float* sh_gate;
+  RecOffs o;
+  float* h_buf;
+  float* o_buf;
+  float* out;
+  uint16_t* y;
+  int32_t* err;
+};
+
+SSB_DEV void load_x16(const DecodeArgs& a, int64_t r, int u, float* x16) {
+  if (a.x_f32) {
+    const float4* p = reinterpret_cast<const float4*>((const float*)a.x + r * a.H + (int64_t)u * 16);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 v = p[q];
+      x16[4 * q] = v.x;
+      x16[4 * q + 1] = v.y;
+      x16[4 * q + 2] = v.z;
+      x16[4 * q + 3] = v.w;
+    }
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>((const uint16_t*)a.x + r * a.H + (int64_t)u * 16);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      uint4 v = p[q];
+      x16[8 * q + 0] = bf16_lo(v.x);
+      x16[8 * q + 1] = bf16_hi(v.x);
+      x16[8 * q + 2] = bf16_lo(v.y);
+      x16[8 * q + 3] = bf16_hi(v.y);
+      x16[8 * q + 4] = bf16_lo(v.z);
+      x16[8 * q + 5] = bf16_hi(v.z);
+      x16[8 * q + 6] = bf16_lo(v.w);
+      x16[8 * q + 7] = bf16_hi(v.w);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ gate/up
+template <int NUX>
+__global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up(DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ const uint8_t* s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t n_routed = a.R * a.topk;
+  const int64_t p = blockIdx.y;
+  const int n0 = blockIdx.x * GU_ROWS;
+  const int H = a.H, gs = a.gs;
+  const uint32_t wbytes = (uint32_t)GU_ROWS * H / 2, sbytes = (uint32_t)GU_ROWS * (H / gs) * 2;
+  uint8_t* gw = sm;
+  uint8_t* uw = gw + wbytes;
+  uint8_t* gsc = uw + wbytes;
+  uint8_t* gb = gsc + sbytes;
+  uint8_t* usc = gb + sbytes;
+  uint8_t* ub = usc + sbytes;
+  const bool is_shared = p >= n_routed;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](const uint8_t* base) {
+    mbar_expect_tx(&bar, 2 * wbytes + 4 * sbytes);
+    bulk_g2s(gw, base + a.o.gw + (int64_t)n0 * H / 2, wbytes, &bar);
+    bulk_g2s(uw, base + a.o.uw + (int64_t)n0 * H / 2, wbytes, &bar);
+    bulk_g2s(gsc, base + a.o.gsc + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+    bulk_g2s(gb, base + a.o.gb + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+    bulk_g2s(usc, base + a.o.usc + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+    bulk_g2s(ub, base + a.o.ub + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+  };
+  if (tid == 0 && is_shared) {  // the shared record is static: start its copies before the wait
+    s_base = a.shared_rec;
+    issue(a.shared_rec);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0 && !is_shared) {
+    const uint8_t* base = resolve_expert(a.ids[p], a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots, a.err);
+    s_base = base;
+    if (base) issue(base);
+  }
+  const int64_t r = is_shared ? p - n_routed : p / a.topk;
+  const int nunits = H / 16;
+  XUnit xu[NUX];
+#pragma unroll
+  for (int i = 0; i < NUX; ++i) {
+    int u = lane + 32 * i;
+    if (u < nunits) {
+      float x16[16];
+      load_x16(a, r, u, x16);
+      xunit_from_f32(xu[i], x16);
+    } else {
+      xunit_zero(xu[i]);
+    }
+  }
+  __syncthreads();
+  const uint8_t* base = s_base;
+  float* hrow = a.h_buf + p * a.I;
+  if (!base) {
+    for (int j = tid; j < GU_ROWS; j += blockDim.x) hrow[n0 + j] = 0.f;
+    return;
+  }
+  if (!mbar_wait(&bar, 0, SSB_WAIT_LIMIT)) {
+    set_err(a.err, SSB_ERR_TIMEOUT);
+    mbar_wait(&bar, 0, SSB_WAIT_LIMIT);  // let the copies land before the CTA's shared memory is released
+    return;
+  }
+  const int ng = H / gs;
+  for (int j = warp; j < GU_ROWS; j += GU_WARPS) {
+    const uint2* gwr = reinterpret_cast<const uint2*>(gw + (size_t)j * H / 2);
+    const uint2* uwr = reinterpret_cast<const uint2*>(uw + (size_t)j * H / 2);
+    const uint16_t* gsr = reinterpret_cast<const uint16_t*>(gsc) + j * ng;
+    const uint16_t* gbr = reinterpret_cast<const uint16_t*>(gb) + j * ng;
+    const uint16_t* usr = reinterpret_cast<const uint16_t*>(usc) + j * ng;
+    const uint16_t* ubr = reinterpret_cast<const uint16_t*>(ub) + j * ng;
+    float ga = 0.f, ua = 0.f;
+#pragma unroll
+    for (int i = 0; i < NUX; ++i) {
+      int u = lane + 32 * i;
+      if (u < nunits) {
+        int g = (u * 16) / gs;
+        ga = unit_dot(gwr[u], bf16_bits(gsr[g]), bf16_bits(gbr[g]), xu[i], ga);
+        ua = unit_dot(uwr[u], bf16_bits(usr[g]), bf16_bits(ubr[g]), xu[i], ua);
+      }
+    }
+    ga = warp_sum(ga);
+    ua = warp_sum(ua);
+    if (lane == 0) hrow[n0 + j] = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u, as kernels/moe_gemv_affine.py:76
+  }
+}
+
+// ------------------------------------------------------------------ down + rank-order combine (+ shared)
+template <int NUI>
+__global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ const uint8_t* s_base[33];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t r = blockIdx.y;
+  const int m0 = blockIdx.x * DN_ROWS;
+  const int I = a.I, gs = a.gs, H = a.H;
+  const bool has_sh = a.shared_rec != nullptr;
+  const int nexp = a.topk + (has_sh ? 1 : 0);
+  const uint32_t wbytes = (uint32_t)DN_ROWS * I / 2, sbytes = (uint32_t)DN_ROWS * (I / gs) * 2;
+  const uint32_t ebytes = wbytes + 2 * sbytes;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    // Expert ids were written before the previous (gate_up) grid started; every grid here triggers its
+    // dependents only after its own wait, so they are complete and visible now (read through L2).
+    uint32_t total = 0;
+    for (int j = 0; j < nexp; ++j) {
+      const uint8_t* base;
+      if (j < a.topk)
+        base = resolve_expert(ld_cg_i32(a.ids + r * a.topk + j), a.layer, a.map, a.map_len, a.slot_ptr,
+                              a.n_slots, nullptr);
+      else
+        base = a.shared_rec;
+      s_base[j] = base;
+      if (base) total += ebytes;
+    }
+    mbar_expect_tx(&bar, total);
+    for (int j = 0; j < nexp; ++j) {
+      const uint8_t* base = s_base[j];
+      if (!base) continue;
+      uint8_t* dst = sm + (size_t)j * ebytes;
+      bulk_g2s(dst, base + a.o.dw + (int64_t)m0 * I / 2, wbytes, &bar);
+      bulk_g2s(dst + wbytes, base + a.o.dsc + (int64_t)m0 * (I / gs) * 2, sbytes, &bar);
+      bulk_g2s(dst + wbytes + sbytes, base + a.o.db + (int64_t)m0 * (I / gs) * 2, sbytes, &bar);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
+  if (!ok) {
+    if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
+    mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
+    return;
+  }
+  constexpr int RPW = DN_ROWS / DN_WARPS;
+  const int nunits = I / 16, ng = I / gs;
+  float acc[RPW], shv[RPW];
+#pragma unroll
+  for (int q = 0; q < RPW; ++q) acc[q] = shv[q] = 0.f;
+  for (int j = 0; j < nexp; ++j) {
+    const uint8_t* base = s_base[j];
+    const bool shared_j = j >= a.topk;
+    const int64_t pair = shared_j ? a.R * a.topk + r : r * a.topk + j;
+    float wt = 0.f;
+    if (base) wt = shared_j ? a.sh_gate[r] : a.wts[r * a.topk + j];
+    XUnit hu[NUI];
+    const float* hrow = a.h_buf + pair * I;
+#pragma unroll
+    for (int i = 0; i < NUI; ++i) {
+      int u = lane + 32 * i;
+      if (u < nunits && base) {
+        float h16[16];
+        const float4* hp = reinterpret_cast<const float4*>(hrow + u * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float4 v = hp[q];
+          h16[4 * q] = v.x;
+          h16[4 * q + 1] = v.y;
+          h16[4 * q + 2] = v.z;
+          h16[4 * q + 3] = v.w;
+        }
+        xunit_from_f32(hu[i], h16);
+      } else {
+        xunit_zero(hu[i]);
+      }
+    }
+    const uint8_t* ew = sm + (size_t)j * ebytes;
+#pragma unroll
+    for (int q = 0; q < RPW; ++q) {
+      const int row = warp * RPW + q;
+      float d = 0.f;
+      if (base) {
+        const uint2* wr = reinterpret_cast<const uint2*>(ew + (size_t)row * I / 2);
+        const uint16_t* sr = reinterpret_cast<const uint16_t*>(ew + wbytes) + row * ng;
+        const uint16_t* br = reinterpret_cast<const uint16_t*>(ew + wbytes + sbytes) + row * ng;
+#pragma unroll
+        for (int i = 0; i < NUI; ++i) {
+          int u = lane + 32 * i;
+          if (u < nunits) {
+            int g = (u * 16) / gs;
+            d = unit_dot(wr[u], bf16_bits(sr[g]), bf16_bits(br[g]), hu[i], d);
+          }
+        }
+        d = warp_sum(d);
+      }
+      const float o = d * wt;   // acc * w, kernels/moe_gemv_affine.py:96-97
+      if (shared_j) {
+        shv[q] = o;
+      } else {
+        acc[q] = (j == 0) ? o : acc[q] + o;   // rank order, kernels/moe_gemv_affine.py:108-109
+        if (lane == 0 && a.o_buf) a.o_buf[pair * H + m0 + row] = o;
+      }
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < RPW; ++q) {
+      const int m = m0 + warp * RPW + q;
+      a.out[r * H + m] = acc[q];
+      if (a.y) a.y[r * H + m] = f32_to_bf16(round_bf16(acc[q]) + round_bf16(shv[q]));
+    }
+  }
+}
+
+template <int N>
+struct Disp {};
+
+int launch_decode(DecodeArgs a, cudaStream_t st, bool pdl) {
+  const int nux = (a.H / 16 + 31) / 32;
+  const int nui = (a.I / 16 + 31) / 32;
+  const int64_t pairs = a.R * a.topk + (a.shared_rec ? a.R : 0);
+  const size_t gu_smem = (size_t)2 * GU_ROWS * a.H / 2 + (size_t)4 * GU_ROWS * (a.H / a.gs) * 2;
+  const size_t dn_smem = (size_t)(a.topk + (a.shared_rec ? 1 : 0)) *
+                         ((size_t)DN_ROWS * a.I / 2 + (size_t)2 * DN_ROWS * (a.I / a.gs) * 2);
+  if (gu_smem > 200 * 1024 || dn_smem > 200 * 1024) return SSB_EUNSUPPORTED;
+  if (pairs > 65535 || a.R > 65535) return SSB_EUNSUPPORTED;
+  void (*gu)(DecodeArgs) = nullptr;
+  void (*dn)(DecodeArgs) = nullptr;
+  switch (nux) {
+    case 1: gu = k_dec_gate_up<1>; break;
+    case 2: gu = k_dec_gate_up<2>; break;
+    case 3: gu = k_dec_gate_up<3>; break;
+    case 4: gu = k_dec_gate_up<4>; break;
+    case 5: gu = k_dec_gate_up<5>; break;
+    case 6: gu = k_dec_gate_up<6>; break;
+    case 8: gu = k_dec_gate_up<8>; break;
+    default: return SSB_EUNSUPPORTED;
+  }
+  switch (nui) {
+    case 1: dn = k_dec_down<1>; break;
+    case 2: dn = k_dec_down<2>; break;
+    case 3: dn = k_dec_down<3>; break;
+    case 4: dn = k_dec_down<4>; break;
+    default: return SSB_EUNSUPPORTED;
+  }
+  cudaFuncSetAttribute(gu, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gu_smem);
+  cudaFuncSetAttribute(dn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem);
+  ssb_note_smem("moe_gate_up", gu, gu_smem);
+  ssb_note_smem("moe_down", dn, dn_smem);
+  int rc = ssb_launch(gu, dim3(a.I / GU_ROWS, (unsigned)pairs), dim3(GU_WARPS * 32), gu_smem, st, pdl, a);
+  if (rc) return rc;
+  return ssb_launch(dn, dim3(a.H / DN_ROWS, (unsigned)a.R), dim3(DN_WARPS * 32), dn_smem, st, true, a);
+}
+
+int check_shape(int64_t rows, int topk, int hidden, int inter) {
+  if (rows < 0 || topk < 1 || topk > 32) return SSB_EINVAL;
+  if (hidden % 512 || hidden <= 0 || hidden > 8192) return SSB_EUNSUPPORTED;
+  if (inter % GU_ROWS || inter <= 0 || inter > 2048 || inter % 64) return SSB_EUNSUPPORTED;
+  if (hidden % DN_ROWS) return SSB_EUNSUPPORTED;
+  return SSB_OK;
+}
+
+}  // namespace
+
+extern "C" int ssb_moe_decode(const void* x, int32_t x_dtype, const int32_t* expert_ids, const float* weights,
+                              int64_t rows, int32_t topk, int32_t hidden, int32_t inter, int32_t layer,
+                              const int32_t* map_t, int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots,
+                              float* h_buf, float* o_buf, float* out, int32_t* err, void* stream) {
+  int rc = check_shape(rows, topk, hidden, inter);
+  if (rc) return rc;
+  SSB_CHECK_ARG(x_dtype == SSB_BF16 || x_dtype == SSB_F32);
+  SSB_CHECK_ARG(layer >= 0 && map_len >= 0 && n_slots >= 0);
+  if (rows == 0) return SSB_OK;
+  SSB_CHECK_ARG(x && expert_ids && weights && map_t && slot_ptr_t && h_buf && out);
+  DecodeArgs a{};
+  a.x = x;
+  a.x_f32 = x_dtype == SSB_F32;
+  a.ids = expert_ids;
+  a.wts = weights;
+  a.R = rows;
+  a.topk = topk;
+  a.H = hidden;
+  a.I = inter;
+  a.gs = 64;
+  a.layer = layer;
+  a.map = map_t;
+  a.map_len = map_len;
+  a.slot_ptr = slot_ptr_t;
+  a.n_slots = n_slots;
+  a.o = rec_offsets(hidden, inter, 64);
+  a.h_buf = h_buf;
+  a.o_buf = o_buf;
+  a.out = out;
+  a.err = err;
+  return launch_decode(a, (cudaStream_t)stream, true);
+}
+
+extern "C" int ssb_moe_decode_layer(const uint16_t* x, const int32_t* expert_ids, const float* weights, int64_t rows,
+                                    int32_t topk, int32_t hidden, int32_t inter, int32_t layer, const int32_t* map_t,
+                                    int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots,
+                                    const void* shared_record, const float* sh_gate, float* h_buf, float* o_buf,
+                                    float* out, uint16_t* y, int32_t flags, int32_t* err, void* stream) {
+  int rc = check_shape(rows, topk, hidden, inter);
+  if (rc) return rc;
+  SSB_CHECK_ARG(layer >= 0 && map_len >= 0 && n_slots >= 0);
+  if (rows == 0) return SSB_OK;
+  SSB_CHECK_ARG(x && expert_ids && weights && map_t && slot_ptr_t && h_buf && out && shared_record && sh_gate && y);
+  SSB_CHECK_ARG(((uintptr_t)shared_record & 15) == 0);
+  DecodeArgs a{};
+  a.x = x;
+  a.x_f32 = 0;
+  a.ids = expert_ids;
+  a.wts = weights;
+  a.R = rows;
+  a.topk = topk;
+  a.H = hidden;
+  a.I = inter;
+  a.gs = 64;
+  a.layer = layer;
+  a.map = map_t;
+  a.map_len = map_len;
+  a.slot_ptr = slot_ptr_t;
+  a.n_slots = n_slots;
+  a.shared_rec = (const uint8_t*)shared_record;
+  a.sh_gate = sh_gate;
+  a.o = rec_offsets(hidden, inter, 64);
+  a.h_buf = h_buf;
+  a.o_buf = o_buf;
+  a.out = out;
+  a.y = y;
+  a.err = err;
+  return launch_decode(a, (cudaStream_t)stream, (flags & SSB_DECODE_PDL) != 0);
+}

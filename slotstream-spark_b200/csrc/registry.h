@@ -1,0 +1,15 @@
+// Per-kernel shared-memory bookkeeping behind ssb_kernel_smem (the reference's SHARED_BYTES).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+void ssb_note_smem_bytes(const char* name, int bytes);
+
+template <typename K>
+static inline void ssb_note_smem(const char* name, K kern, size_t dyn) {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, (const void*)kern) == cudaSuccess)
+    ssb_note_smem_bytes(name, (int)(a.sharedSizeBytes + dyn));
+  else
+    (void)cudaGetLastError();
+}

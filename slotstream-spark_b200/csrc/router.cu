@@ -1,0 +1,351 @@
+// Router: logits GEMV, fused softmax + stable top-k + renormalise (warp per token), and the generic
+// stable top-k of the reference's topk_stable API.
+//
+// Selection rule (slotstream_spark/kernels/topk_stable.py:1-13): scores map to order-preserving uint32
+// keys (positive: flip the sign bit; negative: bitwise not; NaN: 0, the lowest), larger keys first,
+// ties to the lower index. Here each candidate becomes the 64-bit composite (key << 32) | ~index, so
+// "largest composite first" is exactly that order and every composite is distinct.
+#include <cub/block/block_scan.cuh>
+
+#include "common.cuh"
+#include "registry.h"
+
+namespace {
+
+SSB_DEV uint32_t order_key(float f) {
+  uint32_t b = __float_as_uint(f);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) return 0u;  // NaN: lowest
+  return (b & 0x80000000u) ? ~b : (b ^ 0x80000000u);
+}
+SSB_DEV unsigned long long composite(uint32_t key, uint32_t idx) {
+  return ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+
+// ------------------------------------------------------------------ logits
+// Warp per weight row, the row held in registers (lane l owns 16-byte chunks l, l+32, ...); a CTA covers
+// 4 rows and a tile of up to TT tokens staged in shared memory. The sum order of one logit is fixed by
+// (hidden) alone: lane-sequential over its chunks, then a butterfly -- the same for any token count.
+constexpr int RL_WARPS = 4;
+constexpr int RL_TT = 8;
+constexpr int RL_MAXC = 16;  // chunks of 8 bf16 per lane: hidden <= 4096
+
+__global__ void __launch_bounds__(RL_WARPS * 32) k_router_logits(const uint16_t* __restrict__ x,
+                                                                  const uint16_t* __restrict__ w,
+                                                                  const uint16_t* __restrict__ w_extra, int64_t tokens,
+                                                                  int hidden, int n_rows, int ld,
+                                                                  float* __restrict__ logits) {
+  extern __shared__ __align__(16) uint4 xs[];  // [RL_TT][hidden / 8]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n_total = n_rows + (w_extra ? 1 : 0);
+  const int row = blockIdx.x * RL_WARPS + warp;
+  const int nch = hidden >> 3;       // 16-byte chunks per row
+  const int cpl = nch >> 5;          // chunks per lane (hidden % 256 == 0)
+  const int64_t t0 = (int64_t)blockIdx.y * RL_TT;
+  const int tt = (int)(tokens - t0 < RL_TT ? tokens - t0 : RL_TT);
+
+  uint4 wr[RL_MAXC];
+  const uint16_t* wrow = nullptr;
+  if (row < n_total) wrow = (row < n_rows) ? w + (int64_t)row * hidden : w_extra;
+  // weights are static: prefetch them before waiting for the producer of x
+#pragma unroll
+  for (int i = 0; i < RL_MAXC; ++i)
+    if (i < cpl && wrow) wr[i] = ld_stream_u4(wrow + (size_t)(lane + 32 * i) * 8);
+  pdl_wait();
+  for (int c = threadIdx.x; c < tt * nch; c += blockDim.x) {
+    int t = c / nch, j = c - t * nch;
+    xs[t * nch + j] = *reinterpret_cast<const uint4*>(x + (t0 + t) * hidden + (int64_t)j * 8);
+  }
+  __syncthreads();
+  pdl_trigger();
+  if (!wrow) return;
+  for (int t = 0; t < tt; ++t) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < RL_MAXC; ++i) {
+      if (i < cpl) {
+        uint4 xv = xs[t * nch + lane + 32 * i];
+        uint4 wv = wr[i];
+        acc = fmaf(bf16_lo(wv.x), bf16_lo(xv.x), acc);
+        acc = fmaf(bf16_hi(wv.x), bf16_hi(xv.x), acc);
+        acc = fmaf(bf16_lo(wv.y), bf16_lo(xv.y), acc);
+        acc = fmaf(bf16_hi(wv.y), bf16_hi(xv.y), acc);
+        acc = fmaf(bf16_lo(wv.z), bf16_lo(xv.z), acc);
+        acc = fmaf(bf16_hi(wv.z), bf16_hi(xv.z), acc);
+        acc = fmaf(bf16_lo(wv.w), bf16_lo(xv.w), acc);
+        acc = fmaf(bf16_hi(wv.w), bf16_hi(xv.w), acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[(t0 + t) * ld + row] = acc;
+  }
+}
+
+// ------------------------------------------------------------------ select (softmax + top-k + renorm)
+constexpr int RS_WARPS = 4;
+constexpr int RS_MAXE = 32;  // experts per lane: experts <= 1024
+
+__global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __restrict__ logits, int ld,
+                                                                  int64_t tokens, int experts, int k,
+                                                                  const float* __restrict__ bias, int flags,
+                                                                  int32_t* __restrict__ out_idx,
+                                                                  float* __restrict__ out_w,
+                                                                  float* __restrict__ out_probs,
+                                                                  float* __restrict__ out_sh_gate) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * RS_WARPS + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  const float* lrow = logits + t * ld;
+  float v[RS_MAXE];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < RS_MAXE; ++i) {
+    int e = lane + 32 * i;
+    float l = -INFINITY;
+    if (e < experts) {
+      l = __ldcg(lrow + e);
+      if (bias) l = l + bias[e];
+      if (flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
+      m = fmaxf(m, l);
+    }
+    v[i] = l;
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < RS_MAXE; ++i) {
+    int e = lane + 32 * i;
+    float ex = 0.f;
+    if (e < experts) ex = expf(v[i] - m);
+    v[i] = ex;
+    s += ex;
+  }
+  s = warp_sum(s);
+  unsigned long long c[RS_MAXE];
+#pragma unroll
+  for (int i = 0; i < RS_MAXE; ++i) {
+    int e = lane + 32 * i;
+    float p = v[i] / s;
+    v[i] = p;
+    c[i] = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
+    if (out_probs && e < experts) out_probs[t * experts + e] = p;
+  }
+  // k rounds of warp arg-max; round j's winner is the j-th output (value desc, index asc)
+  int my_idx = -1;
+  float my_p = 0.f;
+  for (int j = 0; j < k; ++j) {
+    unsigned long long lm = 0ull;
+#pragma unroll
+    for (int i = 0; i < RS_MAXE; ++i) lm = c[i] > lm ? c[i] : lm;
+    unsigned long long g = warp_max_u64(lm);
+    uint32_t e = 0xFFFFFFFFu - (uint32_t)(g & 0xFFFFFFFFull);
+    float p = 0.f;
+    if ((int)(e & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < RS_MAXE; ++i)
+        if (lane + 32 * i == (int)e) {
+          p = v[i];
+          c[i] = 0ull;
+        }
+    }
+    p = __shfl_sync(0xFFFFFFFFu, p, e & 31);
+    if (lane == j) {
+      my_idx = (int)e;
+      my_p = p;
+    }
+  }
+  float sum = 0.f;  // sequential in rank order
+  for (int j = 0; j < k; ++j) sum += __shfl_sync(0xFFFFFFFFu, my_p, j);
+  if (lane < k) {
+    out_idx[t * k + lane] = my_idx;
+    out_w[t * k + lane] = my_p / sum;
+  }
+  if ((flags & SSB_ROUTER_SHARED_GATE) && lane == 0) {
+    float gl = __ldcg(lrow + experts);
+    out_sh_gate[t] = 1.f / (1.f + expf(-gl));
+  }
+}
+
+// ------------------------------------------------------------------ generic stable top-k
+constexpr int TK_THREADS = 512;
+constexpr int TK_ITEMS = 4;
+
+__global__ void __launch_bounds__(TK_THREADS) k_topk_stable(const float* __restrict__ scores,
+                                                             const int32_t* __restrict__ n_valid, int n, int k,
+                                                             int32_t* __restrict__ out_idx,
+                                                             float* __restrict__ out_val) {
+  using Scan = cub::BlockScan<int, TK_THREADS>;
+  __shared__ typename Scan::TempStorage scan_tmp;
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_digit, s_kleft;
+  __shared__ int s_base_sel, s_base_eq;
+  __shared__ unsigned long long cand[16];
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  const float* x = scores + row * n;
+  int nv = n;
+  if (n_valid) nv = max(0, min(n_valid[row], n));
+  const int tid = threadIdx.x;
+  const bool take_all = nv <= k;
+
+  uint32_t prefix = 0, pmask = 0, kleft = (uint32_t)k;
+  if (!take_all) {
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      if (tid < 256) hist[tid] = 0;
+      __syncthreads();
+      for (int i = tid; i < nv; i += TK_THREADS) {
+        uint32_t key = order_key(x[i]);
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t cum = 0, d = 0, kl = kleft;
+        for (int b = 255; b >= 0; --b) {
+          uint32_t h = hist[b];
+          if (cum + h >= kl) {
+            d = (uint32_t)b;
+            kl -= cum;
+            break;
+          }
+          cum += h;
+        }
+        s_digit = d;
+        s_kleft = kl;
+      }
+      __syncthreads();
+      prefix |= s_digit << shift;
+      pmask |= 255u << shift;
+      kleft = s_kleft;
+      __syncthreads();
+    }
+  }
+  const uint32_t thr = prefix;   // the k-th largest key; `kleft` entries equal to it are taken, lowest index first
+  if (tid == 0) {
+    s_base_sel = 0;
+    s_base_eq = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < nv; base += TK_THREADS * TK_ITEMS) {
+    int gt[TK_ITEMS], eq[TK_ITEMS];
+    int n_eq = 0;
+#pragma unroll
+    for (int it = 0; it < TK_ITEMS; ++it) {
+      int i = base + tid * TK_ITEMS + it;
+      gt[it] = eq[it] = 0;
+      if (i < nv) {
+        if (take_all) {
+          gt[it] = 1;
+        } else {
+          uint32_t key = order_key(x[i]);
+          gt[it] = key > thr;
+          eq[it] = key == thr;
+        }
+      }
+      n_eq += eq[it];
+    }
+    int eq_before, eq_total;
+    Scan(scan_tmp).ExclusiveSum(n_eq, eq_before, eq_total);
+    __syncthreads();
+    int eq_run = s_base_eq + eq_before;
+    int sel[TK_ITEMS], n_sel = 0;
+#pragma unroll
+    for (int it = 0; it < TK_ITEMS; ++it) {
+      sel[it] = gt[it];
+      if (eq[it]) {
+        sel[it] = eq_run < (int)kleft;
+        ++eq_run;
+      }
+      n_sel += sel[it];
+    }
+    int sel_before, sel_total;
+    Scan(scan_tmp).ExclusiveSum(n_sel, sel_before, sel_total);
+    int pos = s_base_sel + sel_before;
+#pragma unroll
+    for (int it = 0; it < TK_ITEMS; ++it) {
+      if (!sel[it]) continue;
+      int i = base + tid * TK_ITEMS + it;
+      if (k <= 16) {
+        cand[pos] = composite(order_key(x[i]), (uint32_t)i);
+      } else {
+        out_idx[row * k + pos] = i;
+        if (out_val) out_val[row * k + pos] = x[i];
+      }
+      ++pos;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      s_base_sel += sel_total;
+      s_base_eq += eq_total;
+    }
+    __syncthreads();
+  }
+  const int count = s_base_sel;
+  if (k <= 16) {
+    if (tid == 0) {
+      for (int a = 1; a < count; ++a) {  // insertion sort, descending composite
+        unsigned long long v = cand[a];
+        int b = a - 1;
+        while (b >= 0 && cand[b] < v) {
+          cand[b + 1] = cand[b];
+          --b;
+        }
+        cand[b + 1] = v;
+      }
+      for (int j = 0; j < count; ++j) {
+        int i = (int)(0xFFFFFFFFu - (uint32_t)(cand[j] & 0xFFFFFFFFull));
+        out_idx[row * k + j] = i;
+        if (out_val) out_val[row * k + j] = x[i];
+      }
+    }
+  }
+  for (int j = count + tid; j < k; j += TK_THREADS) {
+    out_idx[row * k + j] = -1;
+    if (out_val) out_val[row * k + j] = -INFINITY;
+  }
+}
+
+}  // namespace
+
+extern "C" int ssb_router_logits(const uint16_t* x, const uint16_t* w, const uint16_t* w_extra, int64_t tokens,
+                                 int32_t hidden, int32_t n_rows, int32_t ld, float* logits, void* stream) {
+  SSB_CHECK_ARG(x && w && logits && tokens >= 0 && n_rows >= 1);
+  if (hidden % 256 || hidden <= 0 || hidden > 4096) return SSB_EUNSUPPORTED;
+  SSB_CHECK_ARG(ld >= n_rows + (w_extra ? 1 : 0));
+  if (tokens == 0) return SSB_OK;
+  const int n_total = n_rows + (w_extra ? 1 : 0);
+  dim3 grid((n_total + RL_WARPS - 1) / RL_WARPS, (unsigned)((tokens + RL_TT - 1) / RL_TT));
+  SSB_CHECK_ARG(grid.y <= 65535u);
+  size_t smem = (size_t)RL_TT * hidden * 2;
+  ssb_note_smem("router_logits", k_router_logits, smem);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  return ssb_launch(k_router_logits, grid, dim3(RL_WARPS * 32), smem, (cudaStream_t)stream, true, x, w, w_extra,
+                    tokens, hidden, n_rows, ld, logits);
+}
+
+extern "C" int ssb_router_select(const float* logits, int32_t ld, int64_t tokens, int32_t experts, int32_t k,
+                                 const float* bias, int32_t flags, int32_t* out_idx, float* out_w, float* out_probs,
+                                 float* out_sh_gate, void* stream) {
+  SSB_CHECK_ARG(logits && out_idx && out_w && tokens >= 0);
+  SSB_CHECK_ARG(experts >= 1 && experts <= 32 * RS_MAXE && k >= 1 && k <= 32 && k <= experts);
+  SSB_CHECK_ARG(ld >= experts + ((flags & SSB_ROUTER_SHARED_GATE) ? 1 : 0));
+  SSB_CHECK_ARG(!(flags & SSB_ROUTER_SHARED_GATE) || out_sh_gate);
+  if (tokens == 0) return SSB_OK;
+  dim3 grid((unsigned)((tokens + RS_WARPS - 1) / RS_WARPS));
+  ssb_note_smem("router_select", k_router_select, 0);
+  return ssb_launch(k_router_select, grid, dim3(RS_WARPS * 32), 0, (cudaStream_t)stream, true, logits, ld, tokens,
+                    experts, k, bias, flags, out_idx, out_w, out_probs, out_sh_gate);
+}
+
+extern "C" int ssb_topk_stable(const float* scores, const int32_t* n_valid, int64_t rows, int32_t n, int32_t k,
+                               int32_t* out_idx, float* out_val, void* stream) {
+  SSB_CHECK_ARG(scores && out_idx && rows >= 0 && n >= 1 && n <= 65536 && k >= 1 && k <= n);
+  if (rows == 0) return SSB_OK;
+  SSB_CHECK_ARG(rows <= 2147483647LL);
+  ssb_note_smem("topk_stable", k_topk_stable, 0);
+  return ssb_launch(k_topk_stable, dim3((unsigned)rows), dim3(TK_THREADS), 0, (cudaStream_t)stream, true, scores,
+                    n_valid, n, k, out_idx, out_val);
+}

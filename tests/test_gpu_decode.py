@@ -1,0 +1,214 @@
+"""Decode grouped GEMV (moe_decode) and the fused decode layer against the fp64 oracle (GPU).
+
+Mirrors the reference's tests/t0/test_moe_gemv_affine.py: fp64 reference within 1e-4 (:91-100), slot-placement
+bitwise invariance (:103-116), row invariance with duplicate experts (:119-130), config errors (:133-157),
+plus error bits for unmapped experts and the shape-generic record layout.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from gpu_helpers import DevicePool, bf16_tensor, record, to_np_bf16_bits
+from oracle import moe_oracle as O
+from slotstream_b200 import synth
+from slotstream_b200.records import BASELINE_LAYOUT, REFERENCE_LAYOUT
+
+pytestmark = pytest.mark.gpu
+LAYER = 3
+SEED = 100
+
+
+def _experts(layout, n):
+    return [record(layout, SEED, LAYER, e) for e in range(n)]
+
+
+def _run(pool, x, ids, w, topk=10, cfg=None, err=None):
+    from slotstream_b200.kernels.moe_gemv_affine import moe_decode
+    r = x.shape[0]
+    lay = pool.layout
+    h = torch.empty(r, topk, lay.inter, device="cuda")
+    o = torch.empty(r, topk, lay.hidden, device="cuda")
+    out = torch.empty(r, lay.hidden, device="cuda")
+    moe_decode(x, ids, w, pool.layer, pool.map, pool.slot_ptr, h, o, out, cfg=cfg, err=err)
+    torch.cuda.synchronize()
+    return out, o
+
+
+def _inputs(layout, r, seed, n_experts, dtype=torch.bfloat16):
+    rng = np.random.default_rng(seed)
+    xb = synth.activations(seed, r, layout.hidden)
+    x = bf16_tensor(xb)
+    if dtype == torch.float32:
+        x = x.float() + torch.from_numpy(rng.standard_normal((r, layout.hidden)).astype(np.float32) * 1e-3).cuda()
+    ids = np.stack([rng.permutation(n_experts)[:10] for _ in range(r)]).astype(np.int32)
+    w = rng.dirichlet(np.ones(10), size=r).astype(np.float32)
+    return x, torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda()
+
+
+def _oracle(layout, recs, x, ids, w):
+    dense = {}
+
+    def ex(e):
+        if e not in dense:
+            dense[e] = O.record_dense(layout, recs[e])
+        return dense[e]
+    return O.moe_decode(layout, x.float().cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy(), ex)
+
+
+@pytest.mark.parametrize("layout", [BASELINE_LAYOUT, REFERENCE_LAYOUT], ids=["2048x512", "2560x640"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+def test_matches_fp64_oracle(layout, dtype):
+    recs = _experts(layout, 16)
+    slots = [(i * 5 + 2) % 16 for i in range(16)]
+    pool = DevicePool(layout, recs, range(16), slots, 16, LAYER)
+    x, ids, w = _inputs(layout, 3, 1, 16, dtype)
+    out, o = _run(pool, x, ids, w)
+    ref = _oracle(layout, recs, x, ids, w)
+    assert O.rel_l2(out.cpu().numpy(), ref) <= 1e-4
+    # o_buf holds the weighted per-rank rows, and out is their rank-order sum (bitwise)
+    o_np = o.cpu().numpy()
+    acc = o_np[:, 0].copy()
+    for k in range(1, 10):
+        acc = (acc + o_np[:, k]).astype(np.float32)
+    assert np.array_equal(acc.view(np.uint32), out.cpu().numpy().view(np.uint32))
+
+
+def test_reference_shape_golden():
+    """2560/640 against the reference test helper's fp64 output (decode_ref.npz)."""
+    g = np.load(GOLDEN / "decode_ref.npz")
+    lay = REFERENCE_LAYOUT
+    n = int(g["n_exp"])
+    recs = [synth.expert_record(lay, int(g["seed"]), 0, e) for e in range(n)]
+    pool = DevicePool(lay, recs, range(n), list(range(n)), n, layer=0)
+    out, _ = _run(pool, bf16_tensor(g["x_bits"]), torch.from_numpy(g["ids"]).cuda(), torch.from_numpy(g["w"]).cuda())
+    assert O.rel_l2(out.cpu().numpy(), g["out"]) <= 1e-4
+
+
+@pytest.mark.parametrize("n_slots", [13, 64])
+def test_placement_bitwise(n_slots):
+    lay = BASELINE_LAYOUT
+    recs = _experts(lay, 13)
+    x, ids, w = _inputs(lay, 2, 2, 13)
+    base = DevicePool(lay, recs, range(13), list(range(13)), 13, LAYER)
+    ref, _ = _run(base, x, ids, w)
+    moved = [(i * 7 + 3) % n_slots for i in range(13)]
+    assert len(set(moved)) == 13
+    pool = DevicePool(lay, recs, range(13), moved, n_slots, LAYER, pad_bytes=4096)
+    out, _ = _run(pool, x, ids, w)
+    assert torch.equal(out, ref)
+
+
+def test_row_invariance_and_duplicates():
+    lay = BASELINE_LAYOUT
+    recs = _experts(lay, 16)
+    pool = DevicePool(lay, recs, range(16), list(range(16)), 16, LAYER)
+    x, ids, w = _inputs(lay, 3, 3, 16)
+    ids[1] = ids[0]
+    ids[2, :5] = ids[0, :5]
+    out, _ = _run(pool, x, ids, w)
+    for r in range(3):
+        one, _ = _run(pool, x[r:r + 1].contiguous(), ids[r:r + 1].contiguous(), w[r:r + 1].contiguous())
+        assert torch.equal(one[0], out[r])
+
+
+def test_config_errors():
+    lay = BASELINE_LAYOUT
+    recs = _experts(lay, 16)
+    pool = DevicePool(lay, recs, range(16), list(range(16)), 16, LAYER)
+    x, ids, w = _inputs(lay, 1, 4, 16)
+    with pytest.raises(ValueError):
+        _run(pool, x, ids, w, cfg={"bn": 4, "br": 32, "bk": 96, "bkd": 128, "num_warps": 4})
+    with pytest.raises(ValueError):
+        _run(pool, x, ids.to(torch.int64), w)
+
+
+def test_unmapped_expert_sets_error_and_contributes_zero():
+    lay = BASELINE_LAYOUT
+    recs = _experts(lay, 16)
+    pool = DevicePool(lay, recs, range(16), list(range(16)), 16, LAYER)
+    x, ids, w = _inputs(lay, 1, 6, 16)
+    bad = ids.clone()
+    bad[0, 3] = 300           # not in the map
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out, _ = _run(pool, x, bad, w, err=err)
+    assert int(err.item()) & 2
+    w2 = w.clone()
+    w2[0, 3] = 0.0
+    ref = _oracle(lay, recs, x, ids, w2)
+    assert O.rel_l2(out.cpu().numpy(), ref) <= 1e-4
+
+
+# ------------------------------------------------------------------ fused decode layer
+@pytest.fixture(scope="module")
+def layer_world():
+    """BASELINE config-[0]: 512 experts of layer 0 (seed 0), shared expert = record index 512."""
+    lay = BASELINE_LAYOUT
+    recs = [record(lay, 0, 0, e) for e in range(513)]
+    pool = DevicePool(lay, recs[:512], range(512), list(range(512)), 512, layer=0)
+    shared = torch.from_numpy(recs[512]).cuda()
+    return lay, recs, pool, shared
+
+
+def test_decode_layer_matches_reference_moe_ref(layer_world):
+    """Routed + shared output of the fused layer vs the reference's moe_ref (fp32 mode, moe_ref.npz)."""
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    lay, recs, pool, shared = layer_world
+    g = np.load(GOLDEN / "moe_ref.npz")
+    T = int(g["T"])
+    x = synth.activations(0, T, lay.hidden)
+    rw = synth.router_weight(0, 512, lay.hidden, 0)
+    sg = synth.shared_gate_weight(0, lay.hidden, 0)
+    bufs = DecodeLayerBuffers(T, 10, lay.hidden, lay.inter)
+    y = moe_layer_decode(bf16_tensor(x), bf16_tensor(rw), 0, pool.map, pool.slot_ptr, shared, bf16_tensor(sg), 10, bufs)
+    torch.cuda.synchronize()
+    assert int(bufs.err.item()) == 0
+    ids_ref, _, logits = O.router(x, rw, 10)
+    O.ids_match(bufs.ids.cpu().numpy(), ids_ref, logits)
+    assert np.array_equal(ids_ref, g["ids"])
+    # fp32 golden: routed + sigmoid-gated shared, before any bf16 rounding
+    sh = bufs.out.cpu().numpy()        # routed only
+    got_y = O.bf16_to_f32(to_np_bf16_bits(y)).astype(np.float64)
+    ref = g["out"].astype(np.float64)
+    assert O.rel_l2(got_y, ref) <= 1e-2
+    assert np.max(np.abs(got_y - ref) - O.bf16_ulp(ref)) <= 2e-2
+    # routed part against the oracle in fp64
+    dense = {}
+
+    def ex(e):
+        if e not in dense:
+            dense[e] = O.record_dense(lay, recs[e])
+        return dense[e]
+    routed = O.moe_decode(lay, O.bf16_to_f32(x), bufs.ids.cpu().numpy(), bufs.w.cpu().numpy(), ex)
+    assert O.rel_l2(sh, routed) <= 1e-4
+
+
+def test_decode_layer_matches_bf16_oracle_and_is_row_invariant(layer_world):
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    lay, recs, pool, shared = layer_world
+    T = 16
+    x = synth.activations(11, T, lay.hidden)
+    rw = synth.router_weight(0, 512, lay.hidden, 0)
+    sg = synth.shared_gate_weight(0, lay.hidden, 0)
+    bias = synth.zipf_bias(512)
+    bufs = DecodeLayerBuffers(T, 10, lay.hidden, lay.inter)
+    args = (bf16_tensor(rw), 0, pool.map, pool.slot_ptr, shared, bf16_tensor(sg), 10)
+    y = moe_layer_decode(bf16_tensor(x), *args, bufs, bias=torch.from_numpy(bias).cuda()).clone()
+    torch.cuda.synchronize()
+    dense = {}
+
+    def ex(e):
+        if e not in dense:
+            dense[e] = O.record_dense(lay, recs[e])
+        return dense[e]
+    out_ref, routed, ids, w, logits = O.moe_layer(lay, x, rw, 10, ex, O.record_dense(lay, recs[512], np.float32), sg,
+                                                  bias=bias)
+    O.ids_match(bufs.ids.cpu().numpy(), ids, logits)
+    got = O.bf16_to_f32(to_np_bf16_bits(y)).astype(np.float64)
+    assert O.rel_l2(got, out_ref) <= 1e-2
+    assert np.max(np.abs(got - out_ref) - O.bf16_ulp(out_ref)) <= 2e-2
+    one = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
+    xt = bf16_tensor(x)
+    for r in (0, 7, 15):
+        y1 = moe_layer_decode(xt[r:r + 1].contiguous(), *args, one, bias=torch.from_numpy(bias).cuda())
+        assert torch.equal(y1[0], y[r])
