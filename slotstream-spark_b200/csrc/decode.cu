@@ -163,7 +163,15 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up(DecodeArgs a) {
     }
     ga = warp_sum(ga);
     ua = warp_sum(ua);
-    if (lane == 0) hrow[n0 + j] = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u, as kernels/moe_gemv_affine.py:76
+    if (lane == 0) {
+      if (is_shared) {
+        // shared expert: lin() returns bf16, silu and the product round to bf16 (model/layers.py:398-400)
+        const float gb = round_bf16(ga), ub = round_bf16(ua);
+        hrow[n0 + j] = round_bf16(round_bf16(gb / (1.f + expf(-gb))) * ub);
+      } else {
+        hrow[n0 + j] = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u in fp32, kernels/moe_gemv_affine.py:76
+      }
+    }
   }
 }
 
@@ -171,7 +179,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up(DecodeArgs a) {
 template <int NUI>
 __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bar, bar_h;
   __shared__ const uint8_t* s_base[33];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t r = blockIdx.y;
@@ -181,22 +189,24 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
   const int nexp = a.topk + (has_sh ? 1 : 0);
   const uint32_t wbytes = (uint32_t)DN_ROWS * I / 2, sbytes = (uint32_t)DN_ROWS * (I / gs) * 2;
   const uint32_t ebytes = wbytes + 2 * sbytes;
+  float* hsm = reinterpret_cast<float*>(sm + (size_t)nexp * ebytes);   // [nexp][I] staged activations
   if (tid == 0) {
     mbar_init(&bar, 1);
+    mbar_init(&bar_h, 1);
     fence_mbar_init();
-    // Expert ids were written before the previous (gate_up) grid started; every grid here triggers its
-    // dependents only after its own wait, so they are complete and visible now (read through L2).
+  }
+  // One thread per expert resolves its record. The expert ids were written before the previous (gate_up)
+  // grid started, and every grid here triggers its dependents only after its own wait, so they are complete
+  // and visible now (read through L2).
+  if (tid < nexp) {
+    s_base[tid] = tid < a.topk ? resolve_expert(ld_cg_i32(a.ids + r * a.topk + tid), a.layer, a.map, a.map_len,
+                                                a.slot_ptr, a.n_slots, nullptr)
+                               : a.shared_rec;
+  }
+  __syncthreads();
+  if (tid == 0) {
     uint32_t total = 0;
-    for (int j = 0; j < nexp; ++j) {
-      const uint8_t* base;
-      if (j < a.topk)
-        base = resolve_expert(ld_cg_i32(a.ids + r * a.topk + j), a.layer, a.map, a.map_len, a.slot_ptr,
-                              a.n_slots, nullptr);
-      else
-        base = a.shared_rec;
-      s_base[j] = base;
-      if (base) total += ebytes;
-    }
+    for (int j = 0; j < nexp; ++j) total += s_base[j] ? ebytes : 0u;
     mbar_expect_tx(&bar, total);
     for (int j = 0; j < nexp; ++j) {
       const uint8_t* base = s_base[j];
@@ -209,11 +219,21 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
   }
   pdl_wait();
   pdl_trigger();
-  __syncthreads();
-  const bool ok = mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
+  if (tid == 0) {   // h was written by the gate_up grid: stage it only after the wait
+    uint32_t total = 0;
+    for (int j = 0; j < nexp; ++j) total += s_base[j] ? (uint32_t)I * 4u : 0u;
+    mbar_expect_tx(&bar_h, total);
+    for (int j = 0; j < nexp; ++j) {
+      if (!s_base[j]) continue;
+      const int64_t pair = j >= a.topk ? a.R * a.topk + r : r * a.topk + j;
+      bulk_g2s(hsm + (size_t)j * I, a.h_buf + pair * I, (uint32_t)I * 4u, &bar_h);
+    }
+  }
+  const bool ok = mbar_wait(&bar, 0, SSB_WAIT_LIMIT) && mbar_wait(&bar_h, 0, SSB_WAIT_LIMIT);
   if (!ok) {
     if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
     mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
+    mbar_wait(&bar_h, 0, SSB_WAIT_LIMIT);
     return;
   }
   constexpr int RPW = DN_ROWS / DN_WARPS;
@@ -228,7 +248,7 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
     float wt = 0.f;
     if (base) wt = shared_j ? a.sh_gate[r] : a.wts[r * a.topk + j];
     XUnit hu[NUI];
-    const float* hrow = a.h_buf + pair * I;
+    const float* hrow = hsm + (size_t)j * I;
 #pragma unroll
     for (int i = 0; i < NUI; ++i) {
       int u = lane + 32 * i;
@@ -267,10 +287,12 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
         }
         d = warp_sum(d);
       }
-      const float o = d * wt;   // acc * w, kernels/moe_gemv_affine.py:96-97
       if (shared_j) {
-        shv[q] = o;
+        // shared expert with the reference's bf16 roundings: lin(h, D) -> bf16, then sigmoid-gate * sh -> bf16
+        // (model/layers.py:398-402); sh_gate already holds bf16(sigmoid(bf16(x . g)))
+        shv[q] = round_bf16(wt * round_bf16(d));
       } else {
+        const float o = d * wt;   // acc * w, kernels/moe_gemv_affine.py:96-97
         acc[q] = (j == 0) ? o : acc[q] + o;   // rank order, kernels/moe_gemv_affine.py:108-109
         if (lane == 0 && a.o_buf) a.o_buf[pair * H + m0 + row] = o;
       }
@@ -281,7 +303,7 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
     for (int q = 0; q < RPW; ++q) {
       const int m = m0 + warp * RPW + q;
       a.out[r * H + m] = acc[q];
-      if (a.y) a.y[r * H + m] = f32_to_bf16(round_bf16(acc[q]) + round_bf16(shv[q]));
+      if (a.y) a.y[r * H + m] = f32_to_bf16(round_bf16(acc[q]) + shv[q]);   // routed.to(bf16) + sh
     }
   }
 }
@@ -295,7 +317,7 @@ int launch_decode(DecodeArgs a, cudaStream_t st, bool pdl) {
   const int64_t pairs = a.R * a.topk + (a.shared_rec ? a.R : 0);
   const size_t gu_smem = (size_t)2 * GU_ROWS * a.H / 2 + (size_t)4 * GU_ROWS * (a.H / a.gs) * 2;
   const size_t dn_smem = (size_t)(a.topk + (a.shared_rec ? 1 : 0)) *
-                         ((size_t)DN_ROWS * a.I / 2 + (size_t)2 * DN_ROWS * (a.I / a.gs) * 2);
+                         ((size_t)DN_ROWS * a.I / 2 + (size_t)2 * DN_ROWS * (a.I / a.gs) * 2 + (size_t)a.I * 4);
   if (gu_smem > 200 * 1024 || dn_smem > 200 * 1024) return SSB_EUNSUPPORTED;
   if (pairs > 65535 || a.R > 65535) return SSB_EUNSUPPORTED;
   void (*gu)(DecodeArgs) = nullptr;

@@ -84,6 +84,7 @@ __global__ void __launch_bounds__(RL_WARPS * 32) k_router_logits(const uint16_t*
 constexpr int RS_WARPS = 4;
 constexpr int RS_MAXE = 32;  // experts per lane: experts <= 1024
 
+template <int EPL>
 __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __restrict__ logits, int ld,
                                                                   int64_t tokens, int experts, int k,
                                                                   const float* __restrict__ bias, int flags,
@@ -97,10 +98,10 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
   const int64_t t = (int64_t)blockIdx.x * RS_WARPS + (threadIdx.x >> 5);
   if (t >= tokens) return;
   const float* lrow = logits + t * ld;
-  float v[RS_MAXE];
+  float v[EPL];
   float m = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < RS_MAXE; ++i) {
+  for (int i = 0; i < EPL; ++i) {
     int e = lane + 32 * i;
     float l = -INFINITY;
     if (e < experts) {
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
   m = warp_max(m);
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < RS_MAXE; ++i) {
+  for (int i = 0; i < EPL; ++i) {
     int e = lane + 32 * i;
     float ex = 0.f;
     if (e < experts) ex = expf(v[i] - m);
@@ -122,9 +123,9 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
     s += ex;
   }
   s = warp_sum(s);
-  unsigned long long c[RS_MAXE];
+  unsigned long long c[EPL];
 #pragma unroll
-  for (int i = 0; i < RS_MAXE; ++i) {
+  for (int i = 0; i < EPL; ++i) {
     int e = lane + 32 * i;
     float p = v[i] / s;
     v[i] = p;
@@ -137,13 +138,13 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
   for (int j = 0; j < k; ++j) {
     unsigned long long lm = 0ull;
 #pragma unroll
-    for (int i = 0; i < RS_MAXE; ++i) lm = c[i] > lm ? c[i] : lm;
+    for (int i = 0; i < EPL; ++i) lm = c[i] > lm ? c[i] : lm;
     unsigned long long g = warp_max_u64(lm);
     uint32_t e = 0xFFFFFFFFu - (uint32_t)(g & 0xFFFFFFFFull);
     float p = 0.f;
     if ((int)(e & 31) == lane) {
 #pragma unroll
-      for (int i = 0; i < RS_MAXE; ++i)
+      for (int i = 0; i < EPL; ++i)
         if (lane + 32 * i == (int)e) {
           p = v[i];
           c[i] = 0ull;
@@ -162,8 +163,9 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
     out_w[t * k + lane] = my_p / sum;
   }
   if ((flags & SSB_ROUTER_SHARED_GATE) && lane == 0) {
-    float gl = __ldcg(lrow + experts);
-    out_sh_gate[t] = 1.f / (1.f + expf(-gl));
+    // sigmoid(lin(x, shared_expert_gate)) with lin's bf16 output and a bf16 sigmoid (model/layers.py:401)
+    const float gl = round_bf16(__ldcg(lrow + experts));
+    out_sh_gate[t] = round_bf16(1.f / (1.f + expf(-gl)));
   }
 }
 
@@ -335,8 +337,12 @@ extern "C" int ssb_router_select(const float* logits, int32_t ld, int64_t tokens
   SSB_CHECK_ARG(!(flags & SSB_ROUTER_SHARED_GATE) || out_sh_gate);
   if (tokens == 0) return SSB_OK;
   dim3 grid((unsigned)((tokens + RS_WARPS - 1) / RS_WARPS));
-  ssb_note_smem("router_select", k_router_select, 0);
-  return ssb_launch(k_router_select, grid, dim3(RS_WARPS * 32), 0, (cudaStream_t)stream, true, logits, ld, tokens,
+  const int epl = (experts + 31) / 32;
+  void (*kern)(const float*, int, int64_t, int, int, const float*, int, int32_t*, float*, float*, float*) =
+      epl <= 4 ? k_router_select<4> : epl <= 8 ? k_router_select<8> : epl <= 16 ? k_router_select<16>
+                                                                      : k_router_select<32>;
+  ssb_note_smem("router_select", kern, 0);
+  return ssb_launch(kern, grid, dim3(RS_WARPS * 32), 0, (cudaStream_t)stream, true, logits, ld, tokens,
                     experts, k, bias, flags, out_idx, out_w, out_probs, out_sh_gate);
 }
 
