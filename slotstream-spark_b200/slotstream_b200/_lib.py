@@ -36,6 +36,9 @@ SIGNATURES = {
     "ssb_combine_layer": [_P, _I64, _I32, _I32, _P, _P, _P, _P],
     "ssb_gemv_affine": [_P, _I32, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P],
     "ssb_gemv_dense": [_P, _I32, _I64, _P, _I32, _I32, _P, _P],
+    "ssb_fused_moe_gate_up": [_P, _I64, _I32, _I32, _P, _I64, _P, _P, _P, _I64, _P, _I32, _P, _P, _P],
+    "ssb_fused_moe_down": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _I64, _P, _I32, _P, _P, _P],
+    "ssb_gemm_affine4": [_P, _I64, _I32, _P, _P, _P, _I32, _I32, _P, _P],
 }
 
 _lib = None
