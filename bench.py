@@ -261,14 +261,133 @@ def bench_decode(args, world, rank):
     return res
 
 
+# ------------------------------------------------------------------ prefill workload (configs[2], configs[3] per GPU)
+FLOP_PER_TOKEN = 10 * 6_291_456 + 6_291_456 + 2 * 2048 * 512 + 4096   # routed + shared + router + shared gate
+
+
+def bench_prefill(args, world, rank):
+    from slotstream_b200 import _lib, synth
+    from slotstream_b200.kernels.moe_layer import PrefillLayerBuffers, moe_layer_prefill
+    from slotstream_b200.records import BASELINE_LAYOUT as LAY
+    E, K, T = 512, 10, args.tokens
+    dev = torch.device("cuda")
+    rb = LAY.record_bytes
+    seed = 2000 + rank
+    recs = torch.empty((E + 1, rb), dtype=torch.uint8, device=dev)
+    synth.fill_records_device(LAY, recs, seed)
+    group_ptr = recs.data_ptr() + torch.arange(E + 1, dtype=torch.int64, device=dev) * rb
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    router_w = (torch.randn(E, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    sh_gate_w = (torch.randn(LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.from_numpy(synth.zipf_bias(E)).to(dev) if args.routing == "zipf" else None
+    x = torch.randn(T, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
+    bufs = PrefillLayerBuffers(T, K, LAY.hidden, LAY.inter, E, dev)
+
+    def step():
+        moe_layer_prefill(x, router_w, group_ptr, sh_gate_w, K, bufs, bias=bias)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    torch.cuda.synchronize()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    times = timed_steps(graph.replay, args.steps, flush, world, clocks)
+    clocks.stop()
+    ms = max_over_ranks(sum(times) / len(times), world)
+    errs = int(bufs.err.item())
+    counts = torch.bincount(bufs.ids.reshape(-1).long(), minlength=E)
+    n_padded = int(bufs.num_padded.item())
+
+    # dominant launches, timed alone on the aligned rows the step produced (L2 flushed before each)
+    st = torch.cuda.current_stream()
+    L = _lib.lib()
+
+    def timed(fn, reps=3):
+        out = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            out.append(e0.elapsed_time(e1))
+        return sum(out) / len(out)
+
+    sr, be, npd = bufs.sorted_rows, bufs.block_expert, bufs.num_padded
+    gu_ms = timed(lambda: _lib.check(L.ssb_fused_moe_gate_up(
+        _lib.ptr(x), T, LAY.hidden, LAY.inter, _lib.ptr(bufs.row_token), bufs.rows, _lib.ptr(sr), _lib.ptr(be),
+        _lib.ptr(npd), sr.numel(), _lib.ptr(group_ptr), E + 1, _lib.ptr(bufs.h), None, _lib.stream()), "gate_up"))
+    dn_ms = timed(lambda: _lib.check(L.ssb_fused_moe_down(
+        _lib.ptr(bufs.h), bufs.rows, LAY.hidden, LAY.inter, _lib.ptr(bufs.row_weight), _lib.ptr(sr), _lib.ptr(be),
+        _lib.ptr(npd), sr.numel(), _lib.ptr(group_ptr), E + 1, _lib.ptr(bufs.out_rows), None, _lib.stream()), "down"))
+    gu_flop = 2.0 * bufs.rows * 2 * LAY.inter * LAY.hidden
+    dn_flop = 2.0 * bufs.rows * LAY.inter * LAY.hidden
+    pk = peaks()
+    gu_tf = gu_flop / (gu_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": "fused_moe gate_up (tcgen05 grouped GEMM, SwiGLU epilogue)",
+                "achieved": round(gu_tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(gu_tf / pk["bf16_tflops"], 4), "peak_source": pk["source"] + " (burst)",
+                "traffic": None, "flop_per_launch": gu_flop, "launch_ms": round(gu_ms, 4),
+                "padded_rows": n_padded, "rows": bufs.rows,
+                "down": {"achieved": round(dn_flop / (dn_ms * 1e-3) / 1e12, 1), "launch_ms": round(dn_ms, 4)}}
+
+    # e2e through the public API with host buffers: x H2D, the layer, y D2H
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T, LAY.hidden), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        graph.replay()
+        y_host.copy_(bufs.y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_times = timed_steps(e2e_step, args.steps, flush, world)
+    e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
+
+    value = world * T / (ms * 1e-3)
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"prefill_layer_{T}tok_per_gpu", "tokens_per_gpu": T, "hidden": LAY.hidden,
+                   "inter": LAY.inter, "experts": E, "topk": K, "shared_experts": 1, "routing": f"{args.routing}"
+                   + ("_s1.1" if args.routing == "zipf" else ""), "weights": "affine4_gs64 resident in HBM",
+                   "cuda_graph": True, "l2": "flushed before every step (256 MiB write); inputs > L2",
+                   "parallelism": f"replicas{world}" if world > 1 else "single"},
+        "tflops": round(world * T * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12, 1),
+        "flop_per_token": FLOP_PER_TOKEN,
+        "expert_rows": {"max": int(counts.max()), "zero_experts": int((counts == 0).sum()), "padded": n_padded},
+        "roofline": roofline,
+        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y_host.numel() * 2)},
+        "gpu_launches": 7 * args.steps,
+        "clocks": clocks.summary(),
+        "device_errors": errs,
+    }
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=["decode"], default="decode")
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
+    ap.add_argument("--tokens", type=int, default=32768, help="prefill tokens per GPU")
+    ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
+    ap.add_argument("--batch", type=int, default=1, help="decode batch")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement at N=1")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -280,11 +399,23 @@ def main():
             print(json.dumps(reference_arm(args, int(os.environ.get("WORLD_SIZE", "1")))), flush=True)
         return
     world, rank, _ = dist_setup()
-    res = bench_decode(args, world, rank)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        from oracle.cpu_baseline import time_decode
-        from slotstream_b200.records import BASELINE_LAYOUT
-        res["cpu_baseline"] = time_decode(BASELINE_LAYOUT, seconds=args.cpu_seconds)
+    from slotstream_b200.records import BASELINE_LAYOUT
+    if args.workload == "decode":
+        res = bench_decode(args, world, rank)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            from oracle.cpu_baseline import time_decode
+            res["cpu_baseline"] = time_decode(BASELINE_LAYOUT, seconds=args.cpu_seconds)
+    else:
+        res = bench_prefill(args, world, rank)
+        torch.cuda.empty_cache()
+        if world == 1 and not args.no_decode:
+            d = bench_decode(args, world, rank)
+            res["decode"] = {k: d[k] for k in ("value", "unit", "ms_per_step", "config", "hbm_gbs_per_step",
+                                               "bytes_per_step", "roofline", "e2e", "clocks")}
+            torch.cuda.empty_cache()
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            from oracle.cpu_baseline import time_prefill
+            res["cpu_baseline"] = time_prefill(BASELINE_LAYOUT, args.tokens, seconds=args.cpu_seconds)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
@@ -295,23 +426,33 @@ def reference_arm(args, world):
     """The reference's own CPU path (oracle torch port of moe_ref / affine_ref) on all host cores, same
     metric and config; each step is a bounded sample."""
     sys.path.insert(0, str(ROOT))
-    from oracle.cpu_baseline import time_decode
+    from oracle.cpu_baseline import CpuLayer, time_decode, time_prefill
     from slotstream_b200.records import BASELINE_LAYOUT
     per_step = max(1.0, min(10.0, 60.0 / max(args.steps, 1)))
     vals = []
-    for _ in range(args.warmup):
-        time_decode(BASELINE_LAYOUT, seconds=0.5)
+    b = args.batch
+    if args.workload == "decode":
+        run = lambda s: time_decode(BASELINE_LAYOUT, seconds=s)  # noqa: E731
+        config = {"workload": f"decode_step_48layer_b{b}", "layers": 48, "batch": b, "hidden": 2048, "inter": 512,
+                  "experts": 512, "topk": 10, "routing": "zipf_s1.1"}
+        dtype = "f32"
+    else:
+        layer = CpuLayer(BASELINE_LAYOUT, 0)
+        run = lambda s: time_prefill(BASELINE_LAYOUT, args.tokens, seconds=s, layer=layer)  # noqa: E731
+        config = {"workload": f"prefill_layer_{args.tokens}tok_per_gpu", "tokens_per_gpu": args.tokens,
+                  "hidden": 2048, "inter": 512, "experts": 512, "topk": 10,
+                  "routing": args.routing + ("_s1.1" if args.routing == "zipf" else "")}
+        dtype = "bf16"
+    for _ in range(min(args.warmup, 1)):
+        run(0.5)
     for _ in range(args.steps):
-        vals.append(time_decode(BASELINE_LAYOUT, seconds=per_step))
+        vals.append(run(per_step))
     v = statistics.mean(r["value"] for r in vals)
     cb = dict(vals[-1])
     cb["value"] = v
-    b = args.batch
     return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"decode_step_48layer_b{b}", "layers": 48, "batch": b, "hidden": 2048,
-                       "inter": 512, "experts": 512, "topk": 10, "routing": "zipf_s1.1"},
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic", "impl": "reference", "config": config,
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
 

@@ -156,6 +156,24 @@ int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int3
                        int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, float* out_rows, int32_t* err,
                        void* stream);
 
+/* Both prefill expert GEMMs of a fused MoE layer (additive): gate_up then down, as the two entry points
+ * above, with local expert `shared_local` (-1: none) treated as the shared expert -- its h is
+ * bf16(bf16(silu(bf16 g)) * bf16 u) and its down rows bf16(row_weight * bf16(h D^T)), the reference's
+ * bf16 rounding between the shared expert's ops (model/moe_sweep.py:37-43) -- so the shared expert rides
+ * in the same grouped launch as the routed ones with its rows weighted by the sigmoid gate.
+ * Replaces: the per-group fused_moe_affine calls of model/moe_sweep.py:163-176 plus shared_expert
+ * (:37-43) for a layer whose experts are all resident. */
+int ssb_prefill_experts(const uint16_t* x, int32_t hidden, int32_t inter, const int32_t* row_token,
+                        const float* row_weight, int64_t rows, const int32_t* sorted_rows, const int32_t* block_expert,
+                        const int32_t* num_padded, int64_t padded_len, const int64_t* group_ptr, int32_t n_groups,
+                        int32_t shared_local, uint16_t* h_buf, float* out_rows, int32_t* err, void* stream);
+
+/* Dense bf16 GEMM on tcgen05 (router logits of a prefill chunk): out[m, n] = sum_k x[m, k] * w[n, k],
+ * fp32 into rows of `ldo` floats (ldo % 4 == 0). k % 64 == 0, n % 256 == 0; row-invariant.
+ * Replaces: the router lin() of model/layers.py:339 inside the prefill GEMM scope (kernels/gemm_affine.py:40-59). */
+int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uint16_t* w, int32_t n, float* out, int64_t ldo,
+                   void* stream);
+
 /* Dense prefill GEMM with an affine 4-bit weight on tcgen05: out[m, n] = sum_k x[m, k] * bf16(q*s + b)[n, k],
  * fp32 out. k % 64 == 0, (k/gs) even, n % 256 == 0; row-invariant (fixed k order per output).
  * Replaces: gemm(x, AffineWeight), slotstream_spark/kernels/gemm_affine.py:62-98 (kernel :19-37). */

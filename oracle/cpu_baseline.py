@@ -108,11 +108,11 @@ def time_decode(layout, seed=0, seconds=10.0, threads=None, layers_per_token=48)
                       f"tokens/s = 1/(mean token-layer time x {layers_per_token} layers); torch {torch.__version__}"}
 
 
-def time_prefill(layout, tokens, seed=0, seconds=10.0, threads=None, sample_tokens=1024):
+def time_prefill(layout, tokens, seed=0, seconds=10.0, threads=None, sample_tokens=1024, layer=None):
     """Tokens/s of the CPU prefill path on chunks of `sample_tokens` tokens until `seconds` pass."""
     threads = threads or os.cpu_count()
     torch.set_num_threads(threads)
-    L = CpuLayer(layout, seed)
+    L = layer if layer is not None else CpuLayer(layout, seed)
     rng = np.random.default_rng(seed + 1)
     n, t0 = 0, time.perf_counter()
     with torch.no_grad():

@@ -244,14 +244,18 @@ def fused_rows_bf16_path(x, row_token, row_weight, row_expert, expert_f32, rows)
     accumulation, h = silu(g)*u stored bf16, y = (D_bf16 h) * w in fp32
     (kernels/fused_moe_affine.py:14-16, :38-50, :76-80, :103-108). ``expert_f32(e)`` gives fp32 dequant."""
     x = np.asarray(x, dtype=np.float64)
-    out = []
-    for r in rows:
-        g, u, d = (round_bf16(m).astype(np.float64) for m in expert_f32(int(row_expert[r])))
-        xr = x[int(row_token[r])]
-        gg, uu = (g @ xr).astype(np.float32), (u @ xr).astype(np.float32)
+    rows = np.asarray(list(rows), dtype=np.int64)
+    out = np.zeros((rows.size, x.shape[1]), dtype=np.float64)
+    ex = np.asarray(row_expert)[rows]
+    for e in np.unique(ex):          # rows are independent; grouping by expert only batches the products
+        sel = np.nonzero(ex == e)[0]
+        g, u, d = (round_bf16(m).astype(np.float64) for m in expert_f32(int(e)))
+        xr = x[np.asarray(row_token)[rows[sel]].astype(np.int64)]
+        gg, uu = (xr @ g.T).astype(np.float32), (xr @ u.T).astype(np.float32)
         h = round_bf16(gg.astype(np.float64) / (1.0 + np.exp(-gg.astype(np.float64))) * uu).astype(np.float64)
-        out.append(((d @ h).astype(np.float32) * np.float32(row_weight[r])).astype(np.float64))
-    return np.stack(out) if out else np.zeros((0, x.shape[1]))
+        wt = np.asarray(row_weight, dtype=np.float32)[rows[sel]]
+        out[sel] = ((h @ d.T).astype(np.float32) * wt[:, None]).astype(np.float64)
+    return out
 
 
 def shared_expert(x_bf16, gate, up, down, sh_gate_bf16):
@@ -280,6 +284,24 @@ def moe_layer(layout, x_bf16, router_w_bf16, k, expert_dense, sh_dense, sh_gate_
     sh = shared_expert(x_bf16, *sh_dense, sh_gate_bf16)
     out = round_bf16(round_bf16(routed).astype(np.float64) + sh)
     return out, routed, ids, w, logits
+
+
+def moe_layer_prefill(layout, x_bf16, router_w_bf16, k, expert_f32, sh_f32, sh_gate_bf16, bias=None,
+                      logits_round_bf16=False):
+    """Whole MoE block on the reference's prefill rounding path: routed rows as fused_rows_bf16_path
+    (kernels/fused_moe_affine.py:14-16) summed in rank order in fp32 (combine_rank_order), the shared expert
+    through gemm() with bf16-rounded weight tiles and bf16 between ops (model/moe_sweep.py:37-43,
+    kernels/gemm_affine.py:32-37), final add in bf16 (model/moe_sweep.py:161 + engine/prefill.py:201).
+    ``expert_f32(e)`` -> fp32 (G, U, D). Returns (out bf16-valued fp32 [T, H], ids, weights, logits)."""
+    ids, w, logits = router(x_bf16, router_w_bf16, k, bias=bias, logits_round_bf16=logits_round_bf16)
+    t = ids.shape[0]
+    x = bf16_to_f32(x_bf16)
+    rows = fused_rows_bf16_path(x, np.repeat(np.arange(t), k), w.reshape(-1), ids.reshape(-1), expert_f32,
+                                range(t * k))
+    routed = combine_rank_order(rows.astype(np.float32), t, k)
+    sh = shared_expert(x_bf16, *(round_bf16(m) for m in sh_f32), sh_gate_bf16)
+    out = round_bf16(round_bf16(routed).astype(np.float64) + sh)
+    return out, ids, w, logits
 
 
 def rel_l2(a, b):

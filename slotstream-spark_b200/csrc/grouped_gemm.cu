@@ -49,6 +49,9 @@ struct GemmArgs {
   int n_groups;
   int64_t off_w[2], off_s[2], off_b[2];   // byte offsets of weight piece 0 (and 1 for gate_up) from the base
   int K, gs;
+  int dense_b;                // B rows are plain bf16 (ldb elements apart) instead of affine 4-bit pieces
+  int64_t ldb;
+  int shared_local;           // local index of the shared expert (bf16 rounding between its ops), -1: none
   const float* row_weight;
   void* out;
   int64_t ldo;
@@ -220,6 +223,21 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
       piece = 0;
       nrow = nb * BN + p;
     }
+    if (a.dense_b) {
+      // plain bf16 weight rows: 16-byte cp.async straight into the swizzled tile, no dequantisation
+      const uint16_t* drow = (const uint16_t*)base + (int64_t)nrow * a.ldb;
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % STAGES, r = kb / STAGES;
+        if (!mbar_wait_ns(&S.empty[s], (r & 1) ^ 1, SSB_WAIT_NS)) {
+          s_fail = 1;
+          break;
+        }
+        const uint32_t bt = smem_u32(S.b + s * B_STAGE);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + kb * BK + c * 8, 16);
+        cp_async_arrive(&S.full_b[s]);
+      }
+    }
     const int ng = a.K / a.gs;
     const uint8_t* wrow = base + a.off_w[piece] + (int64_t)nrow * (a.K / 2);
     const uint16_t* srow = (const uint16_t*)(base + a.off_s[piece]) + (int64_t)nrow * ng;
@@ -236,11 +254,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
       asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + SB_STG + p * 4)),
                    "l"(brow + (g0 & ~1)) : "memory");
     };
-    for (int kb = 0; kb < PD - 1 && kb < KB; ++kb) {
+    for (int kb = 0; kb < PD - 1 && kb < KB && !a.dense_b; ++kb) {
       issue(kb);
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    for (int kb = 0; kb < KB; ++kb) {
+    for (int kb = 0; kb < KB && !a.dense_b; ++kb) {
       if (kb + PD - 1 < KB) issue(kb + PD - 1);
       asm volatile("cp.async.commit_group;" ::: "memory");
       asm volatile("cp.async.wait_group %0;" ::"n"(PD - 1) : "memory");
@@ -291,8 +309,33 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
     const int q = (warp - PROD_WARP0) & 3, half = (warp - PROD_WARP0) >> 2;
     const int orow = S.orow[32 * q + lane];
     const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
+    // the shared expert follows the reference's bf16 rounding between ops (model/moe_sweep.py:37-43)
+    const bool shared_e = e == a.shared_local;
     if (!ok) {
       s_fail = 1;
+    } else if (EPI == EPI_SWIGLU && shared_e) {
+      uint16_t* out = (uint16_t*)a.out;
+#pragma unroll 1
+      for (int cc = 0; cc < 2; ++cc) {
+        const int col = 64 * half + 32 * cc;
+        float g[32], u[32];
+        tmem_ld32(taddr + col, g);
+        tmem_ld32(taddr + 128 + col, u);
+        if (orow >= 0) {
+          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)orow * a.ldo + nb * (BN / 2) + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float h[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              const float gb = round_bf16(g[8 * j + t]), ub = round_bf16(u[8 * j + t]);
+              h[t] = round_bf16(gb / (1.f + expf(-gb))) * ub;   // bf16(silu(bf16 g)) * bf16 u -> bf16 below
+            }
+            dst[j] = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
+                                pack_bf16x2(h[6], h[7]));
+          }
+        }
+      }
     } else if (EPI == EPI_SWIGLU) {
       uint16_t* out = (uint16_t*)a.out;
 #pragma unroll 1
@@ -327,13 +370,22 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
         if (orow >= 0) {
           float4* dst = reinterpret_cast<float4*>(out + (int64_t)orow * a.ldo + nb * BN + col);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 o;
-            o.x = EPI == EPI_SCALE ? v[4 * j] * wt : v[4 * j];
-            o.y = EPI == EPI_SCALE ? v[4 * j + 1] * wt : v[4 * j + 1];
-            o.z = EPI == EPI_SCALE ? v[4 * j + 2] * wt : v[4 * j + 2];
-            o.w = EPI == EPI_SCALE ? v[4 * j + 3] * wt : v[4 * j + 3];
-            dst[j] = o;
+          if (EPI == EPI_SCALE && shared_e) {   // bf16(sigmoid gate * bf16(D h))
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(round_bf16(wt * round_bf16(v[4 * j])), round_bf16(wt * round_bf16(v[4 * j + 1])),
+                                   round_bf16(wt * round_bf16(v[4 * j + 2])),
+                                   round_bf16(wt * round_bf16(v[4 * j + 3])));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o;
+              o.x = EPI == EPI_SCALE ? v[4 * j] * wt : v[4 * j];
+              o.y = EPI == EPI_SCALE ? v[4 * j + 1] * wt : v[4 * j + 1];
+              o.z = EPI == EPI_SCALE ? v[4 * j + 2] * wt : v[4 * j + 2];
+              o.w = EPI == EPI_SCALE ? v[4 * j + 3] * wt : v[4 * j + 3];
+              dst[j] = o;
+            }
           }
         }
       }
@@ -385,14 +437,11 @@ void set_record_offsets(GemmArgs& g, int hidden, int inter, bool gate_up) {
   }
 }
 
-}  // namespace
-
-extern "C" int ssb_fused_moe_gate_up(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter,
-                                     const int32_t* row_token, int64_t rows, const int32_t* sorted_rows,
-                                     const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
-                                     const int64_t* group_ptr, int32_t n_groups, uint16_t* h_buf, int32_t* err,
-                                     void* stream) {
-  SSB_CHECK_ARG(tokens >= 0 && rows >= 0 && padded_len >= 0 && n_groups >= 1);
+int gate_up_impl(const uint16_t* x, int32_t hidden, int32_t inter, const int32_t* row_token, int64_t rows,
+                 const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded,
+                 int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, int32_t shared_local,
+                 uint16_t* h_buf, int32_t* err, void* stream) {
+  SSB_CHECK_ARG(rows >= 0 && padded_len >= 0 && n_groups >= 1);
   if (hidden % BK || hidden <= 0 || inter % (BN / 2) || inter <= 0 || (hidden / 64) % 2) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
   SSB_CHECK_ARG(x && row_token && sorted_rows && block_expert && num_padded && group_ptr && h_buf);
@@ -410,16 +459,17 @@ extern "C" int ssb_fused_moe_gate_up(const uint16_t* x, int64_t tokens, int32_t 
   set_record_offsets(g, hidden, inter, true);
   g.K = hidden;
   g.gs = 64;
+  g.shared_local = shared_local;
   g.out = h_buf;
   g.ldo = inter;
   g.err = err;
   return launch(EPI_SWIGLU, g, padded_len / BM, inter / (BN / 2), (cudaStream_t)stream);
 }
 
-extern "C" int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter,
-                                  const float* row_weight, const int32_t* sorted_rows, const int32_t* block_expert,
-                                  const int32_t* num_padded, int64_t padded_len, const int64_t* group_ptr,
-                                  int32_t n_groups, float* out_rows, int32_t* err, void* stream) {
+int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter, const float* row_weight,
+              const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
+              const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, float* out_rows, int32_t* err,
+              void* stream) {
   SSB_CHECK_ARG(rows >= 0 && padded_len >= 0 && n_groups >= 1);
   if (inter % BK || inter <= 0 || hidden % BN || hidden <= 0 || (inter / 64) % 2) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
@@ -437,11 +487,44 @@ extern "C" int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t h
   set_record_offsets(g, hidden, inter, false);
   g.K = inter;
   g.gs = 64;
+  g.shared_local = shared_local;
   g.row_weight = row_weight;
   g.out = out_rows;
   g.ldo = hidden;
   g.err = err;
   return launch(EPI_SCALE, g, padded_len / BM, hidden / BN, (cudaStream_t)stream);
+}
+
+}  // namespace
+
+extern "C" int ssb_fused_moe_gate_up(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter,
+                                     const int32_t* row_token, int64_t rows, const int32_t* sorted_rows,
+                                     const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
+                                     const int64_t* group_ptr, int32_t n_groups, uint16_t* h_buf, int32_t* err,
+                                     void* stream) {
+  SSB_CHECK_ARG(tokens >= 0);
+  return gate_up_impl(x, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len, group_ptr,
+                      n_groups, -1, h_buf, err, stream);
+}
+
+extern "C" int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter,
+                                  const float* row_weight, const int32_t* sorted_rows, const int32_t* block_expert,
+                                  const int32_t* num_padded, int64_t padded_len, const int64_t* group_ptr,
+                                  int32_t n_groups, float* out_rows, int32_t* err, void* stream) {
+  return down_impl(h_buf, rows, hidden, inter, row_weight, sorted_rows, block_expert, num_padded, padded_len,
+                   group_ptr, n_groups, -1, out_rows, err, stream);
+}
+
+extern "C" int ssb_prefill_experts(const uint16_t* x, int32_t hidden, int32_t inter, const int32_t* row_token,
+                                   const float* row_weight, int64_t rows, const int32_t* sorted_rows,
+                                   const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
+                                   const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, uint16_t* h_buf,
+                                   float* out_rows, int32_t* err, void* stream) {
+  int rc = gate_up_impl(x, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len,
+                        group_ptr, n_groups, shared_local, h_buf, err, stream);
+  if (rc) return rc;
+  return down_impl(h_buf, rows, hidden, inter, row_weight, sorted_rows, block_expert, num_padded, padded_len,
+                   group_ptr, n_groups, shared_local, out_rows, err, stream);
 }
 
 extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const int32_t* q, const uint16_t* s,
@@ -460,11 +543,35 @@ extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const i
   g.n_groups = 1;
   g.K = k;
   g.gs = gs;
+  g.shared_local = -1;
   g.out = out;
   g.ldo = n;
   g.off_w[0] = g.off_w[1] = 0;
   g.off_s[0] = g.off_s[1] = (int64_t)((const uint8_t*)s - (const uint8_t*)q);
   g.off_b[0] = g.off_b[1] = (int64_t)((const uint8_t*)b - (const uint8_t*)q);
+  g.err = nullptr;
+  return launch(EPI_PLAIN, g, (m + BM - 1) / BM, n / BN, (cudaStream_t)stream);
+}
+
+extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uint16_t* w, int32_t n, float* out,
+                              int64_t ldo, void* stream) {
+  SSB_CHECK_ARG(m >= 0 && k >= 1 && n >= 1 && ldo >= n && ldo % 4 == 0);
+  if (k % BK || n % BN || k % 8) return SSB_EUNSUPPORTED;
+  if (m == 0) return SSB_OK;
+  SSB_CHECK_ARG(x && w && out && ((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0);
+  GemmArgs g{};
+  g.a = x;
+  g.lda = k;
+  g.R = m;
+  g.base0 = (const uint8_t*)w;
+  g.n_groups = 1;
+  g.K = k;
+  g.gs = 64;
+  g.dense_b = 1;
+  g.ldb = k;
+  g.shared_local = -1;
+  g.out = out;
+  g.ldo = ldo;
   g.err = nullptr;
   return launch(EPI_PLAIN, g, (m + BM - 1) / BM, n / BN, (cudaStream_t)stream);
 }

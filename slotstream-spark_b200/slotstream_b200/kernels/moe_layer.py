@@ -30,6 +30,78 @@ class DecodeLayerBuffers:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
 
 
+class PrefillLayerBuffers:
+    """Every output and workspace of one prefill layer call for `tokens` tokens.
+
+    Row r < T*topk is (token r // topk, rank r % topk); rows T*topk + t are the shared expert's rows of token t.
+    The router writes its ids / weights / shared gate straight into row_expert / row_weight, so the grouped
+    GEMM reads them without any gather or concatenation."""
+
+    def __init__(self, tokens: int, topk: int, hidden: int, inter: int, experts: int = 512, device="cuda"):
+        from .moe_align import padded_rows
+        from .fused_moe_affine import BLOCK_M
+        t, r = tokens, tokens * topk
+        self.tokens, self.topk, self.hidden, self.inter, self.experts = tokens, topk, hidden, inter, experts
+        self.rows = r + t
+        self.ld = experts + 4                                   # column `experts` holds the shared-gate logit
+        f32 = dict(dtype=torch.float32, device=device)
+        self.logits = torch.empty(t * self.ld, **f32)
+        self.row_expert = torch.empty(self.rows, dtype=torch.int32, device=device)
+        self.row_expert[r:] = experts                           # the shared expert is local expert `experts`
+        self.row_token = torch.cat([torch.arange(r, device=device, dtype=torch.int32) // topk,
+                                    torch.arange(t, device=device, dtype=torch.int32)])
+        self.row_weight = torch.empty(self.rows, **f32)
+        self.ids = self.row_expert[:r].view(t, topk)
+        self.w = self.row_weight[:r].view(t, topk)
+        self.sh_gate = self.row_weight[r:]
+        p = padded_rows(self.rows, experts + 1, BLOCK_M)
+        self.sorted_rows = torch.empty(p, dtype=torch.int32, device=device)
+        self.block_expert = torch.empty(p // BLOCK_M, dtype=torch.int32, device=device)
+        self.num_padded = torch.empty(1, dtype=torch.int32, device=device)
+        self.h = torch.empty(self.rows, inter, dtype=torch.bfloat16, device=device)
+        self.out_rows = torch.empty(self.rows, hidden, **f32)
+        self.y = torch.empty(t, hidden, dtype=torch.bfloat16, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLayerBuffers, *, bias=None,
+                      logits_round_bf16: bool = False):
+    """x bf16 [T, H] -> bufs.y bf16 [T, H]: one MoE layer over a prefill chunk, every expert resident.
+
+    ``group_ptr`` int64 [E + 1]: record base of expert e at index e and of the shared expert at index E.
+    Launches: router GEMM (tcgen05, dense bf16) + shared-gate logits, router select, align, gate_up + down
+    (tcgen05 grouped GEMM, shared expert as local expert E), rank-order combine + shared add."""
+    from .moe_align import moe_align
+    t, h = x.shape
+    e = bufs.experts
+    if (t, h) != (bufs.tokens, bufs.hidden) or k != bufs.topk or tuple(w_router.shape) != (e, h):
+        raise ValueError("buffers were sized for another call shape")
+    if group_ptr.dtype != torch.int64 or group_ptr.numel() != e + 1:
+        raise ValueError("group_ptr must be int64 [E + 1] (routed experts, then the shared expert)")
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous bf16 [T, H] tensor")
+    L = _lib.lib()
+    st = _lib.stream()
+    lg = bufs.logits
+    _lib.check(L.ssb_gemm_dense(_lib.ptr(x), t, h, _lib.ptr(w_router), e, _lib.ptr(lg), bufs.ld, st), "router gemm")
+    _lib.check(L.ssb_router_logits(_lib.ptr(x), _lib.ptr(sh_gate_w), None, t, h, 1, bufs.ld, lg.data_ptr() + 4 * e, st),
+               "shared gate logits")
+    flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0)
+    _lib.check(L.ssb_router_select(_lib.ptr(lg), bufs.ld, t, e, k, _lib.ptr(bias), flags, _lib.ptr(bufs.ids),
+                                   _lib.ptr(bufs.w), None, _lib.ptr(bufs.sh_gate), st), "router select")
+    aligned = moe_align(bufs.row_expert, e + 1, 128, out=(bufs.sorted_rows, bufs.block_expert, bufs.num_padded))
+    _lib.check(L.ssb_prefill_experts(
+        _lib.ptr(x), h, bufs.inter, _lib.ptr(bufs.row_token), _lib.ptr(bufs.row_weight), bufs.rows,
+        _lib.ptr(aligned[0]), _lib.ptr(aligned[1]), _lib.ptr(aligned[2]), aligned[0].numel(), _lib.ptr(group_ptr),
+        e + 1, e, _lib.ptr(bufs.h), _lib.ptr(bufs.out_rows), _lib.ptr(bufs.err), st), "prefill experts")
+    r = t * k
+    _lib.check(L.ssb_combine_layer(_lib.ptr(bufs.out_rows), t, k, h, bufs.out_rows.data_ptr() + 4 * r * h, None,
+                                   _lib.ptr(bufs.y), st), "combine")
+    _note("fused_moe_gate_up")
+    _note("fused_moe_down")
+    return bufs.y
+
+
 def _addr(rec) -> int:
     if isinstance(rec, torch.Tensor):
         if not rec.is_cuda:

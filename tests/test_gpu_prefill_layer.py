@@ -1,0 +1,98 @@
+"""Fused prefill MoE layer (router GEMM -> select -> align -> grouped tcgen05 GEMMs -> combine) vs the oracle (GPU).
+
+The layer contract: top-k ids bit-exact except router-logit ties within 1e-6; outputs within relative L2 1e-2
+of the exact oracle, and within max-abs 2e-2 (plus one bf16 ulp of the final rounding) of the oracle that
+follows the reference's prefill rounding path.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import bf16_tensor, record, to_np_bf16_bits
+from oracle import moe_oracle as O
+from slotstream_b200 import synth
+from slotstream_b200.records import BASELINE_LAYOUT
+
+pytestmark = pytest.mark.gpu
+E, K = 512, 10
+
+
+@pytest.fixture(scope="module")
+def layer():
+    lay = BASELINE_LAYOUT
+    recs = [record(lay, 0, 0, e) for e in range(E + 1)]
+    pool = torch.from_numpy(np.stack(recs)).cuda()
+    gp = (pool.data_ptr() + torch.arange(E + 1, dtype=torch.int64) * lay.record_bytes).cuda()
+    rw = synth.router_weight(0, E, lay.hidden, 0)
+    sg = synth.shared_gate_weight(0, lay.hidden, 0)
+    f32 = {}
+
+    def expert_f32(e):
+        if e not in f32:
+            f32[e] = O.record_dense(lay, recs[e], np.float32)
+        return f32[e]
+    return dict(lay=lay, recs=recs, pool=pool, gp=gp, rw=rw, sg=sg, f32=expert_f32)
+
+
+def _run(L, x_bits, bias=None):
+    from slotstream_b200.kernels.moe_layer import PrefillLayerBuffers, moe_layer_prefill
+    t = x_bits.shape[0]
+    bufs = PrefillLayerBuffers(t, K, L["lay"].hidden, L["lay"].inter, E)
+    y = moe_layer_prefill(bf16_tensor(x_bits), bf16_tensor(L["rw"]), L["gp"], bf16_tensor(L["sg"]), K, bufs,
+                          bias=None if bias is None else torch.from_numpy(bias).cuda())
+    torch.cuda.synchronize()
+    assert int(bufs.err.item()) == 0
+    return y.clone(), bufs
+
+
+@pytest.mark.parametrize("zipf", [False, True])
+def test_prefill_layer_matches_oracle(layer, zipf):
+    L = layer
+    t = 192
+    x = synth.activations(21, t, L["lay"].hidden)
+    bias = synth.zipf_bias(E) if zipf else None
+    y, bufs = _run(L, x, bias)
+    ref, ids, w, logits = O.moe_layer_prefill(L["lay"], x, L["rw"], K, L["f32"], L["f32"](E), L["sg"], bias=bias)
+    O.ids_match(bufs.ids.cpu().numpy(), ids, logits)
+    np.testing.assert_allclose(bufs.w.cpu().numpy(), w, rtol=2e-5, atol=1e-7)
+    got = O.bf16_to_f32(to_np_bf16_bits(y)).astype(np.float64)
+    assert O.rel_l2(got, ref) <= 1e-2
+    assert np.max(np.abs(got - ref) - O.bf16_ulp(ref)) <= 2e-2
+    # exact-dequant oracle (fp64 routed experts, fp32 shared): within the layer's relative L2 contract
+    dense = {}
+
+    def ex(e):
+        if e not in dense:
+            dense[e] = O.record_dense(L["lay"], L["recs"][e])
+        return dense[e]
+    exact, *_ = O.moe_layer(L["lay"], x, L["rw"], K, ex, L["f32"](E), L["sg"], bias=bias)
+    assert O.rel_l2(got, exact) <= 1e-2
+
+
+def test_prefill_layer_row_invariance(layer):
+    L = layer
+    x = synth.activations(33, 300, L["lay"].hidden)
+    y, _ = _run(L, x)
+    y17, _ = _run(L, x[:17])
+    assert torch.equal(y[:17], y17)
+    y1, _ = _run(L, x[123:124])
+    assert torch.equal(y[123:124], y1)
+
+
+def test_prefill_layer_matches_decode_layer_routing(layer):
+    """The prefill (tensor-core logits) and decode (CUDA-core logits) routers pick the same experts with the same
+    weights up to fp32 summation order: ids equal except logit ties within 1e-6, weights within 2e-5."""
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    from gpu_helpers import DevicePool
+    L = layer
+    x = synth.activations(44, 8, L["lay"].hidden)
+    _, pb = _run(L, x)
+    pool = DevicePool(L["lay"], L["recs"][:E], range(E), list(range(E)), E, layer=0)
+    db = DecodeLayerBuffers(8, K, L["lay"].hidden, L["lay"].inter, E)
+    moe_layer_decode(bf16_tensor(x), bf16_tensor(L["rw"]), 0, pool.map, pool.slot_ptr,
+                     torch.from_numpy(L["recs"][E]).cuda(), bf16_tensor(L["sg"]), K, db)
+    torch.cuda.synchronize()
+    _, _, logits = O.router(x, L["rw"], K)
+    O.ids_match(pb.ids.cpu().numpy(), db.ids.cpu().numpy(), logits)
+    same = (pb.ids == db.ids).all(dim=1).cpu().numpy()
+    np.testing.assert_allclose(pb.w.cpu().numpy()[same], db.w.cpu().numpy()[same], rtol=2e-5, atol=1e-7)
