@@ -1,6 +1,7 @@
 // Shared device helpers of the sm_100a MoE kernels: bf16 bit tricks, nibble decoding, warp reductions,
 // programmatic-dependent-launch (PDL) controls, L2 bulk prefetch and the launch helper.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -14,13 +15,8 @@ SSB_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 SSB_DEV float bf16_at(const uint16_t* p) { return __uint_as_float(((uint32_t)*p) << 16); }
 SSB_DEV float bf16_bits(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
 
-// Round-to-nearest-even fp32 -> bf16 bits (finite inputs; NaN keeps a quiet NaN).
-SSB_DEV uint16_t f32_to_bf16(float f) {
-  uint32_t u = __float_as_uint(f);
-  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40u);
-  u += 0x7FFFu + ((u >> 16) & 1u);
-  return (uint16_t)(u >> 16);
-}
+// Round-to-nearest-even fp32 -> bf16 bits (the hardware cvt.rn.bf16.f32).
+SSB_DEV uint16_t f32_to_bf16(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 SSB_DEV float round_bf16(float f) { return __uint_as_float(((uint32_t)f32_to_bf16(f)) << 16); }
 
 // ---------------------------------------------------------------- 4-bit codes

@@ -2,14 +2,17 @@
 // (slotstream_spark/kernels/moe_gemv_affine.py:113-147), plus the fused shared expert of the decode layer.
 //
 // Two launches:
-//  * gate_up: CTA = (pair p = (row, rank) or the shared expert, 32 rows of inter). One thread copies the
-//    slice of gate/up codes, scales and biases into shared memory with six bulk async copies; eight warps
-//    then form h = silu(G x) * (U x) in fp32 with the activation held in registers.
-//  * down   : CTA = (row, 16 rows of hidden). It stages the down slices of all of the row's experts with bulk
+//  * gate_up: CTA = (pair p = (row, rank) or the shared expert, 16 rows of inter). One thread copies the
+//    slice of gate/up codes, scales and biases into shared memory with six bulk async copies; each of the
+//    eight warps forms two rows of h = silu(G x) * (U x) in fp32, four independent dot products at once, with
+//    the activation held in registers.
+//  * down   : CTA = (row, 8 rows of hidden). It stages the down slices of all of the row's experts with bulk
 //    copies issued BEFORE waiting on the gate_up grid (the records are static and the expert ids were
 //    written two launches back), so under programmatic dependent launch the down weights stream in while
-//    gate_up runs. It then forms o_k = w_k * (D_k h_k) and sums the ranks in order (out = o_0 + o_1 + ...),
-//    fusing the reference's separate _rank_sum kernel.
+//    gate_up runs. The staged activations h_k are converted once per CTA into the pre-scaled per-unit form;
+//    each warp then owns one output row and all experts, forms o_k = w_k * (D_k h_k) with the per-expert warp
+//    reductions batched, and sums the ranks in order (out = o_0 + o_1 + ...), fusing the reference's
+//    separate _rank_sum kernel.
 // Every (row, rank, output) value is the same op sequence whatever the row count or slot placement, so a
 // 3-row call equals three 1-row calls bit for bit.
 #include "affine.cuh"
@@ -17,10 +20,11 @@
 
 namespace {
 
-constexpr int GU_ROWS = 32;    // inter rows per gate_up CTA
+constexpr int GU_ROWS = 16;    // inter rows per gate_up CTA (two per warp)
 constexpr int GU_WARPS = 8;
-constexpr int DN_ROWS = 16;    // hidden rows per down CTA
-constexpr int DN_WARPS = 4;
+constexpr int DN_ROWS = 8;     // hidden rows per down CTA (one per warp)
+constexpr int DN_WARPS = 8;
+constexpr int DN_CHUNK = 8;    // experts whose warp reductions are batched together
 
 struct DecodeArgs {
   const void* x;
@@ -43,6 +47,12 @@ struct DecodeArgs {
   float* out;
   uint16_t* y;
   int32_t* err;
+};
+
+// XUnit as stored in shared memory: 16-byte aligned, 80 bytes.
+struct __align__(16) XUnitS {
+  float2 v[8];
+  float sum, pad0, pad1, pad2;
 };
 
 SSB_DEV void load_x16(const DecodeArgs& a, int64_t r, int u, float* x16) {
@@ -70,6 +80,17 @@ SSB_DEV void load_x16(const DecodeArgs& a, int64_t r, int u, float* x16) {
       x16[8 * q + 6] = bf16_lo(v.w);
       x16[8 * q + 7] = bf16_hi(v.w);
     }
+  }
+}
+
+// four independent warp sums, interleaved
+SSB_DEV void warp_sum4(float& a, float& b, float& c, float& d) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+    b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
+    c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
   }
 }
 
@@ -144,34 +165,39 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up(DecodeArgs a) {
     return;
   }
   const int ng = H / gs;
-  for (int j = warp; j < GU_ROWS; j += GU_WARPS) {
-    const uint2* gwr = reinterpret_cast<const uint2*>(gw + (size_t)j * H / 2);
-    const uint2* uwr = reinterpret_cast<const uint2*>(uw + (size_t)j * H / 2);
-    const uint16_t* gsr = reinterpret_cast<const uint16_t*>(gsc) + j * ng;
-    const uint16_t* gbr = reinterpret_cast<const uint16_t*>(gb) + j * ng;
-    const uint16_t* usr = reinterpret_cast<const uint16_t*>(usc) + j * ng;
-    const uint16_t* ubr = reinterpret_cast<const uint16_t*>(ub) + j * ng;
-    float ga = 0.f, ua = 0.f;
+  const int j0 = 2 * warp, j1 = j0 + 1;
+  const uint2* g0r = reinterpret_cast<const uint2*>(gw + (size_t)j0 * H / 2);
+  const uint2* u0r = reinterpret_cast<const uint2*>(uw + (size_t)j0 * H / 2);
+  const uint2* g1r = reinterpret_cast<const uint2*>(gw + (size_t)j1 * H / 2);
+  const uint2* u1r = reinterpret_cast<const uint2*>(uw + (size_t)j1 * H / 2);
+  const uint16_t* gs16 = reinterpret_cast<const uint16_t*>(gsc);
+  const uint16_t* gb16 = reinterpret_cast<const uint16_t*>(gb);
+  const uint16_t* us16 = reinterpret_cast<const uint16_t*>(usc);
+  const uint16_t* ub16 = reinterpret_cast<const uint16_t*>(ub);
+  float ga0 = 0.f, ua0 = 0.f, ga1 = 0.f, ua1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < NUX; ++i) {
-      int u = lane + 32 * i;
-      if (u < nunits) {
-        int g = (u * 16) / gs;
-        ga = unit_dot(gwr[u], bf16_bits(gsr[g]), bf16_bits(gbr[g]), xu[i], ga);
-        ua = unit_dot(uwr[u], bf16_bits(usr[g]), bf16_bits(ubr[g]), xu[i], ua);
-      }
+  for (int i = 0; i < NUX; ++i) {
+    int u = lane + 32 * i;
+    if (u < nunits) {
+      const int g = (u * 16) / gs;
+      ga0 = unit_dot(g0r[u], bf16_bits(gs16[j0 * ng + g]), bf16_bits(gb16[j0 * ng + g]), xu[i], ga0);
+      ua0 = unit_dot(u0r[u], bf16_bits(us16[j0 * ng + g]), bf16_bits(ub16[j0 * ng + g]), xu[i], ua0);
+      ga1 = unit_dot(g1r[u], bf16_bits(gs16[j1 * ng + g]), bf16_bits(gb16[j1 * ng + g]), xu[i], ga1);
+      ua1 = unit_dot(u1r[u], bf16_bits(us16[j1 * ng + g]), bf16_bits(ub16[j1 * ng + g]), xu[i], ua1);
     }
-    ga = warp_sum(ga);
-    ua = warp_sum(ua);
-    if (lane == 0) {
-      if (is_shared) {
-        // shared expert: lin() returns bf16, silu and the product round to bf16 (model/layers.py:398-400)
-        const float gb = round_bf16(ga), ub = round_bf16(ua);
-        hrow[n0 + j] = round_bf16(round_bf16(gb / (1.f + expf(-gb))) * ub);
-      } else {
-        hrow[n0 + j] = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u in fp32, kernels/moe_gemv_affine.py:76
-      }
+  }
+  warp_sum4(ga0, ua0, ga1, ua1);
+  if (lane < 2) {
+    const float ga = lane ? ga1 : ga0, ua = lane ? ua1 : ua0;
+    float h;
+    if (is_shared) {
+      // shared expert: lin() returns bf16, silu and the product round to bf16 (model/layers.py:398-400)
+      const float gbv = round_bf16(ga), ubv = round_bf16(ua);
+      h = round_bf16(round_bf16(gbv / (1.f + expf(-gbv))) * ubv);
+    } else {
+      h = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u in fp32, kernels/moe_gemv_affine.py:76
     }
+    hrow[n0 + j0 + lane] = h;
   }
 }
 
@@ -187,9 +213,11 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
   const int I = a.I, gs = a.gs, H = a.H;
   const bool has_sh = a.shared_rec != nullptr;
   const int nexp = a.topk + (has_sh ? 1 : 0);
+  const int nunits = I / 16, ng = I / gs;
   const uint32_t wbytes = (uint32_t)DN_ROWS * I / 2, sbytes = (uint32_t)DN_ROWS * (I / gs) * 2;
   const uint32_t ebytes = wbytes + 2 * sbytes;
-  float* hsm = reinterpret_cast<float*>(sm + (size_t)nexp * ebytes);   // [nexp][I] staged activations
+  float* hraw = reinterpret_cast<float*>(sm + (size_t)nexp * ebytes);                  // [nexp][I]
+  XUnitS* hx = reinterpret_cast<XUnitS*>(sm + (size_t)nexp * ebytes + (size_t)nexp * I * 4);  // [nexp][nunits]
   if (tid == 0) {
     mbar_init(&bar, 1);
     mbar_init(&bar_h, 1);
@@ -226,98 +254,111 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
     for (int j = 0; j < nexp; ++j) {
       if (!s_base[j]) continue;
       const int64_t pair = j >= a.topk ? a.R * a.topk + r : r * a.topk + j;
-      bulk_g2s(hsm + (size_t)j * I, a.h_buf + pair * I, (uint32_t)I * 4u, &bar_h);
+      bulk_g2s(hraw + (size_t)j * I, a.h_buf + pair * I, (uint32_t)I * 4u, &bar_h);
     }
   }
-  const bool ok = mbar_wait(&bar, 0, SSB_WAIT_LIMIT) && mbar_wait(&bar_h, 0, SSB_WAIT_LIMIT);
-  if (!ok) {
+  // the decision to give up is made for the whole CTA, so no thread is left at the barrier below
+  if (__syncthreads_or(!mbar_wait(&bar_h, 0, SSB_WAIT_LIMIT))) {
     if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
     mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
     mbar_wait(&bar_h, 0, SSB_WAIT_LIMIT);
     return;
   }
-  constexpr int RPW = DN_ROWS / DN_WARPS;
-  const int nunits = I / 16, ng = I / gs;
-  float acc[RPW], shv[RPW];
+  // pre-scaled per-unit form of every expert's activation, once per CTA
+  for (int idx = tid; idx < nexp * nunits; idx += DN_WARPS * 32) {
+    const int j = idx / nunits, u = idx - j * nunits;
+    XUnit xu;
+    if (s_base[j]) {
+      float h16[16];
+      const float4* hp = reinterpret_cast<const float4*>(hraw + (size_t)j * I + u * 16);
 #pragma unroll
-  for (int q = 0; q < RPW; ++q) acc[q] = shv[q] = 0.f;
-  for (int j = 0; j < nexp; ++j) {
-    const uint8_t* base = s_base[j];
-    const bool shared_j = j >= a.topk;
-    const int64_t pair = shared_j ? a.R * a.topk + r : r * a.topk + j;
-    float wt = 0.f;
-    if (base) wt = shared_j ? a.sh_gate[r] : a.wts[r * a.topk + j];
-    XUnit hu[NUI];
-    const float* hrow = hsm + (size_t)j * I;
-#pragma unroll
-    for (int i = 0; i < NUI; ++i) {
-      int u = lane + 32 * i;
-      if (u < nunits && base) {
-        float h16[16];
-        const float4* hp = reinterpret_cast<const float4*>(hrow + u * 16);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float4 v = hp[q];
-          h16[4 * q] = v.x;
-          h16[4 * q + 1] = v.y;
-          h16[4 * q + 2] = v.z;
-          h16[4 * q + 3] = v.w;
-        }
-        xunit_from_f32(hu[i], h16);
-      } else {
-        xunit_zero(hu[i]);
+      for (int q = 0; q < 4; ++q) {
+        float4 v = hp[q];
+        h16[4 * q] = v.x;
+        h16[4 * q + 1] = v.y;
+        h16[4 * q + 2] = v.z;
+        h16[4 * q + 3] = v.w;
       }
+      xunit_from_f32(xu, h16);
+    } else {
+      xunit_zero(xu);
     }
-    const uint8_t* ew = sm + (size_t)j * ebytes;
+    XUnitS& d = hx[idx];
 #pragma unroll
-    for (int q = 0; q < RPW; ++q) {
-      const int row = warp * RPW + q;
-      float d = 0.f;
-      if (base) {
+    for (int q = 0; q < 8; ++q) d.v[q] = xu.v[q];
+    d.sum = xu.sum;
+  }
+  __syncthreads();
+  if (!mbar_wait(&bar, 0, SSB_WAIT_LIMIT)) {
+    if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
+    mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
+    return;
+  }
+  const int row = warp;
+  const int m = m0 + row;
+  float acc = 0.f, shv = 0.f;
+  for (int c0 = 0; c0 < nexp; c0 += DN_CHUNK) {
+    float d[DN_CHUNK];
+#pragma unroll
+    for (int jj = 0; jj < DN_CHUNK; ++jj) {
+      d[jj] = 0.f;
+      const int j = c0 + jj;
+      if (j < nexp && s_base[j]) {
+        const uint8_t* ew = sm + (size_t)j * ebytes;
         const uint2* wr = reinterpret_cast<const uint2*>(ew + (size_t)row * I / 2);
         const uint16_t* sr = reinterpret_cast<const uint16_t*>(ew + wbytes) + row * ng;
         const uint16_t* br = reinterpret_cast<const uint16_t*>(ew + wbytes + sbytes) + row * ng;
 #pragma unroll
         for (int i = 0; i < NUI; ++i) {
-          int u = lane + 32 * i;
+          const int u = lane + 32 * i;
           if (u < nunits) {
-            int g = (u * 16) / gs;
-            d = unit_dot(wr[u], bf16_bits(sr[g]), bf16_bits(br[g]), hu[i], d);
+            const XUnitS& xs = hx[(size_t)j * nunits + u];
+            XUnit xu;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) xu.v[q] = xs.v[q];
+            xu.sum = xs.sum;
+            const int g = (u * 16) / gs;
+            d[jj] = unit_dot(wr[u], bf16_bits(sr[g]), bf16_bits(br[g]), xu, d[jj]);
           }
         }
-        d = warp_sum(d);
       }
-      if (shared_j) {
-        // shared expert with the reference's bf16 roundings: lin(h, D) -> bf16, then sigmoid-gate * sh -> bf16
-        // (model/layers.py:398-402); sh_gate already holds bf16(sigmoid(bf16(x . g)))
-        shv[q] = round_bf16(wt * round_bf16(d));
-      } else {
-        const float o = d * wt;   // acc * w, kernels/moe_gemv_affine.py:96-97
-        acc[q] = (j == 0) ? o : acc[q] + o;   // rank order, kernels/moe_gemv_affine.py:108-109
-        if (lane == 0 && a.o_buf) a.o_buf[pair * H + m0 + row] = o;
+    }
+#pragma unroll
+    for (int jj = 0; jj < DN_CHUNK; jj += 4) warp_sum4(d[jj], d[jj + 1], d[jj + 2], d[jj + 3]);
+    if (lane == 0) {
+#pragma unroll
+      for (int jj = 0; jj < DN_CHUNK; ++jj) {
+        const int j = c0 + jj;
+        if (j >= nexp) break;
+        const bool shared_j = j >= a.topk;
+        float wt = 0.f;
+        if (s_base[j]) wt = shared_j ? a.sh_gate[r] : a.wts[r * a.topk + j];
+        if (shared_j) {
+          // shared expert with the reference's bf16 roundings: lin(h, D) -> bf16, then sigmoid-gate * sh -> bf16
+          // (model/layers.py:398-402); sh_gate already holds bf16(sigmoid(bf16(x . g)))
+          shv = round_bf16(wt * round_bf16(d[jj]));
+        } else {
+          const float o = d[jj] * wt;   // acc * w, kernels/moe_gemv_affine.py:96-97
+          acc = (j == 0) ? o : acc + o;   // rank order, kernels/moe_gemv_affine.py:108-109
+          if (a.o_buf) a.o_buf[(r * a.topk + j) * H + m] = o;
+        }
       }
     }
   }
   if (lane == 0) {
-#pragma unroll
-    for (int q = 0; q < RPW; ++q) {
-      const int m = m0 + warp * RPW + q;
-      a.out[r * H + m] = acc[q];
-      if (a.y) a.y[r * H + m] = f32_to_bf16(round_bf16(acc[q]) + shv[q]);   // routed.to(bf16) + sh
-    }
+    a.out[r * H + m] = acc;
+    if (a.y) a.y[r * H + m] = f32_to_bf16(round_bf16(acc) + shv);   // routed.to(bf16) + sh
   }
 }
-
-template <int N>
-struct Disp {};
 
 int launch_decode(DecodeArgs a, cudaStream_t st, bool pdl) {
   const int nux = (a.H / 16 + 31) / 32;
   const int nui = (a.I / 16 + 31) / 32;
+  const int nexp = a.topk + (a.shared_rec ? 1 : 0);
   const int64_t pairs = a.R * a.topk + (a.shared_rec ? a.R : 0);
   const size_t gu_smem = (size_t)2 * GU_ROWS * a.H / 2 + (size_t)4 * GU_ROWS * (a.H / a.gs) * 2;
-  const size_t dn_smem = (size_t)(a.topk + (a.shared_rec ? 1 : 0)) *
-                         ((size_t)DN_ROWS * a.I / 2 + (size_t)2 * DN_ROWS * (a.I / a.gs) * 2 + (size_t)a.I * 4);
+  const size_t dn_smem = (size_t)nexp * ((size_t)DN_ROWS * a.I / 2 + (size_t)2 * DN_ROWS * (a.I / a.gs) * 2 +
+                                         (size_t)a.I * 4 + (size_t)(a.I / 16) * sizeof(XUnitS));
   if (gu_smem > 200 * 1024 || dn_smem > 200 * 1024) return SSB_EUNSUPPORTED;
   if (pairs > 65535 || a.R > 65535) return SSB_EUNSUPPORTED;
   void (*gu)(DecodeArgs) = nullptr;

@@ -1,22 +1,25 @@
 // Grouped affine-4-bit GEMM on the 5th-generation tensor cores (tcgen05 + TMEM) for the prefill MoE
-// (slotstream_spark/kernels/fused_moe_affine.py:53-127) and the dense prefill GEMM (kernels/gemm_affine.py).
+// (slotstream_spark/kernels/fused_moe_affine.py:53-127) and the dense prefill GEMMs (kernels/gemm_affine.py).
 //
-// One CTA computes a 128-row block (one expert's rows, from moe_align) times 256 B-rows:
-//  * gate_up: the 256 B-rows are 128 gate rows + 128 up rows of the same inter columns, so one
-//    M128xN256 accumulator holds both and the epilogue forms h = silu(g) * u -> bf16
-//    (kernels/fused_moe_affine.py:76-81);
+// Tiles are 128 rows (one expert's rows, from moe_align) x 256 B-rows:
+//  * gate_up: the 256 B-rows are 128 gate rows + 128 up rows of the same inter columns, so one M128xN256
+//    accumulator holds both and the epilogue forms h = silu(g) * u -> bf16 (kernels/fused_moe_affine.py:76-81);
 //  * down / plain: 256 output columns; the epilogue scales by the row's routing weight (fp32 out,
 //    kernels/fused_moe_affine.py:103-108) or stores plain fp32 (kernels/gemm_affine.py:19-37).
-// Warp roles (12 warps):
-//  * warp 0      gathers the block's activation rows with 16-byte cp.async into 128B-swizzled K-major tiles;
-//  * warp 1      owns TMEM (256 columns) and issues tcgen05.mma (M128 N256 K16, four per 64-wide k-block);
-//  * warps 4..11 stage their weight row's packed nibbles and bf16 scale/bias with cp.async, dequantise
-//                q*s + b in fp32 (two roundings, as kernels/affine_ref.py:22-31) -> bf16 (the reference's
-//                _wtile rounding, kernels/fused_moe_affine.py:38-50) into the swizzled B tile, then run
-//                the epilogue from TMEM.
-// Stages are handed over with mbarriers (full_a / full_b / empty); every wait gives up after a bounded time
-// and sets SSB_ERR_TIMEOUT instead of hanging. A row's result depends only on that row and that expert's
-// bytes: the k order is fixed, so any row count or group composition gives the same bits.
+// The kernel is persistent: one CTA per SM walks tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (m-block
+// major, so concurrent CTAs share activation rows and expert weights in L2). TMEM holds two accumulators, so
+// the epilogue of tile i overlaps the MMAs of tile i+1, and the operand pipelines run across tile borders.
+// Warp roles (16 warps):
+//  * warp 0      gathers the tile's activation rows with 16-byte cp.async into 128B-swizzled K-major tiles;
+//  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma (M128 N256 K16, four per 64-wide k-block);
+//  * warps 4..7  epilogue: TMEM -> registers -> global, one accumulator row per thread;
+//  * warps 8..15 weight producers: stage their B-row's packed nibbles and bf16 scale/bias with cp.async,
+//                dequantise q*s + b -> bf16 (the reference kernel's _wtile, kernels/fused_moe_affine.py:38-50,
+//                whose q * sc + bi compiles to a fused multiply-add) into the swizzled B tile; or, for bf16
+//                weights, cp.async the row straight into the tile.
+// Stages are handed over with mbarriers; every wait gives up after a bounded time and sets SSB_ERR_TIMEOUT
+// instead of hanging. A row's result depends only on that row and that expert's bytes: the k order is fixed,
+// so any row count or group composition gives the same bits.
 #include "registry.h"
 #include "tc_common.cuh"
 
@@ -25,14 +28,14 @@ namespace {
 constexpr int BM = 128, BK = 64, BN = 256;
 constexpr int STAGES = 3;        // A/B operand stages
 constexpr int PD = 3;            // weight staging depth of each producer thread
-constexpr int THREADS = 384;
-constexpr int A_WARP = 0, MMA_WARP = 1, PROD_WARP0 = 4, N_PROD = 256;
+constexpr int THREADS = 512;
+constexpr int A_WARP = 0, MMA_WARP = 1, EPI_WARP0 = 4, PROD_WARP0 = 8, N_PROD = 256;
 constexpr uint32_t A_STAGE = BM * 128;           // 16 KB
 constexpr uint32_t B_STAGE = BN * 128;           // 32 KB
 constexpr uint32_t W_STG = N_PROD * 32;          // packed nibbles of one k-block, 32 B per B-row
 constexpr uint32_t SB_STG = N_PROD * 4;          // 4-byte words holding the scale (or bias) of the k-block
 constexpr uint32_t STG = W_STG + 2 * SB_STG;
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_COLS = 512;              // two M128 x N256 fp32 accumulators
 
 enum { EPI_SWIGLU = 0, EPI_SCALE = 1, EPI_PLAIN = 2 };
 
@@ -42,7 +45,9 @@ struct GemmArgs {
   const int32_t* row_token;   // nullable: the A row of row r is r
   const int32_t* sorted_rows; // nullable: identity (rows m < R)
   const int32_t* block_expert;
-  const int32_t* num_padded;
+  const int32_t* num_padded;  // nullable: n_mblocks blocks
+  int64_t n_mblocks;
+  int n_nblocks;
   int64_t R;                  // rows; sorted_rows entries >= R are padding
   const int64_t* group_base;  // record (or weight) base address per local expert; nullable: base0
   const uint8_t* base0;
@@ -65,14 +70,13 @@ struct Smem {
   uint64_t* full_a;
   uint64_t* full_b;
   uint64_t* empty;
-  uint64_t* acc_full;
+  uint64_t* tmem_full;    // [2]
+  uint64_t* tmem_empty;   // [2]
   uint32_t* tmem;
-  int64_t* arow;
-  int32_t* orow;
+  int64_t* arow;          // A-row offsets of the tile the gather warp is loading
 };
 
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + PD * STG + 8 * (3 * STAGES + 1) + 16 +
-                              BM * 8 + BM * 4;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + PD * STG + 8 * (3 * STAGES + 4) + 16 + BM * 8;
 
 SSB_DEV Smem carve(uint8_t* raw) {
   Smem s;
@@ -86,48 +90,48 @@ SSB_DEV Smem carve(uint8_t* raw) {
   s.full_a = (uint64_t*)p;
   s.full_b = s.full_a + STAGES;
   s.empty = s.full_b + STAGES;
-  s.acc_full = s.empty + STAGES;
-  p += 8 * (3 * STAGES + 1);
+  s.tmem_full = s.empty + STAGES;
+  s.tmem_empty = s.tmem_full + 2;
+  p += 8 * (3 * STAGES + 4);
   s.tmem = (uint32_t*)p;
   p += 16;
   s.arow = (int64_t*)p;
-  p += BM * 8;
-  s.orow = (int32_t*)p;
   return s;
 }
 
-SSB_DEV uint32_t pack_bf16x2(float lo, float hi) {
-  return (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
+// Hardware round-to-nearest-even of two floats into packed bf16 (lo in the low half).
+SSB_DEV uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
-// fl(fl(q*s) + b) for the 8 nibbles of w; sc[j] = s * 16^-j' matches the magic-number scale of nibble j
-SSB_DEV void dequant_word(uint32_t w, const float* sc, float b, float* o) {
+// 8 nibbles of w -> 8 bf16 values fma(q, s, b) in one uint4. The magic-number floats are q * 16^j' exactly;
+// sc2 holds s * 16^-j' for the matching lanes, so each product is formed exactly before the fused add.
+SSB_DEV uint4 dequant8(uint32_t w, const float2* sc2, float2 b2) {
   const uint32_t M = 0x4B000000u;
   const uint32_t w5 = w >> 12;
-  const float m = 8388608.f;
-  float f[8];
-  f[0] = __uint_as_float((w & 0xFu) | M) - m;
-  f[1] = __uint_as_float((w & 0xF0u) | M) - m;
-  f[2] = __uint_as_float((w & 0xF00u) | M) - m;
-  f[3] = __uint_as_float((w & 0xF000u) | M) - m;
-  f[4] = __uint_as_float((w & 0xF0000u) | M) - m;
-  f[5] = __uint_as_float((w5 & 0xF00u) | M) - m;
-  f[6] = __uint_as_float((w5 & 0xF000u) | M) - m;
-  f[7] = __uint_as_float((w5 & 0xF0000u) | M) - m;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(__fmul_rn(f[j], sc[j]), b);
+  const float2 m2 = make_float2(-8388608.f, -8388608.f);
+  float2 f0 = make_float2(__uint_as_float((w & 0xFu) | M), __uint_as_float((w & 0xF0u) | M));
+  float2 f1 = make_float2(__uint_as_float((w & 0xF00u) | M), __uint_as_float((w & 0xF000u) | M));
+  float2 f2 = make_float2(__uint_as_float((w & 0xF0000u) | M), __uint_as_float((w5 & 0xF00u) | M));
+  float2 f3 = make_float2(__uint_as_float((w5 & 0xF000u) | M), __uint_as_float((w5 & 0xF0000u) | M));
+  f0 = __ffma2_rn(__fadd2_rn(f0, m2), sc2[0], b2);
+  f1 = __ffma2_rn(__fadd2_rn(f1, m2), sc2[1], b2);
+  f2 = __ffma2_rn(__fadd2_rn(f2, m2), sc2[2], b2);
+  f3 = __ffma2_rn(__fadd2_rn(f3, m2), sc2[3], b2);
+  return make_uint4(cvt_bf16x2(f0.x, f0.y), cvt_bf16x2(f1.x, f1.y), cvt_bf16x2(f2.x, f2.y), cvt_bf16x2(f3.x, f3.y));
 }
 
-SSB_DEV void scales_for(float s, float* sc) {
-  sc[0] = s;
-  sc[1] = s * 0.0625f;
-  sc[2] = s * 0.00390625f;
-  sc[3] = s * 0.000244140625f;
-  sc[4] = s * 1.52587890625e-05f;
-  sc[5] = sc[2];
-  sc[6] = sc[3];
-  sc[7] = sc[4];
+SSB_DEV void scales2(float s, float2* sc2) {
+  const float s1 = s * 0.0625f, s2 = s * 0.00390625f, s3 = s * 0.000244140625f, s4 = s * 1.52587890625e-05f;
+  sc2[0] = make_float2(s, s1);
+  sc2[1] = make_float2(s2, s3);
+  sc2[2] = make_float2(s4, s2);
+  sc2[3] = make_float2(s3, s4);
 }
+
+SSB_DEV float silu_fast(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
@@ -135,24 +139,24 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
   Smem S = carve(smraw);
   __shared__ int s_fail;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int mb = blockIdx.y, nb = blockIdx.x;
   pdl_wait();
   pdl_trigger();
-  if (a.num_padded && (int64_t)mb * BM >= (int64_t)__ldcg(a.num_padded)) return;
-  const int e = a.block_expert ? __ldcg(a.block_expert + mb) : 0;
-  if (e < 0 || e >= a.n_groups) return;
-  const uint8_t* base = a.group_base ? (const uint8_t*)a.group_base[e] : a.base0;
-  if (((uintptr_t)base & 15) || base == nullptr) {
-    if (tid == 0) set_err(a.err, SSB_ERR_MISALIGNED);
-    return;
-  }
-  if (tid < BM) {
-    const int64_t m = (int64_t)mb * BM + tid;
-    const int64_t row = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
-    const bool ok = row >= 0 && row < a.R;
-    S.orow[tid] = ok ? (int32_t)row : -1;
-    S.arow[tid] = ok ? (a.row_token ? (int64_t)__ldcg(a.row_token + row) : row) * a.lda : -1;
-  }
+  const int NB = a.n_nblocks;
+  const int64_t n_mb = a.num_padded ? (int64_t)__ldcg(a.num_padded) / BM : a.n_mblocks;
+  const int64_t n_tiles = n_mb * NB;
+  if ((int64_t)blockIdx.x >= n_tiles) return;
+  const int my_tiles = (int)((n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x);
+  const int KB = a.K / BK;
+  const int64_t steps = (int64_t)my_tiles * KB;
+  auto tile_of = [&](int i) -> int64_t { return (int64_t)blockIdx.x + (int64_t)i * gridDim.x; };
+  // local expert and weight base of m-block mb (nullptr: unusable, its B tile is zero)
+  auto expert_of = [&](int64_t mb) -> int { return a.block_expert ? __ldcg(a.block_expert + mb) : 0; };
+  auto base_of = [&](int e) -> const uint8_t* {
+    if (e < 0 || e >= a.n_groups) return nullptr;
+    const uint8_t* b = a.group_base ? (const uint8_t*)__ldg(a.group_base + e) : a.base0;
+    return ((uintptr_t)b & 15) ? nullptr : b;
+  };
+
   if (tid == 0) {
     s_fail = 0;
     for (int s = 0; s < STAGES; ++s) {
@@ -160,7 +164,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
       mbar_init(&S.full_b[s], N_PROD);
       mbar_init(&S.empty[s], 1);
     }
-    mbar_init(S.acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.tmem_full[i], 1);
+      mbar_init(&S.tmem_empty[i], 4);
+    }
     fence_mbar_init();
   }
   if (warp == MMA_WARP) tmem_alloc(S.tmem, TMEM_COLS);
@@ -168,14 +175,26 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *S.tmem;
-  const int KB = a.K / BK;
 
   if (warp == A_WARP) {
     // ---------------- activation gather: 1024 16-byte chunks per k-block, 32 per lane
     const int c = lane & 7;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES, r = kb / STAGES;
-      if (!mbar_wait_ns(&S.empty[s], (r & 1) ^ 1, SSB_WAIT_NS)) {
+    for (int64_t j = 0; j < steps; ++j) {
+      const int kb = (int)(j % KB);
+      if (kb == 0) {   // new tile: this warp alone owns the row table
+        const int64_t mb = tile_of((int)(j / KB)) / NB;
+        __syncwarp();
+        for (int r = lane; r < BM; r += 32) {
+          const int64_t m = mb * BM + r;
+          const int64_t row = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
+          const bool ok = row >= 0 && row < a.R;
+          S.arow[r] = ok ? (a.row_token ? (int64_t)__ldcg(a.row_token + row) : row) * a.lda : -1;
+        }
+        __syncwarp();
+      }
+      const int s = (int)(j % STAGES);
+      const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+      if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
         s_fail = 1;
         break;
       }
@@ -191,211 +210,229 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
     }
     cp_async_wait_all();
   } else if (warp == MMA_WARP) {
-    // ---------------- single-thread MMA issue
+    // ---------------- single-thread MMA issue, double-buffered accumulators
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(BM, BN);
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES, r = kb / STAGES;
-        if (!mbar_wait_ns(&S.full_a[s], r & 1, SSB_WAIT_NS) || !mbar_wait_ns(&S.full_b[s], r & 1, SSB_WAIT_NS)) {
+      int64_t j = 0;
+      for (int i = 0; i < my_tiles && !s_fail; ++i) {
+        const int acc = i & 1;
+        if (!mbar_wait_ns(&S.tmem_empty[acc], ((i >> 1) & 1) ^ 1, SSB_WAIT_NS)) {
           s_fail = 1;
           break;
         }
-        fence_proxy_async_smem();
         tc_fence_after();
-        const uint64_t da = umma_desc_sw128(smem_u32(S.a + s * A_STAGE));
-        const uint64_t db = umma_desc_sw128(smem_u32(S.b + s * B_STAGE));
+        const uint32_t d = tmem + (uint32_t)acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++j) {
+          const int s = (int)(j % STAGES);
+          const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+          if (!mbar_wait_ns(&S.full_a[s], ph, SSB_WAIT_NS) || !mbar_wait_ns(&S.full_b[s], ph, SSB_WAIT_NS)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128(smem_u32(S.a + s * A_STAGE));
+          const uint64_t db = umma_desc_sw128(smem_u32(S.b + s * B_STAGE));
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          umma_bf16(tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb | k) != 0);
-        umma_commit(&S.empty[s]);
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+          umma_commit(&S.empty[s]);
+        }
+        umma_commit(&S.tmem_full[acc]);
+        if (!ok) {
+          s_fail = 1;
+          break;
+        }
       }
-      umma_commit(S.acc_full);
     }
     __syncwarp();
+  } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
+    // ---------------- epilogue: one accumulator row per thread
+    const int q = warp & 3;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int acc = i & 1;
+      const int64_t t = tile_of(i), mb = t / NB;
+      const int nb = (int)(t % NB);
+      const int64_t m = mb * BM + 32 * q + lane;
+      const int64_t row = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
+      const bool valid = row >= 0 && row < a.R;
+      const bool shared_e = a.shared_local >= 0 && expert_of(mb) == a.shared_local;
+      const float wt = (EPI == EPI_SCALE && valid) ? __ldcg(a.row_weight + row) : 1.f;
+      const bool ok = mbar_wait_ns(&S.tmem_full[acc], (i >> 1) & 1, SSB_WAIT_NS);
+      tc_fence_after();
+      if (!ok) {
+        s_fail = 1;
+        break;
+      }
+      const uint32_t taddr = tmem + (uint32_t)acc * BN + ((uint32_t)(32 * q) << 16);
+      if (EPI == EPI_SWIGLU) {
+        uint16_t* out = (uint16_t*)a.out;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          const int col = 32 * cc;
+          float g[32], u[32];
+          tmem_ld32(taddr + col, g);
+          tmem_ld32(taddr + BN / 2 + col, u);
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(out + row * a.ldo + (int64_t)nb * (BN / 2) + col);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              float h[8];
+#pragma unroll
+              for (int tt = 0; tt < 8; ++tt) {
+                const float gg = g[8 * jj + tt], uu = u[8 * jj + tt];
+                if (shared_e) {   // shared expert: bf16(silu(bf16 g)) * bf16 u (model/moe_sweep.py:37-43)
+                  const float gb = round_bf16(gg);
+                  h[tt] = round_bf16(gb / (1.f + expf(-gb))) * round_bf16(uu);
+                } else {
+                  h[tt] = silu_fast(gg) * uu;   // accg / (1 + exp(-accg)) * accu, kernels/fused_moe_affine.py:80
+                }
+              }
+              dst[jj] = make_uint4(cvt_bf16x2(h[0], h[1]), cvt_bf16x2(h[2], h[3]), cvt_bf16x2(h[4], h[5]),
+                                   cvt_bf16x2(h[6], h[7]));
+            }
+          }
+        }
+      } else {
+        float* out = (float*)a.out;
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          const int col = 32 * cc;
+          float v[32];
+          tmem_ld32(taddr + col, v);
+          if (valid) {
+            float4* dst = reinterpret_cast<float4*>(out + row * a.ldo + (int64_t)nb * BN + col);
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              float4 o;
+              if (EPI == EPI_SCALE && shared_e) {   // bf16(sigmoid gate * bf16(h D^T))
+                o = make_float4(round_bf16(wt * round_bf16(v[4 * jj])), round_bf16(wt * round_bf16(v[4 * jj + 1])),
+                                round_bf16(wt * round_bf16(v[4 * jj + 2])), round_bf16(wt * round_bf16(v[4 * jj + 3])));
+              } else if (EPI == EPI_SCALE) {
+                o = make_float4(v[4 * jj] * wt, v[4 * jj + 1] * wt, v[4 * jj + 2] * wt, v[4 * jj + 3] * wt);
+              } else {
+                o = make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+              }
+              dst[jj] = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.tmem_empty[acc]);   // the accumulator may be overwritten now
+    }
   } else if (warp >= PROD_WARP0) {
     // ---------------- weight producers: one B-row per thread
     const int p = tid - PROD_WARP0 * 32;
-    int piece, nrow;
-    if (EPI == EPI_SWIGLU) {
-      piece = p >> 7;
-      nrow = nb * (BN / 2) + (p & 127);
-    } else {
-      piece = 0;
-      nrow = nb * BN + p;
-    }
+    const int piece = (EPI == EPI_SWIGLU) ? (p >> 7) : 0;
+    const int ng = a.K / a.gs;
+    // weight row of B-row p for step j (nullptr: zero row)
+    auto wrow_of = [&](int64_t j, const uint8_t** base_out) -> int64_t {
+      const int64_t t = tile_of((int)(j / KB));
+      const int64_t mb = t / NB;
+      const int nb = (int)(t % NB);
+      *base_out = base_of(expert_of(mb));
+      return (EPI == EPI_SWIGLU) ? (int64_t)nb * (BN / 2) + (p & 127) : (int64_t)nb * BN + p;
+    };
     if (a.dense_b) {
-      // plain bf16 weight rows: 16-byte cp.async straight into the swizzled tile, no dequantisation
-      const uint16_t* drow = (const uint16_t*)base + (int64_t)nrow * a.ldb;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % STAGES, r = kb / STAGES;
-        if (!mbar_wait_ns(&S.empty[s], (r & 1) ^ 1, SSB_WAIT_NS)) {
+      for (int64_t j = 0; j < steps; ++j) {
+        const int kb = (int)(j % KB);
+        const uint8_t* base;
+        const int64_t nrow = wrow_of(j, &base);
+        const int s = (int)(j % STAGES);
+        const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+        if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
           s_fail = 1;
           break;
         }
         const uint32_t bt = smem_u32(S.b + s * B_STAGE);
+        const uint16_t* drow = base ? (const uint16_t*)base + nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + kb * BK + c * 8, 16);
+        for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + c * 8, base ? 16u : 0u);
         cp_async_arrive(&S.full_b[s]);
       }
-    }
-    const int ng = a.K / a.gs;
-    const uint8_t* wrow = base + a.off_w[piece] + (int64_t)nrow * (a.K / 2);
-    const uint16_t* srow = (const uint16_t*)(base + a.off_s[piece]) + (int64_t)nrow * ng;
-    const uint16_t* brow = (const uint16_t*)(base + a.off_b[piece]) + (int64_t)nrow * ng;
-    auto issue = [&](int kb) {
-      uint8_t* st = S.stg + (kb % PD) * STG;
-      const uint32_t dw = smem_u32(st + p * 32);
-      cp_async16(dw, wrow + kb * 32, 16);
-      cp_async16(dw + 16, wrow + kb * 32 + 16, 16);
-      // the 4-byte-aligned word that holds the k-block's scale (bias): group kb (gs 64) or 2kb, 2kb+1 (gs 32)
-      const int g0 = a.gs == 64 ? kb : 2 * kb;
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + p * 4)),
-                   "l"(srow + (g0 & ~1)) : "memory");
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + SB_STG + p * 4)),
-                   "l"(brow + (g0 & ~1)) : "memory");
-    };
-    for (int kb = 0; kb < PD - 1 && kb < KB && !a.dense_b; ++kb) {
-      issue(kb);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-    for (int kb = 0; kb < KB && !a.dense_b; ++kb) {
-      if (kb + PD - 1 < KB) issue(kb + PD - 1);
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_group %0;" ::"n"(PD - 1) : "memory");
-      const uint8_t* st = S.stg + (kb % PD) * STG;
-      const uint4 w0 = *reinterpret_cast<const uint4*>(st + p * 32);
-      const uint4 w1 = *reinterpret_cast<const uint4*>(st + p * 32 + 16);
-      const uint32_t sw = *reinterpret_cast<const uint32_t*>(st + W_STG + p * 4);
-      const uint32_t bw = *reinterpret_cast<const uint32_t*>(st + W_STG + SB_STG + p * 4);
-      float s0, b0, s1, b1;
-      if (a.gs == 64) {
-        s0 = s1 = (kb & 1) ? bf16_hi(sw) : bf16_lo(sw);
-        b0 = b1 = (kb & 1) ? bf16_hi(bw) : bf16_lo(bw);
-      } else {
-        s0 = bf16_lo(sw);
-        s1 = bf16_hi(sw);
-        b0 = bf16_lo(bw);
-        b1 = bf16_hi(bw);
-      }
-      float sc0[8], sc1[8];
-      scales_for(s0, sc0);
-      scales_for(s1, sc1);
-      const int s = kb % STAGES, r = kb / STAGES;
-      if (!mbar_wait_ns(&S.empty[s], (r & 1) ^ 1, SSB_WAIT_NS)) {
-        s_fail = 1;
-        break;
-      }
-      uint8_t* bt = S.b + s * B_STAGE;
-      const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {     // chunk c = elements 8c..8c+7 = word c
-        float v[8];
-        dequant_word(ws[c], c < 4 ? sc0 : sc1, c < 4 ? b0 : b1, v);
-        uint4 o;
-        o.x = pack_bf16x2(v[0], v[1]);
-        o.y = pack_bf16x2(v[2], v[3]);
-        o.z = pack_bf16x2(v[4], v[5]);
-        o.w = pack_bf16x2(v[6], v[7]);
-        *reinterpret_cast<uint4*>(bt + swz128(p, c)) = o;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&S.full_b[s]);
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-
-    // ---------------- epilogue from TMEM
-    const bool ok = mbar_wait_ns(S.acc_full, 0, SSB_WAIT_NS);
-    tc_fence_after();
-    const int q = (warp - PROD_WARP0) & 3, half = (warp - PROD_WARP0) >> 2;
-    const int orow = S.orow[32 * q + lane];
-    const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
-    // the shared expert follows the reference's bf16 rounding between ops (model/moe_sweep.py:37-43)
-    const bool shared_e = e == a.shared_local;
-    if (!ok) {
-      s_fail = 1;
-    } else if (EPI == EPI_SWIGLU && shared_e) {
-      uint16_t* out = (uint16_t*)a.out;
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int col = 64 * half + 32 * cc;
-        float g[32], u[32];
-        tmem_ld32(taddr + col, g);
-        tmem_ld32(taddr + 128 + col, u);
-        if (orow >= 0) {
-          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)orow * a.ldo + nb * (BN / 2) + col);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float h[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              const float gb = round_bf16(g[8 * j + t]), ub = round_bf16(u[8 * j + t]);
-              h[t] = round_bf16(gb / (1.f + expf(-gb))) * ub;   // bf16(silu(bf16 g)) * bf16 u -> bf16 below
-            }
-            dst[j] = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
-                                pack_bf16x2(h[6], h[7]));
-          }
-        }
-      }
-    } else if (EPI == EPI_SWIGLU) {
-      uint16_t* out = (uint16_t*)a.out;
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int col = 64 * half + 32 * cc;
-        float g[32], u[32];
-        tmem_ld32(taddr + col, g);
-        tmem_ld32(taddr + 128 + col, u);
-        if (orow >= 0) {
-          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)orow * a.ldo + nb * (BN / 2) + col);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float h[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              const float gg = g[8 * j + t];
-              h[t] = gg / (1.f + expf(-gg)) * u[8 * j + t];   // silu(g) * u, kernels/fused_moe_affine.py:80
-            }
-            dst[j] = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
-                                pack_bf16x2(h[6], h[7]));
-          }
-        }
-      }
     } else {
-      float* out = (float*)a.out;
-      const float wt = (EPI == EPI_SCALE && orow >= 0) ? a.row_weight[orow] : 1.f;
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        const int col = 128 * half + 32 * cc;
-        float v[32];
-        tmem_ld32(taddr + col, v);
-        if (orow >= 0) {
-          float4* dst = reinterpret_cast<float4*>(out + (int64_t)orow * a.ldo + nb * BN + col);
-#pragma unroll
-          if (EPI == EPI_SCALE && shared_e) {   // bf16(sigmoid gate * bf16(D h))
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(round_bf16(wt * round_bf16(v[4 * j])), round_bf16(wt * round_bf16(v[4 * j + 1])),
-                                   round_bf16(wt * round_bf16(v[4 * j + 2])),
-                                   round_bf16(wt * round_bf16(v[4 * j + 3])));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 o;
-              o.x = EPI == EPI_SCALE ? v[4 * j] * wt : v[4 * j];
-              o.y = EPI == EPI_SCALE ? v[4 * j + 1] * wt : v[4 * j + 1];
-              o.z = EPI == EPI_SCALE ? v[4 * j + 2] * wt : v[4 * j + 2];
-              o.w = EPI == EPI_SCALE ? v[4 * j + 3] * wt : v[4 * j + 3];
-              dst[j] = o;
-            }
-          }
-        }
+      auto issue = [&](int64_t j) {
+        const int kb = (int)(j % KB);
+        const uint8_t* base;
+        const int64_t nrow = wrow_of(j, &base);
+        uint8_t* st = S.stg + (j % PD) * STG;
+        if (!base) return;
+        const uint8_t* wr = base + a.off_w[piece] + nrow * (a.K / 2) + kb * 32;
+        const uint16_t* sr = (const uint16_t*)(base + a.off_s[piece]) + nrow * ng;
+        const uint16_t* br = (const uint16_t*)(base + a.off_b[piece]) + nrow * ng;
+        const uint32_t dw = smem_u32(st + p * 32);
+        cp_async16(dw, wr, 16);
+        cp_async16(dw + 16, wr + 16, 16);
+        // the 4-byte-aligned word that holds the k-block's scale (bias): group kb (gs 64) or 2kb, 2kb+1 (gs 32)
+        const int g0 = a.gs == 64 ? kb : 2 * kb;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + p * 4)),
+                     "l"(sr + (g0 & ~1)) : "memory");
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + SB_STG + p * 4)),
+                     "l"(br + (g0 & ~1)) : "memory");
+      };
+      for (int64_t j = 0; j < PD - 1 && j < steps; ++j) {
+        issue(j);
+        asm volatile("cp.async.commit_group;" ::: "memory");
       }
+      for (int64_t j = 0; j < steps; ++j) {
+        if (j + PD - 1 < steps) issue(j + PD - 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(PD - 1) : "memory");
+        const int kb = (int)(j % KB);
+        const uint8_t* base;
+        (void)wrow_of(j, &base);
+        const uint8_t* st = S.stg + (j % PD) * STG;
+        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+        float s0 = 0.f, b0 = 0.f, s1 = 0.f, b1 = 0.f;
+        if (base) {
+          w0 = *reinterpret_cast<const uint4*>(st + p * 32);
+          w1 = *reinterpret_cast<const uint4*>(st + p * 32 + 16);
+          const uint32_t sw = *reinterpret_cast<const uint32_t*>(st + W_STG + p * 4);
+          const uint32_t bw = *reinterpret_cast<const uint32_t*>(st + W_STG + SB_STG + p * 4);
+          if (a.gs == 64) {
+            s0 = s1 = (kb & 1) ? bf16_hi(sw) : bf16_lo(sw);
+            b0 = b1 = (kb & 1) ? bf16_hi(bw) : bf16_lo(bw);
+          } else {
+            s0 = bf16_lo(sw);
+            s1 = bf16_hi(sw);
+            b0 = bf16_lo(bw);
+            b1 = bf16_hi(bw);
+          }
+        } else if (p == 0) {
+          set_err(a.err, SSB_ERR_MISALIGNED);
+        }
+        float2 sc0[4], sc1[4];
+        scales2(s0, sc0);
+        scales2(s1, sc1);
+        const float2 bb0 = make_float2(b0, b0), bb1 = make_float2(b1, b1);
+        const int s = (int)(j % STAGES);
+        const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+        if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
+          s_fail = 1;
+          break;
+        }
+        uint8_t* bt = S.b + s * B_STAGE;
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c)   // 16-byte chunk c = elements 8c..8c+7 = word c
+          *reinterpret_cast<uint4*>(bt + swz128(p, c)) = dequant8(ws[c], c < 4 ? sc0 : sc1, c < 4 ? bb0 : bb1);
+        fence_proxy_async_smem();
+        mbar_arrive(&S.full_b[s]);
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == MMA_WARP) {
-    if (s_fail) {   // let every issued MMA finish before the accumulator is released
-      if (lane == 0) mbar_wait_ns(S.acc_full, 0, SSB_WAIT_NS);
+    if (s_fail) {   // every committed MMA group finishes before the accumulators are released
+      if (lane == 0) {
+        mbar_wait_ns(&S.tmem_full[0], 0, SSB_WAIT_NS);
+        if (my_tiles > 1) mbar_wait_ns(&S.tmem_full[1], 0, SSB_WAIT_NS);
+      }
       __syncwarp();
     }
     tc_fence_after();
@@ -404,21 +441,33 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
   if (tid == 0 && s_fail) set_err(a.err, SSB_ERR_TIMEOUT);
 }
 
-int launch(int epi, const GemmArgs& a, int64_t n_mblocks, int n_nblocks, cudaStream_t st) {
+int num_sms() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+int launch(int epi, GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t st) {
   void (*k)(GemmArgs) = epi == EPI_SWIGLU ? k_moe_gemm<EPI_SWIGLU> : epi == EPI_SCALE ? k_moe_gemm<EPI_SCALE>
                                                                                       : k_moe_gemm<EPI_PLAIN>;
   if (n_mblocks <= 0) return SSB_OK;
-  if (n_mblocks > 65535 * 16) return SSB_EUNSUPPORTED;
   static bool attr_set[3] = {false, false, false};
   if (!attr_set[epi]) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
     attr_set[epi] = true;
   }
-  ssb_note_smem(epi == EPI_SWIGLU ? "fused_moe_gate_up" : epi == EPI_SCALE ? "fused_moe_down" : "gemm_affine4", k,
+  ssb_note_smem(epi == EPI_SWIGLU ? "fused_moe_gate_up" : epi == EPI_SCALE ? "fused_moe_down" : "gemm_tc", k,
                 SMEM_BYTES);
-  if (n_mblocks > 65535) return SSB_EUNSUPPORTED;
-  return ssb_launch(k, dim3(n_nblocks, (unsigned)n_mblocks), dim3(THREADS), SMEM_BYTES, st, true, a);
+  a.n_mblocks = n_mblocks;
+  a.n_nblocks = n_nblocks;
+  const int64_t tiles = n_mblocks * n_nblocks;
+  const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  return ssb_launch(k, dim3(grid), dim3(THREADS), SMEM_BYTES, st, true, a);
 }
 
 void set_record_offsets(GemmArgs& g, int hidden, int inter, bool gate_up) {
@@ -556,7 +605,7 @@ extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const i
 extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uint16_t* w, int32_t n, float* out,
                               int64_t ldo, void* stream) {
   SSB_CHECK_ARG(m >= 0 && k >= 1 && n >= 1 && ldo >= n && ldo % 4 == 0);
-  if (k % BK || n % BN || k % 8) return SSB_EUNSUPPORTED;
+  if (k % BK || n % BN) return SSB_EUNSUPPORTED;
   if (m == 0) return SSB_OK;
   SSB_CHECK_ARG(x && w && out && ((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0);
   GemmArgs g{};

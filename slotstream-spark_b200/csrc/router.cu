@@ -84,6 +84,42 @@ __global__ void __launch_bounds__(RL_WARPS * 32) k_router_logits(const uint16_t*
 constexpr int RS_WARPS = 4;
 constexpr int RS_MAXE = 32;  // experts per lane: experts <= 1024
 
+SSB_DEV void cswap_desc(unsigned long long& a, unsigned long long& b) {
+  const unsigned long long hi = a > b ? a : b, lo = a > b ? b : a;
+  a = hi;
+  b = lo;
+}
+// Sort 16 composites descending (bitonic network, fully unrolled).
+SSB_DEV void bitonic_sort_desc16(unsigned long long* x) {
+#pragma unroll
+  for (int size = 2; size <= 16; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          if ((i & size) == 0) cswap_desc(x[i], x[j]);
+          else cswap_desc(x[j], x[i]);
+        }
+      }
+    }
+  }
+}
+// A bitonic sequence of 16 -> descending.
+SSB_DEV void bitonic_merge_desc16(unsigned long long* x) {
+#pragma unroll
+  for (int stride = 8; stride > 0; stride >>= 1) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if ((i & stride) == 0) cswap_desc(x[i], x[i + stride]);
+  }
+}
+// The fp32 value whose order key is `key` (inverse of order_key for non-NaN values).
+SSB_DEV float key_value(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key ^ 0x80000000u) : ~key);
+}
+
 template <int EPL>
 __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __restrict__ logits, int ld,
                                                                   int64_t tokens, int experts, int k,
@@ -131,6 +167,44 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
     v[i] = p;
     c[i] = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
     if (out_probs && e < experts) out_probs[t * experts + e] = p;
+  }
+  if (EPL <= 16 && k <= 16) {
+    // Warp-wide top 16: each lane sorts its composites, then five butterfly steps merge the lanes' sorted
+    // lists (top 16 of two sorted lists = bitonic max, then a bitonic merge); every lane ends with the global
+    // top 16 in (value desc, index asc) order.
+    unsigned long long L[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) L[i] = i < EPL ? c[i < EPL ? i : 0] : 0ull;
+    bitonic_sort_desc16(L);
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      unsigned long long o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, L[i], off);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) L[i] = L[i] > o[15 - i] ? L[i] : o[15 - i];
+      bitonic_merge_desc16(L);
+    }
+    float sum = 0.f, my_p = 0.f;   // renormalise: sequential sum in rank order
+    unsigned long long mine = 0ull;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float pj = key_value((uint32_t)(L[j] >> 32));
+      if (j < k) sum += pj;
+      if (j == lane) {
+        mine = L[j];
+        my_p = pj;
+      }
+    }
+    if (lane < k) {
+      out_idx[t * k + lane] = (int32_t)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull));
+      out_w[t * k + lane] = my_p / sum;
+    }
+    if ((flags & SSB_ROUTER_SHARED_GATE) && lane == 0) {
+      const float gl = round_bf16(__ldcg(lrow + experts));
+      out_sh_gate[t] = round_bf16(1.f / (1.f + expf(-gl)));
+    }
+    return;
   }
   // k rounds of warp arg-max; round j's winner is the j-th output (value desc, index asc)
   int my_idx = -1;
