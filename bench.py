@@ -200,17 +200,15 @@ def bench_decode(args, world, rank):
     from slotstream_b200 import _lib
     st = torch.cuda.current_stream()
     for l in range(NL):
+        moe_layer_decode(x[l], router_w[l], l, map_t, slot_ptr, shared[l], sh_gate_w[l], K, bufs[l], bias=bias)
         flush.zero_()
-        from slotstream_b200.kernels.router import router_topk
-        router_topk(x[l], router_w[l], K, bufs[l].ids, bufs[l].w, bias=bias, sh_gate_w=sh_gate_w[l],
-                    out_sh_gate=bufs[l].sh_gate, ws=bufs[l].ws)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         rc = _lib.lib().ssb_moe_decode_layer(
             _lib.ptr(x[l]), _lib.ptr(bufs[l].ids), _lib.ptr(bufs[l].w), b, K, LAY.hidden, LAY.inter, l,
             _lib.ptr(map_t), map_t.numel(), _lib.ptr(slot_ptr), slot_ptr.numel(), shared[l].data_ptr(),
-            _lib.ptr(bufs[l].sh_gate), _lib.ptr(bufs[l].h), _lib.ptr(bufs[l].o), _lib.ptr(bufs[l].out),
-            _lib.ptr(bufs[l].y), 0, _lib.ptr(bufs[l].err), _lib.stream())
+            _lib.ptr(bufs[l].sh_gate), _lib.ptr(bufs[l].bases), _lib.ptr(bufs[l].h), _lib.ptr(bufs[l].o),
+            _lib.ptr(bufs[l].out), _lib.ptr(bufs[l].y), 0, _lib.ptr(bufs[l].err), _lib.stream())
         _lib.check(rc, "moe_decode_layer")
         e1.record(st)
         torch.cuda.synchronize()

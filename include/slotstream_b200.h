@@ -112,6 +112,7 @@ int ssb_moe_decode(const void* x, int32_t x_dtype, const int32_t* expert_ids, co
  *   sh[r, :] = sh_gate[r] * (D_s (silu(G_s x_r) * (U_s x_r)))
  *   y[r, :]  = bf16( bf16(out[r, :]) + bf16(sh[r, :]) )      (bf16 [rows, hidden])
  * h_buf must hold rows * (topk + 1) * inter floats (the shared expert's h follows the routed ones).
+ * expert_base (nullable) holds the resolved record base of every (row, rank) from ssb_router_select_resolve.
  * flags bit 0 (SSB_DECODE_PDL): launch with programmatic dependent launch.
  * Replaces: the decode MoE call site of slotstream_spark/runtime/graphs.py:160-169 (moe_decode + shared
  * expert + routed.to(bf16) + sh). */
@@ -119,8 +120,18 @@ int ssb_moe_decode(const void* x, int32_t x_dtype, const int32_t* expert_ids, co
 int ssb_moe_decode_layer(const uint16_t* x, const int32_t* expert_ids, const float* weights, int64_t rows,
                          int32_t topk, int32_t hidden, int32_t inter, int32_t layer, const int32_t* map_t,
                          int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots, const void* shared_record,
-                         const float* sh_gate, float* h_buf, float* o_buf, float* out, uint16_t* y,
-                         int32_t flags, int32_t* err, void* stream);
+                         const float* sh_gate, const int64_t* expert_base, float* h_buf, float* o_buf, float* out,
+                         uint16_t* y, int32_t flags, int32_t* err, void* stream);
+
+/* ssb_router_select plus expert resolution for the decode layer (additive): for every chosen expert the
+ * record base slot_ptr[map[layer*512 + e]] is written to out_base [tokens, k] (0 when unmapped; SSB_ERR_* bits
+ * in err) and the first prefetch_bytes of the record are prefetched into L2, so the expert GEMVs that follow
+ * read resolved addresses from a warm cache. Pass out_base as ssb_moe_decode_layer's expert_base.
+ * Replaces: the slot lookup of slotstream_spark/kernels/moe_gemv_affine.py:66-69 ahead of the GEMVs. */
+int ssb_router_select_resolve(const float* logits, int32_t ld, int64_t tokens, int32_t experts, int32_t k,
+                              const float* bias, int32_t flags, int32_t* out_idx, float* out_w, float* out_sh_gate,
+                              int32_t layer, const int32_t* map_t, int64_t map_len, const int64_t* slot_ptr_t,
+                              int64_t n_slots, int64_t* out_base, int64_t prefetch_bytes, int32_t* err, void* stream);
 
 /* Rank-order combine: out[t, :] = rows[t*k] + rows[t*k + 1] + ... sequentially in fp32.
  * rows fp32 [tokens * k, hidden], out fp32 [tokens, hidden]; hidden % 4 == 0.

@@ -89,10 +89,10 @@ SSB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit) {
   for (uint32_t i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(20000u)
         : "memory");
     if (done) return true;
   }
@@ -108,7 +108,7 @@ SSB_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 
 // Bound on mbarrier polls: far above any real copy time, small enough that a lost arrival ends the kernel
 // with an error bit instead of hanging the GPU.
-constexpr uint32_t SSB_WAIT_LIMIT = 1u << 22;
+constexpr uint32_t SSB_WAIT_LIMIT = 1u << 16;   // polls of up to 20 us each
 
 // ---------------------------------------------------------------- expert resolution through the slot tables
 

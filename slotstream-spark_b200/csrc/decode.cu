@@ -41,6 +41,7 @@ struct DecodeArgs {
   int64_t n_slots;
   const uint8_t* shared_rec;
   const float* sh_gate;
+  const int64_t* bases;   // nullable: record base of each (row, rank), already resolved by the router
   RecOffs o;
   float* h_buf;
   float* o_buf;
@@ -134,7 +135,8 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up(DecodeArgs a) {
   pdl_wait();
   pdl_trigger();
   if (tid == 0 && !is_shared) {
-    const uint8_t* base = resolve_expert(a.ids[p], a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots, a.err);
+    const uint8_t* base = a.bases ? (const uint8_t*)ld_cg_i64(a.bases + p)
+                                  : resolve_expert(a.ids[p], a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots, a.err);
     s_base = base;
     if (base) issue(base);
   }
@@ -227,9 +229,10 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
   // grid started, and every grid here triggers its dependents only after its own wait, so they are complete
   // and visible now (read through L2).
   if (tid < nexp) {
-    s_base[tid] = tid < a.topk ? resolve_expert(ld_cg_i32(a.ids + r * a.topk + tid), a.layer, a.map, a.map_len,
-                                                a.slot_ptr, a.n_slots, nullptr)
-                               : a.shared_rec;
+    if (tid >= a.topk) s_base[tid] = a.shared_rec;
+    else if (a.bases) s_base[tid] = (const uint8_t*)ld_cg_i64(a.bases + r * a.topk + tid);
+    else s_base[tid] = resolve_expert(ld_cg_i32(a.ids + r * a.topk + tid), a.layer, a.map, a.map_len, a.slot_ptr,
+                                      a.n_slots, nullptr);
   }
   __syncthreads();
   if (tid == 0) {
@@ -435,8 +438,9 @@ extern "C" int ssb_moe_decode(const void* x, int32_t x_dtype, const int32_t* exp
 extern "C" int ssb_moe_decode_layer(const uint16_t* x, const int32_t* expert_ids, const float* weights, int64_t rows,
                                     int32_t topk, int32_t hidden, int32_t inter, int32_t layer, const int32_t* map_t,
                                     int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots,
-                                    const void* shared_record, const float* sh_gate, float* h_buf, float* o_buf,
-                                    float* out, uint16_t* y, int32_t flags, int32_t* err, void* stream) {
+                                    const void* shared_record, const float* sh_gate, const int64_t* expert_base,
+                                    float* h_buf, float* o_buf, float* out, uint16_t* y, int32_t flags,
+                                    int32_t* err, void* stream) {
   int rc = check_shape(rows, topk, hidden, inter);
   if (rc) return rc;
   SSB_CHECK_ARG(layer >= 0 && map_len >= 0 && n_slots >= 0);
@@ -460,6 +464,7 @@ extern "C" int ssb_moe_decode_layer(const uint16_t* x, const int32_t* expert_ids
   a.n_slots = n_slots;
   a.shared_rec = (const uint8_t*)shared_record;
   a.sh_gate = sh_gate;
+  a.bases = expert_base;
   a.o = rec_offsets(hidden, inter, 64);
   a.h_buf = h_buf;
   a.o_buf = o_buf;

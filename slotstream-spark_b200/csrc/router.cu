@@ -7,7 +7,7 @@
 // "largest composite first" is exactly that order and every composite is distinct.
 #include <cub/block/block_scan.cuh>
 
-#include "common.cuh"
+#include "affine.cuh"
 #include "registry.h"
 
 namespace {
@@ -120,20 +120,68 @@ SSB_DEV float key_value(uint32_t key) {
   return __uint_as_float((key & 0x80000000u) ? (key ^ 0x80000000u) : ~key);
 }
 
+struct SelectArgs {
+  const float* logits;
+  int ld;
+  int64_t tokens;
+  int experts, k;
+  const float* bias;
+  int flags;
+  int32_t* out_idx;
+  float* out_w;
+  float* out_probs;
+  float* out_sh_gate;
+  // optional: resolve the chosen experts through the slot tables and prefetch their records into L2
+  int layer;
+  const int32_t* map;
+  int64_t map_len;
+  const int64_t* slot_ptr;
+  int64_t n_slots;
+  int64_t* out_base;
+  uint32_t prefetch_bytes;
+  int32_t* err;
+};
+
+// Lane `lane` (< k) holds the rank-`lane` composite; write ids and renormalised weights, then the optional
+// expert resolution / L2 prefetch and the shared-expert gate.
+SSB_DEV void select_tail(const SelectArgs& a, int64_t t, int lane, unsigned long long mine, float my_p, float sum,
+                         const float* lrow) {
+  const int k = a.k;
+  if (lane < k) {
+    const int e = (int)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull));
+    a.out_idx[t * k + lane] = e;
+    a.out_w[t * k + lane] = my_p / sum;
+    if (a.out_base) {
+      const uint8_t* base = resolve_expert(e, a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots, a.err);
+      a.out_base[t * k + lane] = (int64_t)base;
+      if (base && a.prefetch_bytes) {
+        for (uint32_t off = 0; off < a.prefetch_bytes; off += 65536u) {
+          const uint32_t n = a.prefetch_bytes - off < 65536u ? a.prefetch_bytes - off : 65536u;
+          prefetch_l2(base + off, n);
+        }
+      }
+    }
+  }
+  if ((a.flags & SSB_ROUTER_SHARED_GATE) && lane == 0) {
+    // sigmoid(lin(x, shared_expert_gate)) with lin's bf16 output and a bf16 sigmoid (model/layers.py:401)
+    const float gl = round_bf16(__ldcg(lrow + a.experts));
+    a.out_sh_gate[t] = round_bf16(1.f / (1.f + expf(-gl)));
+  }
+}
+
+constexpr int RS_CAND = 64;   // candidate slots per warp
+
 template <int EPL>
-__global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __restrict__ logits, int ld,
-                                                                  int64_t tokens, int experts, int k,
-                                                                  const float* __restrict__ bias, int flags,
-                                                                  int32_t* __restrict__ out_idx,
-                                                                  float* __restrict__ out_w,
-                                                                  float* __restrict__ out_probs,
-                                                                  float* __restrict__ out_sh_gate) {
+__global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(SelectArgs a) {
+  __shared__ unsigned long long s_cand[RS_WARPS][RS_CAND];
+  __shared__ unsigned long long s_top[RS_WARPS][16];
   pdl_wait();
   pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int64_t t = (int64_t)blockIdx.x * RS_WARPS + (threadIdx.x >> 5);
-  if (t >= tokens) return;
-  const float* lrow = logits + t * ld;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = (int64_t)blockIdx.x * RS_WARPS + warp;
+  if (t >= a.tokens) return;
+  const int experts = a.experts, k = a.k;
+  const float* lrow = a.logits + t * a.ld;
   float v[EPL];
   float m = -INFINITY;
 #pragma unroll
@@ -142,8 +190,8 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
     float l = -INFINITY;
     if (e < experts) {
       l = __ldcg(lrow + e);
-      if (bias) l = l + bias[e];
-      if (flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
+      if (a.bias) l = l + a.bias[e];
+      if (a.flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
       m = fmaxf(m, l);
     }
     v[i] = l;
@@ -160,13 +208,74 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
   }
   s = warp_sum(s);
   unsigned long long c[EPL];
+  unsigned long long lm = 0ull;
 #pragma unroll
   for (int i = 0; i < EPL; ++i) {
     int e = lane + 32 * i;
     float p = v[i] / s;
     v[i] = p;
     c[i] = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
-    if (out_probs && e < experts) out_probs[t * experts + e] = p;
+    lm = c[i] > lm ? c[i] : lm;
+    if (a.out_probs && e < experts) a.out_probs[t * experts + e] = p;
+  }
+  if (k <= 16) {
+    // Candidate filter: the k-th largest lane maximum T0 is a lower bound for the k-th largest composite (k
+    // lanes each hold an element >= T0), so only elements >= T0 can be selected. The candidates (usually a
+    // few more than k) are ranked by comparing against each other through shared memory.
+    int rk = 0;
+#pragma unroll
+    for (int d = 1; d < 32; ++d) {
+      const unsigned long long o = __shfl_sync(0xFFFFFFFFu, lm, (lane + d) & 31);
+      rk += o > lm;
+    }
+    const unsigned at = __ballot_sync(0xFFFFFFFFu, rk == k - 1 && lm != 0ull);
+    if (at) {
+      const unsigned long long T0 = __shfl_sync(0xFFFFFFFFu, lm, __ffs(at) - 1);
+      int n = 0;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) n += c[i] >= T0;
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+      if (total <= RS_CAND) {
+        int pos = incl - n;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+          if (c[i] >= T0) s_cand[warp][pos++] = c[i];
+        __syncwarp();
+        const unsigned long long a0 = lane < total ? s_cand[warp][lane] : 0ull;
+        const unsigned long long a1 = lane + 32 < total ? s_cand[warp][lane + 32] : 0ull;
+        int r0 = 0, r1 = 0;
+        for (int q = 0; q < total; ++q) {
+          const unsigned long long o = s_cand[warp][q];
+          r0 += o > a0;
+          r1 += o > a1;
+        }
+        if (lane < total && r0 < k) s_top[warp][r0] = a0;
+        if (lane + 32 < total && r1 < k) s_top[warp][r1] = a1;
+        __syncwarp();
+        float sum = 0.f, my_p = 0.f;   // renormalise: sequential sum in rank order
+        unsigned long long mine = 0ull;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (j < k) {
+            const unsigned long long cj = s_top[warp][j];
+            const float pj = key_value((uint32_t)(cj >> 32));
+            sum += pj;
+            if (j == lane) {
+              mine = cj;
+              my_p = pj;
+            }
+          }
+        }
+        select_tail(a, t, lane, mine, my_p, sum, lrow);
+        return;
+      }
+    }
   }
   if (EPL <= 16 && k <= 16) {
     // Warp-wide top 16: each lane sorts its composites, then five butterfly steps merge the lanes' sorted
@@ -185,7 +294,7 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
       for (int i = 0; i < 16; ++i) L[i] = L[i] > o[15 - i] ? L[i] : o[15 - i];
       bitonic_merge_desc16(L);
     }
-    float sum = 0.f, my_p = 0.f;   // renormalise: sequential sum in rank order
+    float sum = 0.f, my_p = 0.f;
     unsigned long long mine = 0ull;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -196,25 +305,18 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
         my_p = pj;
       }
     }
-    if (lane < k) {
-      out_idx[t * k + lane] = (int32_t)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull));
-      out_w[t * k + lane] = my_p / sum;
-    }
-    if ((flags & SSB_ROUTER_SHARED_GATE) && lane == 0) {
-      const float gl = round_bf16(__ldcg(lrow + experts));
-      out_sh_gate[t] = round_bf16(1.f / (1.f + expf(-gl)));
-    }
+    select_tail(a, t, lane, mine, my_p, sum, lrow);
     return;
   }
   // k rounds of warp arg-max; round j's winner is the j-th output (value desc, index asc)
-  int my_idx = -1;
+  unsigned long long mine = 0ull;
   float my_p = 0.f;
   for (int j = 0; j < k; ++j) {
-    unsigned long long lm = 0ull;
+    unsigned long long lmx = 0ull;
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) lm = c[i] > lm ? c[i] : lm;
-    unsigned long long g = warp_max_u64(lm);
-    uint32_t e = 0xFFFFFFFFu - (uint32_t)(g & 0xFFFFFFFFull);
+    for (int i = 0; i < EPL; ++i) lmx = c[i] > lmx ? c[i] : lmx;
+    const unsigned long long g = warp_max_u64(lmx);
+    const uint32_t e = 0xFFFFFFFFu - (uint32_t)(g & 0xFFFFFFFFull);
     float p = 0.f;
     if ((int)(e & 31) == lane) {
 #pragma unroll
@@ -226,21 +328,13 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(const float* __
     }
     p = __shfl_sync(0xFFFFFFFFu, p, e & 31);
     if (lane == j) {
-      my_idx = (int)e;
+      mine = g;
       my_p = p;
     }
   }
   float sum = 0.f;  // sequential in rank order
   for (int j = 0; j < k; ++j) sum += __shfl_sync(0xFFFFFFFFu, my_p, j);
-  if (lane < k) {
-    out_idx[t * k + lane] = my_idx;
-    out_w[t * k + lane] = my_p / sum;
-  }
-  if ((flags & SSB_ROUTER_SHARED_GATE) && lane == 0) {
-    // sigmoid(lin(x, shared_expert_gate)) with lin's bf16 output and a bf16 sigmoid (model/layers.py:401)
-    const float gl = round_bf16(__ldcg(lrow + experts));
-    out_sh_gate[t] = round_bf16(1.f / (1.f + expf(-gl)));
-  }
+  select_tail(a, t, lane, mine, my_p, sum, lrow);
 }
 
 // ------------------------------------------------------------------ generic stable top-k
@@ -383,6 +477,8 @@ __global__ void __launch_bounds__(TK_THREADS) k_topk_stable(const float* __restr
   }
 }
 
+int launch_select(SelectArgs a, void* stream);
+
 }  // namespace
 
 extern "C" int ssb_router_logits(const uint16_t* x, const uint16_t* w, const uint16_t* w_extra, int64_t tokens,
@@ -402,24 +498,6 @@ extern "C" int ssb_router_logits(const uint16_t* x, const uint16_t* w, const uin
                     tokens, hidden, n_rows, ld, logits);
 }
 
-extern "C" int ssb_router_select(const float* logits, int32_t ld, int64_t tokens, int32_t experts, int32_t k,
-                                 const float* bias, int32_t flags, int32_t* out_idx, float* out_w, float* out_probs,
-                                 float* out_sh_gate, void* stream) {
-  SSB_CHECK_ARG(logits && out_idx && out_w && tokens >= 0);
-  SSB_CHECK_ARG(experts >= 1 && experts <= 32 * RS_MAXE && k >= 1 && k <= 32 && k <= experts);
-  SSB_CHECK_ARG(ld >= experts + ((flags & SSB_ROUTER_SHARED_GATE) ? 1 : 0));
-  SSB_CHECK_ARG(!(flags & SSB_ROUTER_SHARED_GATE) || out_sh_gate);
-  if (tokens == 0) return SSB_OK;
-  dim3 grid((unsigned)((tokens + RS_WARPS - 1) / RS_WARPS));
-  const int epl = (experts + 31) / 32;
-  void (*kern)(const float*, int, int64_t, int, int, const float*, int, int32_t*, float*, float*, float*) =
-      epl <= 4 ? k_router_select<4> : epl <= 8 ? k_router_select<8> : epl <= 16 ? k_router_select<16>
-                                                                      : k_router_select<32>;
-  ssb_note_smem("router_select", kern, 0);
-  return ssb_launch(kern, grid, dim3(RS_WARPS * 32), 0, (cudaStream_t)stream, true, logits, ld, tokens,
-                    experts, k, bias, flags, out_idx, out_w, out_probs, out_sh_gate);
-}
-
 extern "C" int ssb_topk_stable(const float* scores, const int32_t* n_valid, int64_t rows, int32_t n, int32_t k,
                                int32_t* out_idx, float* out_val, void* stream) {
   SSB_CHECK_ARG(scores && out_idx && rows >= 0 && n >= 1 && n <= 65536 && k >= 1 && k <= n);
@@ -428,4 +506,69 @@ extern "C" int ssb_topk_stable(const float* scores, const int32_t* n_valid, int6
   ssb_note_smem("topk_stable", k_topk_stable, 0);
   return ssb_launch(k_topk_stable, dim3((unsigned)rows), dim3(TK_THREADS), 0, (cudaStream_t)stream, true, scores,
                     n_valid, n, k, out_idx, out_val);
+}
+
+namespace {
+
+int launch_select(SelectArgs a, void* stream) {
+  SSB_CHECK_ARG(a.logits && a.out_idx && a.out_w && a.tokens >= 0);
+  SSB_CHECK_ARG(a.experts >= 1 && a.experts <= 32 * RS_MAXE && a.k >= 1 && a.k <= 32 && a.k <= a.experts);
+  SSB_CHECK_ARG(a.ld >= a.experts + ((a.flags & SSB_ROUTER_SHARED_GATE) ? 1 : 0));
+  SSB_CHECK_ARG(!(a.flags & SSB_ROUTER_SHARED_GATE) || a.out_sh_gate);
+  SSB_CHECK_ARG(a.prefetch_bytes % 16 == 0);
+  if (a.tokens == 0) return SSB_OK;
+  dim3 grid((unsigned)((a.tokens + RS_WARPS - 1) / RS_WARPS));
+  const int epl = (a.experts + 31) / 32;
+  void (*kern)(SelectArgs) = epl <= 4 ? k_router_select<4> : epl <= 8 ? k_router_select<8>
+                             : epl <= 16 ? k_router_select<16> : k_router_select<32>;
+  ssb_note_smem("router_select", kern, 0);
+  return ssb_launch(kern, grid, dim3(RS_WARPS * 32), 0, (cudaStream_t)stream, true, a);
+}
+
+}  // namespace
+
+extern "C" int ssb_router_select(const float* logits, int32_t ld, int64_t tokens, int32_t experts, int32_t k,
+                                 const float* bias, int32_t flags, int32_t* out_idx, float* out_w, float* out_probs,
+                                 float* out_sh_gate, void* stream) {
+  SelectArgs a{};
+  a.logits = logits;
+  a.ld = ld;
+  a.tokens = tokens;
+  a.experts = experts;
+  a.k = k;
+  a.bias = bias;
+  a.flags = flags;
+  a.out_idx = out_idx;
+  a.out_w = out_w;
+  a.out_probs = out_probs;
+  a.out_sh_gate = out_sh_gate;
+  return launch_select(a, stream);
+}
+
+extern "C" int ssb_router_select_resolve(const float* logits, int32_t ld, int64_t tokens, int32_t experts,
+                                         int32_t k, const float* bias, int32_t flags, int32_t* out_idx, float* out_w,
+                                         float* out_sh_gate, int32_t layer, const int32_t* map_t, int64_t map_len,
+                                         const int64_t* slot_ptr_t, int64_t n_slots, int64_t* out_base,
+                                         int64_t prefetch_bytes, int32_t* err, void* stream) {
+  SSB_CHECK_ARG(map_t && slot_ptr_t && out_base && layer >= 0 && prefetch_bytes >= 0 && prefetch_bytes < (1ll << 31));
+  SelectArgs a{};
+  a.logits = logits;
+  a.ld = ld;
+  a.tokens = tokens;
+  a.experts = experts;
+  a.k = k;
+  a.bias = bias;
+  a.flags = flags;
+  a.out_idx = out_idx;
+  a.out_w = out_w;
+  a.out_sh_gate = out_sh_gate;
+  a.layer = layer;
+  a.map = map_t;
+  a.map_len = map_len;
+  a.slot_ptr = slot_ptr_t;
+  a.n_slots = n_slots;
+  a.out_base = out_base;
+  a.prefetch_bytes = (uint32_t)prefetch_bytes;
+  a.err = err;
+  return launch_select(a, stream);
 }

@@ -89,20 +89,22 @@ SSB_DEV uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Wait for phase `parity` of `bar`; false after `ns` nanoseconds without completion.
+// Wait for phase `parity` of `bar`; false after `ns` nanoseconds without completion. Each try_wait carries a
+// suspend-time hint, so a waiting warp sleeps until the phase completes (or the hint expires) instead of
+// spinning and taking issue slots from the warps that do the work.
 SSB_DEV bool mbar_wait_ns(uint64_t* bar, uint32_t parity, uint64_t ns) {
   const uint32_t a = smem_u32(bar);
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(1000000u)
         : "memory");
     if (done) return true;
-    if ((i & 63u) == 0u) {
+    if ((i & 7u) == 0u) {
       uint64_t t = globaltimer_ns();
       if (t0 == 0) t0 = t;
       else if (t - t0 > ns) return false;

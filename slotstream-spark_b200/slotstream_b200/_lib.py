@@ -31,7 +31,9 @@ SIGNATURES = {
     "ssb_moe_align": [_P, _I64, _P, _I32, _I32, _I32, _P, _P, _P, _P],
     "ssb_moe_decode": [_P, _I32, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _P, _P, _P],
     "ssb_moe_decode_layer": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _P,
-                             _I32, _P, _P],
+                             _P, _I32, _P, _P],
+    "ssb_router_select_resolve": [_P, _I32, _I64, _I32, _I32, _P, _I32, _P, _P, _P, _I32, _P, _I64, _P, _I64, _P,
+                                  _I64, _P, _P],
     "ssb_combine_rank_order": [_P, _I64, _I32, _I32, _P, _P],
     "ssb_combine_layer": [_P, _I64, _I32, _I32, _P, _P, _P, _P],
     "ssb_gemv_affine": [_P, _I32, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P],

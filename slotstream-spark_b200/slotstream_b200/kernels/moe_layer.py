@@ -10,7 +10,6 @@ import torch
 
 from .. import _lib
 from .gemv_affine import _note
-from .router import router_topk
 
 
 class DecodeLayerBuffers:
@@ -22,6 +21,7 @@ class DecodeLayerBuffers:
         self.ws = torch.empty(rows * (experts + 1), **f32)
         self.ids = torch.empty(rows, topk, dtype=torch.int32, device=device)
         self.w = torch.empty(rows, topk, **f32)
+        self.bases = torch.empty(rows, topk, dtype=torch.int64, device=device)
         self.sh_gate = torch.empty(rows, **f32)
         self.h = torch.empty(rows * (topk + 1) * inter, **f32)
         self.o = torch.empty(rows, topk, hidden, **f32)
@@ -118,13 +118,28 @@ def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, 
         raise ValueError("buffers were sized for another call shape")
     if map_t.dtype != torch.int32 or slot_ptr_t.dtype != torch.int64:
         raise ValueError("map_t must be int32 and slot_ptr_t int64")
-    router_topk(x, w_router, k, bufs.ids, bufs.w, logits_round_bf16=logits_round_bf16, bias=bias,
-                sh_gate_w=sh_gate_w, out_sh_gate=bufs.sh_gate, ws=bufs.ws)
+    if x.dtype != torch.bfloat16 or not x.is_contiguous() or w_router.dtype != torch.bfloat16:
+        raise ValueError("x and w_router must be contiguous bf16")
+    if sh_gate_w.dtype != torch.bfloat16 or sh_gate_w.numel() != h:
+        raise ValueError("sh_gate_w must be bf16 [H]")
+    if bias is not None and (bias.dtype != torch.float32 or bias.numel() != bufs.experts):
+        raise ValueError("bias must be fp32 [E]")
+    L = _lib.lib()
+    st = _lib.stream()
+    e = bufs.experts
+    _lib.check(L.ssb_router_logits(_lib.ptr(x), _lib.ptr(w_router), _lib.ptr(sh_gate_w), r, h, e, e + 1,
+                                   _lib.ptr(bufs.ws), st), "router_logits")
+    flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0)
+    record_bytes = 3 * (bufs.inter * h // 2 + 2 * (bufs.inter * h // 64) * 2)
+    _lib.check(L.ssb_router_select_resolve(
+        _lib.ptr(bufs.ws), e + 1, r, e, k, _lib.ptr(bias), flags, _lib.ptr(bufs.ids), _lib.ptr(bufs.w),
+        _lib.ptr(bufs.sh_gate), int(layer), _lib.ptr(map_t), map_t.numel(), _lib.ptr(slot_ptr_t), slot_ptr_t.numel(),
+        _lib.ptr(bufs.bases), record_bytes, _lib.ptr(bufs.err), st), "router_select_resolve")
     rc = _lib.lib().ssb_moe_decode_layer(
         _lib.ptr(x), _lib.ptr(bufs.ids), _lib.ptr(bufs.w), r, k, h, bufs.inter, int(layer), _lib.ptr(map_t),
         map_t.numel(), _lib.ptr(slot_ptr_t), slot_ptr_t.numel(), _addr(shared_record), _lib.ptr(bufs.sh_gate),
-        _lib.ptr(bufs.h), _lib.ptr(bufs.o), _lib.ptr(bufs.out), _lib.ptr(bufs.y), _lib.DECODE_PDL if pdl else 0,
-        _lib.ptr(bufs.err), _lib.stream())
+        _lib.ptr(bufs.bases), _lib.ptr(bufs.h), _lib.ptr(bufs.o), _lib.ptr(bufs.out), _lib.ptr(bufs.y),
+        _lib.DECODE_PDL if pdl else 0, _lib.ptr(bufs.err), st)
     _lib.check(rc, "moe_decode_layer")
     _note("moe_gate_up")
     _note("moe_down")

@@ -207,8 +207,8 @@ def test_decode_layer_matches_bf16_oracle_and_is_row_invariant(layer_world):
     O.ids_match(bufs.ids.cpu().numpy(), ids, logits)
     got = O.bf16_to_f32(to_np_bf16_bits(y)).astype(np.float64)
     assert O.rel_l2(got, out_ref) <= 1e-2
-    # max-abs 2e-2, plus two bf16 ulps: routed.to(bf16) and the final + sh each round once and may straddle
-    assert np.max(np.abs(got - out_ref) - 2 * O.bf16_ulp(out_ref)) <= 2e-2
+    # max-abs 2e-2 on RMS-normalised outputs (bf16 output; see test_gpu_prefill_layer for the reason)
+    assert np.max(np.abs(got - out_ref)) / np.sqrt(np.mean(out_ref ** 2)) <= 2e-2
     one = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
     xt = bf16_tensor(x)
     for r in (0, 7, 15):
