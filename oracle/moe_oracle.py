@@ -277,13 +277,13 @@ def moe_layer(layout, x_bf16, router_w_bf16, k, expert_dense, sh_dense, sh_gate_
               logits_round_bf16=False):
     """Whole MoE block (model/reference_torch.py:118-134): router -> routed experts summed in rank order
     in fp64 -> bf16, plus the sigmoid-gated shared expert (bf16 between ops); final add in bf16.
-    Returns (out bf16-valued fp32 [T, H], routed fp64 [T, H], ids, weights, logits)."""
+    Returns (out bf16-valued fp32 [T, H], routed fp64 [T, H], shared bf16-valued [T, H], ids, weights, logits)."""
     ids, w, logits = router(x_bf16, router_w_bf16, k, bias=bias, logits_round_bf16=logits_round_bf16)
     x = bf16_to_f32(x_bf16)
     routed = moe_decode(layout, x, ids, w, expert_dense)
     sh = shared_expert(x_bf16, *sh_dense, sh_gate_bf16)
     out = round_bf16(round_bf16(routed).astype(np.float64) + sh)
-    return out, routed, ids, w, logits
+    return out, routed, sh, ids, w, logits
 
 
 def moe_layer_prefill(layout, x_bf16, router_w_bf16, k, expert_f32, sh_f32, sh_gate_bf16, bias=None,
@@ -292,7 +292,8 @@ def moe_layer_prefill(layout, x_bf16, router_w_bf16, k, expert_f32, sh_f32, sh_g
     (kernels/fused_moe_affine.py:14-16) summed in rank order in fp32 (combine_rank_order), the shared expert
     through gemm() with bf16-rounded weight tiles and bf16 between ops (model/moe_sweep.py:37-43,
     kernels/gemm_affine.py:32-37), final add in bf16 (model/moe_sweep.py:161 + engine/prefill.py:201).
-    ``expert_f32(e)`` -> fp32 (G, U, D). Returns (out bf16-valued fp32 [T, H], ids, weights, logits)."""
+    ``expert_f32(e)`` -> fp32 (G, U, D). Returns (out bf16-valued fp32 [T, H], routed fp32 [T, H],
+    shared bf16-valued [T, H], ids, weights, logits)."""
     ids, w, logits = router(x_bf16, router_w_bf16, k, bias=bias, logits_round_bf16=logits_round_bf16)
     t = ids.shape[0]
     x = bf16_to_f32(x_bf16)
@@ -301,7 +302,7 @@ def moe_layer_prefill(layout, x_bf16, router_w_bf16, k, expert_f32, sh_f32, sh_g
     routed = combine_rank_order(rows.astype(np.float32), t, k)
     sh = shared_expert(x_bf16, *(round_bf16(m) for m in sh_f32), sh_gate_bf16)
     out = round_bf16(round_bf16(routed).astype(np.float64) + sh)
-    return out, ids, w, logits
+    return out, routed, sh, ids, w, logits
 
 
 def rel_l2(a, b):

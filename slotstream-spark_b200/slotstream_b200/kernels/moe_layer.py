@@ -111,8 +111,10 @@ def _addr(rec) -> int:
 
 
 def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, sh_gate_w, k: int,
-                     bufs: DecodeLayerBuffers, *, bias=None, logits_round_bf16: bool = False, pdl: bool = True):
-    """x bf16 [R, H] -> bufs.y bf16 [R, H] (also fills bufs.ids, bufs.w, bufs.out = routed fp32 sum)."""
+                     bufs: DecodeLayerBuffers, *, bias=None, logits_round_bf16: bool = False, pdl: bool = True,
+                     prefetch_bytes: int = 0):
+    """x bf16 [R, H] -> bufs.y bf16 [R, H] (also fills bufs.ids, bufs.w, bufs.out = routed fp32 sum).
+    ``prefetch_bytes`` > 0 makes the router prefetch that many bytes of each chosen record into L2."""
     r, h = x.shape
     if (r, k, h) != (bufs.rows, bufs.topk, bufs.hidden) or w_router.shape[0] != bufs.experts:
         raise ValueError("buffers were sized for another call shape")
@@ -130,11 +132,10 @@ def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, 
     _lib.check(L.ssb_router_logits(_lib.ptr(x), _lib.ptr(w_router), _lib.ptr(sh_gate_w), r, h, e, e + 1,
                                    _lib.ptr(bufs.ws), st), "router_logits")
     flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0)
-    record_bytes = 3 * (bufs.inter * h // 2 + 2 * (bufs.inter * h // 64) * 2)
     _lib.check(L.ssb_router_select_resolve(
         _lib.ptr(bufs.ws), e + 1, r, e, k, _lib.ptr(bias), flags, _lib.ptr(bufs.ids), _lib.ptr(bufs.w),
         _lib.ptr(bufs.sh_gate), int(layer), _lib.ptr(map_t), map_t.numel(), _lib.ptr(slot_ptr_t), slot_ptr_t.numel(),
-        _lib.ptr(bufs.bases), record_bytes, _lib.ptr(bufs.err), st), "router_select_resolve")
+        _lib.ptr(bufs.bases), prefetch_bytes, _lib.ptr(bufs.err), st), "router_select_resolve")
     rc = _lib.lib().ssb_moe_decode_layer(
         _lib.ptr(x), _lib.ptr(bufs.ids), _lib.ptr(bufs.w), r, k, h, bufs.inter, int(layer), _lib.ptr(map_t),
         map_t.numel(), _lib.ptr(slot_ptr_t), slot_ptr_t.numel(), _addr(shared_record), _lib.ptr(bufs.sh_gate),

@@ -202,13 +202,15 @@ def test_decode_layer_matches_bf16_oracle_and_is_row_invariant(layer_world):
         if e not in dense:
             dense[e] = O.record_dense(lay, recs[e])
         return dense[e]
-    out_ref, routed, ids, w, logits = O.moe_layer(lay, x, rw, 10, ex, O.record_dense(lay, recs[512], np.float32), sg,
-                                                  bias=bias)
+    out_ref, routed, sh_ref, ids, w, logits = O.moe_layer(lay, x, rw, 10, ex,
+                                                          O.record_dense(lay, recs[512], np.float32), sg, bias=bias)
     O.ids_match(bufs.ids.cpu().numpy(), ids, logits)
     got = O.bf16_to_f32(to_np_bf16_bits(y)).astype(np.float64)
     assert O.rel_l2(got, out_ref) <= 1e-2
-    # max-abs 2e-2 on RMS-normalised outputs (bf16 output; see test_gpu_prefill_layer for the reason)
-    assert np.max(np.abs(got - out_ref)) / np.sqrt(np.mean(out_ref ** 2)) <= 2e-2
+    # routed fp32 sum: max-abs 2e-2 outright; the bf16 output adds the shared expert's bf16 chain (one straddled
+    # intermediate moves it by 2^-8 of its size) and the output's two roundings
+    assert np.max(np.abs(bufs.out.cpu().numpy() - routed)) <= 2e-2
+    assert np.all(np.abs(got - out_ref) <= 2e-2 + 2.0 ** -6 * np.abs(sh_ref) + 2 * O.bf16_ulp(out_ref))
     one = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
     xt = bf16_tensor(x)
     for r in (0, 7, 15):
