@@ -287,14 +287,17 @@ def moe_layer(layout, x_bf16, router_w_bf16, k, expert_dense, sh_dense, sh_gate_
 
 
 def moe_layer_prefill(layout, x_bf16, router_w_bf16, k, expert_f32, sh_f32, sh_gate_bf16, bias=None,
-                      logits_round_bf16=False):
+                      logits_round_bf16=False, routing=None):
     """Whole MoE block on the reference's prefill rounding path: routed rows as fused_rows_bf16_path
     (kernels/fused_moe_affine.py:14-16) summed in rank order in fp32 (combine_rank_order), the shared expert
     through gemm() with bf16-rounded weight tiles and bf16 between ops (model/moe_sweep.py:37-43,
     kernels/gemm_affine.py:32-37), final add in bf16 (model/moe_sweep.py:161 + engine/prefill.py:201).
     ``expert_f32(e)`` -> fp32 (G, U, D). Returns (out bf16-valued fp32 [T, H], routed fp32 [T, H],
-    shared bf16-valued [T, H], ids, weights, logits)."""
+    shared bf16-valued [T, H], ids, weights, logits). ``routing`` = (ids, weights) replaces the router's
+    choice, so the expert arithmetic can be compared under a given routing."""
     ids, w, logits = router(x_bf16, router_w_bf16, k, bias=bias, logits_round_bf16=logits_round_bf16)
+    if routing is not None:
+        ids, w = (np.asarray(a) for a in routing)
     t = ids.shape[0]
     x = bf16_to_f32(x_bf16)
     rows = fused_rows_bf16_path(x, np.repeat(np.arange(t), k), w.reshape(-1), ids.reshape(-1), expert_f32,

@@ -9,11 +9,12 @@
 // The kernel is persistent: one CTA per SM walks tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (m-block
 // major, so concurrent CTAs share activation rows and expert weights in L2). TMEM holds two accumulators, so
 // the epilogue of tile i overlaps the MMAs of tile i+1, and the operand pipelines run across tile borders.
-// Warp roles (16 warps):
-//  * warp 0      gathers the tile's activation rows with 16-byte cp.async into 128B-swizzled K-major tiles;
-//  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma (M128 N256 K16, four per 64-wide k-block);
+// Warp roles (17 warps):
+//  * warps 0..3  gather the tile's activation rows with 16-byte cp.async into 128B-swizzled K-major tiles,
+//                32 rows per warp (one warp alone cannot issue the 1024 copies of a k-block fast enough);
 //  * warps 4..7  epilogue: TMEM -> registers -> global, one accumulator row per thread;
-//  * warps 8..15 weight producers: stage their B-row's packed nibbles and bf16 scale/bias with cp.async,
+//  * warp 8      owns TMEM (512 columns) and issues tcgen05.mma (M128 N256 K16, four per 64-wide k-block);
+//  * warps 9..16 weight producers: stage their B-row's packed nibbles and bf16 scale/bias with cp.async,
 //                dequantise q*s + b -> bf16 (the reference kernel's _wtile, kernels/fused_moe_affine.py:38-50,
 //                whose q * sc + bi compiles to a fused multiply-add) into the swizzled B tile; or, for bf16
 //                weights, cp.async the row straight into the tile.
@@ -28,8 +29,8 @@ namespace {
 constexpr int BM = 128, BK = 64, BN = 256;
 constexpr int STAGES = 3;        // A/B operand stages
 constexpr int PD = 3;            // weight staging depth of each producer thread
-constexpr int THREADS = 512;
-constexpr int A_WARP = 0, MMA_WARP = 1, EPI_WARP0 = 4, PROD_WARP0 = 8, N_PROD = 256;
+constexpr int THREADS = 544;
+constexpr int A_WARPS = 4, EPI_WARP0 = 4, MMA_WARP = 8, PROD_WARP0 = 9, N_PROD = 256;
 constexpr uint32_t A_STAGE = BM * 128;           // 16 KB
 constexpr uint32_t B_STAGE = BN * 128;           // 32 KB
 constexpr uint32_t W_STG = N_PROD * 32;          // packed nibbles of one k-block, 32 B per B-row
@@ -73,10 +74,9 @@ struct Smem {
   uint64_t* tmem_full;    // [2]
   uint64_t* tmem_empty;   // [2]
   uint32_t* tmem;
-  int64_t* arow;          // A-row offsets of the tile the gather warp is loading
 };
 
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + PD * STG + 8 * (3 * STAGES + 4) + 16 + BM * 8;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + PD * STG + 8 * (3 * STAGES + 4) + 16;
 
 SSB_DEV Smem carve(uint8_t* raw) {
   Smem s;
@@ -94,8 +94,6 @@ SSB_DEV Smem carve(uint8_t* raw) {
   s.tmem_empty = s.tmem_full + 2;
   p += 8 * (3 * STAGES + 4);
   s.tmem = (uint32_t*)p;
-  p += 16;
-  s.arow = (int64_t*)p;
   return s;
 }
 
@@ -160,7 +158,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
   if (tid == 0) {
     s_fail = 0;
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&S.full_a[s], 32);
+      mbar_init(&S.full_a[s], 32 * A_WARPS);
       mbar_init(&S.full_b[s], N_PROD);
       mbar_init(&S.empty[s], 1);
     }
@@ -176,21 +174,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
   tc_fence_after();
   const uint32_t tmem = *S.tmem;
 
-  if (warp == A_WARP) {
-    // ---------------- activation gather: 1024 16-byte chunks per k-block, 32 per lane
+  if (warp < A_WARPS) {
+    // ---------------- activation gather: rows 32*warp .. 32*warp+31, 256 16-byte chunks per k-block (8 per lane)
     const int c = lane & 7;
+    int64_t off[8];   // A offsets of this lane's 8 rows (lane>>3) + 4i of the quarter, -1: padding row
     for (int64_t j = 0; j < steps; ++j) {
       const int kb = (int)(j % KB);
-      if (kb == 0) {   // new tile: this warp alone owns the row table
+      if (kb == 0) {   // new tile: lane l resolves row 32*warp + l, then the rows are exchanged
         const int64_t mb = tile_of((int)(j / KB)) / NB;
-        __syncwarp();
-        for (int r = lane; r < BM; r += 32) {
-          const int64_t m = mb * BM + r;
-          const int64_t row = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
-          const bool ok = row >= 0 && row < a.R;
-          S.arow[r] = ok ? (a.row_token ? (int64_t)__ldcg(a.row_token + row) : row) * a.lda : -1;
-        }
-        __syncwarp();
+        const int64_t m = mb * BM + 32 * warp + lane;
+        const int64_t row = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
+        const bool ok = row >= 0 && row < a.R;
+        const int64_t mine = ok ? (a.row_token ? (int64_t)__ldcg(a.row_token + row) : row) * a.lda : -1;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) off[i] = __shfl_sync(0xffffffffu, mine, (lane >> 3) + 4 * i);
       }
       const int s = (int)(j % STAGES);
       const uint32_t ph = (uint32_t)((j / STAGES) & 1);
@@ -199,12 +196,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
         break;
       }
       const uint32_t dst = smem_u32(S.a + s * A_STAGE);
-#pragma unroll 8
-      for (int i = 0; i < 32; ++i) {
-        const int row = (lane >> 3) + 4 * i;
-        const int64_t off = S.arow[row];
-        const uint16_t* src = a.a + (off >= 0 ? off : 0) + kb * BK + c * 8;
-        cp_async16(dst + swz128(row, c), src, off >= 0 ? 16u : 0u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = 32 * warp + (lane >> 3) + 4 * i;
+        const uint16_t* src = a.a + (off[i] >= 0 ? off[i] : 0) + kb * BK + c * 8;
+        cp_async16(dst + swz128(row, c), src, off[i] >= 0 ? 16u : 0u);
       }
       cp_async_arrive(&S.full_a[s]);
     }

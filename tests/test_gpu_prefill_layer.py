@@ -1,8 +1,8 @@
 """Fused prefill MoE layer (router GEMM -> select -> align -> grouped tcgen05 GEMMs -> combine) vs the oracle (GPU).
 
 The layer contract: top-k ids bit-exact except router-logit ties within 1e-6; outputs within relative L2 1e-2
-of the exact oracle, and within max-abs 2e-2 (on RMS-normalised outputs) of the oracle that follows the
-reference's prefill rounding path.
+of the exact oracle, and, component by component under the kernel's routing, within max-abs 2e-2 (in units of
+the output RMS) of the oracle that follows the reference's prefill rounding path.
 """
 import numpy as np
 import pytest
@@ -58,17 +58,24 @@ def test_prefill_layer_matches_oracle(layer, zipf):
     np.testing.assert_allclose(bufs.w.cpu().numpy(), w, rtol=2e-5, atol=1e-7)
     got = O.bf16_to_f32(to_np_bf16_bits(y)).astype(np.float64)
     assert O.rel_l2(got, ref) <= 1e-2
-    # component by component: the routed fp32 rank-order sum follows the same rounding points as the oracle, so
-    # it meets max-abs 2e-2 outright; the shared expert rounds to bf16 between its ops (the reference's chain),
-    # where one straddled intermediate moves the result by 2^-8 of its size; the bf16 output adds its two
-    # roundings (routed.to(bf16) and the final sum)
+    # component by component, under the kernel's own routing (ids already checked above): the routed fp32
+    # rank-order sum rounds h to bf16 at the same points as the oracle, so a straddled h element moves a row by
+    # 2^-8 of one down-projection term; max-abs 2e-2 is applied to outputs in units of their RMS (the synthetic
+    # experts give routed sums with an RMS of a few units). The shared expert rounds to bf16 between its ops
+    # (the reference's chain), where one straddled intermediate moves the result by 2^-8 of its size. The bf16
+    # output adds routed.to(bf16) and the final sum, one bf16 ulp of each.
+    ids_k, w_k = bufs.ids.cpu().numpy(), bufs.w.cpu().numpy()
+    ref_k, routed_ref, sh_ref, *_ = O.moe_layer_prefill(L["lay"], x, L["rw"], K, L["f32"], L["f32"](E), L["sg"],
+                                                         bias=bias, routing=(ids_k, w_k))
     rows = bufs.out_rows.cpu().numpy()
     r = t * K
     routed = O.combine_rank_order(rows[:r], t, K).astype(np.float64)
     sh = rows[r:].astype(np.float64)
-    assert np.max(np.abs(routed - routed_ref)) <= 2e-2
+    rms = max(1.0, float(np.sqrt(np.mean(routed_ref ** 2))))
+    assert np.max(np.abs(routed - routed_ref)) <= 2e-2 * rms
     assert np.max(np.abs(sh - sh_ref)) <= 2.0 ** -6 * np.max(np.abs(sh_ref))
-    assert np.all(np.abs(got - ref) <= 2e-2 + np.abs(sh - sh_ref) + 2 * O.bf16_ulp(ref))
+    bound = 2e-2 * rms + np.abs(sh - sh_ref) + O.bf16_ulp(routed_ref) + O.bf16_ulp(ref_k)
+    assert np.all(np.abs(got - ref_k) <= bound)
     # exact-dequant oracle (fp64 routed experts, fp32 shared): within the layer's relative L2 contract
     dense = {}
 
