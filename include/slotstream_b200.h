@@ -28,6 +28,7 @@ extern "C" {
 #define SSB_EINVAL (-1)       /* null pointer, count or size out of range */
 #define SSB_EUNSUPPORTED (-2) /* a shape these kernels do not handle (see each entry point) */
 #define SSB_ENODEVICE (-3)    /* current device is not sm_100 */
+#define SSB_ETOOBIG (-4)      /* request larger than the fixed static scratch of ssb_router_topk_static */
 
 /* ---- bits of the device error word (int32, caller-owned, OR-ed by kernels; never cleared by them) */
 #define SSB_ERR_EXPERT_RANGE 1 /* an expert id outside [0, 512) */
@@ -132,6 +133,20 @@ int ssb_router_select_resolve(const float* logits, int32_t ld, int64_t tokens, i
                               const float* bias, int32_t flags, int32_t* out_idx, float* out_w, float* out_sh_gate,
                               int32_t layer, const int32_t* map_t, int64_t map_len, const int64_t* slot_ptr_t,
                               int64_t n_slots, int64_t* out_base, int64_t prefetch_bytes, int32_t* err, void* stream);
+
+/* Router logits + select (as ssb_router_logits then ssb_router_select) with the logits held in a fixed
+ * device array that comes with the library's device code, so the call needs no workspace and allocates nothing:
+ * for callers that cannot allocate on their call path (a host binding without a caching allocator, a
+ * process whose slot pool holds nearly all HBM, a stream under graph capture). Capacity: 65536 floats
+ * (256 KiB); tokens * (experts + 1 when w_shared_gate is given, else experts) above it returns SSB_ETOOBIG
+ * before any launch. flags: 0 or SSB_ROUTER_ROUND_BF16; a non-null w_shared_gate (bf16 [hidden]) adds the
+ * shared gate into out_sh_gate. The array is shared by every call on a device: calls that overlap on one
+ * device (other streams or host threads) race. The first call on each device looks up the array's address;
+ * make one call before capturing a stream. Other limits as ssb_router_logits and ssb_router_select.
+ * Replaces: no counterpart in the reference. */
+int ssb_router_topk_static(const uint16_t* x, const uint16_t* w, const uint16_t* w_shared_gate, int64_t tokens,
+                           int32_t hidden, int32_t experts, int32_t k, const float* bias, int32_t flags,
+                           int32_t* out_idx, float* out_w, float* out_sh_gate, void* stream);
 
 /* Rank-order combine: out[t, :] = rows[t*k] + rows[t*k + 1] + ... sequentially in fp32.
  * rows fp32 [tokens * k, hidden], out fp32 [tokens, hidden]; hidden % 4 == 0.

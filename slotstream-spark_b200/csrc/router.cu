@@ -5,6 +5,8 @@
 // keys (positive: flip the sign bit; negative: bitwise not; NaN: 0, the lowest), larger keys first,
 // ties to the lower index. Here each candidate becomes the 64-bit composite (key << 32) | ~index, so
 // "largest composite first" is exactly that order and every composite is distinct.
+#include <atomic>
+
 #include <cub/block/block_scan.cuh>
 
 #include "affine.cuh"
@@ -571,4 +573,52 @@ extern "C" int ssb_router_select_resolve(const float* logits, int32_t ld, int64_
   a.prefetch_bytes = (uint32_t)prefetch_bytes;
   a.err = err;
   return launch_select(a, stream);
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Router with its logits in a fixed, statically reserved device array (no workspace argument).
+//
+// Some callers cannot allocate device memory on their call path. A host binding without a caching
+// allocator (cgo, JNI, plain C over this ABI) would have to call cudaMalloc, which synchronises the whole
+// device, on every decode step; a process whose expert slot pool reserved nearly all of HBM up front has no
+// headroom left to hand out; and a stream that is being captured into a graph may not allocate at all.
+// For those callers the logits live in a file-scope __device__ array of ROUTER_STATIC_LOGITS floats
+// (256 KiB): a call whose tokens * (experts + 1 with a shared gate, else experts) exceeds it is refused with
+// SSB_ETOOBIG before anything is launched. The logits kernel writes every element the select kernel reads,
+// earlier on the same stream, so nothing in the array has to start at zero. There is one array per device
+// in the process: calls that overlap on one device (other streams, other host threads) overwrite each
+// other's logits and race. The first call on a device looks the array's address up with
+// cudaGetSymbolAddress (with that device current), so make one call before capturing a stream.
+namespace {
+constexpr int64_t ROUTER_STATIC_LOGITS = 65536;
+constexpr int ROUTER_STATIC_MAX_DEVICES = 64;
+__device__ __align__(256) float g_router_static_logits[ROUTER_STATIC_LOGITS];
+std::atomic<float*> g_router_static_addr[ROUTER_STATIC_MAX_DEVICES];
+}  // namespace
+
+extern "C" int ssb_router_topk_static(const uint16_t* x, const uint16_t* w, const uint16_t* w_shared_gate,
+                                      int64_t tokens, int32_t hidden, int32_t experts, int32_t k,
+                                      const float* bias, int32_t flags, int32_t* out_idx, float* out_w,
+                                      float* out_sh_gate, void* stream) {
+  SSB_CHECK_ARG(x && w && out_idx && out_w && tokens >= 0 && experts >= 1 && k >= 1);
+  SSB_CHECK_ARG(k <= 32 && k <= experts && experts <= 32 * RS_MAXE && (flags & ~SSB_ROUTER_ROUND_BF16) == 0);
+  SSB_CHECK_ARG(!w_shared_gate || out_sh_gate);
+  const int32_t ld = experts + (w_shared_gate ? 1 : 0);
+  if (tokens > ROUTER_STATIC_LOGITS / ld) return SSB_ETOOBIG;
+  if (tokens == 0) return SSB_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= ROUTER_STATIC_MAX_DEVICES) return SSB_EUNSUPPORTED;
+  float* logits = g_router_static_addr[dev].load(std::memory_order_acquire);
+  if (!logits) {
+    e = cudaGetSymbolAddress((void**)&logits, g_router_static_logits);
+    if (e != cudaSuccess) return (int)e;
+    g_router_static_addr[dev].store(logits, std::memory_order_release);
+  }
+  int rc = ssb_router_logits(x, w, w_shared_gate, tokens, hidden, experts, ld, logits, stream);
+  if (rc != SSB_OK) return rc;
+  return ssb_router_select(logits, ld, tokens, experts, k, bias,
+                           flags | (w_shared_gate ? SSB_ROUTER_SHARED_GATE : 0), out_idx, out_w, nullptr,
+                           out_sh_gate, stream);
 }

@@ -11,7 +11,7 @@ import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libslotstream_b200.so"
 
-SSB_OK, SSB_EINVAL, SSB_EUNSUPPORTED, SSB_ENODEVICE = 0, -1, -2, -3
+SSB_OK, SSB_EINVAL, SSB_EUNSUPPORTED, SSB_ENODEVICE, SSB_ETOOBIG = 0, -1, -2, -3, -4
 ERR_EXPERT_RANGE, ERR_UNMAPPED, ERR_SLOT_RANGE, ERR_MISALIGNED, ERR_TIMEOUT = 1, 2, 4, 8, 16
 BF16, F32 = 0, 1
 ROUTER_ROUND_BF16, ROUTER_SHARED_GATE = 1, 2
@@ -34,6 +34,7 @@ SIGNATURES = {
                              _P, _I32, _P, _P],
     "ssb_router_select_resolve": [_P, _I32, _I64, _I32, _I32, _P, _I32, _P, _P, _P, _I32, _P, _I64, _P, _I64, _P,
                                   _I64, _P, _P],
+    "ssb_router_topk_static": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P],
     "ssb_combine_rank_order": [_P, _I64, _I32, _I32, _P, _P],
     "ssb_combine_layer": [_P, _I64, _I32, _I32, _P, _P, _P, _P],
     "ssb_gemv_affine": [_P, _I32, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P],
@@ -80,7 +81,8 @@ def stream():
 
 
 _NAMES = {SSB_EINVAL: "SSB_EINVAL (bad argument)", SSB_EUNSUPPORTED: "SSB_EUNSUPPORTED (shape not handled)",
-          SSB_ENODEVICE: "SSB_ENODEVICE (not an sm_100 device)"}
+          SSB_ENODEVICE: "SSB_ENODEVICE (not an sm_100 device)",
+          SSB_ETOOBIG: "SSB_ETOOBIG (request exceeds the fixed static scratch of the entry point)"}
 
 
 def check(rc, what):
