@@ -186,11 +186,12 @@ int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int3
  * above, with local expert `shared_local` (-1: none) treated as the shared expert -- its h is
  * bf16(bf16(silu(bf16 g)) * bf16 u) and its down rows bf16(row_weight * bf16(h D^T)), the reference's
  * bf16 rounding between the shared expert's ops (model/moe_sweep.py:37-43) -- so the shared expert rides
- * in the same grouped launch as the routed ones with its rows weighted by the sigmoid gate.
+ * in the same grouped launch as the routed ones with its rows weighted by the sigmoid gate. x holds `tokens`
+ * rows (row_token < tokens).
  * Replaces: the per-group fused_moe_affine calls of model/moe_sweep.py:163-176 plus shared_expert
  * (:37-43) for a layer whose experts are all resident. */
-int ssb_prefill_experts(const uint16_t* x, int32_t hidden, int32_t inter, const int32_t* row_token,
-                        const float* row_weight, int64_t rows, const int32_t* sorted_rows, const int32_t* block_expert,
+int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter,
+                        const int32_t* row_token, const float* row_weight, int64_t rows, const int32_t* sorted_rows, const int32_t* block_expert,
                         const int32_t* num_padded, int64_t padded_len, const int64_t* group_ptr, int32_t n_groups,
                         int32_t shared_local, uint16_t* h_buf, float* out_rows, int32_t* err, void* stream);
 

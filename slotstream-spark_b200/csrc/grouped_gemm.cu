@@ -9,12 +9,12 @@
 // The kernel is persistent: one CTA per SM walks tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (m-block
 // major, so concurrent CTAs share activation rows and expert weights in L2). TMEM holds two accumulators, so
 // the epilogue of tile i overlaps the MMAs of tile i+1, and the operand pipelines run across tile borders.
-// Warp roles (17 warps):
-//  * warps 0..3  gather the tile's activation rows with 16-byte cp.async into 128B-swizzled K-major tiles,
-//                32 rows per warp (one warp alone cannot issue the 1024 copies of a k-block fast enough);
+// Warp roles (16 warps):
+//  * warp 0      gathers the tile's activation rows with TMA: lane l issues one tile::gather4 of rows
+//                4l..4l+3 per k-block into the 128B-swizzled K-major tile (the tensor map applies the swizzle);
+//  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma (M128 N256 K16, four per 64-wide k-block);
 //  * warps 4..7  epilogue: TMEM -> registers -> global, one accumulator row per thread;
-//  * warp 8      owns TMEM (512 columns) and issues tcgen05.mma (M128 N256 K16, four per 64-wide k-block);
-//  * warps 9..16 weight producers: stage their B-row's packed nibbles and bf16 scale/bias with cp.async,
+//  * warps 8..15 weight producers: stage their B-row's packed nibbles and bf16 scale/bias with cp.async,
 //                dequantise q*s + b -> bf16 (the reference kernel's _wtile, kernels/fused_moe_affine.py:38-50,
 //                whose q * sc + bi compiles to a fused multiply-add) into the swizzled B tile; or, for bf16
 //                weights, cp.async the row straight into the tile.
@@ -29,8 +29,8 @@ namespace {
 constexpr int BM = 128, BK = 64, BN = 256;
 constexpr int STAGES = 3;        // A/B operand stages
 constexpr int PD = 3;            // weight staging depth of each producer thread
-constexpr int THREADS = 544;
-constexpr int A_WARPS = 4, EPI_WARP0 = 4, MMA_WARP = 8, PROD_WARP0 = 9, N_PROD = 256;
+constexpr int THREADS = 512;
+constexpr int A_WARP = 0, MMA_WARP = 1, EPI_WARP0 = 4, PROD_WARP0 = 8, N_PROD = 256;
 constexpr uint32_t A_STAGE = BM * 128;           // 16 KB
 constexpr uint32_t B_STAGE = BN * 128;           // 32 KB
 constexpr uint32_t W_STG = N_PROD * 32;          // packed nibbles of one k-block, 32 B per B-row
@@ -41,8 +41,9 @@ constexpr uint32_t TMEM_COLS = 512;              // two M128 x N256 fp32 accumul
 enum { EPI_SWIGLU = 0, EPI_SCALE = 1, EPI_PLAIN = 2 };
 
 struct GemmArgs {
-  const uint16_t* a;          // bf16 activation rows, `lda` elements apart
+  const uint16_t* a;          // bf16 activation rows, `lda` elements apart (read through the A tensor map)
   int64_t lda;
+  int64_t a_rows;             // rows of the activation matrix (extent of the tensor map)
   const int32_t* row_token;   // nullable: the A row of row r is r
   const int32_t* sorted_rows; // nullable: identity (rows m < R)
   const int32_t* block_expert;
@@ -132,7 +133,7 @@ SSB_DEV void scales2(float s, float2* sc2) {
 SSB_DEV float silu_fast(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
 template <int EPI>
-__global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__ CUtensorMap tm_a, GemmArgs a) {
   extern __shared__ uint8_t smraw[];
   Smem S = carve(smraw);
   __shared__ int s_fail;
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
   if (tid == 0) {
     s_fail = 0;
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&S.full_a[s], 32 * A_WARPS);
+      mbar_init(&S.full_a[s], 1);
       mbar_init(&S.full_b[s], N_PROD);
       mbar_init(&S.empty[s], 1);
     }
@@ -174,37 +175,63 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
   tc_fence_after();
   const uint32_t tmem = *S.tmem;
 
-  if (warp < A_WARPS) {
-    // ---------------- activation gather: rows 32*warp .. 32*warp+31, 256 16-byte chunks per k-block (8 per lane)
-    const int c = lane & 7;
-    int64_t off[8];   // A offsets of this lane's 8 rows (lane>>3) + 4i of the quarter, -1: padding row
+  if (warp == A_WARP) {
+    // ---------------- activation gather: 32 tile::gather4 copies (16 KB) per k-block, one per lane
+    // Tile rows 4*lane .. 4*lane+3 come from sorted_rows, then row_token; the next tile's lookups are started
+    // during the current tile (sorted_rows at its first k-block, row_token at its second) so that the two
+    // dependent loads do not stall the copies at tile borders. Padding rows read activation row 0.
+    int32_t rc[4], nrc[4], nsr[4];
+    auto load_rows = [&](int i) {
+      const int64_t mb = tile_of(i) / NB;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int64_t m = mb * BM + 4 * lane + q;
+        nsr[q] = a.sorted_rows ? __ldcg(a.sorted_rows + m) : (int32_t)m;
+      }
+    };
+    auto to_coords = [&]() {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const bool ok = nsr[q] >= 0 && nsr[q] < a.R;
+        nrc[q] = ok ? (a.row_token ? __ldcg(a.row_token + nsr[q]) : nsr[q]) : 0;
+      }
+    };
+    int64_t issued = 0;
+    if (lane == 0) prefetch_tensormap(&tm_a);
+    load_rows(0);
+    to_coords();
     for (int64_t j = 0; j < steps; ++j) {
       const int kb = (int)(j % KB);
-      if (kb == 0) {   // new tile: lane l resolves row 32*warp + l, then the rows are exchanged
-        const int64_t mb = tile_of((int)(j / KB)) / NB;
-        const int64_t m = mb * BM + 32 * warp + lane;
-        const int64_t row = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
-        const bool ok = row >= 0 && row < a.R;
-        const int64_t mine = ok ? (a.row_token ? (int64_t)__ldcg(a.row_token + row) : row) * a.lda : -1;
+      const int i = (int)(j / KB);
+      if (kb == 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) off[i] = __shfl_sync(0xffffffffu, mine, (lane >> 3) + 4 * i);
+        for (int q = 0; q < 4; ++q) rc[q] = nrc[q];
+        if (i + 1 < my_tiles) {
+          load_rows(i + 1);
+          if (KB == 1) to_coords();
+        }
+      } else if (kb == 1 && i + 1 < my_tiles) {
+        to_coords();
       }
       const int s = (int)(j % STAGES);
       const uint32_t ph = (uint32_t)((j / STAGES) & 1);
-      if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
+      bool ok = lane == 0 ? mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS) : true;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
         s_fail = 1;
         break;
       }
-      const uint32_t dst = smem_u32(S.a + s * A_STAGE);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int row = 32 * warp + (lane >> 3) + 4 * i;
-        const uint16_t* src = a.a + (off[i] >= 0 ? off[i] : 0) + kb * BK + c * 8;
-        cp_async16(dst + swz128(row, c), src, off[i] >= 0 ? 16u : 0u);
-      }
-      cp_async_arrive(&S.full_a[s]);
+      if (lane == 0) mbar_expect_tx(&S.full_a[s], A_STAGE);
+      __syncwarp();
+      tma_gather4(smem_u32(S.a + s * A_STAGE + lane * 512), &tm_a, kb * BK, rc[0], rc[1], rc[2], rc[3],
+                  &S.full_a[s]);
+      ++issued;
     }
-    cp_async_wait_all();
+    // no copy may still be writing shared memory when the CTA exits: wait for the last stages to land
+    if (lane == 0)
+      for (int64_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+        mbar_wait_ns(&S.full_a[j % STAGES], (uint32_t)((j / STAGES) & 1), SSB_WAIT_NS);
+    __syncwarp();
   } else if (warp == MMA_WARP) {
     // ---------------- single-thread MMA issue, double-buffered accumulators
     if (lane == 0) {
@@ -324,19 +351,25 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
     const int p = tid - PROD_WARP0 * 32;
     const int piece = (EPI == EPI_SWIGLU) ? (p >> 7) : 0;
     const int ng = a.K / a.gs;
-    // weight row of B-row p for step j (nullptr: zero row)
-    auto wrow_of = [&](int64_t j, const uint8_t** base_out) -> int64_t {
-      const int64_t t = tile_of((int)(j / KB));
-      const int64_t mb = t / NB;
-      const int nb = (int)(t % NB);
-      *base_out = base_of(expert_of(mb));
-      return (EPI == EPI_SWIGLU) ? (int64_t)nb * (BN / 2) + (p & 127) : (int64_t)nb * BN + p;
+    // weight base and B-row of this thread for the tile of step j, resolved once per tile (two dependent
+    // L2 loads: block_expert, then the group's base); base nullptr: zero row
+    int64_t t_tile = -1, t_nrow = 0;
+    const uint8_t* t_base = nullptr;
+    auto tile_info = [&](int64_t j) {
+      const int64_t i = j / KB;
+      if (i != t_tile) {
+        t_tile = i;
+        const int64_t t = tile_of((int)i);
+        const int64_t mb = t / NB;
+        const int nb = (int)(t % NB);
+        t_base = base_of(expert_of(mb));
+        t_nrow = (EPI == EPI_SWIGLU) ? (int64_t)nb * (BN / 2) + (p & 127) : (int64_t)nb * BN + p;
+      }
     };
     if (a.dense_b) {
       for (int64_t j = 0; j < steps; ++j) {
         const int kb = (int)(j % KB);
-        const uint8_t* base;
-        const int64_t nrow = wrow_of(j, &base);
+        tile_info(j);
         const int s = (int)(j % STAGES);
         const uint32_t ph = (uint32_t)((j / STAGES) & 1);
         if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
@@ -344,21 +377,23 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
           break;
         }
         const uint32_t bt = smem_u32(S.b + s * B_STAGE);
-        const uint16_t* drow = base ? (const uint16_t*)base + nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
+        const uint16_t* drow = t_base ? (const uint16_t*)t_base + t_nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + c * 8, base ? 16u : 0u);
+        for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + c * 8, t_base ? 16u : 0u);
         cp_async_arrive(&S.full_b[s]);
       }
     } else {
+      uint32_t valid = 0;   // bit (j % PD): staging slot of step j holds a real weight row
       auto issue = [&](int64_t j) {
         const int kb = (int)(j % KB);
-        const uint8_t* base;
-        const int64_t nrow = wrow_of(j, &base);
+        tile_info(j);
         uint8_t* st = S.stg + (j % PD) * STG;
-        if (!base) return;
-        const uint8_t* wr = base + a.off_w[piece] + nrow * (a.K / 2) + kb * 32;
-        const uint16_t* sr = (const uint16_t*)(base + a.off_s[piece]) + nrow * ng;
-        const uint16_t* br = (const uint16_t*)(base + a.off_b[piece]) + nrow * ng;
+        const uint32_t bit = 1u << (j % PD);
+        valid = t_base ? (valid | bit) : (valid & ~bit);
+        if (!t_base) return;
+        const uint8_t* wr = t_base + a.off_w[piece] + t_nrow * (a.K / 2) + kb * 32;
+        const uint16_t* sr = (const uint16_t*)(t_base + a.off_s[piece]) + t_nrow * ng;
+        const uint16_t* br = (const uint16_t*)(t_base + a.off_b[piece]) + t_nrow * ng;
         const uint32_t dw = smem_u32(st + p * 32);
         cp_async16(dw, wr, 16);
         cp_async16(dw + 16, wr + 16, 16);
@@ -378,12 +413,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(GemmArgs a) {
         asm volatile("cp.async.commit_group;" ::: "memory");
         asm volatile("cp.async.wait_group %0;" ::"n"(PD - 1) : "memory");
         const int kb = (int)(j % KB);
-        const uint8_t* base;
-        (void)wrow_of(j, &base);
         const uint8_t* st = S.stg + (j % PD) * STG;
         uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
         float s0 = 0.f, b0 = 0.f, s1 = 0.f, b1 = 0.f;
-        if (base) {
+        if ((valid >> (j % PD)) & 1u) {
           w0 = *reinterpret_cast<const uint4*>(st + p * 32);
           w1 = *reinterpret_cast<const uint4*>(st + p * 32 + 16);
           const uint32_t sw = *reinterpret_cast<const uint32_t*>(st + W_STG + p * 4);
@@ -447,10 +480,43 @@ int num_sms() {
   return sms;
 }
 
+// The driver's tensor-map encoder, looked up through the runtime so the library needs no link-time libcuda.
+using EncodeTiledFn = decltype(&cuTensorMapEncodeTiled);
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D tensor map over the activation rows: K elements x a_rows rows, box 64 x 1, 128-byte swizzle.
+int encode_a_map(CUtensorMap* map, const GemmArgs& a) {
+  if (((uintptr_t)a.a & 15) || (a.lda * 2) % 16 || a.a_rows < 1 || a.a_rows > 0x7fffffffLL) return SSB_EINVAL;
+  EncodeTiledFn encode = encode_tiled_fn();
+  if (!encode) return SSB_ENODEVICE;
+  cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.a_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)a.lda * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)a.a, dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SSB_OK : SSB_EINVAL;
+}
+
 int launch(int epi, GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t st) {
-  void (*k)(GemmArgs) = epi == EPI_SWIGLU ? k_moe_gemm<EPI_SWIGLU> : epi == EPI_SCALE ? k_moe_gemm<EPI_SCALE>
-                                                                                      : k_moe_gemm<EPI_PLAIN>;
+  void (*k)(CUtensorMap, GemmArgs) = epi == EPI_SWIGLU ? k_moe_gemm<EPI_SWIGLU>
+                                     : epi == EPI_SCALE ? k_moe_gemm<EPI_SCALE>
+                                                        : k_moe_gemm<EPI_PLAIN>;
   if (n_mblocks <= 0) return SSB_OK;
+  CUtensorMap tm;
+  int rc = encode_a_map(&tm, a);
+  if (rc) return rc;
   static bool attr_set[3] = {false, false, false};
   if (!attr_set[epi]) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
@@ -463,7 +529,7 @@ int launch(int epi, GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t s
   a.n_nblocks = n_nblocks;
   const int64_t tiles = n_mblocks * n_nblocks;
   const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-  return ssb_launch(k, dim3(grid), dim3(THREADS), SMEM_BYTES, st, true, a);
+  return ssb_launch(k, dim3(grid), dim3(THREADS), SMEM_BYTES, st, true, tm, a);
 }
 
 void set_record_offsets(GemmArgs& g, int hidden, int inter, bool gate_up) {
@@ -482,7 +548,8 @@ void set_record_offsets(GemmArgs& g, int hidden, int inter, bool gate_up) {
   }
 }
 
-int gate_up_impl(const uint16_t* x, int32_t hidden, int32_t inter, const int32_t* row_token, int64_t rows,
+int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter, const int32_t* row_token,
+                 int64_t rows,
                  const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded,
                  int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, int32_t shared_local,
                  uint16_t* h_buf, int32_t* err, void* stream) {
@@ -494,6 +561,7 @@ int gate_up_impl(const uint16_t* x, int32_t hidden, int32_t inter, const int32_t
   GemmArgs g{};
   g.a = x;
   g.lda = hidden;
+  g.a_rows = tokens;
   g.row_token = row_token;
   g.sorted_rows = sorted_rows;
   g.block_expert = block_expert;
@@ -523,6 +591,7 @@ int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter
   GemmArgs g{};
   g.a = h_buf;
   g.lda = inter;
+  g.a_rows = rows;
   g.sorted_rows = sorted_rows;
   g.block_expert = block_expert;
   g.num_padded = num_padded;
@@ -548,7 +617,7 @@ extern "C" int ssb_fused_moe_gate_up(const uint16_t* x, int64_t tokens, int32_t 
                                      const int64_t* group_ptr, int32_t n_groups, uint16_t* h_buf, int32_t* err,
                                      void* stream) {
   SSB_CHECK_ARG(tokens >= 0);
-  return gate_up_impl(x, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len, group_ptr,
+  return gate_up_impl(x, tokens, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len, group_ptr,
                       n_groups, -1, h_buf, err, stream);
 }
 
@@ -560,12 +629,14 @@ extern "C" int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t h
                    group_ptr, n_groups, -1, out_rows, err, stream);
 }
 
-extern "C" int ssb_prefill_experts(const uint16_t* x, int32_t hidden, int32_t inter, const int32_t* row_token,
+extern "C" int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter,
+                                   const int32_t* row_token,
                                    const float* row_weight, int64_t rows, const int32_t* sorted_rows,
                                    const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
                                    const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, uint16_t* h_buf,
                                    float* out_rows, int32_t* err, void* stream) {
-  int rc = gate_up_impl(x, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len,
+  SSB_CHECK_ARG(tokens >= 0);
+  int rc = gate_up_impl(x, tokens, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len,
                         group_ptr, n_groups, shared_local, h_buf, err, stream);
   if (rc) return rc;
   return down_impl(h_buf, rows, hidden, inter, row_weight, sorted_rows, block_expert, num_padded, padded_len,
@@ -583,6 +654,7 @@ extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const i
   GemmArgs g{};
   g.a = x;
   g.lda = k;
+  g.a_rows = m;
   g.R = m;
   g.base0 = (const uint8_t*)q;
   g.n_groups = 1;
@@ -607,6 +679,7 @@ extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uin
   GemmArgs g{};
   g.a = x;
   g.lda = k;
+  g.a_rows = m;
   g.R = m;
   g.base0 = (const uint8_t*)w;
   g.n_groups = 1;

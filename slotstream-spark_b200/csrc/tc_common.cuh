@@ -6,6 +6,8 @@
 // a tile has start address >> 4, LBO 1 (unused for swizzled K-major), SBO 1024 >> 4, version 1, layout
 // SWIZZLE_128B (2); the K step of 16 elements inside the 64-element row advances the start address by 32 B.
 #pragma once
+#include <cuda.h>
+
 #include "affine.cuh"
 
 SSB_DEV uint32_t swz128(uint32_t row, uint32_t chunk) { return row * 128u + (((chunk ^ (row & 7u)) & 7u) << 4); }
@@ -82,6 +84,22 @@ SSB_DEV void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 SSB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// ---------------------------------------------------------------- TMA row gather
+// Four rows (r0..r3) of a 2-D bf16 tensor map whose box is 64 elements x 1 row, starting at element column
+// `col` (a multiple of 64, so the 16-byte rule on the inner coordinate holds), land as four consecutive
+// 128-byte rows at dst with the map's 128-byte swizzle; completion is counted in bytes on `bar`.
+SSB_DEV void tma_gather4(uint32_t dst, const CUtensorMap* map, int32_t col, int32_t r0, int32_t r1, int32_t r2,
+                         int32_t r3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
+}
+SSB_DEV void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
+}
 
 // ---------------------------------------------------------------- bounded waits on the global timer
 SSB_DEV uint64_t globaltimer_ns() {

@@ -42,7 +42,7 @@ SIGNATURES = {
     "ssb_fused_moe_gate_up": [_P, _I64, _I32, _I32, _P, _I64, _P, _P, _P, _I64, _P, _I32, _P, _P, _P],
     "ssb_fused_moe_down": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _I64, _P, _I32, _P, _P, _P],
     "ssb_gemm_affine4": [_P, _I64, _I32, _P, _P, _P, _I32, _I32, _P, _P],
-    "ssb_prefill_experts": [_P, _I32, _I32, _P, _P, _I64, _P, _P, _P, _I64, _P, _I32, _I32, _P, _P, _P, _P],
+    "ssb_prefill_experts": [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P, _P, _I64, _P, _I32, _I32, _P, _P, _P, _P],
     "ssb_gemm_dense": [_P, _I64, _I32, _P, _I32, _P, _I64, _P],
 }
 

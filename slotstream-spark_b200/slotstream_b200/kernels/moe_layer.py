@@ -91,7 +91,7 @@ def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLa
                                    _lib.ptr(bufs.w), None, _lib.ptr(bufs.sh_gate), st), "router select")
     aligned = moe_align(bufs.row_expert, e + 1, 128, out=(bufs.sorted_rows, bufs.block_expert, bufs.num_padded))
     _lib.check(L.ssb_prefill_experts(
-        _lib.ptr(x), h, bufs.inter, _lib.ptr(bufs.row_token), _lib.ptr(bufs.row_weight), bufs.rows,
+        _lib.ptr(x), t, h, bufs.inter, _lib.ptr(bufs.row_token), _lib.ptr(bufs.row_weight), bufs.rows,
         _lib.ptr(aligned[0]), _lib.ptr(aligned[1]), _lib.ptr(aligned[2]), aligned[0].numel(), _lib.ptr(group_ptr),
         e + 1, e, _lib.ptr(bufs.h), _lib.ptr(bufs.out_rows), _lib.ptr(bufs.err), st), "prefill experts")
     r = t * k

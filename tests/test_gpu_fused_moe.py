@@ -226,3 +226,22 @@ def test_gemm_errors():
     for bad in (torch.empty(3, 512, device="cuda"), torch.empty(4, 512, dtype=torch.bfloat16, device="cuda")):
         with pytest.raises(ValueError):
             gemm(x, w, out=bad)
+
+
+@pytest.mark.parametrize("m,k,n,pad", [(300, 64, 256, 0), (5000, 128, 512, 4), (20000, 256, 512, 0), (129, 2048, 512, 4)])
+def test_gemm_dense_matches_fp64(m, k, n, pad):
+    """Plain bf16 GEMM (the prefill router logits): fp32 accumulation of exact bf16 products vs fp64; several
+    tiles per CTA, one-k-block tiles (k = 64) and a row stride wider than n."""
+    from slotstream_b200 import _lib
+    g = torch.Generator().manual_seed(m + k)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    out = torch.full((m, n + pad), -5.0, dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().ssb_gemm_dense(_lib.ptr(x), m, k, _lib.ptr(w), n, _lib.ptr(out), n + pad, _lib.stream()),
+               "gemm_dense")
+    torch.cuda.synchronize()
+    ref = x.double().cpu() @ w.double().cpu().T
+    got = out[:, :n].double().cpu()
+    assert float((got - ref).norm() / ref.norm()) <= 1e-5
+    if pad:
+        assert bool((out[:, n:] == -5.0).all())
