@@ -195,29 +195,40 @@ def bench_decode(args, world, rank):
     step_bytes = sum(u * rb for u in uniq) + NL * per_layer_fixed
     errs = sum(int(bf.err.item()) for bf in bufs)
 
-    # dominant launch: the gate_up + down pair of moe_decode_layer, timed per layer outside the graph
-    lt = []
+    # dominant launch, timed per layer outside the graph after an L2 flush: at b <= 2 the whole layer is one
+    # cooperative launch (moe_decode_fused); above, the gate_up + down pair of moe_decode_layer
     from slotstream_b200 import _lib
+    from slotstream_b200.kernels.moe_layer import FUSED_MAX_ROWS
+    fused = b <= FUSED_MAX_ROWS
     st = torch.cuda.current_stream()
+    lt = []
     for l in range(NL):
         moe_layer_decode(x[l], router_w[l], l, map_t, slot_ptr, shared[l], sh_gate_w[l], K, bufs[l], bias=bias)
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        rc = _lib.lib().ssb_moe_decode_layer(
-            _lib.ptr(x[l]), _lib.ptr(bufs[l].ids), _lib.ptr(bufs[l].w), b, K, LAY.hidden, LAY.inter, l,
-            _lib.ptr(map_t), map_t.numel(), _lib.ptr(slot_ptr), slot_ptr.numel(), shared[l].data_ptr(),
-            _lib.ptr(bufs[l].sh_gate), _lib.ptr(bufs[l].bases), _lib.ptr(bufs[l].h), _lib.ptr(bufs[l].o),
-            _lib.ptr(bufs[l].out), _lib.ptr(bufs[l].y), 0, _lib.ptr(bufs[l].err), _lib.stream())
-        _lib.check(rc, "moe_decode_layer")
+        if fused:
+            moe_layer_decode(x[l], router_w[l], l, map_t, slot_ptr, shared[l], sh_gate_w[l], K, bufs[l], bias=bias)
+        else:
+            rc = _lib.lib().ssb_moe_decode_layer(
+                _lib.ptr(x[l]), _lib.ptr(bufs[l].ids), _lib.ptr(bufs[l].w), b, K, LAY.hidden, LAY.inter, l,
+                _lib.ptr(map_t), map_t.numel(), _lib.ptr(slot_ptr), slot_ptr.numel(), shared[l].data_ptr(),
+                _lib.ptr(bufs[l].sh_gate), _lib.ptr(bufs[l].bases), _lib.ptr(bufs[l].h), _lib.ptr(bufs[l].o),
+                _lib.ptr(bufs[l].out), _lib.ptr(bufs[l].y), 0, _lib.ptr(bufs[l].err), _lib.stream())
+            _lib.check(rc, "moe_decode_layer")
         e1.record(st)
         torch.cuda.synchronize()
         lt.append(e0.elapsed_time(e1))
     launch_ms = sum(lt) / len(lt)
-    launch_bytes = (sum(u * rb for u in uniq) + NL * (rb + b * LAY.hidden * 2 * 2)) / NL
+    if fused:
+        launch_bytes = step_bytes / NL
+        kname = "moe_decode_fused (whole layer: router, select, gate_up, down, combine)"
+    else:
+        launch_bytes = (sum(u * rb for u in uniq) + NL * (rb + b * LAY.hidden * 2 * 2)) / NL
+        kname = "moe_decode_layer (gate_up + down)"
     pk = peaks()
     achieved = launch_bytes / (launch_ms * 1e-3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "moe_decode_layer (gate_up + down)", "achieved": round(achieved, 1),
+    roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                 "peak_source": pk["source"], "traffic": None,
                 "bytes_per_launch": int(launch_bytes), "launch_us": round(launch_ms * 1e3, 2)}
@@ -252,7 +263,7 @@ def bench_decode(args, world, rank):
         "roofline": roofline,
         "e2e": {"value": round(world * b / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y_host.numel() * 2)},
-        "gpu_launches": 4 * NL * args.steps,
+        "gpu_launches": (1 if b <= FUSED_MAX_ROWS else 4) * NL * args.steps,
         "clocks": clocks.summary(),
         "device_errors": errs,
     }
@@ -322,12 +333,15 @@ def bench_prefill(args, world, rank):
         return sum(out) / len(out)
 
     sr, be, npd = bufs.sorted_rows, bufs.block_expert, bufs.num_padded
-    gu_ms = timed(lambda: _lib.check(L.ssb_fused_moe_gate_up(
-        _lib.ptr(x), T, LAY.hidden, LAY.inter, _lib.ptr(bufs.row_token), bufs.rows, _lib.ptr(sr), _lib.ptr(be),
-        _lib.ptr(npd), sr.numel(), _lib.ptr(group_ptr), E + 1, _lib.ptr(bufs.h), None, _lib.stream()), "gate_up"))
-    dn_ms = timed(lambda: _lib.check(L.ssb_fused_moe_down(
+    # the two grouped GEMMs exactly as the layer launches them (rows permuted into expert order by the step)
+    gu_ms = timed(lambda: _lib.check(L.ssb_sorted_gate_up(
+        _lib.ptr(bufs.x_sorted), LAY.hidden, LAY.inter, _lib.ptr(bufs.row_token), bufs.rows, _lib.ptr(sr),
+        _lib.ptr(be), _lib.ptr(npd), sr.numel(), _lib.ptr(group_ptr), E + 1, E, _lib.ptr(bufs.h), None,
+        _lib.stream()), "gate_up"))
+    dn_ms = timed(lambda: _lib.check(L.ssb_sorted_down(
         _lib.ptr(bufs.h), bufs.rows, LAY.hidden, LAY.inter, _lib.ptr(bufs.row_weight), _lib.ptr(sr), _lib.ptr(be),
-        _lib.ptr(npd), sr.numel(), _lib.ptr(group_ptr), E + 1, _lib.ptr(bufs.out_rows), None, _lib.stream()), "down"))
+        _lib.ptr(npd), sr.numel(), _lib.ptr(group_ptr), E + 1, E, _lib.ptr(bufs.out_rows), None, _lib.stream()),
+        "down"))
     gu_flop = 2.0 * bufs.rows * 2 * LAY.inter * LAY.hidden
     dn_flop = 2.0 * bufs.rows * LAY.inter * LAY.hidden
     pk = peaks()
@@ -369,9 +383,81 @@ def bench_prefill(args, world, rank):
         "roofline": roofline,
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y_host.numel() * 2)},
-        "gpu_launches": 7 * args.steps,
+        "gpu_launches": 8 * args.steps,
         "clocks": clocks.summary(),
         "device_errors": errs,
+    }
+
+
+# ------------------------------------------------------------------ expert-parallel prefill (configs[3], N > 1)
+def bench_prefill_ep(args, world, rank):
+    from slotstream_b200 import synth
+    from slotstream_b200.ep import CudaOps, ep_forward, owned_experts
+    from slotstream_b200.records import BASELINE_LAYOUT as LAY
+    E, K, T = 512, 10, args.tokens
+    dev = torch.device("cuda")
+    rb = LAY.record_bytes
+    owned = owned_experts(rank, E, world, strided=True)
+    recs = torch.empty((len(owned) + 1, rb), dtype=torch.uint8, device=dev)   # this rank's experts + the shared one
+    synth.fill_records_device(LAY, recs, 3000 + rank)
+    group_ptr = recs.data_ptr() + torch.arange(len(owned), dtype=torch.int64, device=dev) * rb
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000)                       # router and shared gate replicated: same on every rank
+    router_w = (torch.randn(E, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    sh_gate_w = (torch.randn(LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.from_numpy(synth.zipf_bias(E)).to(dev) if args.routing == "zipf" else None
+    g.manual_seed(2100 + rank)                # each rank its own tokens
+    x = torch.randn(T, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
+    ops = CudaOps(router_w, sh_gate_w, group_ptr, recs.data_ptr() + len(owned) * rb, K, LAY.inter, world,
+                  strided=True, bias=bias)
+
+    def step():
+        return ep_forward(ops, x, K, world)
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    times = timed_steps(step, args.steps, flush, world, clocks)
+    clocks.stop()
+    ms = max_over_ranks(sum(times) / len(times), world)
+    value = world * T / (ms * 1e-3)
+    errs = int(ops.err.item())
+
+    # e2e: this rank's tokens from pinned host memory, the layer, y back to the host
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T, LAY.hidden), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        y = step()
+        y_host.copy_(y, non_blocking=True)
+
+    e2e_step()
+    e2e_times = timed_steps(e2e_step, args.steps, flush, world)
+    e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
+    pk = peaks()
+    tf = T * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12      # per GPU: each rank's share of the layer's FLOPs
+    roofline = {"bound": "tensor", "kernel": "whole expert-parallel layer step per GPU (FLOPs of its tokens)",
+                "achieved": round(tf, 1), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": round(tf / pk["bf16_tflops_sustained"], 4), "peak_source": pk["source"] + " (sustained)",
+                "traffic": None}
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"ep_prefill_layer_{T}tok_per_gpu", "tokens_per_gpu": T, "hidden": LAY.hidden,
+                   "inter": LAY.inter, "experts": E, "experts_per_gpu": len(owned), "placement": "strided (e % G)",
+                   "topk": K, "shared_experts": 1, "routing": "zipf_s1.1" if args.routing == "zipf" else "uniform",
+                   "exchange": "NCCL all-to-all-v (dispatch rows + metadata, fp32 partial sums back)",
+                   "l2": "flushed before every step (256 MiB write); inputs > L2", "parallelism": f"ep{world}"},
+        "tflops_per_gpu": round(tf, 1), "roofline": roofline,
+        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * LAY.hidden * 2, "d2h_bytes_per_step": T * LAY.hidden * 2},
+        "gpu_launches": 16 * args.steps, "clocks": clocks.summary(), "device_errors": errs,
     }
 
 
@@ -389,6 +475,7 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -403,6 +490,8 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_baseline import time_decode
             res["cpu_baseline"] = time_decode(BASELINE_LAYOUT, seconds=args.cpu_seconds)
+    elif world > 1 and not args.replicas:
+        res = bench_prefill_ep(args, world, rank)
     else:
         res = bench_prefill(args, world, rank)
         torch.cuda.empty_cache()

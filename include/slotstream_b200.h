@@ -134,6 +134,46 @@ int ssb_router_select_resolve(const float* logits, int32_t ld, int64_t tokens, i
                               int32_t layer, const int32_t* map_t, int64_t map_len, const int64_t* slot_ptr_t,
                               int64_t n_slots, int64_t* out_base, int64_t prefetch_bytes, int32_t* err, void* stream);
 
+/* ---- expert-parallel prefill (experts sharded over n_ranks <= 8 GPUs; the exchange itself is NCCL
+ * all-to-all-v between these calls). Placement: strided = 1 puts expert e on rank e % n_ranks (local index
+ * e / n_ranks), strided = 0 on rank e / experts_per_rank (local e % experts_per_rank). k <= 15.
+ * Replaces: no counterpart in the reference, which runs on one GPU; the per-rank expert work is
+ * ssb_prefill_experts and the sums keep the rank order of kernels/fused_moe_affine.py:164-172. */
+
+/* Dispatch plan of one rank's routed tokens ids/w [tokens, k]: dest_count int32 [n_ranks, 2] (rows, entries
+ * per destination); send_token int32 [>= tokens * min(n_ranks, k)] (rows ordered by destination, then
+ * token); send_meta int32 [same, 2k + 2] (local expert or -1 per choice, weight bits, entry base, entry
+ * count); tok_slot / tok_entry int32 [tokens, n_ranks] (send row and entry base of (t, d), -1 if none). */
+int ssb_ep_plan(const int32_t* ids, const float* w, int64_t tokens, int32_t k, int32_t experts_per_rank,
+                int32_t n_ranks, int32_t strided, int32_t* dest_count, int32_t* send_token, int32_t* send_meta,
+                int32_t* tok_slot, int32_t* tok_entry, int32_t* err, void* stream);
+
+/* dst[i] = src[idx[i]] for rows of row_bytes (multiple of 16) bytes; an index outside [0, src_rows) gives a
+ * zero row and SSB_ERR_EXPERT_RANGE in err. */
+int ssb_gather_rows(const void* src, int64_t src_rows, const int32_t* idx, int64_t n, int64_t row_bytes, void* dst,
+                    int32_t* err, void* stream);
+
+/* Received metadata [rows, 2k + 2] (rows of source s at src_row_off[s] .. src_row_off[s+1], their entries at
+ * src_entry_off[s] ..) -> compacted entries row_expert / row_token / row_weight [n_entries] (entries of a row
+ * contiguous in rank-k order) and row_e0 int64 / row_cnt int32 [rows]. */
+int ssb_ep_unpack(const int32_t* meta, int64_t rows, int32_t k, const int32_t* src_row_off,
+                  const int64_t* src_entry_off, int32_t n_ranks, int64_t n_entries, int32_t* row_expert,
+                  int32_t* row_token, float* row_weight, int64_t* row_e0, int32_t* row_cnt, int32_t* err,
+                  void* stream);
+
+/* partial[r, :] = rows[row_e0[r]] + ... + rows[row_e0[r] + row_cnt[r] - 1], sequential fp32. */
+int ssb_combine_rows(const float* rows, const int64_t* row_e0, const int32_t* row_cnt, int64_t n, int32_t hidden,
+                     float* partial, void* stream);
+
+/* Home combine of the returned rows: exact = 0 sums the partial rows ret[tok_slot[t, d]] over d ascending;
+ * exact = 1 sums the entry rows ret[ret_entry_off[d] + tok_entry[t, d] + i] in router-rank order (bit-equal
+ * to the one-GPU layer). out fp32 [tokens, hidden] (nullable); y bf16 = bf16(bf16(routed) + bf16(sh))
+ * (nullable; sh fp32 bf16-valued [tokens, hidden], nullable). */
+int ssb_ep_combine(const float* ret, const int32_t* tok_slot, const int32_t* tok_entry, const int64_t* ret_entry_off,
+                   const int32_t* ids, int64_t tokens, int32_t k, int32_t experts_per_rank, int32_t n_ranks,
+                   int32_t strided, int32_t exact, int32_t hidden, const float* sh, float* out, uint16_t* y,
+                   void* stream);
+
 /* Router logits + select (as ssb_router_logits then ssb_router_select) with the logits held in a fixed
  * device array that comes with the library's device code, so the call needs no workspace and allocates nothing:
  * for callers that cannot allocate on their call path (a host binding without a caching allocator, a
@@ -147,6 +187,24 @@ int ssb_router_select_resolve(const float* logits, int32_t ld, int64_t tokens, i
 int ssb_router_topk_static(const uint16_t* x, const uint16_t* w, const uint16_t* w_shared_gate, int64_t tokens,
                            int32_t hidden, int32_t experts, int32_t k, const float* bias, int32_t flags,
                            int32_t* out_idx, float* out_w, float* out_sh_gate, void* stream);
+
+/* Whole decode MoE layer for rows <= 2 tokens in ONE cooperative launch (one CTA per SM, two grid barriers):
+ * router logits (x . w_router^T and the shared gate x . sh_gate_w, fp32), select as ssb_router_select (bias,
+ * flags 0 or SSB_ROUTER_ROUND_BF16), expert resolution through the slot tables as ssb_moe_decode, then
+ * ssb_moe_decode_layer's gate_up / down / rank-order sum / shared add. Outputs and their bits equal the
+ * separate calls: out_idx / out_w [rows, topk], out_sh_gate [rows], out_base [rows, topk] (nullable), h_buf
+ * [rows * (topk + 1), inter], o_buf [rows, topk, hidden] (nullable), out fp32 / y bf16 [rows, hidden].
+ * logits_ws: fp32 [rows, experts + 1]. sync: two uint32 words, zero before the first call and after a call
+ * that reported SSB_ERR_TIMEOUT; calls sharing sync must not overlap. Limits: hidden % 512 == 0 and <= 4096,
+ * inter in {512, 1024, 2048}, experts <= 512, topk <= 16, gs 64; other shapes return SSB_EUNSUPPORTED.
+ * Replaces: the router of model/layers.py:336-347 plus the decode MoE call site of
+ * slotstream_spark/runtime/graphs.py:160-169, for callers that opt in. */
+int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t topk, int32_t hidden, int32_t inter, int32_t experts,
+                         const uint16_t* w_router, const uint16_t* sh_gate_w, const float* bias, int32_t flags,
+                         int32_t layer, const int32_t* map_t, int64_t map_len, const int64_t* slot_ptr_t,
+                         int64_t n_slots, const void* shared_record, float* logits_ws, int32_t* out_idx, float* out_w,
+                         float* out_sh_gate, int64_t* out_base, float* h_buf, float* o_buf, float* out, uint16_t* y,
+                         uint32_t* sync, int32_t* err, void* stream);
 
 /* Rank-order combine: out[t, :] = rows[t*k] + rows[t*k + 1] + ... sequentially in fp32.
  * rows fp32 [tokens * k, hidden], out fp32 [tokens, hidden]; hidden % 4 == 0.
@@ -182,18 +240,39 @@ int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int3
                        int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, float* out_rows, int32_t* err,
                        void* stream);
 
-/* Both prefill expert GEMMs of a fused MoE layer (additive): gate_up then down, as the two entry points
- * above, with local expert `shared_local` (-1: none) treated as the shared expert -- its h is
- * bf16(bf16(silu(bf16 g)) * bf16 u) and its down rows bf16(row_weight * bf16(h D^T)), the reference's
- * bf16 rounding between the shared expert's ops (model/moe_sweep.py:37-43) -- so the shared expert rides
- * in the same grouped launch as the routed ones with its rows weighted by the sigmoid gate. x holds `tokens`
- * rows (row_token < tokens).
+/* Both prefill expert GEMMs of a fused MoE layer (additive), on activation rows permuted into expert order:
+ * ssb_permute_rows, then ssb_sorted_gate_up, then ssb_sorted_down below, so the grouped GEMMs read whole
+ * 128-row 2-D tiles instead of gathering rows. Local expert `shared_local` (-1: none) is the shared expert --
+ * its h is bf16(bf16(silu(bf16 g)) * bf16 u) and its down rows bf16(row_weight * bf16(h D^T)), the
+ * reference's bf16 rounding between the shared expert's ops (model/moe_sweep.py:37-43) -- so it rides in the
+ * same grouped launch as the routed experts with its rows weighted by the sigmoid gate. x holds `tokens` rows
+ * (row_token < tokens); x_sorted bf16 [padded_len, hidden] and h_sorted bf16 [padded_len, inter] are scratch
+ * (h in sorted order); out_rows fp32 [rows, hidden] indexed by row as ssb_fused_moe_down.
  * Replaces: the per-group fused_moe_affine calls of model/moe_sweep.py:163-176 plus shared_expert
  * (:37-43) for a layer whose experts are all resident. */
 int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter,
-                        const int32_t* row_token, const float* row_weight, int64_t rows, const int32_t* sorted_rows, const int32_t* block_expert,
-                        const int32_t* num_padded, int64_t padded_len, const int64_t* group_ptr, int32_t n_groups,
-                        int32_t shared_local, uint16_t* h_buf, float* out_rows, int32_t* err, void* stream);
+                        const int32_t* row_token, const float* row_weight, int64_t rows, const int32_t* sorted_rows,
+                        const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
+                        const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, uint16_t* x_sorted,
+                        uint16_t* h_sorted, float* out_rows, int32_t* err, void* stream);
+
+/* x_sorted[m, :] = x[row_token[sorted_rows[m]], :] for m < num_padded (zero rows for padding). */
+int ssb_permute_rows(const uint16_t* x, int64_t tokens, int32_t hidden, const int32_t* row_token, int64_t rows,
+                     const int32_t* sorted_rows, const int32_t* num_padded, int64_t padded_len, uint16_t* x_sorted,
+                     void* stream);
+
+/* The gate_up GEMM of ssb_prefill_experts on permuted rows: h_sorted[m] = SwiGLU of x_sorted[m] for the
+ * m-block's expert (shapes as ssb_fused_moe_gate_up). */
+int ssb_sorted_gate_up(const uint16_t* x_sorted, int32_t hidden, int32_t inter, const int32_t* row_token,
+                       int64_t rows, const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded,
+                       int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, int32_t shared_local,
+                       uint16_t* h_sorted, int32_t* err, void* stream);
+
+/* The down GEMM of ssb_prefill_experts on h in sorted order: out_rows[sorted_rows[m]] = (h_sorted[m] D^T) * w. */
+int ssb_sorted_down(const uint16_t* h_sorted, int64_t rows, int32_t hidden, int32_t inter, const float* row_weight,
+                    const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded,
+                    int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, int32_t shared_local,
+                    float* out_rows, int32_t* err, void* stream);
 
 /* Dense bf16 GEMM on tcgen05 (router logits of a prefill chunk): out[m, n] = sum_k x[m, k] * w[n, k],
  * fp32 into rows of `ldo` floats (ldo % 4 == 0). k % 64 == 0, n % 256 == 0; row-invariant.

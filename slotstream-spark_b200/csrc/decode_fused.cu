@@ -1,0 +1,504 @@
+// Fused decode MoE layer for one or two tokens: router logits, select, expert resolution, gate_up + SwiGLU,
+// down + rank-order sum + shared expert in ONE cooperative launch with one CTA per SM and two grid barriers,
+// instead of four dependent launches (router_logits -> router_select -> gate_up -> down).
+//
+// At batch 1 the layer is a chain of four tiny dependent phases; separate launches pay a grid drain and a
+// launch for each, which dominated the old path. Here:
+//  phase 1  every CTA computes ~(E + 1) / #SMs router logits (warp per weight row; the shared-gate row last)
+//           while its other warps resolve the record base of every expert of the layer through the slot
+//           tables into shared memory (static inputs: this overlaps the logits instead of following select);
+//  barrier
+//  phase 2  every CTA runs the warp select for every token itself (identical results everywhere, no extra
+//           barrier); CTA 0 writes ids / weights / shared gate; each CTA issues L2 prefetches for the down
+//           rows it will need in phase 4;
+//  phase 3  gate_up: the (entry, row pair) items are split evenly over the CTAs, each warp streams its weight
+//           words straight from HBM into registers and forms h = silu(G x) * (U x) (shared expert: bf16 chain);
+//  barrier
+//  phase 4  every CTA owns a contiguous slice of output columns for ALL entries, so the rank-order sum, the
+//           shared add and the bf16 output need no further exchange.
+// Every dot product keeps the summation order of the separate kernels (lane-sequential over 16-element units,
+// then a butterfly), so the fused layer reproduces router_logits + router_select + moe_decode_layer bit for
+// bit. Grid barriers spin with a bounded wait on a caller-owned pair of words and give up with
+// SSB_ERR_TIMEOUT; the words must be zero before the first call and again after a timeout.
+#include "registry.h"
+#include "select.cuh"
+#include "tc_common.cuh"
+
+namespace {
+
+constexpr int FT = 512;   // threads per CTA
+constexpr int FW = FT / 32;
+constexpr int F_MAXR = 2;
+constexpr int F_MAXK = 16;
+constexpr int F_MAXE = 512;
+
+struct FusedArgs {
+  const uint16_t* x;
+  int R, k, H, I, E, gs;
+  const uint16_t* w_router;
+  const uint16_t* sh_gate_w;
+  const float* bias;
+  int flags;
+  int layer;
+  const int32_t* map;
+  int64_t map_len;
+  const int64_t* slot_ptr;
+  int64_t n_slots;
+  const uint8_t* shared_rec;
+  RecOffs o;
+  float* logits;   // [R, E + 1]
+  int32_t* out_idx;
+  float* out_w;
+  float* out_sh_gate;
+  int64_t* out_base;   // nullable
+  float* h_buf;        // [R * k + R, I]
+  float* o_buf;        // nullable [R, k, H]
+  float* out;          // [R, H]
+  uint16_t* y;         // [R, H]
+  uint32_t* sync;      // [2]
+  int32_t* err;
+};
+
+struct __align__(16) XUnitS {
+  float2 v[8];
+  float sum, pad0, pad1, pad2;
+};
+
+// All CTAs meet; false when the wait gave up (then SSB_ERR_TIMEOUT is set and the caller must stop).
+SSB_DEV bool grid_sync(uint32_t* sync, int32_t* err, int* s_ok) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    volatile uint32_t* gen = sync + 1;
+    const uint32_t g0 = *gen;   // read before arriving: the release below needs every arrival
+    __threadfence();
+    const uint32_t arrived = atomicAdd(sync, 1u);
+    if (arrived == gridDim.x - 1) {
+      atomicExch(sync, 0u);
+      __threadfence();
+      atomicAdd(sync + 1, 1u);
+    } else {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t polls = 0;
+      while (*gen == g0) {
+        __nanosleep(64);
+        if ((++polls & 63u) == 0 && globaltimer_ns() - t0 > SSB_WAIT_NS) {
+          ok = 0;
+          set_err(err, SSB_ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+    __threadfence();
+    *s_ok = ok;
+  }
+  __syncthreads();
+  return *s_ok != 0;
+}
+
+SSB_DEV void xunit_store(XUnitS& d, const float* v16) {
+  XUnit xu;
+  xunit_from_f32(xu, v16);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) d.v[q] = xu.v[q];
+  d.sum = xu.sum;
+}
+SSB_DEV void xunit_load(XUnit& xu, const XUnitS& s) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) xu.v[q] = s.v[q];
+  xu.sum = s.sum;
+}
+
+SSB_DEV void warp_sum4f(float& a, float& b, float& c, float& d) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+    b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
+    c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+  }
+}
+
+// NUX: 16-element units of x per lane (H / 512); NUI: units of h per lane (I / 512); EPL: experts per lane.
+template <int NUX, int NUI, int EPL>
+__global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ int s_ok;
+  __shared__ int32_t s_ids[F_MAXR][F_MAXK];
+  __shared__ float s_w[F_MAXR][F_MAXK];
+  __shared__ float s_shg[F_MAXR];
+  __shared__ unsigned long long s_cand[F_MAXR][RS_CAND];
+  __shared__ unsigned long long s_top[F_MAXR][16];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = a.R, k = a.k, H = a.H, I = a.I, E = a.E, gs = a.gs;
+  const int P = R * k + R;                      // entries: routed (r, j) at r*k + j, shared of token r at R*k + r
+  const int nux = H / 16, nui = I / 16;
+  // shared memory: x (bf16 raw) | x units | h units | expert bases
+  uint16_t* xs = reinterpret_cast<uint16_t*>(sm);
+  XUnitS* xu_s = reinterpret_cast<XUnitS*>(sm + (size_t)F_MAXR * H * 2);
+  XUnitS* hx = xu_s + (size_t)F_MAXR * nux;
+  const uint8_t** bases = reinterpret_cast<const uint8_t**>(hx + (size_t)F_MAXR * (F_MAXK + 1) * nui);
+
+  // ---------------- phase 1: x, router logits, expert bases
+  const int nrows = E + 1;   // router rows, then the shared-expert gate row
+  const int rpc = (nrows + gridDim.x - 1) / gridDim.x;
+  const int cpl = (H >> 3) >> 5;   // 16-byte chunks of a weight row per lane
+  uint4 wr[2 * NUX];
+  const int row0 = blockIdx.x * rpc + warp;
+  if (warp < 4 && warp < rpc && row0 < nrows) {   // the weights are static: load them first
+    const uint16_t* wrow = row0 < E ? a.w_router + (int64_t)row0 * H : a.sh_gate_w;
+#pragma unroll
+    for (int i = 0; i < 2 * NUX; ++i)
+      if (i < cpl) wr[i] = ld_stream_u4(wrow + (size_t)(lane + 32 * i) * 8);
+  }
+  for (int c = tid; c < R * H / 8; c += FT)
+    reinterpret_cast<uint4*>(xs)[c] = __ldg(reinterpret_cast<const uint4*>(a.x) + c);
+  __syncthreads();
+  if (warp < 4) {
+    for (int rr = warp; rr < rpc; rr += 4) {
+      const int row = blockIdx.x * rpc + rr;
+      if (row >= nrows) break;
+      if (rr != warp) {
+        const uint16_t* wrow = row < E ? a.w_router + (int64_t)row * H : a.sh_gate_w;
+#pragma unroll
+        for (int i = 0; i < 2 * NUX; ++i)
+          if (i < cpl) wr[i] = ld_stream_u4(wrow + (size_t)(lane + 32 * i) * 8);
+      }
+      for (int t = 0; t < R; ++t) {   // the summation order of k_router_logits
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 2 * NUX; ++i) {
+          if (i < cpl) {
+            const uint4 xv = reinterpret_cast<const uint4*>(xs + (size_t)t * H)[lane + 32 * i];
+            const uint4 wv = wr[i];
+            acc = fmaf(bf16_lo(wv.x), bf16_lo(xv.x), acc);
+            acc = fmaf(bf16_hi(wv.x), bf16_hi(xv.x), acc);
+            acc = fmaf(bf16_lo(wv.y), bf16_lo(xv.y), acc);
+            acc = fmaf(bf16_hi(wv.y), bf16_hi(xv.y), acc);
+            acc = fmaf(bf16_lo(wv.z), bf16_lo(xv.z), acc);
+            acc = fmaf(bf16_hi(wv.z), bf16_hi(xv.z), acc);
+            acc = fmaf(bf16_lo(wv.w), bf16_lo(xv.w), acc);
+            acc = fmaf(bf16_hi(wv.w), bf16_hi(xv.w), acc);
+          }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) a.logits[(int64_t)t * (E + 1) + row] = acc;
+      }
+    }
+  } else {   // the other warps resolve every expert of the layer meanwhile (unchosen misses are not errors)
+    for (int e = tid - 4 * 32; e < E; e += FT - 4 * 32)
+      bases[e] = resolve_expert(e, a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots, nullptr);
+  }
+  // x in the pre-scaled unit form for the gate/up dot products (every CTA)
+  for (int idx = tid; idx < R * nux; idx += FT) {
+    const int t = idx / nux, u = idx - t * nux;
+    float v16[16];
+    const uint4* p = reinterpret_cast<const uint4*>(xs + (size_t)t * H + u * 16);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint4 v = p[q];
+      v16[8 * q + 0] = bf16_lo(v.x);
+      v16[8 * q + 1] = bf16_hi(v.x);
+      v16[8 * q + 2] = bf16_lo(v.y);
+      v16[8 * q + 3] = bf16_hi(v.y);
+      v16[8 * q + 4] = bf16_lo(v.z);
+      v16[8 * q + 5] = bf16_hi(v.z);
+      v16[8 * q + 6] = bf16_lo(v.w);
+      v16[8 * q + 7] = bf16_hi(v.w);
+    }
+    xunit_store(xu_s[idx], v16);
+  }
+  if (!grid_sync(a.sync, a.err, &s_ok)) return;
+
+  // ---------------- phase 2: select (each CTA, warp per token)
+  if (warp < R) {
+    const float* lrow = a.logits + (int64_t)warp * (E + 1);
+    unsigned long long mine;
+    float my_p, sum;
+    warp_select<EPL>(lrow, E, k, a.bias, a.flags, nullptr, s_cand[warp], s_top[warp], lane, mine, my_p, sum);
+    if (lane < k) {
+      s_ids[warp][lane] = (int)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull));
+      s_w[warp][lane] = my_p / sum;
+    }
+    if (lane == 0) {   // sigmoid(lin(x, shared_expert_gate)), bf16 output and bf16 sigmoid (model/layers.py:401)
+      const float gl = round_bf16(__ldcg(lrow + E));
+      s_shg[warp] = round_bf16(1.f / (1.f + expf(-gl)));
+    }
+  }
+  __syncthreads();
+  auto entry_base = [&](int p) -> const uint8_t* {
+    if (p >= R * k) return a.shared_rec;
+    const int e = s_ids[p / k][p % k];
+    return (e >= 0 && e < E) ? bases[e] : nullptr;
+  };
+  if (blockIdx.x == 0 && tid < R * k) {
+    const int r = tid / k, j = tid % k;
+    const int e = s_ids[r][j];
+    a.out_idx[tid] = e;
+    a.out_w[tid] = s_w[r][j];
+    // report an unusable choice with the precise reason (resolution errors of unchosen experts are normal)
+    const uint8_t* b = resolve_expert(e, a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots, a.err);
+    if (a.out_base) a.out_base[tid] = (int64_t)b;
+  }
+  if (blockIdx.x == 0 && tid < R) a.out_sh_gate[tid] = s_shg[tid];
+  // this CTA's output columns, and L2 prefetches of their down rows (needed after the next barrier)
+  const int c0 = (int)((int64_t)blockIdx.x * H / gridDim.x), c1 = (int)((int64_t)(blockIdx.x + 1) * H / gridDim.x);
+  for (int pe = lane; warp == FW - 1 && pe < P && c1 > c0; pe += 32) {
+    const uint8_t* base = entry_base(pe);
+    if (base) {
+      const int ng = I / gs;
+      auto pf = [&](const uint8_t* p, int64_t bytes) {
+        const uintptr_t s0 = (uintptr_t)p & ~(uintptr_t)15;
+        const uintptr_t s1 = ((uintptr_t)p + bytes + 15) & ~(uintptr_t)15;
+        prefetch_l2((const void*)s0, (uint32_t)(s1 - s0));
+      };
+      pf(base + a.o.dw + (int64_t)c0 * I / 2, (int64_t)(c1 - c0) * I / 2);
+      pf(base + a.o.dsc + (int64_t)c0 * ng * 2, (int64_t)(c1 - c0) * ng * 2);
+      pf(base + a.o.db + (int64_t)c0 * ng * 2, (int64_t)(c1 - c0) * ng * 2);
+    }
+  }
+
+  // ---------------- phase 3: gate_up, items (entry p, row pair q) split evenly over the grid's warps
+  {
+    const int pairs = I / 2;
+    const int64_t items = (int64_t)P * pairs;
+    const int ng = H / gs;
+    for (int64_t it = (int64_t)blockIdx.x * FW + warp; it < items; it += (int64_t)gridDim.x * FW) {
+      const int p = (int)(it / pairs), q = (int)(it - (int64_t)p * pairs);
+      const int j0 = 2 * q, j1 = j0 + 1;
+      const uint8_t* base = entry_base(p);
+      float* hrow = a.h_buf + (int64_t)p * I;
+      if (!base) {
+        if (lane < 2) hrow[j0 + lane] = 0.f;
+        continue;
+      }
+      const int t = p >= R * k ? p - R * k : p / k;
+      const uint2* g0r = reinterpret_cast<const uint2*>(base + a.o.gw + (int64_t)j0 * H / 2);
+      const uint2* g1r = reinterpret_cast<const uint2*>(base + a.o.gw + (int64_t)j1 * H / 2);
+      const uint2* u0r = reinterpret_cast<const uint2*>(base + a.o.uw + (int64_t)j0 * H / 2);
+      const uint2* u1r = reinterpret_cast<const uint2*>(base + a.o.uw + (int64_t)j1 * H / 2);
+      const uint16_t* gsc = reinterpret_cast<const uint16_t*>(base + a.o.gsc);
+      const uint16_t* gbi = reinterpret_cast<const uint16_t*>(base + a.o.gb);
+      const uint16_t* usc = reinterpret_cast<const uint16_t*>(base + a.o.usc);
+      const uint16_t* ubi = reinterpret_cast<const uint16_t*>(base + a.o.ub);
+      uint2 wg0[NUX], wg1[NUX], wu0[NUX], wu1[NUX];
+#pragma unroll
+      for (int i = 0; i < NUX; ++i) {   // all of the item's weight words in flight at once
+        const int u = lane + 32 * i;
+        wg0[i] = ld_stream_u2(g0r + u);
+        wg1[i] = ld_stream_u2(g1r + u);
+        wu0[i] = ld_stream_u2(u0r + u);
+        wu1[i] = ld_stream_u2(u1r + u);
+      }
+      float ga0 = 0.f, ua0 = 0.f, ga1 = 0.f, ua1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NUX; ++i) {
+        const int u = lane + 32 * i;
+        const int g = (u * 16) / gs;
+        XUnit xu;
+        xunit_load(xu, xu_s[(size_t)t * nux + u]);
+        ga0 = unit_dot(wg0[i], bf16_bits(__ldg(gsc + j0 * ng + g)), bf16_bits(__ldg(gbi + j0 * ng + g)), xu, ga0);
+        ua0 = unit_dot(wu0[i], bf16_bits(__ldg(usc + j0 * ng + g)), bf16_bits(__ldg(ubi + j0 * ng + g)), xu, ua0);
+        ga1 = unit_dot(wg1[i], bf16_bits(__ldg(gsc + j1 * ng + g)), bf16_bits(__ldg(gbi + j1 * ng + g)), xu, ga1);
+        ua1 = unit_dot(wu1[i], bf16_bits(__ldg(usc + j1 * ng + g)), bf16_bits(__ldg(ubi + j1 * ng + g)), xu, ua1);
+      }
+      warp_sum4f(ga0, ua0, ga1, ua1);
+      if (lane < 2) {
+        const float ga = lane ? ga1 : ga0, ua = lane ? ua1 : ua0;
+        float h;
+        if (p >= R * k) {   // shared expert: lin() returns bf16, silu and the product round to bf16
+          const float gbv = round_bf16(ga), ubv = round_bf16(ua);
+          h = round_bf16(round_bf16(gbv / (1.f + expf(-gbv))) * ubv);
+        } else {
+          h = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u in fp32, kernels/moe_gemv_affine.py:76
+        }
+        hrow[j0 + lane] = h;
+      }
+    }
+  }
+  if (!grid_sync(a.sync, a.err, &s_ok)) return;
+
+  // ---------------- phase 4: down for columns [c0, c1) of every entry, rank-order sum, shared add
+  for (int idx = tid; idx < P * nui; idx += FT) {
+    const int p = idx / nui, u = idx - p * nui;
+    float v16[16];
+    const float4* hp = reinterpret_cast<const float4*>(a.h_buf + (int64_t)p * I + u * 16);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = __ldcg(hp + q);
+      v16[4 * q] = v.x;
+      v16[4 * q + 1] = v.y;
+      v16[4 * q + 2] = v.z;
+      v16[4 * q + 3] = v.w;
+    }
+    xunit_store(hx[idx], v16);
+  }
+  __syncthreads();
+  const int ng4 = I / gs;
+  constexpr int CH = F_MAXK + 1;   // a token's entries: its routed choices in rank order, then its shared entry
+  constexpr int CH4 = (CH + 3) / 4 * 4;
+  for (int m = c0 + warp; m < c1; m += FW) {
+    for (int r = 0; r < R; ++r) {
+      const int nexp = k + 1;
+      float d[CH4];
+#pragma unroll
+      for (int j = 0; j < CH4; ++j) d[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < NUI; ++i) {
+        const int u = lane + 32 * i;
+        const int g = (u * 16) / gs;
+        uint2 wv[CH];
+        float sc[CH], bi[CH];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {   // every entry's words in flight before the first dot product
+          wv[j] = make_uint2(0u, 0u);
+          sc[j] = bi[j] = 0.f;
+          if (j < nexp) {
+            const int p = j < k ? r * k + j : R * k + r;
+            const uint8_t* base = entry_base(p);
+            if (base) {
+              wv[j] = __ldcg(reinterpret_cast<const uint2*>(base + a.o.dw + (int64_t)m * I / 2) + u);
+              sc[j] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(base + a.o.dsc) + (int64_t)m * ng4 + g));
+              bi[j] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(base + a.o.db) + (int64_t)m * ng4 + g));
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          if (j < nexp) {
+            const int p = j < k ? r * k + j : R * k + r;
+            XUnit xu;
+            xunit_load(xu, hx[(size_t)p * nui + u]);
+            d[j] = unit_dot(wv[j], sc[j], bi[j], xu, d[j]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < CH4; j += 4) warp_sum4f(d[j], d[j + 1], d[j + 2], d[j + 3]);
+      if (lane == 0) {
+        float acc = 0.f, shv = 0.f;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          if (j >= nexp) break;
+          const int p = j < k ? r * k + j : R * k + r;
+          const bool ok = entry_base(p) != nullptr;
+          if (j >= k) {
+            shv = round_bf16((ok ? s_shg[r] : 0.f) * round_bf16(d[j]));   // bf16(sigmoid gate * bf16(h D^T))
+          } else {
+            const float o = d[j] * (ok ? s_w[r][j] : 0.f);   // acc * w, kernels/moe_gemv_affine.py:96-97
+            acc = (j == 0) ? o : acc + o;                      // rank order, kernels/moe_gemv_affine.py:108-109
+            if (a.o_buf) a.o_buf[((int64_t)r * k + j) * H + m] = o;
+          }
+        }
+        a.out[(int64_t)r * H + m] = acc;
+        a.y[(int64_t)r * H + m] = f32_to_bf16(round_bf16(acc) + shv);   // routed.to(bf16) + sh
+      }
+    }
+  }
+}
+
+size_t fused_smem(int H, int I) {
+  return (size_t)F_MAXR * H * 2 + sizeof(XUnitS) * ((size_t)F_MAXR * (H / 16) + (size_t)F_MAXR * (F_MAXK + 1) * (I / 16)) +
+         (size_t)F_MAXE * sizeof(void*);
+}
+
+template <int NUX, int NUI>
+void* pick_epl(int epl) {
+  return epl <= 4 ? (void*)k_dec_fused<NUX, NUI, 4> : epl <= 8 ? (void*)k_dec_fused<NUX, NUI, 8>
+                                                                : (void*)k_dec_fused<NUX, NUI, 16>;
+}
+template <int NUX>
+void* pick_nui(int nui, int epl) {
+  switch (nui) {
+    case 1: return pick_epl<NUX, 1>(epl);
+    case 2: return pick_epl<NUX, 2>(epl);
+    case 4: return pick_epl<NUX, 4>(epl);
+    default: return nullptr;
+  }
+}
+
+}  // namespace
+
+extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t topk, int32_t hidden, int32_t inter,
+                                    int32_t experts, const uint16_t* w_router, const uint16_t* sh_gate_w,
+                                    const float* bias, int32_t flags, int32_t layer, const int32_t* map_t,
+                                    int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots,
+                                    const void* shared_record, float* logits_ws, int32_t* out_idx, float* out_w,
+                                    float* out_sh_gate, int64_t* out_base, float* h_buf, float* o_buf, float* out,
+                                    uint16_t* y, uint32_t* sync, int32_t* err, void* stream) {
+  SSB_CHECK_ARG(rows >= 0 && topk >= 1 && topk <= F_MAXK && topk <= experts && experts >= 1 && layer >= 0);
+  if (rows > F_MAXR || experts > F_MAXE || hidden % 512 || hidden <= 0 || hidden > 4096 || inter % 512 ||
+      inter <= 0 || inter > 2048 || inter == 1536)
+    return SSB_EUNSUPPORTED;
+  SSB_CHECK_ARG((flags & ~SSB_ROUTER_ROUND_BF16) == 0 && map_len >= 0 && n_slots >= 0);
+  if (rows == 0) return SSB_OK;
+  SSB_CHECK_ARG(x && w_router && sh_gate_w && map_t && slot_ptr_t && shared_record && logits_ws && out_idx && out_w &&
+                out_sh_gate && h_buf && out && y && sync);
+  SSB_CHECK_ARG(((uintptr_t)shared_record & 15) == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w_router & 15) == 0);
+  const int nux = hidden / 512, nui = inter / 512, epl = (experts + 31) / 32;
+  void* kern = nullptr;
+  switch (nux) {
+    case 1: kern = pick_nui<1>(nui, epl); break;
+    case 2: kern = pick_nui<2>(nui, epl); break;
+    case 4: kern = pick_nui<4>(nui, epl); break;
+    case 8: kern = pick_nui<8>(nui, epl); break;
+    default: break;
+  }
+  if (!kern) return SSB_EUNSUPPORTED;
+  const size_t smem = fused_smem(hidden, inter);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return (int)e;
+  ssb_note_smem("moe_decode_fused", (void (*)(FusedArgs))kern, smem);
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FT, smem);
+  if (e != cudaSuccess) return (int)e;
+  if (per_sm < 1 || sms < 1) return SSB_EUNSUPPORTED;
+  FusedArgs a{};
+  a.x = x;
+  a.R = (int)rows;
+  a.k = topk;
+  a.H = hidden;
+  a.I = inter;
+  a.E = experts;
+  a.gs = 64;
+  a.w_router = w_router;
+  a.sh_gate_w = sh_gate_w;
+  a.bias = bias;
+  a.flags = flags;
+  a.layer = layer;
+  a.map = map_t;
+  a.map_len = map_len;
+  a.slot_ptr = slot_ptr_t;
+  a.n_slots = n_slots;
+  a.shared_rec = (const uint8_t*)shared_record;
+  a.o = rec_offsets(hidden, inter, 64);
+  a.logits = logits_ws;
+  a.out_idx = out_idx;
+  a.out_w = out_w;
+  a.out_sh_gate = out_sh_gate;
+  a.out_base = out_base;
+  a.h_buf = h_buf;
+  a.o_buf = o_buf;
+  a.out = out;
+  a.y = y;
+  a.sync = sync;
+  a.err = err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)sms);   // one CTA per SM: all resident (the launch fails otherwise)
+  cfg.blockDim = dim3(FT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, (void (*)(FusedArgs))kern, a);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return (int)e;
+  }
+  return SSB_OK;
+}

@@ -44,6 +44,8 @@ struct GemmArgs {
   const uint16_t* a;          // bf16 activation rows, `lda` elements apart (read through the A tensor map)
   int64_t lda;
   int64_t a_rows;             // rows of the activation matrix (extent of the tensor map)
+  int a_box_rows;             // rows per A copy: 1 (tile::gather4 of four rows) or BM (one 2-D box, identity rows)
+  int out_sorted;             // SwiGLU epilogue: h row at the sorted position m instead of at row sorted_rows[m]
   const int32_t* row_token;   // nullable: the A row of row r is r
   const int32_t* sorted_rows; // nullable: identity (rows m < R)
   const int32_t* block_expert;
@@ -198,12 +200,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
     };
     int64_t issued = 0;
     if (lane == 0) prefetch_tensormap(&tm_a);
-    load_rows(0);
-    to_coords();
+    const bool gather = a.a_box_rows != BM;
+    if (gather) {
+      load_rows(0);
+      to_coords();
+    }
     for (int64_t j = 0; j < steps; ++j) {
       const int kb = (int)(j % KB);
       const int i = (int)(j / KB);
-      if (kb == 0) {
+      if (!gather) {
+      } else if (kb == 0) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) rc[q] = nrc[q];
         if (i + 1 < my_tiles) {
@@ -223,8 +229,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       }
       if (lane == 0) mbar_expect_tx(&S.full_a[s], A_STAGE);
       __syncwarp();
-      tma_gather4(smem_u32(S.a + s * A_STAGE + lane * 512), &tm_a, kb * BK, rc[0], rc[1], rc[2], rc[3],
-                  &S.full_a[s]);
+      if (a.a_box_rows == BM) {   // rows m-block*128 .. +127 of the activation matrix in one copy
+        if (lane == 0)
+          tma_load_2d(smem_u32(S.a + s * A_STAGE), &tm_a, kb * BK, (int32_t)((tile_of(i) / NB) * BM), &S.full_a[s]);
+      } else {
+        tma_gather4(smem_u32(S.a + s * A_STAGE + lane * 512), &tm_a, kb * BK, rc[0], rc[1], rc[2], rc[3],
+                    &S.full_a[s]);
+      }
       ++issued;
     }
     // no copy may still be writing shared memory when the CTA exits: wait for the last stages to land
@@ -253,7 +264,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
             ok = false;
             break;
           }
-          fence_proxy_async_smem();
           tc_fence_after();
           const uint64_t da = umma_desc_sw128(smem_u32(S.a + s * A_STAGE));
           const uint64_t db = umma_desc_sw128(smem_u32(S.b + s * B_STAGE));
@@ -298,7 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
           tmem_ld32(taddr + col, g);
           tmem_ld32(taddr + BN / 2 + col, u);
           if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(out + row * a.ldo + (int64_t)nb * (BN / 2) + col);
+            uint4* dst = reinterpret_cast<uint4*>(out + (a.out_sorted ? m : row) * a.ldo + (int64_t)nb * (BN / 2) + col);
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
               float h[8];
@@ -367,21 +377,36 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       }
     };
     if (a.dense_b) {
-      for (int64_t j = 0; j < steps; ++j) {
-        const int kb = (int)(j % KB);
-        tile_info(j);
-        const int s = (int)(j % STAGES);
-        const uint32_t ph = (uint32_t)((j / STAGES) & 1);
-        if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
-          s_fail = 1;
-          break;
-        }
-        const uint32_t bt = smem_u32(S.b + s * B_STAGE);
-        const uint16_t* drow = t_base ? (const uint16_t*)t_base + t_nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
+      // bf16 weights: cp.async straight into the swizzled tile, DB steps in flight; a step is handed to the MMA
+      // only after this thread's copies landed and were made visible to the tensor core's (async) proxy
+      constexpr int DB = STAGES - 1;
+      bool fail = false;
+      for (int64_t j = 0; j < steps + DB; ++j) {
+        if (j < steps) {
+          const int kb = (int)(j % KB);
+          tile_info(j);
+          const int s = (int)(j % STAGES);
+          const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+          if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
+            s_fail = 1;
+            fail = true;
+          } else {
+            const uint32_t bt = smem_u32(S.b + s * B_STAGE);
+            const uint16_t* drow =
+                t_base ? (const uint16_t*)t_base + t_nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + c * 8, t_base ? 16u : 0u);
-        cp_async_arrive(&S.full_b[s]);
+            for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + c * 8, t_base ? 16u : 0u);
+          }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if (fail) break;
+        if (j >= DB) {
+          asm volatile("cp.async.wait_group %0;" ::"n"(DB) : "memory");
+          fence_proxy_async_smem();
+          mbar_arrive(&S.full_b[(j - DB) % STAGES]);
+        }
       }
+      asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
       uint32_t valid = 0;   // bit (j % PD): staging slot of step j holds a real weight row
       auto issue = [&](int64_t j) {
@@ -470,6 +495,27 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
   if (tid == 0 && s_fail) set_err(a.err, SSB_ERR_TIMEOUT);
 }
 
+// x_sorted[m, :] = x[row_token[sorted_rows[m]], :] for m < num_padded (zero rows for padding), one warp per row:
+// the activation rows in expert order, so the grouped GEMM reads its A tiles as whole 2-D boxes.
+__global__ void __launch_bounds__(256) k_permute_rows(const uint4* __restrict__ x, int64_t x_rows, int64_t row_vecs,
+                                                      const int32_t* __restrict__ row_token,
+                                                      const int32_t* __restrict__ sorted_rows,
+                                                      const int32_t* __restrict__ num_padded, int64_t R,
+                                                      int64_t padded_len, uint4* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t np = __ldcg(num_padded);
+  const int64_t n = np < padded_len ? np : padded_len;
+  for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < n; m += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = __ldcg(sorted_rows + m);
+    const int64_t t = (r >= 0 && r < R) ? (int64_t)__ldcg(row_token + r) : -1;
+    const bool ok = t >= 0 && t < x_rows;
+    for (int64_t c = lane; c < row_vecs; c += 32)
+      out[m * row_vecs + c] = ok ? __ldg(x + t * row_vecs + c) : make_uint4(0, 0, 0, 0);
+  }
+}
+
 int num_sms() {
   static int sms = 0;
   if (!sms) {
@@ -497,11 +543,12 @@ EncodeTiledFn encode_tiled_fn() {
 // 2-D tensor map over the activation rows: K elements x a_rows rows, box 64 x 1, 128-byte swizzle.
 int encode_a_map(CUtensorMap* map, const GemmArgs& a) {
   if (((uintptr_t)a.a & 15) || (a.lda * 2) % 16 || a.a_rows < 1 || a.a_rows > 0x7fffffffLL) return SSB_EINVAL;
+  if (a.a_box_rows != 1 && a.a_box_rows != BM) return SSB_EINVAL;
   EncodeTiledFn encode = encode_tiled_fn();
   if (!encode) return SSB_ENODEVICE;
   cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.a_rows};
   cuuint64_t strides[1] = {(cuuint64_t)a.lda * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, 1};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)a.a_box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)a.a, dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -552,7 +599,7 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
                  int64_t rows,
                  const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded,
                  int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, int32_t shared_local,
-                 uint16_t* h_buf, int32_t* err, void* stream) {
+                 uint16_t* h_buf, int32_t* err, void* stream, bool sorted = false) {
   SSB_CHECK_ARG(rows >= 0 && padded_len >= 0 && n_groups >= 1);
   if (hidden % BK || hidden <= 0 || inter % (BN / 2) || inter <= 0 || (hidden / 64) % 2) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
@@ -561,7 +608,9 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
   GemmArgs g{};
   g.a = x;
   g.lda = hidden;
-  g.a_rows = tokens;
+  g.a_rows = sorted ? padded_len : tokens;   // sorted: x is the permuted [padded_len, hidden] matrix
+  g.a_box_rows = sorted ? BM : 1;
+  g.out_sorted = sorted;
   g.row_token = row_token;
   g.sorted_rows = sorted_rows;
   g.block_expert = block_expert;
@@ -582,7 +631,7 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
 int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter, const float* row_weight,
               const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
               const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, float* out_rows, int32_t* err,
-              void* stream) {
+              void* stream, bool sorted = false) {
   SSB_CHECK_ARG(rows >= 0 && padded_len >= 0 && n_groups >= 1);
   if (inter % BK || inter <= 0 || hidden % BN || hidden <= 0 || (inter / 64) % 2) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
@@ -591,7 +640,8 @@ int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter
   GemmArgs g{};
   g.a = h_buf;
   g.lda = inter;
-  g.a_rows = rows;
+  g.a_rows = sorted ? padded_len : rows;     // sorted: h rows at their sorted positions
+  g.a_box_rows = sorted ? BM : 1;
   g.sorted_rows = sorted_rows;
   g.block_expert = block_expert;
   g.num_padded = num_padded;
@@ -629,18 +679,58 @@ extern "C" int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t h
                    group_ptr, n_groups, -1, out_rows, err, stream);
 }
 
+int permute_impl(const uint16_t* x, int64_t tokens, int32_t hidden, const int32_t* row_token, int64_t rows,
+                 const int32_t* sorted_rows, const int32_t* num_padded, int64_t padded_len, uint16_t* x_sorted,
+                 cudaStream_t st) {
+  SSB_CHECK_ARG(tokens >= 0 && rows >= 0 && padded_len >= 0 && hidden > 0 && hidden % 8 == 0);
+  if (padded_len == 0) return SSB_OK;
+  SSB_CHECK_ARG(x && row_token && sorted_rows && num_padded && x_sorted);
+  SSB_CHECK_ARG((((uintptr_t)x | (uintptr_t)x_sorted) & 15) == 0);
+  const int64_t blocks = (padded_len + 7) / 8;
+  return ssb_launch(k_permute_rows, dim3((unsigned)(blocks < 148 * 8 ? blocks : 148 * 8)), dim3(256), 0, st, true,
+                    (const uint4*)x, tokens, (int64_t)hidden / 8, row_token, sorted_rows, num_padded, rows, padded_len,
+                    (uint4*)x_sorted);
+}
+
+extern "C" int ssb_permute_rows(const uint16_t* x, int64_t tokens, int32_t hidden, const int32_t* row_token,
+                                int64_t rows, const int32_t* sorted_rows, const int32_t* num_padded,
+                                int64_t padded_len, uint16_t* x_sorted, void* stream) {
+  return permute_impl(x, tokens, hidden, row_token, rows, sorted_rows, num_padded, padded_len, x_sorted,
+                      (cudaStream_t)stream);
+}
+
+extern "C" int ssb_sorted_gate_up(const uint16_t* x_sorted, int32_t hidden, int32_t inter, const int32_t* row_token,
+                                  int64_t rows, const int32_t* sorted_rows, const int32_t* block_expert,
+                                  const int32_t* num_padded, int64_t padded_len, const int64_t* group_ptr,
+                                  int32_t n_groups, int32_t shared_local, uint16_t* h_sorted, int32_t* err,
+                                  void* stream) {
+  return gate_up_impl(x_sorted, padded_len, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded,
+                      padded_len, group_ptr, n_groups, shared_local, h_sorted, err, stream, true);
+}
+
+extern "C" int ssb_sorted_down(const uint16_t* h_sorted, int64_t rows, int32_t hidden, int32_t inter,
+                               const float* row_weight, const int32_t* sorted_rows, const int32_t* block_expert,
+                               const int32_t* num_padded, int64_t padded_len, const int64_t* group_ptr,
+                               int32_t n_groups, int32_t shared_local, float* out_rows, int32_t* err, void* stream) {
+  return down_impl(h_sorted, rows, hidden, inter, row_weight, sorted_rows, block_expert, num_padded, padded_len,
+                   group_ptr, n_groups, shared_local, out_rows, err, stream, true);
+}
+
 extern "C" int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter,
-                                   const int32_t* row_token,
-                                   const float* row_weight, int64_t rows, const int32_t* sorted_rows,
-                                   const int32_t* block_expert, const int32_t* num_padded, int64_t padded_len,
-                                   const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, uint16_t* h_buf,
-                                   float* out_rows, int32_t* err, void* stream) {
+                                   const int32_t* row_token, const float* row_weight, int64_t rows,
+                                   const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded,
+                                   int64_t padded_len, const int64_t* group_ptr, int32_t n_groups,
+                                   int32_t shared_local, uint16_t* x_sorted, uint16_t* h_sorted, float* out_rows,
+                                   int32_t* err, void* stream) {
   SSB_CHECK_ARG(tokens >= 0);
-  int rc = gate_up_impl(x, tokens, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len,
-                        group_ptr, n_groups, shared_local, h_buf, err, stream);
+  int rc = permute_impl(x, tokens, hidden, row_token, rows, sorted_rows, num_padded, padded_len, x_sorted,
+                        (cudaStream_t)stream);
   if (rc) return rc;
-  return down_impl(h_buf, rows, hidden, inter, row_weight, sorted_rows, block_expert, num_padded, padded_len,
-                   group_ptr, n_groups, shared_local, out_rows, err, stream);
+  rc = ssb_sorted_gate_up(x_sorted, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len,
+                          group_ptr, n_groups, shared_local, h_sorted, err, stream);
+  if (rc) return rc;
+  return ssb_sorted_down(h_sorted, rows, hidden, inter, row_weight, sorted_rows, block_expert, num_padded, padded_len,
+                         group_ptr, n_groups, shared_local, out_rows, err, stream);
 }
 
 extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const int32_t* q, const uint16_t* s,
@@ -655,6 +745,7 @@ extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const i
   g.a = x;
   g.lda = k;
   g.a_rows = m;
+  g.a_box_rows = BM;   // identity rows: one 2-D box per k-block (the tail past m reads zeros)
   g.R = m;
   g.base0 = (const uint8_t*)q;
   g.n_groups = 1;
@@ -680,6 +771,7 @@ extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uin
   g.a = x;
   g.lda = k;
   g.a_rows = m;
+  g.a_box_rows = BM;   // identity rows: one 2-D box per k-block (the tail past m reads zeros)
   g.R = m;
   g.base0 = (const uint8_t*)w;
   g.n_groups = 1;

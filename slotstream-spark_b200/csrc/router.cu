@@ -11,17 +11,9 @@
 
 #include "affine.cuh"
 #include "registry.h"
+#include "select.cuh"
 
 namespace {
-
-SSB_DEV uint32_t order_key(float f) {
-  uint32_t b = __float_as_uint(f);
-  if ((b & 0x7FFFFFFFu) > 0x7F800000u) return 0u;  // NaN: lowest
-  return (b & 0x80000000u) ? ~b : (b ^ 0x80000000u);
-}
-SSB_DEV unsigned long long composite(uint32_t key, uint32_t idx) {
-  return ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
-}
 
 // ------------------------------------------------------------------ logits
 // Warp per weight row, the row held in registers (lane l owns 16-byte chunks l, l+32, ...); a CTA covers
@@ -86,42 +78,6 @@ __global__ void __launch_bounds__(RL_WARPS * 32) k_router_logits(const uint16_t*
 constexpr int RS_WARPS = 4;
 constexpr int RS_MAXE = 32;  // experts per lane: experts <= 1024
 
-SSB_DEV void cswap_desc(unsigned long long& a, unsigned long long& b) {
-  const unsigned long long hi = a > b ? a : b, lo = a > b ? b : a;
-  a = hi;
-  b = lo;
-}
-// Sort 16 composites descending (bitonic network, fully unrolled).
-SSB_DEV void bitonic_sort_desc16(unsigned long long* x) {
-#pragma unroll
-  for (int size = 2; size <= 16; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int j = i ^ stride;
-        if (j > i) {
-          if ((i & size) == 0) cswap_desc(x[i], x[j]);
-          else cswap_desc(x[j], x[i]);
-        }
-      }
-    }
-  }
-}
-// A bitonic sequence of 16 -> descending.
-SSB_DEV void bitonic_merge_desc16(unsigned long long* x) {
-#pragma unroll
-  for (int stride = 8; stride > 0; stride >>= 1) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if ((i & stride) == 0) cswap_desc(x[i], x[i + stride]);
-  }
-}
-// The fp32 value whose order key is `key` (inverse of order_key for non-NaN values).
-SSB_DEV float key_value(uint32_t key) {
-  return __uint_as_float((key & 0x80000000u) ? (key ^ 0x80000000u) : ~key);
-}
-
 struct SelectArgs {
   const float* logits;
   int ld;
@@ -171,8 +127,6 @@ SSB_DEV void select_tail(const SelectArgs& a, int64_t t, int lane, unsigned long
   }
 }
 
-constexpr int RS_CAND = 64;   // candidate slots per warp
-
 template <int EPL>
 __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(SelectArgs a) {
   __shared__ unsigned long long s_cand[RS_WARPS][RS_CAND];
@@ -182,160 +136,11 @@ __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(SelectArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t t = (int64_t)blockIdx.x * RS_WARPS + warp;
   if (t >= a.tokens) return;
-  const int experts = a.experts, k = a.k;
   const float* lrow = a.logits + t * a.ld;
-  float v[EPL];
-  float m = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    int e = lane + 32 * i;
-    float l = -INFINITY;
-    if (e < experts) {
-      l = __ldcg(lrow + e);
-      if (a.bias) l = l + a.bias[e];
-      if (a.flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
-      m = fmaxf(m, l);
-    }
-    v[i] = l;
-  }
-  m = warp_max(m);
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    int e = lane + 32 * i;
-    float ex = 0.f;
-    if (e < experts) ex = expf(v[i] - m);
-    v[i] = ex;
-    s += ex;
-  }
-  s = warp_sum(s);
-  unsigned long long c[EPL];
-  unsigned long long lm = 0ull;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    int e = lane + 32 * i;
-    float p = v[i] / s;
-    v[i] = p;
-    c[i] = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
-    lm = c[i] > lm ? c[i] : lm;
-    if (a.out_probs && e < experts) a.out_probs[t * experts + e] = p;
-  }
-  if (k <= 16) {
-    // Candidate filter: the k-th largest lane maximum T0 is a lower bound for the k-th largest composite (k
-    // lanes each hold an element >= T0), so only elements >= T0 can be selected. The candidates (usually a
-    // few more than k) are ranked by comparing against each other through shared memory.
-    int rk = 0;
-#pragma unroll
-    for (int d = 1; d < 32; ++d) {
-      const unsigned long long o = __shfl_sync(0xFFFFFFFFu, lm, (lane + d) & 31);
-      rk += o > lm;
-    }
-    const unsigned at = __ballot_sync(0xFFFFFFFFu, rk == k - 1 && lm != 0ull);
-    if (at) {
-      const unsigned long long T0 = __shfl_sync(0xFFFFFFFFu, lm, __ffs(at) - 1);
-      int n = 0;
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) n += c[i] >= T0;
-      int incl = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
-      if (total <= RS_CAND) {
-        int pos = incl - n;
-#pragma unroll
-        for (int i = 0; i < EPL; ++i)
-          if (c[i] >= T0) s_cand[warp][pos++] = c[i];
-        __syncwarp();
-        const unsigned long long a0 = lane < total ? s_cand[warp][lane] : 0ull;
-        const unsigned long long a1 = lane + 32 < total ? s_cand[warp][lane + 32] : 0ull;
-        int r0 = 0, r1 = 0;
-        for (int q = 0; q < total; ++q) {
-          const unsigned long long o = s_cand[warp][q];
-          r0 += o > a0;
-          r1 += o > a1;
-        }
-        if (lane < total && r0 < k) s_top[warp][r0] = a0;
-        if (lane + 32 < total && r1 < k) s_top[warp][r1] = a1;
-        __syncwarp();
-        float sum = 0.f, my_p = 0.f;   // renormalise: sequential sum in rank order
-        unsigned long long mine = 0ull;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j < k) {
-            const unsigned long long cj = s_top[warp][j];
-            const float pj = key_value((uint32_t)(cj >> 32));
-            sum += pj;
-            if (j == lane) {
-              mine = cj;
-              my_p = pj;
-            }
-          }
-        }
-        select_tail(a, t, lane, mine, my_p, sum, lrow);
-        return;
-      }
-    }
-  }
-  if (EPL <= 16 && k <= 16) {
-    // Warp-wide top 16: each lane sorts its composites, then five butterfly steps merge the lanes' sorted
-    // lists (top 16 of two sorted lists = bitonic max, then a bitonic merge); every lane ends with the global
-    // top 16 in (value desc, index asc) order.
-    unsigned long long L[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) L[i] = i < EPL ? c[i < EPL ? i : 0] : 0ull;
-    bitonic_sort_desc16(L);
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      unsigned long long o[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, L[i], off);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) L[i] = L[i] > o[15 - i] ? L[i] : o[15 - i];
-      bitonic_merge_desc16(L);
-    }
-    float sum = 0.f, my_p = 0.f;
-    unsigned long long mine = 0ull;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float pj = key_value((uint32_t)(L[j] >> 32));
-      if (j < k) sum += pj;
-      if (j == lane) {
-        mine = L[j];
-        my_p = pj;
-      }
-    }
-    select_tail(a, t, lane, mine, my_p, sum, lrow);
-    return;
-  }
-  // k rounds of warp arg-max; round j's winner is the j-th output (value desc, index asc)
-  unsigned long long mine = 0ull;
-  float my_p = 0.f;
-  for (int j = 0; j < k; ++j) {
-    unsigned long long lmx = 0ull;
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) lmx = c[i] > lmx ? c[i] : lmx;
-    const unsigned long long g = warp_max_u64(lmx);
-    const uint32_t e = 0xFFFFFFFFu - (uint32_t)(g & 0xFFFFFFFFull);
-    float p = 0.f;
-    if ((int)(e & 31) == lane) {
-#pragma unroll
-      for (int i = 0; i < EPL; ++i)
-        if (lane + 32 * i == (int)e) {
-          p = v[i];
-          c[i] = 0ull;
-        }
-    }
-    p = __shfl_sync(0xFFFFFFFFu, p, e & 31);
-    if (lane == j) {
-      mine = g;
-      my_p = p;
-    }
-  }
-  float sum = 0.f;  // sequential in rank order
-  for (int j = 0; j < k; ++j) sum += __shfl_sync(0xFFFFFFFFu, my_p, j);
+  unsigned long long mine;
+  float my_p, sum;
+  warp_select<EPL>(lrow, a.experts, a.k, a.bias, a.flags, a.out_probs ? a.out_probs + t * a.experts : nullptr,
+                   s_cand[warp], s_top[warp], lane, mine, my_p, sum);
   select_tail(a, t, lane, mine, my_p, sum, lrow);
 }
 

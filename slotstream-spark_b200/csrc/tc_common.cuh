@@ -97,6 +97,15 @@ SSB_DEV void tma_gather4(uint32_t dst, const CUtensorMap* map, int32_t col, int3
       "l"((uint64_t)map), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
       : "memory");
 }
+// One cache line into L2 through the load/store path (no register result, nothing to wait for).
+SSB_DEV void prefetch_line_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+// One 2-D box of the tensor map at (col, row) into dst (the map's box size and swizzle), bytes counted on `bar`.
+SSB_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t col, int32_t row, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"((uint64_t)map), "r"(col), "r"(row), "r"(smem_u32(bar))
+      : "memory");
+}
 SSB_DEV void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
 }

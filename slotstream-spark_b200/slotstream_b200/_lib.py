@@ -34,6 +34,13 @@ SIGNATURES = {
                              _P, _I32, _P, _P],
     "ssb_router_select_resolve": [_P, _I32, _I64, _I32, _I32, _P, _I32, _P, _P, _P, _I32, _P, _I64, _P, _I64, _P,
                                   _I64, _P, _P],
+    "ssb_ep_plan": [_P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P],
+    "ssb_gather_rows": [_P, _I64, _P, _I64, _I64, _P, _P, _P],
+    "ssb_ep_unpack": [_P, _I64, _I32, _P, _P, _I32, _I64, _P, _P, _P, _P, _P, _P, _P],
+    "ssb_combine_rows": [_P, _P, _P, _I64, _I32, _P, _P],
+    "ssb_ep_combine": [_P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "ssb_moe_decode_fused": [_P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _P,
+                             _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "ssb_router_topk_static": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P],
     "ssb_combine_rank_order": [_P, _I64, _I32, _I32, _P, _P],
     "ssb_combine_layer": [_P, _I64, _I32, _I32, _P, _P, _P, _P],
@@ -42,7 +49,10 @@ SIGNATURES = {
     "ssb_fused_moe_gate_up": [_P, _I64, _I32, _I32, _P, _I64, _P, _P, _P, _I64, _P, _I32, _P, _P, _P],
     "ssb_fused_moe_down": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _I64, _P, _I32, _P, _P, _P],
     "ssb_gemm_affine4": [_P, _I64, _I32, _P, _P, _P, _I32, _I32, _P, _P],
-    "ssb_prefill_experts": [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P, _P, _I64, _P, _I32, _I32, _P, _P, _P, _P],
+    "ssb_prefill_experts": [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P, _P, _I64, _P, _I32, _I32, _P, _P, _P, _P, _P],
+    "ssb_permute_rows": [_P, _I64, _I32, _P, _I64, _P, _P, _I64, _P, _P],
+    "ssb_sorted_gate_up": [_P, _I32, _I32, _P, _I64, _P, _P, _P, _I64, _P, _I32, _I32, _P, _P, _P],
+    "ssb_sorted_down": [_P, _I64, _I32, _I32, _P, _P, _P, _P, _I64, _P, _I32, _I32, _P, _P, _P],
     "ssb_gemm_dense": [_P, _I64, _I32, _P, _I32, _P, _I64, _P],
 }
 

@@ -1,0 +1,233 @@
+"""Expert-parallel prefill MoE layer: experts sharded by id over the ranks of a process group.
+
+The reference runs on one GPU and has no multi-GPU path; this module adds the one exchange the MoE layer has
+when its experts are spread over G GPUs. Every rank routes its own tokens (router and shared expert are
+replicated), then:
+
+1. plan      -- dedupe (token, destination rank), order rows by destination then token, one metadata row per
+                sent token: the local expert and weight of each top-k choice that rank owns (-1 otherwise),
+                the row's entry base inside the destination block and its entry count;
+2. dispatch  -- all-to-all of the per-destination (rows, entries) counts, then all-to-all-v of the bf16 token
+                rows and of the metadata;
+3. experts   -- the receiving rank compacts the valid (row, choice) entries and runs the grouped tcgen05
+                GEMMs (gate_up + SwiGLU, down x weight) over its own experts;
+4. combine   -- default: each received row's entries are summed in rank-k order and that fp32 partial goes
+                back; the home rank adds the partials of its destinations in rank order. exact: the entry
+                rows themselves go back and the home rank sums every token's k rows in router-rank order,
+                which reproduces the one-GPU layer bit for bit (kernels/fused_moe_affine.py:164-172);
+5. output    -- y = bf16(bf16(routed) + bf16(shared)), as the one-GPU layer.
+
+Placement: ``strided`` puts expert e on rank e % G (local index e // G), spreading the popular low ids of a
+Zipf-skewed router over all ranks; contiguous puts it on rank e // (E / G).
+
+The exchange runs through torch.distributed collectives only (NCCL on GPUs; the same code drives gloo on CPU
+tensors in the host-side tests), with the per-destination counts copied to the host to size the all-to-all-v
+-- one host synchronisation per layer call, so this path is eager, not graph-captured.
+"""
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+MAX_RANKS = 8
+
+
+def owner(e: int, experts: int, n_ranks: int, strided: bool) -> tuple[int, int]:
+    """(rank, local index) of expert e."""
+    epr = experts // n_ranks
+    return (e % n_ranks, e // n_ranks) if strided else (e // epr, e % epr)
+
+
+def owned_experts(rank: int, experts: int, n_ranks: int, strided: bool) -> list[int]:
+    """Global ids of the experts rank `rank` owns, in local-index order."""
+    epr = experts // n_ranks
+    return [rank + n_ranks * i for i in range(epr)] if strided else list(range(rank * epr, (rank + 1) * epr))
+
+
+@dataclass
+class Plan:
+    dest_count: torch.Tensor   # int32 [G, 2]: rows, entries per destination
+    send_token: torch.Tensor   # int32 [rows sent]
+    send_meta: torch.Tensor    # int32 [rows sent, 2k + 2]
+    tok_slot: torch.Tensor     # int32 [T, G]: send row of (t, d) or -1
+    tok_entry: torch.Tensor    # int32 [T, G]: entry base of (t, d) in d's block or -1
+
+
+@dataclass
+class Entries:
+    row_expert: torch.Tensor   # int32 [n]: local expert of entry
+    row_token: torch.Tensor    # int32 [n]: received row of entry
+    row_weight: torch.Tensor   # fp32 [n]
+    row_e0: torch.Tensor       # int64 [received rows]: first entry of the row
+    row_cnt: torch.Tensor      # int32 [received rows]
+
+
+def _prefix(v: list[int]) -> list[int]:
+    out, s = [0], 0
+    for x in v:
+        s += x
+        out.append(s)
+    return out
+
+
+def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bool = False):
+    """One expert-parallel MoE layer over this rank's tokens x [T, H] -> y bf16 [T, H].
+    ``ops`` supplies the per-rank compute (``CudaOps`` on B200); the exchange is the same for every backend."""
+    G = n_ranks
+    ids, w, sh_gate = ops.route(x)
+    sh = ops.shared(x, sh_gate)
+    plan = ops.plan(ids, w)
+    send_x = ops.gather(x, plan.send_token)
+    recv_count = torch.empty_like(plan.dest_count)
+    dist.all_to_all_single(recv_count.view(-1), plan.dest_count.view(-1), group=group)
+    sc = plan.dest_count.cpu().tolist()
+    rc = recv_count.cpu().tolist()
+    send_rows, send_ent = [c[0] for c in sc], [c[1] for c in sc]
+    recv_rows, recv_ent = [c[0] for c in rc], [c[1] for c in rc]
+    n_recv = sum(recv_rows)
+    recv_x = x.new_empty((n_recv, x.shape[1]))
+    dist.all_to_all_single(recv_x, send_x, recv_rows, send_rows, group=group)
+    recv_meta = plan.send_meta.new_empty((n_recv, plan.send_meta.shape[1]))
+    dist.all_to_all_single(recv_meta, plan.send_meta, recv_rows, send_rows, group=group)
+    entries = ops.unpack(recv_meta, _prefix(recv_rows), _prefix(recv_ent), sum(recv_ent))
+    out_rows = ops.experts(recv_x, entries)
+    if exact:
+        ret = out_rows.new_empty((sum(send_ent), out_rows.shape[1]))
+        dist.all_to_all_single(ret, out_rows, send_ent, recv_ent, group=group)
+        return ops.combine(ret, plan, ids, _prefix(send_ent)[:G], sh, exact=True)
+    partial = ops.combine_rows(out_rows, entries)
+    ret = partial.new_empty((sum(send_rows), partial.shape[1]))
+    dist.all_to_all_single(ret, partial, send_rows, recv_rows, group=group)
+    return ops.combine(ret, plan, ids, None, sh, exact=False)
+
+
+class CudaOps:
+    """The B200 kernels of one rank's share of an expert-parallel layer.
+
+    ``group_ptr`` int64 [E / G]: record base of each owned expert in local-index order; ``shared_ptr``: record
+    base of the shared expert; w_router bf16 [E, H] and sh_gate_w bf16 [H] are replicated on every rank."""
+
+    def __init__(self, w_router, sh_gate_w, group_ptr, shared_ptr: int, k: int, inter: int, n_ranks: int,
+                 strided: bool = True, bias=None, logits_round_bf16: bool = False):
+        e, h = w_router.shape
+        if n_ranks < 1 or n_ranks > MAX_RANKS or e % n_ranks:
+            raise ValueError(f"need 1 <= n_ranks <= {MAX_RANKS} dividing the expert count")
+        if group_ptr.dtype != torch.int64 or group_ptr.numel() != e // n_ranks or not group_ptr.is_cuda:
+            raise ValueError("group_ptr must be a CUDA int64 [E / G] tensor")
+        self.w_router, self.sh_gate_w, self.group_ptr = w_router, sh_gate_w, group_ptr
+        self.k, self.hidden, self.inter, self.n_experts = k, h, inter, e
+        self.G, self.epr, self.strided = n_ranks, e // n_ranks, bool(strided)
+        self.bias, self.round = bias, logits_round_bf16
+        dev = w_router.device
+        self.shared_ptr = torch.tensor([int(shared_ptr)], dtype=torch.int64, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._static = {}
+
+    # ---------------------------------------------------------------- helpers
+    def _aligned(self, row_expert, num_local):
+        from .kernels.moe_align import moe_align
+        return moe_align(row_expert, num_local, 128)
+
+    def _experts(self, a, tokens, row_token, row_weight, row_expert, group_ptr, n_groups, shared_local):
+        n = row_token.numel()
+        out = torch.empty((n, self.hidden), dtype=torch.float32, device=a.device)
+        if n == 0:
+            return out
+        sr, be, npd = self._aligned(row_expert, n_groups)
+        x_sorted = torch.empty((sr.numel(), self.hidden), dtype=torch.bfloat16, device=a.device)
+        h_sorted = torch.empty((sr.numel(), self.inter), dtype=torch.bfloat16, device=a.device)
+        L, P = _lib.lib(), _lib.ptr
+        _lib.check(L.ssb_prefill_experts(P(a), tokens, self.hidden, self.inter, P(row_token), P(row_weight), n, P(sr),
+                                         P(be), P(npd), sr.numel(), P(group_ptr), n_groups, shared_local, P(x_sorted),
+                                         P(h_sorted), P(out), P(self.err), _lib.stream()), "prefill experts")
+        return out
+
+    # ---------------------------------------------------------------- the steps of ep_forward
+    def route(self, x):
+        t, h = x.shape
+        e, k = self.n_experts, self.k
+        L, P, st = _lib.lib(), _lib.ptr, _lib.stream()
+        ld = e + 4
+        lg = torch.empty(t * ld, dtype=torch.float32, device=x.device)
+        _lib.check(L.ssb_gemm_dense(P(x), t, h, P(self.w_router), e, P(lg), ld, st), "router gemm")
+        _lib.check(L.ssb_router_logits(P(x), P(self.sh_gate_w), None, t, h, 1, ld, lg.data_ptr() + 4 * e, st),
+                   "shared gate logits")
+        ids = torch.empty((t, k), dtype=torch.int32, device=x.device)
+        w = torch.empty((t, k), dtype=torch.float32, device=x.device)
+        sh_gate = torch.empty(t, dtype=torch.float32, device=x.device)
+        flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if self.round else 0)
+        _lib.check(L.ssb_router_select(P(lg), ld, t, e, k, P(self.bias), flags, P(ids), P(w), None, P(sh_gate), st),
+                   "router select")
+        return ids, w, sh_gate
+
+    def shared(self, x, sh_gate):
+        t = x.shape[0]
+        key = ("shared", t)
+        if key not in self._static:
+            self._static[key] = (torch.arange(t, dtype=torch.int32, device=x.device),
+                                 torch.zeros(t, dtype=torch.int32, device=x.device))
+        tok, zero = self._static[key]
+        return self._experts(x, t, tok, sh_gate, zero, self.shared_ptr, 1, 0)
+
+    def plan(self, ids, w):
+        t, k, G = ids.shape[0], self.k, self.G
+        dev = ids.device
+        cap = t * min(G, k)
+        p = Plan(torch.empty((G, 2), dtype=torch.int32, device=dev), torch.empty(cap, dtype=torch.int32, device=dev),
+                 torch.empty((cap, 2 * k + 2), dtype=torch.int32, device=dev),
+                 torch.empty((t, G), dtype=torch.int32, device=dev), torch.empty((t, G), dtype=torch.int32, device=dev))
+        P = _lib.ptr
+        _lib.check(_lib.lib().ssb_ep_plan(P(ids), P(w), t, k, self.epr, G, int(self.strided), P(p.dest_count),
+                                          P(p.send_token), P(p.send_meta), P(p.tok_slot), P(p.tok_entry), P(self.err),
+                                          _lib.stream()), "ep plan")
+        n = int(p.dest_count[:, 0].sum())   # rows actually used (the buffers were sized for the worst case)
+        p.send_token, p.send_meta = p.send_token[:n], p.send_meta[:n]
+        return p
+
+    def gather(self, x, idx):
+        out = x.new_empty((idx.numel(), x.shape[1]))
+        P = _lib.ptr
+        _lib.check(_lib.lib().ssb_gather_rows(P(x), x.shape[0], P(idx), idx.numel(), x.shape[1] * x.element_size(),
+                                              P(out), P(self.err), _lib.stream()), "gather rows")
+        return out
+
+    def unpack(self, meta, src_row_off, src_entry_off, n_entries):
+        dev, n = meta.device, meta.shape[0]
+        ent = Entries(torch.empty(n_entries, dtype=torch.int32, device=dev),
+                      torch.empty(n_entries, dtype=torch.int32, device=dev),
+                      torch.empty(n_entries, dtype=torch.float32, device=dev),
+                      torch.empty(n, dtype=torch.int64, device=dev), torch.empty(n, dtype=torch.int32, device=dev))
+        ro = torch.tensor(src_row_off, dtype=torch.int32).to(dev, non_blocking=True)
+        eo = torch.tensor(src_entry_off, dtype=torch.int64).to(dev, non_blocking=True)
+        P = _lib.ptr
+        _lib.check(_lib.lib().ssb_ep_unpack(P(meta), n, self.k, P(ro), P(eo), self.G, n_entries, P(ent.row_expert),
+                                            P(ent.row_token), P(ent.row_weight), P(ent.row_e0), P(ent.row_cnt),
+                                            P(self.err), _lib.stream()), "ep unpack")
+        return ent
+
+    def experts(self, recv_x, ent):
+        return self._experts(recv_x, recv_x.shape[0], ent.row_token, ent.row_weight, ent.row_expert, self.group_ptr,
+                             self.epr, -1)
+
+    def combine_rows(self, out_rows, ent):
+        n = ent.row_e0.numel()
+        partial = torch.empty((n, self.hidden), dtype=torch.float32, device=out_rows.device)
+        P = _lib.ptr
+        _lib.check(_lib.lib().ssb_combine_rows(P(out_rows), P(ent.row_e0), P(ent.row_cnt), n, self.hidden, P(partial),
+                                               _lib.stream()), "combine rows")
+        return partial
+
+    def combine(self, ret, plan, ids, ret_entry_off, sh, exact):
+        t = ids.shape[0]
+        dev = ids.device
+        self.routed = torch.empty((t, self.hidden), dtype=torch.float32, device=dev)
+        y = torch.empty((t, self.hidden), dtype=torch.bfloat16, device=dev)
+        reo = (torch.tensor(ret_entry_off, dtype=torch.int64).to(dev, non_blocking=True)
+               if ret_entry_off is not None else None)
+        P = _lib.ptr
+        _lib.check(_lib.lib().ssb_ep_combine(P(ret), P(plan.tok_slot), P(plan.tok_entry), P(reo), P(ids), t, self.k,
+                                             self.epr, self.G, int(self.strided), int(exact), self.hidden, P(sh),
+                                             P(self.routed), P(y), _lib.stream()), "ep combine")
+        return y

@@ -11,6 +11,8 @@ import torch
 from .. import _lib
 from .gemv_affine import _note
 
+FUSED_MAX_ROWS = 2
+
 
 class DecodeLayerBuffers:
     """Every output and workspace of one decode layer call for `rows` tokens."""
@@ -28,6 +30,7 @@ class DecodeLayerBuffers:
         self.out = torch.empty(rows, hidden, **f32)
         self.y = torch.empty(rows, hidden, dtype=torch.bfloat16, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.sync = torch.zeros(2, dtype=torch.int32, device=device)   # grid-barrier words of the fused kernel
 
 
 class PrefillLayerBuffers:
@@ -58,7 +61,8 @@ class PrefillLayerBuffers:
         self.sorted_rows = torch.empty(p, dtype=torch.int32, device=device)
         self.block_expert = torch.empty(p // BLOCK_M, dtype=torch.int32, device=device)
         self.num_padded = torch.empty(1, dtype=torch.int32, device=device)
-        self.h = torch.empty(self.rows, inter, dtype=torch.bfloat16, device=device)
+        self.x_sorted = torch.empty(p, hidden, dtype=torch.bfloat16, device=device)   # activation rows in expert order
+        self.h = torch.empty(p, inter, dtype=torch.bfloat16, device=device)           # h in the same (sorted) order
         self.out_rows = torch.empty(self.rows, hidden, **f32)
         self.y = torch.empty(t, hidden, dtype=torch.bfloat16, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
@@ -69,8 +73,9 @@ def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLa
     """x bf16 [T, H] -> bufs.y bf16 [T, H]: one MoE layer over a prefill chunk, every expert resident.
 
     ``group_ptr`` int64 [E + 1]: record base of expert e at index e and of the shared expert at index E.
-    Launches: router GEMM (tcgen05, dense bf16) + shared-gate logits, router select, align, gate_up + down
-    (tcgen05 grouped GEMM, shared expert as local expert E), rank-order combine + shared add."""
+    Launches: router GEMM (tcgen05, dense bf16) + shared-gate logits, router select, align, row permute into
+    expert order, gate_up + down (tcgen05 grouped GEMM, shared expert as local expert E), rank-order combine +
+    shared add."""
     from .moe_align import moe_align
     t, h = x.shape
     e = bufs.experts
@@ -93,7 +98,8 @@ def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLa
     _lib.check(L.ssb_prefill_experts(
         _lib.ptr(x), t, h, bufs.inter, _lib.ptr(bufs.row_token), _lib.ptr(bufs.row_weight), bufs.rows,
         _lib.ptr(aligned[0]), _lib.ptr(aligned[1]), _lib.ptr(aligned[2]), aligned[0].numel(), _lib.ptr(group_ptr),
-        e + 1, e, _lib.ptr(bufs.h), _lib.ptr(bufs.out_rows), _lib.ptr(bufs.err), st), "prefill experts")
+        e + 1, e, _lib.ptr(bufs.x_sorted), _lib.ptr(bufs.h), _lib.ptr(bufs.out_rows), _lib.ptr(bufs.err), st),
+        "prefill experts")
     r = t * k
     _lib.check(L.ssb_combine_layer(_lib.ptr(bufs.out_rows), t, k, h, bufs.out_rows.data_ptr() + 4 * r * h, None,
                                    _lib.ptr(bufs.y), st), "combine")
@@ -112,9 +118,11 @@ def _addr(rec) -> int:
 
 def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, sh_gate_w, k: int,
                      bufs: DecodeLayerBuffers, *, bias=None, logits_round_bf16: bool = False, pdl: bool = True,
-                     prefetch_bytes: int = 0):
+                     prefetch_bytes: int = 0, fused: bool = True):
     """x bf16 [R, H] -> bufs.y bf16 [R, H] (also fills bufs.ids, bufs.w, bufs.out = routed fp32 sum).
-    ``prefetch_bytes`` > 0 makes the router prefetch that many bytes of each chosen record into L2."""
+    ``fused`` (R <= 2): the whole layer in one cooperative launch (ssb_moe_decode_fused), the same bits as the
+    four-launch path router_logits -> router_select_resolve -> moe_decode_layer used otherwise.
+    ``prefetch_bytes`` > 0 makes the four-launch router prefetch that many bytes of each chosen record into L2."""
     r, h = x.shape
     if (r, k, h) != (bufs.rows, bufs.topk, bufs.hidden) or w_router.shape[0] != bufs.experts:
         raise ValueError("buffers were sized for another call shape")
@@ -129,6 +137,17 @@ def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, 
     L = _lib.lib()
     st = _lib.stream()
     e = bufs.experts
+    if fused and r <= FUSED_MAX_ROWS:
+        rc = L.ssb_moe_decode_fused(
+            _lib.ptr(x), r, k, h, bufs.inter, e, _lib.ptr(w_router), _lib.ptr(sh_gate_w), _lib.ptr(bias),
+            _lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0, int(layer), _lib.ptr(map_t), map_t.numel(),
+            _lib.ptr(slot_ptr_t), slot_ptr_t.numel(), _addr(shared_record), _lib.ptr(bufs.ws), _lib.ptr(bufs.ids),
+            _lib.ptr(bufs.w), _lib.ptr(bufs.sh_gate), _lib.ptr(bufs.bases), _lib.ptr(bufs.h), _lib.ptr(bufs.o),
+            _lib.ptr(bufs.out), _lib.ptr(bufs.y), _lib.ptr(bufs.sync), _lib.ptr(bufs.err), st)
+        if rc != _lib.SSB_EUNSUPPORTED:
+            _lib.check(rc, "moe_decode_fused")
+            _note("moe_decode_fused")
+            return bufs.y
     _lib.check(L.ssb_router_logits(_lib.ptr(x), _lib.ptr(w_router), _lib.ptr(sh_gate_w), r, h, e, e + 1,
                                    _lib.ptr(bufs.ws), st), "router_logits")
     flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0)

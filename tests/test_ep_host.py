@@ -1,0 +1,86 @@
+"""Expert-parallel exchange protocol on CPU: two gloo ranks drive slotstream_b200.ep.ep_forward with
+oracle-backed compute; the routed sums must equal the one-rank layer (exact mode bit for bit, default mode to
+fp32 reassociation), for strided and contiguous expert placement and skewed routing."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from ep_cpu_ops import CpuOps, bits_to_bf16, single_rank_reference
+from oracle import ep_oracle as EO
+from slotstream_b200 import synth
+from slotstream_b200.records import RecordLayout
+
+LAY = RecordLayout(128, 64, 64)
+E, K, T = 16, 4, 12
+
+
+def _world(seed):
+    recs = [synth.expert_record(LAY, seed, 0, e) for e in range(E)]
+    shared = synth.expert_record(LAY, seed, 0, E)
+    rw = synth.router_weight(seed, E, LAY.hidden, 0)
+    sg = synth.shared_gate_weight(seed, LAY.hidden, 0)
+    return recs, shared, rw, sg
+
+
+def _tokens(rank):
+    return synth.activations(70 + rank, T, LAY.hidden)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir, strided, exact, zipf):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from slotstream_b200.ep import ep_forward
+        recs, shared, rw, sg = _world(5)
+        bias = synth.zipf_bias(E) * 4 if zipf else None
+        ops = CpuOps(LAY, recs, shared, rw, sg, K, E, world, rank, strided=strided, bias=bias)
+        y = ep_forward(ops, bits_to_bf16(_tokens(rank)), K, world, exact=exact)
+        np.save(os.path.join(out_dir, f"routed{rank}.npy"), ops.routed.numpy())
+        np.save(os.path.join(out_dir, f"y{rank}.npy"), y.view(torch.int16).numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("strided,exact,zipf", [(True, True, False), (False, True, True), (True, False, True)])
+def test_ep_exchange_matches_single_rank(tmp_path, strided, exact, zipf):
+    world = 2
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), strided, exact, zipf), nprocs=world,
+                       join=True, start_method="spawn")
+    recs, shared, rw, sg = _world(5)
+    bias = synth.zipf_bias(E) * 4 if zipf else None
+    for rank in range(world):
+        got = np.load(tmp_path / f"routed{rank}.npy")
+        ref = single_rank_reference(LAY, recs, shared, rw, sg, K, _tokens(rank), bias=bias)
+        if exact:
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        else:
+            np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_plan_orders_rows_by_destination_then_token():
+    rng = np.random.default_rng(3)
+    ids = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, K)).astype(np.float32)
+    dc, st, sm, ts, te = EO.plan(ids, w, E, 4, True)
+    assert dc[:, 0].sum() == len(st) and dc[:, 1].sum() == T * K
+    off = np.concatenate([[0], np.cumsum(dc[:, 0])])
+    for d in range(4):
+        toks = st[off[d]:off[d + 1]]
+        assert np.all(np.diff(toks) > 0)
+        for r, t in zip(range(off[d], off[d + 1]), toks):
+            assert ts[t, d] == r
+            mine = [j for j in range(K) if ids[t, j] % 4 == d]
+            assert sm[r, 2 * K + 1] == len(mine)
+            assert [sm[r, j] for j in mine] == [ids[t, j] // 4 for j in mine]
+    assert np.all((ts >= 0) == (te >= 0))

@@ -216,3 +216,50 @@ def test_decode_layer_matches_bf16_oracle_and_is_row_invariant(layer_world):
     for r in (0, 7, 15):
         y1 = moe_layer_decode(xt[r:r + 1].contiguous(), *args, one, bias=torch.from_numpy(bias).cuda())
         assert torch.equal(y1[0], y[r])
+
+
+# ------------------------------------------------------------------ fused (one cooperative launch) decode layer
+@pytest.mark.parametrize("rows,zipf,round_bf16", [(1, True, False), (2, True, False), (1, False, True), (2, False, False)])
+def test_fused_layer_equals_four_launch_layer(layer_world, rows, zipf, round_bf16):
+    """ssb_moe_decode_fused reproduces router_logits -> router_select_resolve -> moe_decode_layer bit for bit
+    (ids, weights, shared gate, h, o, routed sum and the bf16 output), on three calls in a row."""
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    lay, recs, pool, shared = layer_world
+    rw = bf16_tensor(synth.router_weight(0, 512, lay.hidden, 0))
+    sg = bf16_tensor(synth.shared_gate_weight(0, lay.hidden, 0))
+    bias = torch.from_numpy(synth.zipf_bias(512)).cuda() if zipf else None
+    fb = DecodeLayerBuffers(rows, 10, lay.hidden, lay.inter)
+    sb = DecodeLayerBuffers(rows, 10, lay.hidden, lay.inter)
+    for call in range(3):
+        x = bf16_tensor(synth.activations(200 + call, rows, lay.hidden))
+        args = (x, rw, 0, pool.map, pool.slot_ptr, shared, sg, 10)
+        moe_layer_decode(*args, fb, bias=bias, logits_round_bf16=round_bf16, fused=True)
+        moe_layer_decode(*args, sb, bias=bias, logits_round_bf16=round_bf16, fused=False)
+        torch.cuda.synchronize()
+        assert int(fb.err.item()) == 0 and int(sb.err.item()) == 0
+        for name in ("ids", "w", "sh_gate", "out", "y", "o"):
+            assert torch.equal(getattr(fb, name), getattr(sb, name)), (call, name)
+        n = rows * 11 * lay.inter
+        assert torch.equal(fb.h[:n], sb.h[:n]), call
+
+
+def test_fused_layer_reports_unmapped_choice(layer_world):
+    """A chosen expert missing from the pool sets SSB_ERR_UNMAPPED and contributes zero, as the four-launch path."""
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    lay, recs, pool, shared = layer_world
+    rw = bf16_tensor(synth.router_weight(0, 512, lay.hidden, 0))
+    sg = bf16_tensor(synth.shared_gate_weight(0, lay.hidden, 0))
+    x = bf16_tensor(synth.activations(300, 1, lay.hidden))
+    probe = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
+    moe_layer_decode(x, rw, 0, pool.map, pool.slot_ptr, shared, sg, 10, probe)
+    torch.cuda.synchronize()
+    gone = int(probe.ids[0, 3].item())
+    holes = pool.map.clone()
+    holes[gone] = -1
+    fb = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
+    sb = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
+    moe_layer_decode(x, rw, 0, holes, pool.slot_ptr, shared, sg, 10, fb, fused=True)
+    moe_layer_decode(x, rw, 0, holes, pool.slot_ptr, shared, sg, 10, sb, fused=False)
+    torch.cuda.synchronize()
+    assert int(fb.err.item()) & 2 and int(sb.err.item()) & 2
+    assert torch.equal(fb.out, sb.out) and torch.equal(fb.y, sb.y)
