@@ -149,7 +149,7 @@ def bench_decode(args, world, rank):
     from slotstream_b200 import synth
     from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
     from slotstream_b200.records import BASELINE_LAYOUT as LAY, MAP_LAYERS
-    NL, E, K, b = 48, 512, 10, args.batch
+    NL, E, K, b = args.layers, 512, 10, args.batch
     dev = torch.device("cuda")
     rb = LAY.record_bytes
     seed = 1000 + rank
@@ -254,7 +254,7 @@ def bench_decode(args, world, rank):
         "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"decode_step_48layer_b{b}", "layers": NL, "batch": b, "hidden": LAY.hidden,
+        "config": {"workload": f"decode_step_{NL}layer_b{b}", "layers": NL, "batch": b, "hidden": LAY.hidden,
                    "inter": LAY.inter, "experts": E, "topk": K, "shared_experts": 1, "routing": "zipf_s1.1",
                    "weights": "affine4_gs64 resident in HBM (48x512 records)", "cuda_graph": True,
                    "l2": "flushed before every step (256 MiB write)", "parallelism": f"replicas{world}"},
@@ -471,6 +471,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=32768, help="prefill tokens per GPU")
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
     ap.add_argument("--batch", type=int, default=1, help="decode batch")
+    ap.add_argument("--layers", type=int, default=48, help="decode layers per step (48 = configs[1])")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement at N=1")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -219,13 +219,13 @@ int ssb_combine_rank_order(const float* rows, int64_t tokens, int32_t k, int32_t
 int ssb_combine_layer(const float* rows, int64_t tokens, int32_t k, int32_t hidden, const float* sh, float* out,
                       uint16_t* y, void* stream);
 
-/* Prefill grouped GEMM, gate/up half, on tcgen05 tensor cores (M128 N256 K16 MMAs, fp32 in TMEM):
+/* Prefill grouped GEMM, gate/up half, on tcgen05 tensor cores (M128 N128 K16 MMAs, fp32 in TMEM):
  *   h[row, :] = bf16( silu(x[row_token[row]] G_e^T) * (x[row_token[row]] U_e^T) )
- * for every row of every 128-row block b < num_padded/128 of the moe_align output, e = block_expert[b],
- * record base group_ptr[e]. The dequantised tiles are rounded to bf16 (q*s + b in fp32 first) and
- * accumulated in fp32, the reference's rounding path. x bf16 [tokens, hidden]; h_buf bf16 [rows, inter];
- * padded_len = sorted_rows length (a multiple of 128). hidden % 64 == 0 and (hidden/64) even,
- * inter % 128 == 0.
+ * for every row of every 256-row block b < num_padded/256 of the moe_align output (block_m = 256),
+ * e = block_expert[b], record base group_ptr[e]. The dequantised tiles are rounded to bf16 (q*s + b in fp32
+ * first) and accumulated in fp32, the reference's rounding path. x bf16 [tokens, hidden]; h_buf bf16
+ * [rows, inter]; padded_len = sorted_rows length (a multiple of 256). hidden % 64 == 0 and (hidden/64) even,
+ * inter % 64 == 0.
  * Replaces: launch_gate_up / _gate_up_kernel, slotstream_spark/kernels/fused_moe_affine.py:53-81, 111-118. */
 int ssb_fused_moe_gate_up(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter, const int32_t* row_token,
                           int64_t rows, const int32_t* sorted_rows, const int32_t* block_expert,
@@ -233,7 +233,7 @@ int ssb_fused_moe_gate_up(const uint16_t* x, int64_t tokens, int32_t hidden, int
                           uint16_t* h_buf, int32_t* err, void* stream);
 
 /* Prefill grouped GEMM, down half: out_rows[row, :] = (h[row] D_e^T) * row_weight[row], fp32; rows outside
- * the aligned blocks are left untouched. inter % 64 == 0 and (inter/64) even, hidden % 256 == 0.
+ * the aligned blocks (block_m = 256) are left untouched. inter % 64 == 0 and (inter/64) even, hidden % 128 == 0.
  * Replaces: launch_down / _down_kernel, slotstream_spark/kernels/fused_moe_affine.py:84-108, 121-127. */
 int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter, const float* row_weight,
                        const int32_t* sorted_rows, const int32_t* block_expert, const int32_t* num_padded,
@@ -242,7 +242,7 @@ int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int3
 
 /* Both prefill expert GEMMs of a fused MoE layer (additive), on activation rows permuted into expert order:
  * ssb_permute_rows, then ssb_sorted_gate_up, then ssb_sorted_down below, so the grouped GEMMs read whole
- * 128-row 2-D tiles instead of gathering rows. Local expert `shared_local` (-1: none) is the shared expert --
+ * 256-row 2-D tiles instead of gathering rows (align with block_m = 256). Local expert `shared_local` (-1: none) is the shared expert --
  * its h is bf16(bf16(silu(bf16 g)) * bf16 u) and its down rows bf16(row_weight * bf16(h D^T)), the
  * reference's bf16 rounding between the shared expert's ops (model/moe_sweep.py:37-43) -- so it rides in the
  * same grouped launch as the routed experts with its rows weighted by the sigmoid gate. x holds `tokens` rows
@@ -275,13 +275,13 @@ int ssb_sorted_down(const uint16_t* h_sorted, int64_t rows, int32_t hidden, int3
                     float* out_rows, int32_t* err, void* stream);
 
 /* Dense bf16 GEMM on tcgen05 (router logits of a prefill chunk): out[m, n] = sum_k x[m, k] * w[n, k],
- * fp32 into rows of `ldo` floats (ldo % 4 == 0). k % 64 == 0, n % 256 == 0; row-invariant.
+ * fp32 into rows of `ldo` floats (ldo % 4 == 0). k % 64 == 0, n % 128 == 0; row-invariant.
  * Replaces: the router lin() of model/layers.py:339 inside the prefill GEMM scope (kernels/gemm_affine.py:40-59). */
 int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uint16_t* w, int32_t n, float* out, int64_t ldo,
                    void* stream);
 
 /* Dense prefill GEMM with an affine 4-bit weight on tcgen05: out[m, n] = sum_k x[m, k] * bf16(q*s + b)[n, k],
- * fp32 out. k % 64 == 0, (k/gs) even, n % 256 == 0; row-invariant (fixed k order per output).
+ * fp32 out. k % 64 == 0, (k/gs) even, n % 128 == 0; row-invariant (fixed k order per output).
  * Replaces: gemm(x, AffineWeight), slotstream_spark/kernels/gemm_affine.py:62-98 (kernel :19-37). */
 int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const int32_t* q, const uint16_t* s, const uint16_t* b,
                      int32_t n, int32_t gs, float* out, void* stream);

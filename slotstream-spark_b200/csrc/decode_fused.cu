@@ -18,8 +18,8 @@
 //           shared add and the bf16 output need no further exchange.
 // Every dot product keeps the summation order of the separate kernels (lane-sequential over 16-element units,
 // then a butterfly), so the fused layer reproduces router_logits + router_select + moe_decode_layer bit for
-// bit. Grid barriers spin with a bounded wait on a caller-owned pair of words and give up with
-// SSB_ERR_TIMEOUT; the words must be zero before the first call and again after a timeout.
+// bit. Grid barriers spin with a bounded wait on a caller-owned counter word and give up with
+// SSB_ERR_TIMEOUT; the word must be zero before the first call and again after a timeout.
 #include "registry.h"
 #include "select.cuh"
 #include "tc_common.cuh"
@@ -65,31 +65,28 @@ struct __align__(16) XUnitS {
 };
 
 // All CTAs meet; false when the wait gave up (then SSB_ERR_TIMEOUT is set and the caller must stop).
+// Ticket barrier on one monotonically increasing word: each CTA adds 1 with release semantics and waits
+// (acquire loads) until the word reaches the end of its round, so nothing has to be reset between rounds and
+// the release costs one atomic per CTA. Wrap-around is harmless (signed difference).
 SSB_DEV bool grid_sync(uint32_t* sync, int32_t* err, int* s_ok) {
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
-    volatile uint32_t* gen = sync + 1;
-    const uint32_t g0 = *gen;   // read before arriving: the release below needs every arrival
-    __threadfence();
-    const uint32_t arrived = atomicAdd(sync, 1u);
-    if (arrived == gridDim.x - 1) {
-      atomicExch(sync, 0u);
-      __threadfence();
-      atomicAdd(sync + 1, 1u);
-    } else {
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t polls = 0;
-      while (*gen == g0) {
-        __nanosleep(64);
-        if ((++polls & 63u) == 0 && globaltimer_ns() - t0 > SSB_WAIT_NS) {
-          ok = 0;
-          set_err(err, SSB_ERR_TIMEOUT);
-          break;
-        }
+    uint32_t old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(sync) : "memory");
+    const uint32_t target = old - old % gridDim.x + gridDim.x;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t polls = 0;
+    for (;;) {
+      uint32_t cur;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(sync) : "memory");
+      if ((int32_t)(cur - target) >= 0) break;
+      if ((++polls & 255u) == 0 && globaltimer_ns() - t0 > SSB_WAIT_NS) {
+        ok = 0;
+        set_err(err, SSB_ERR_TIMEOUT);
+        break;
       }
     }
-    __threadfence();
     *s_ok = ok;
   }
   __syncthreads();
@@ -127,8 +124,7 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   __shared__ int32_t s_ids[F_MAXR][F_MAXK];
   __shared__ float s_w[F_MAXR][F_MAXK];
   __shared__ float s_shg[F_MAXR];
-  __shared__ unsigned long long s_cand[F_MAXR][RS_CAND];
-  __shared__ unsigned long long s_top[F_MAXR][16];
+  __shared__ SelectScratch<EPL> s_sel[F_MAXR];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int R = a.R, k = a.k, H = a.H, I = a.I, E = a.E, gs = a.gs;
   const int P = R * k + R;                      // entries: routed (r, j) at r*k + j, shared of token r at R*k + r
@@ -215,7 +211,7 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
     const float* lrow = a.logits + (int64_t)warp * (E + 1);
     unsigned long long mine;
     float my_p, sum;
-    warp_select<EPL>(lrow, E, k, a.bias, a.flags, nullptr, s_cand[warp], s_top[warp], lane, mine, my_p, sum);
+    warp_select<EPL>(lrow, E, k, a.bias, a.flags, nullptr, s_sel[warp], lane, mine, my_p, sum);
     if (lane < k) {
       s_ids[warp][lane] = (int)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull));
       s_w[warp][lane] = my_p / sum;
@@ -335,61 +331,69 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   }
   __syncthreads();
   const int ng4 = I / gs;
-  constexpr int CH = F_MAXK + 1;   // a token's entries: its routed choices in rank order, then its shared entry
-  constexpr int CH4 = (CH + 3) / 4 * 4;
   for (int m = c0 + warp; m < c1; m += FW) {
     for (int r = 0; r < R; ++r) {
-      const int nexp = k + 1;
-      float d[CH4];
+      const int nexp = k + 1;   // the token's routed entries in rank order, then its shared entry
+      float acc = 0.f, shv = 0.f;
+      // chunks of four entries: their words in flight together, one batched reduction; a rolled loop keeps the
+      // code this once-per-launch phase fetches short
+#pragma unroll 1
+      for (int c = 0; c < nexp; c += 4) {
+        const uint8_t* eb[4];
+        uint2 wv[4][NUI];
+        float sc[4][NUI], bi[4][NUI];
 #pragma unroll
-      for (int j = 0; j < CH4; ++j) d[j] = 0.f;
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = c + jj;
+          const int p = j < k ? r * k + j : R * k + r;
+          eb[jj] = j < nexp ? entry_base(p) : nullptr;
 #pragma unroll
-      for (int i = 0; i < NUI; ++i) {
-        const int u = lane + 32 * i;
-        const int g = (u * 16) / gs;
-        uint2 wv[CH];
-        float sc[CH], bi[CH];
-#pragma unroll
-        for (int j = 0; j < CH; ++j) {   // every entry's words in flight before the first dot product
-          wv[j] = make_uint2(0u, 0u);
-          sc[j] = bi[j] = 0.f;
-          if (j < nexp) {
-            const int p = j < k ? r * k + j : R * k + r;
-            const uint8_t* base = entry_base(p);
-            if (base) {
-              wv[j] = __ldcg(reinterpret_cast<const uint2*>(base + a.o.dw + (int64_t)m * I / 2) + u);
-              sc[j] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(base + a.o.dsc) + (int64_t)m * ng4 + g));
-              bi[j] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(base + a.o.db) + (int64_t)m * ng4 + g));
+          for (int i = 0; i < NUI; ++i) {
+            const int u = lane + 32 * i;
+            const int g = (u * 16) / gs;
+            wv[jj][i] = make_uint2(0u, 0u);
+            sc[jj][i] = bi[jj][i] = 0.f;
+            if (eb[jj] && u < nui) {
+              wv[jj][i] = __ldcg(reinterpret_cast<const uint2*>(eb[jj] + a.o.dw + (int64_t)m * I / 2) + u);
+              sc[jj][i] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(eb[jj] + a.o.dsc) + (int64_t)m * ng4 + g));
+              bi[jj][i] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(eb[jj] + a.o.db) + (int64_t)m * ng4 + g));
             }
           }
         }
+        float d[4];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          if (j < nexp) {
-            const int p = j < k ? r * k + j : R * k + r;
-            XUnit xu;
-            xunit_load(xu, hx[(size_t)p * nui + u]);
-            d[j] = unit_dot(wv[j], sc[j], bi[j], xu, d[j]);
+        for (int jj = 0; jj < 4; ++jj) {
+          d[jj] = 0.f;
+          const int j = c + jj;
+          const int p = j < k ? r * k + j : R * k + r;
+#pragma unroll
+          for (int i = 0; i < NUI; ++i) {
+            const int u = lane + 32 * i;
+            if (eb[jj] && u < nui) {
+              XUnit xu;
+              xunit_load(xu, hx[(size_t)p * nui + u]);
+              d[jj] = unit_dot(wv[jj][i], sc[jj][i], bi[jj][i], xu, d[jj]);
+            }
+          }
+        }
+        warp_sum4f(d[0], d[1], d[2], d[3]);
+        if (lane == 0) {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int j = c + jj;
+            if (j >= nexp) break;
+            const bool ok = eb[jj] != nullptr;
+            if (j >= k) {
+              shv = round_bf16((ok ? s_shg[r] : 0.f) * round_bf16(d[jj]));   // bf16(sigmoid gate * bf16(h D^T))
+            } else {
+              const float o = d[jj] * (ok ? s_w[r][j] : 0.f);   // acc * w, kernels/moe_gemv_affine.py:96-97
+              acc = (j == 0) ? o : acc + o;                      // rank order, kernels/moe_gemv_affine.py:108-109
+              if (a.o_buf) a.o_buf[((int64_t)r * k + j) * H + m] = o;
+            }
           }
         }
       }
-#pragma unroll
-      for (int j = 0; j < CH4; j += 4) warp_sum4f(d[j], d[j + 1], d[j + 2], d[j + 3]);
       if (lane == 0) {
-        float acc = 0.f, shv = 0.f;
-#pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          if (j >= nexp) break;
-          const int p = j < k ? r * k + j : R * k + r;
-          const bool ok = entry_base(p) != nullptr;
-          if (j >= k) {
-            shv = round_bf16((ok ? s_shg[r] : 0.f) * round_bf16(d[j]));   // bf16(sigmoid gate * bf16(h D^T))
-          } else {
-            const float o = d[j] * (ok ? s_w[r][j] : 0.f);   // acc * w, kernels/moe_gemv_affine.py:96-97
-            acc = (j == 0) ? o : acc + o;                      // rank order, kernels/moe_gemv_affine.py:108-109
-            if (a.o_buf) a.o_buf[((int64_t)r * k + j) * H + m] = o;
-          }
-        }
         a.out[(int64_t)r * H + m] = acc;
         a.y[(int64_t)r * H + m] = f32_to_bf16(round_bf16(acc) + shv);   // routed.to(bf16) + sh
       }
@@ -446,15 +450,33 @@ extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t top
   }
   if (!kern) return SSB_EUNSUPPORTED;
   const size_t smem = fused_smem(hidden, inter);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // per (device, kernel, smem) setup once: attribute, occupancy check, SM count (host calls that would
+  // otherwise sit between every launch)
+  struct Prepared {
+    int dev;
+    void* kern;
+    size_t smem;
+    int sms;
+  };
+  static thread_local Prepared prep[16];
+  static thread_local int n_prep = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
-  ssb_note_smem("moe_decode_fused", (void (*)(FusedArgs))kern, smem);
-  int dev = 0, sms = 0, per_sm = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FT, smem);
-  if (e != cudaSuccess) return (int)e;
-  if (per_sm < 1 || sms < 1) return SSB_EUNSUPPORTED;
+  int sms = 0;
+  for (int i = 0; i < n_prep; ++i)
+    if (prep[i].dev == dev && prep[i].kern == kern && prep[i].smem == smem) sms = prep[i].sms;
+  if (!sms) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    ssb_note_smem("moe_decode_fused", (void (*)(FusedArgs))kern, smem);
+    int per_sm = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FT, smem);
+    if (e != cudaSuccess) return (int)e;
+    if (per_sm < 1 || sms < 1) return SSB_EUNSUPPORTED;
+    if (n_prep < 16) prep[n_prep++] = Prepared{dev, kern, smem, sms};
+  }
   FusedArgs a{};
   a.x = x;
   a.R = (int)rows;

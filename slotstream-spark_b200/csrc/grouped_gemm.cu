@@ -1,20 +1,24 @@
 // Grouped affine-4-bit GEMM on the 5th-generation tensor cores (tcgen05 + TMEM) for the prefill MoE
 // (slotstream_spark/kernels/fused_moe_affine.py:53-127) and the dense prefill GEMMs (kernels/gemm_affine.py).
 //
-// Tiles are 128 rows (one expert's rows, from moe_align) x 256 B-rows:
-//  * gate_up: the 256 B-rows are 128 gate rows + 128 up rows of the same inter columns, so one M128xN256
-//    accumulator holds both and the epilogue forms h = silu(g) * u -> bf16 (kernels/fused_moe_affine.py:76-81);
-//  * down / plain: 256 output columns; the epilogue scales by the row's routing weight (fp32 out,
+// Tiles are 256 rows (two 128-row halves of one expert's rows; moe_align pads each expert to 256) x 128 B-rows.
+// Every k-block's dequantised B tile feeds two M128xN128 MMAs, one per half, so the weight producers -- the
+// bottleneck of a fused-dequant GEMM -- do half the work per FLOP of a 128-row tile:
+//  * gate_up: the 128 B-rows are 64 gate rows + 64 up rows of the same inter columns, so each accumulator
+//    holds both and the epilogue forms h = silu(g) * u -> bf16 (kernels/fused_moe_affine.py:76-81);
+//  * down / plain: 128 output columns; the epilogue scales by the row's routing weight (fp32 out,
 //    kernels/fused_moe_affine.py:103-108) or stores plain fp32 (kernels/gemm_affine.py:19-37).
 // The kernel is persistent: one CTA per SM walks tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (m-block
-// major, so concurrent CTAs share activation rows and expert weights in L2). TMEM holds two accumulators, so
-// the epilogue of tile i overlaps the MMAs of tile i+1, and the operand pipelines run across tile borders.
+// major, so concurrent CTAs share activation rows and expert weights in L2). TMEM holds two accumulator pairs,
+// so the epilogue of tile i overlaps the MMAs of tile i+1, and the operand pipelines run across tile borders.
 // Warp roles (16 warps):
-//  * warp 0      gathers the tile's activation rows with TMA: lane l issues one tile::gather4 of rows
-//                4l..4l+3 per k-block into the 128B-swizzled K-major tile (the tensor map applies the swizzle);
-//  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma (M128 N256 K16, four per 64-wide k-block);
+//  * warp 0      loads the tile's activation rows with TMA: one 2-D box of 256 rows when the rows are
+//                contiguous (permuted into expert order beforehand), else lane l gathers rows 4l..4l+3 and
+//                128+4l.. with two tile::gather4 copies; the tensor map applies the 128-byte swizzle;
+//  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma (M128 N128 K16, eight per 64-wide k-block);
 //  * warps 4..7  epilogue: TMEM -> registers -> global, one accumulator row per thread;
-//  * warps 8..15 weight producers: stage their B-row's packed nibbles and bf16 scale/bias with cp.async,
+//  * warps 8..15 weight producers, two threads per B-row (one half of the k-block each): stage the packed
+//                nibbles and the bf16 scale/bias with cp.async,
 //                dequantise q*s + b -> bf16 (the reference kernel's _wtile, kernels/fused_moe_affine.py:38-50,
 //                whose q * sc + bi compiles to a fused multiply-add) into the swizzled B tile; or, for bf16
 //                weights, cp.async the row straight into the tile.
@@ -26,17 +30,18 @@
 
 namespace {
 
-constexpr int BM = 128, BK = 64, BN = 256;
-constexpr int STAGES = 3;        // A/B operand stages
+constexpr int BM = 128, MT = 2, TM = BM * MT, BK = 64, BN = 128;
+constexpr int STAGES = 4;        // A/B operand stages
 constexpr int PD = 3;            // weight staging depth of each producer thread
 constexpr int THREADS = 512;
 constexpr int A_WARP = 0, MMA_WARP = 1, EPI_WARP0 = 4, PROD_WARP0 = 8, N_PROD = 256;
-constexpr uint32_t A_STAGE = BM * 128;           // 16 KB
-constexpr uint32_t B_STAGE = BN * 128;           // 32 KB
-constexpr uint32_t W_STG = N_PROD * 32;          // packed nibbles of one k-block, 32 B per B-row
-constexpr uint32_t SB_STG = N_PROD * 4;          // 4-byte words holding the scale (or bias) of the k-block
-constexpr uint32_t STG = W_STG + 2 * SB_STG;
-constexpr uint32_t TMEM_COLS = 512;              // two M128 x N256 fp32 accumulators
+constexpr uint32_t A_STAGE = TM * 128;           // 32 KB: two 128-row halves
+constexpr uint32_t A_HALF = BM * 128;
+constexpr uint32_t B_STAGE = BN * 128;           // 16 KB
+constexpr uint32_t W_STG = N_PROD * 16;          // packed nibbles of one k-block, 16 B per producer thread
+constexpr uint32_t SB_STG = N_PROD * 8;          // per producer thread: the words holding its scale and bias
+constexpr uint32_t STG = W_STG + SB_STG;
+constexpr uint32_t TMEM_COLS = 512;              // 2 buffers x 2 halves of M128 x N128 fp32 accumulators
 
 enum { EPI_SWIGLU = 0, EPI_SCALE = 1, EPI_PLAIN = 2 };
 
@@ -44,7 +49,7 @@ struct GemmArgs {
   const uint16_t* a;          // bf16 activation rows, `lda` elements apart (read through the A tensor map)
   int64_t lda;
   int64_t a_rows;             // rows of the activation matrix (extent of the tensor map)
-  int a_box_rows;             // rows per A copy: 1 (tile::gather4 of four rows) or BM (one 2-D box, identity rows)
+  int a_box_rows;             // rows per A copy: 1 (tile::gather4 of four rows) or TM (one 2-D box, identity rows)
   int out_sorted;             // SwiGLU epilogue: h row at the sorted position m instead of at row sorted_rows[m]
   const int32_t* row_token;   // nullable: the A row of row r is r
   const int32_t* sorted_rows; // nullable: identity (rows m < R)
@@ -143,14 +148,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
   pdl_wait();
   pdl_trigger();
   const int NB = a.n_nblocks;
-  const int64_t n_mb = a.num_padded ? (int64_t)__ldcg(a.num_padded) / BM : a.n_mblocks;
+  const int64_t n_mb = a.num_padded ? (int64_t)__ldcg(a.num_padded) / TM : a.n_mblocks;
   const int64_t n_tiles = n_mb * NB;
   if ((int64_t)blockIdx.x >= n_tiles) return;
   const int my_tiles = (int)((n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x);
   const int KB = a.K / BK;
   const int64_t steps = (int64_t)my_tiles * KB;
   auto tile_of = [&](int i) -> int64_t { return (int64_t)blockIdx.x + (int64_t)i * gridDim.x; };
-  // local expert and weight base of m-block mb (nullptr: unusable, its B tile is zero)
+  // local expert and weight base of 256-row block mb (nullptr: unusable, its B tile is zero)
   auto expert_of = [&](int64_t mb) -> int { return a.block_expert ? __ldcg(a.block_expert + mb) : 0; };
   auto base_of = [&](int e) -> const uint8_t* {
     if (e < 0 || e >= a.n_groups) return nullptr;
@@ -178,29 +183,29 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
   const uint32_t tmem = *S.tmem;
 
   if (warp == A_WARP) {
-    // ---------------- activation gather: 32 tile::gather4 copies (16 KB) per k-block, one per lane
-    // Tile rows 4*lane .. 4*lane+3 come from sorted_rows, then row_token; the next tile's lookups are started
-    // during the current tile (sorted_rows at its first k-block, row_token at its second) so that the two
-    // dependent loads do not stall the copies at tile borders. Padding rows read activation row 0.
-    int32_t rc[4], nrc[4], nsr[4];
+    // ---------------- activation rows: one 2-D box (identity rows) or 64 tile::gather4 copies per k-block
+    // Gathered rows: tile rows 4*lane .. +3 and 128 + 4*lane .. +3 come from sorted_rows, then row_token; the
+    // next tile's lookups start during the current tile (sorted_rows at its first k-block, row_token at its
+    // second) so the two dependent loads do not stall the copies at tile borders. Padding rows read row 0.
+    int32_t rc[8], nrc[8], nsr[8];
     auto load_rows = [&](int i) {
       const int64_t mb = tile_of(i) / NB;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int64_t m = mb * BM + 4 * lane + q;
+      for (int q = 0; q < 8; ++q) {
+        const int64_t m = mb * TM + (q >> 2) * BM + 4 * lane + (q & 3);
         nsr[q] = a.sorted_rows ? __ldcg(a.sorted_rows + m) : (int32_t)m;
       }
     };
     auto to_coords = [&]() {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 8; ++q) {
         const bool ok = nsr[q] >= 0 && nsr[q] < a.R;
         nrc[q] = ok ? (a.row_token ? __ldcg(a.row_token + nsr[q]) : nsr[q]) : 0;
       }
     };
     int64_t issued = 0;
     if (lane == 0) prefetch_tensormap(&tm_a);
-    const bool gather = a.a_box_rows != BM;
+    const bool gather = a.a_box_rows != TM;
     if (gather) {
       load_rows(0);
       to_coords();
@@ -211,7 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       if (!gather) {
       } else if (kb == 0) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) rc[q] = nrc[q];
+        for (int q = 0; q < 8; ++q) rc[q] = nrc[q];
         if (i + 1 < my_tiles) {
           load_rows(i + 1);
           if (KB == 1) to_coords();
@@ -229,11 +234,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       }
       if (lane == 0) mbar_expect_tx(&S.full_a[s], A_STAGE);
       __syncwarp();
-      if (a.a_box_rows == BM) {   // rows m-block*128 .. +127 of the activation matrix in one copy
+      if (!gather) {   // rows tile*256 .. +255 of the activation matrix in one copy
         if (lane == 0)
-          tma_load_2d(smem_u32(S.a + s * A_STAGE), &tm_a, kb * BK, (int32_t)((tile_of(i) / NB) * BM), &S.full_a[s]);
+          tma_load_2d(smem_u32(S.a + s * A_STAGE), &tm_a, kb * BK, (int32_t)((tile_of(i) / NB) * TM), &S.full_a[s]);
       } else {
         tma_gather4(smem_u32(S.a + s * A_STAGE + lane * 512), &tm_a, kb * BK, rc[0], rc[1], rc[2], rc[3],
+                    &S.full_a[s]);
+        tma_gather4(smem_u32(S.a + s * A_STAGE + A_HALF + lane * 512), &tm_a, kb * BK, rc[4], rc[5], rc[6], rc[7],
                     &S.full_a[s]);
       }
       ++issued;
@@ -255,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)acc * BN;
+        const uint32_t d0 = tmem + (uint32_t)(acc * MT) * BN;   // accumulators of the two halves: d0, d0 + BN
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++j) {
           const int s = (int)(j % STAGES);
@@ -265,11 +272,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
             break;
           }
           tc_fence_after();
-          const uint64_t da = umma_desc_sw128(smem_u32(S.a + s * A_STAGE));
           const uint64_t db = umma_desc_sw128(smem_u32(S.b + s * B_STAGE));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_bf16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+          for (int h = 0; h < MT; ++h) {
+            const uint64_t da = umma_desc_sw128(smem_u32(S.a + s * A_STAGE + h * A_HALF));
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_bf16(d0 + h * BN, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+          }
           umma_commit(&S.empty[s]);
         }
         umma_commit(&S.tmem_full[acc]);
@@ -281,85 +291,100 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
     }
     __syncwarp();
   } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
-    // ---------------- epilogue: one accumulator row per thread
+    // ---------------- epilogue: one accumulator row per thread, both halves of the tile
     const int q = warp & 3;
     for (int i = 0; i < my_tiles; ++i) {
       const int acc = i & 1;
       const int64_t t = tile_of(i), mb = t / NB;
       const int nb = (int)(t % NB);
-      const int64_t m = mb * BM + 32 * q + lane;
-      const int64_t row = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
-      const bool valid = row >= 0 && row < a.R;
       const bool shared_e = a.shared_local >= 0 && expert_of(mb) == a.shared_local;
-      const float wt = (EPI == EPI_SCALE && valid) ? __ldcg(a.row_weight + row) : 1.f;
+      int64_t rows[MT];
+      float wts[MT];
+#pragma unroll
+      for (int h = 0; h < MT; ++h) {
+        const int64_t m = mb * TM + h * BM + 32 * q + lane;
+        rows[h] = a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m) : m;
+        const bool valid = rows[h] >= 0 && rows[h] < a.R;
+        wts[h] = (EPI == EPI_SCALE && valid) ? __ldcg(a.row_weight + rows[h]) : 1.f;
+      }
       const bool ok = mbar_wait_ns(&S.tmem_full[acc], (i >> 1) & 1, SSB_WAIT_NS);
       tc_fence_after();
       if (!ok) {
         s_fail = 1;
         break;
       }
-      const uint32_t taddr = tmem + (uint32_t)acc * BN + ((uint32_t)(32 * q) << 16);
-      if (EPI == EPI_SWIGLU) {
-        uint16_t* out = (uint16_t*)a.out;
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          const int col = 32 * cc;
-          float g[32], u[32];
-          tmem_ld32(taddr + col, g);
-          tmem_ld32(taddr + BN / 2 + col, u);
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(out + (a.out_sorted ? m : row) * a.ldo + (int64_t)nb * (BN / 2) + col);
+      for (int h = 0; h < MT; ++h) {
+        const int64_t m = mb * TM + h * BM + 32 * q + lane;
+        const int64_t row = rows[h];
+        const bool valid = row >= 0 && row < a.R;
+        const float wt = wts[h];
+        const uint32_t taddr = tmem + (uint32_t)(acc * MT + h) * BN + ((uint32_t)(32 * q) << 16);
+        if (EPI == EPI_SWIGLU) {
+          uint16_t* out = (uint16_t*)a.out;
+#pragma unroll 1
+          for (int cc = 0; cc < BN / 64; ++cc) {
+            const int col = 32 * cc;
+            float g[32], u[32];
+            tmem_ld32(taddr + col, g);
+            tmem_ld32(taddr + BN / 2 + col, u);
+            if (valid) {
+              uint4* dst =
+                  reinterpret_cast<uint4*>(out + (a.out_sorted ? m : row) * a.ldo + (int64_t)nb * (BN / 2) + col);
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              float h[8];
+              for (int jj = 0; jj < 4; ++jj) {
+                float hv[8];
 #pragma unroll
-              for (int tt = 0; tt < 8; ++tt) {
-                const float gg = g[8 * jj + tt], uu = u[8 * jj + tt];
-                if (shared_e) {   // shared expert: bf16(silu(bf16 g)) * bf16 u (model/moe_sweep.py:37-43)
-                  const float gb = round_bf16(gg);
-                  h[tt] = round_bf16(gb / (1.f + expf(-gb))) * round_bf16(uu);
-                } else {
-                  h[tt] = silu_fast(gg) * uu;   // accg / (1 + exp(-accg)) * accu, kernels/fused_moe_affine.py:80
+                for (int tt = 0; tt < 8; ++tt) {
+                  const float gg = g[8 * jj + tt], uu = u[8 * jj + tt];
+                  if (shared_e) {   // shared expert: bf16(silu(bf16 g)) * bf16 u (model/moe_sweep.py:37-43)
+                    const float gb = round_bf16(gg);
+                    hv[tt] = round_bf16(gb / (1.f + expf(-gb))) * round_bf16(uu);
+                  } else {
+                    hv[tt] = silu_fast(gg) * uu;   // accg / (1 + exp(-accg)) * accu, kernels/fused_moe_affine.py:80
+                  }
                 }
+                dst[jj] = make_uint4(cvt_bf16x2(hv[0], hv[1]), cvt_bf16x2(hv[2], hv[3]), cvt_bf16x2(hv[4], hv[5]),
+                                     cvt_bf16x2(hv[6], hv[7]));
               }
-              dst[jj] = make_uint4(cvt_bf16x2(h[0], h[1]), cvt_bf16x2(h[2], h[3]), cvt_bf16x2(h[4], h[5]),
-                                   cvt_bf16x2(h[6], h[7]));
             }
           }
-        }
-      } else {
-        float* out = (float*)a.out;
+        } else {
+          float* out = (float*)a.out;
 #pragma unroll 1
-        for (int cc = 0; cc < BN / 32; ++cc) {
-          const int col = 32 * cc;
-          float v[32];
-          tmem_ld32(taddr + col, v);
-          if (valid) {
-            float4* dst = reinterpret_cast<float4*>(out + row * a.ldo + (int64_t)nb * BN + col);
+          for (int cc = 0; cc < BN / 32; ++cc) {
+            const int col = 32 * cc;
+            float v[32];
+            tmem_ld32(taddr + col, v);
+            if (valid) {
+              float4* dst = reinterpret_cast<float4*>(out + row * a.ldo + (int64_t)nb * BN + col);
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-              float4 o;
-              if (EPI == EPI_SCALE && shared_e) {   // bf16(sigmoid gate * bf16(h D^T))
-                o = make_float4(round_bf16(wt * round_bf16(v[4 * jj])), round_bf16(wt * round_bf16(v[4 * jj + 1])),
-                                round_bf16(wt * round_bf16(v[4 * jj + 2])), round_bf16(wt * round_bf16(v[4 * jj + 3])));
-              } else if (EPI == EPI_SCALE) {
-                o = make_float4(v[4 * jj] * wt, v[4 * jj + 1] * wt, v[4 * jj + 2] * wt, v[4 * jj + 3] * wt);
-              } else {
-                o = make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+              for (int jj = 0; jj < 8; ++jj) {
+                float4 o;
+                if (EPI == EPI_SCALE && shared_e) {   // bf16(sigmoid gate * bf16(h D^T))
+                  o = make_float4(round_bf16(wt * round_bf16(v[4 * jj])), round_bf16(wt * round_bf16(v[4 * jj + 1])),
+                                  round_bf16(wt * round_bf16(v[4 * jj + 2])),
+                                  round_bf16(wt * round_bf16(v[4 * jj + 3])));
+                } else if (EPI == EPI_SCALE) {
+                  o = make_float4(v[4 * jj] * wt, v[4 * jj + 1] * wt, v[4 * jj + 2] * wt, v[4 * jj + 3] * wt);
+                } else {
+                  o = make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+                }
+                dst[jj] = o;
               }
-              dst[jj] = o;
             }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.tmem_empty[acc]);   // the accumulator may be overwritten now
+      if (lane == 0) mbar_arrive(&S.tmem_empty[acc]);   // the accumulator pair may be overwritten now
     }
   } else if (warp >= PROD_WARP0) {
-    // ---------------- weight producers: one B-row per thread
+    // ---------------- weight producers: B-row br = p / 2, half hf = p % 2 (elements 32hf .. 32hf+31 of the k-block)
     const int p = tid - PROD_WARP0 * 32;
-    const int piece = (EPI == EPI_SWIGLU) ? (p >> 7) : 0;
+    const int br = p >> 1, hf = p & 1;
+    const int piece = (EPI == EPI_SWIGLU) ? (br >> 6) : 0;
     const int ng = a.K / a.gs;
     // weight base and B-row of this thread for the tile of step j, resolved once per tile (two dependent
     // L2 loads: block_expert, then the group's base); base nullptr: zero row
@@ -373,7 +398,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
         const int64_t mb = t / NB;
         const int nb = (int)(t % NB);
         t_base = base_of(expert_of(mb));
-        t_nrow = (EPI == EPI_SWIGLU) ? (int64_t)nb * (BN / 2) + (p & 127) : (int64_t)nb * BN + p;
+        t_nrow = (EPI == EPI_SWIGLU) ? (int64_t)nb * (BN / 2) + (br & (BN / 2 - 1)) : (int64_t)nb * BN + br;
       }
     };
     if (a.dense_b) {
@@ -395,7 +420,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
             const uint16_t* drow =
                 t_base ? (const uint16_t*)t_base + t_nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) cp_async16(bt + swz128(p, c), drow + c * 8, t_base ? 16u : 0u);
+            for (int c = 4 * hf; c < 4 * hf + 4; ++c) cp_async16(bt + swz128(br, c), drow + c * 8, t_base ? 16u : 0u);
           }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
@@ -416,18 +441,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
         const uint32_t bit = 1u << (j % PD);
         valid = t_base ? (valid | bit) : (valid & ~bit);
         if (!t_base) return;
-        const uint8_t* wr = t_base + a.off_w[piece] + t_nrow * (a.K / 2) + kb * 32;
-        const uint16_t* sr = (const uint16_t*)(t_base + a.off_s[piece]) + t_nrow * ng;
-        const uint16_t* br = (const uint16_t*)(t_base + a.off_b[piece]) + t_nrow * ng;
-        const uint32_t dw = smem_u32(st + p * 32);
-        cp_async16(dw, wr, 16);
-        cp_async16(dw + 16, wr + 16, 16);
-        // the 4-byte-aligned word that holds the k-block's scale (bias): group kb (gs 64) or 2kb, 2kb+1 (gs 32)
+        // this thread's 16 bytes of codes (consecutive threads, consecutive 16-byte slots: no bank conflicts)
+        cp_async16(smem_u32(st + p * 16), t_base + a.off_w[piece] + t_nrow * (a.K / 2) + kb * 32 + hf * 16, 16);
+        // the 4-byte-aligned words that hold the k-block's scale and bias: group kb (gs 64) or groups 2kb, 2kb+1
+        // (gs 32); both threads of a B-row fetch them, so each waits on its own copies only
         const int g0 = a.gs == 64 ? kb : 2 * kb;
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + p * 4)),
+        const uint16_t* sr = (const uint16_t*)(t_base + a.off_s[piece]) + t_nrow * ng;
+        const uint16_t* bsrc = (const uint16_t*)(t_base + a.off_b[piece]) + t_nrow * ng;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + p * 8)),
                      "l"(sr + (g0 & ~1)) : "memory");
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + SB_STG + p * 4)),
-                     "l"(br + (g0 & ~1)) : "memory");
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + p * 8 + 4)),
+                     "l"(bsrc + (g0 & ~1)) : "memory");
       };
       for (int64_t j = 0; j < PD - 1 && j < steps; ++j) {
         issue(j);
@@ -439,29 +463,22 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
         asm volatile("cp.async.wait_group %0;" ::"n"(PD - 1) : "memory");
         const int kb = (int)(j % KB);
         const uint8_t* st = S.stg + (j % PD) * STG;
-        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
-        float s0 = 0.f, b0 = 0.f, s1 = 0.f, b1 = 0.f;
+        uint4 w = make_uint4(0, 0, 0, 0);
+        float sv = 0.f, bv = 0.f;
         if ((valid >> (j % PD)) & 1u) {
-          w0 = *reinterpret_cast<const uint4*>(st + p * 32);
-          w1 = *reinterpret_cast<const uint4*>(st + p * 32 + 16);
-          const uint32_t sw = *reinterpret_cast<const uint32_t*>(st + W_STG + p * 4);
-          const uint32_t bw = *reinterpret_cast<const uint32_t*>(st + W_STG + SB_STG + p * 4);
-          if (a.gs == 64) {
-            s0 = s1 = (kb & 1) ? bf16_hi(sw) : bf16_lo(sw);
-            b0 = b1 = (kb & 1) ? bf16_hi(bw) : bf16_lo(bw);
-          } else {
-            s0 = bf16_lo(sw);
-            s1 = bf16_hi(sw);
-            b0 = bf16_lo(bw);
-            b1 = bf16_hi(bw);
-          }
+          w = *reinterpret_cast<const uint4*>(st + p * 16);
+          const uint2 sbw = *reinterpret_cast<const uint2*>(st + W_STG + p * 8);
+          const uint32_t sw = sbw.x, bw = sbw.y;
+          // gs 64: the k-block's group kb sits in half (kb & 1) of the word; gs 32: half hf covers group 2kb + hf
+          const bool hi = a.gs == 64 ? (kb & 1) : hf;
+          sv = hi ? bf16_hi(sw) : bf16_lo(sw);
+          bv = hi ? bf16_hi(bw) : bf16_lo(bw);
         } else if (p == 0) {
           set_err(a.err, SSB_ERR_MISALIGNED);
         }
-        float2 sc0[4], sc1[4];
-        scales2(s0, sc0);
-        scales2(s1, sc1);
-        const float2 bb0 = make_float2(b0, b0), bb1 = make_float2(b1, b1);
+        float2 sc[4];
+        scales2(sv, sc);
+        const float2 bb = make_float2(bv, bv);
         const int s = (int)(j % STAGES);
         const uint32_t ph = (uint32_t)((j / STAGES) & 1);
         if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
@@ -469,10 +486,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
           break;
         }
         uint8_t* bt = S.b + s * B_STAGE;
-        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int c = 0; c < 8; ++c)   // 16-byte chunk c = elements 8c..8c+7 = word c
-          *reinterpret_cast<uint4*>(bt + swz128(p, c)) = dequant8(ws[c], c < 4 ? sc0 : sc1, c < 4 ? bb0 : bb1);
+        for (int c = 0; c < 4; ++c)   // 16-byte chunk 4hf + c = elements 8(4hf + c) .. +7 = word c of this half
+          *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8(ws[c], sc, bb);
         fence_proxy_async_smem();
         mbar_arrive(&S.full_b[s]);
       }
@@ -543,7 +560,7 @@ EncodeTiledFn encode_tiled_fn() {
 // 2-D tensor map over the activation rows: K elements x a_rows rows, box 64 x 1, 128-byte swizzle.
 int encode_a_map(CUtensorMap* map, const GemmArgs& a) {
   if (((uintptr_t)a.a & 15) || (a.lda * 2) % 16 || a.a_rows < 1 || a.a_rows > 0x7fffffffLL) return SSB_EINVAL;
-  if (a.a_box_rows != 1 && a.a_box_rows != BM) return SSB_EINVAL;
+  if (a.a_box_rows != 1 && a.a_box_rows != TM) return SSB_EINVAL;
   EncodeTiledFn encode = encode_tiled_fn();
   if (!encode) return SSB_ENODEVICE;
   cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.a_rows};
@@ -604,12 +621,12 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
   if (hidden % BK || hidden <= 0 || inter % (BN / 2) || inter <= 0 || (hidden / 64) % 2) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
   SSB_CHECK_ARG(x && row_token && sorted_rows && block_expert && num_padded && group_ptr && h_buf);
-  SSB_CHECK_ARG(padded_len % BM == 0);
+  SSB_CHECK_ARG(padded_len % TM == 0);
   GemmArgs g{};
   g.a = x;
   g.lda = hidden;
   g.a_rows = sorted ? padded_len : tokens;   // sorted: x is the permuted [padded_len, hidden] matrix
-  g.a_box_rows = sorted ? BM : 1;
+  g.a_box_rows = sorted ? TM : 1;
   g.out_sorted = sorted;
   g.row_token = row_token;
   g.sorted_rows = sorted_rows;
@@ -625,7 +642,7 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
   g.out = h_buf;
   g.ldo = inter;
   g.err = err;
-  return launch(EPI_SWIGLU, g, padded_len / BM, inter / (BN / 2), (cudaStream_t)stream);
+  return launch(EPI_SWIGLU, g, padded_len / TM, inter / (BN / 2), (cudaStream_t)stream);
 }
 
 int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter, const float* row_weight,
@@ -636,12 +653,12 @@ int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter
   if (inter % BK || inter <= 0 || hidden % BN || hidden <= 0 || (inter / 64) % 2) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
   SSB_CHECK_ARG(h_buf && row_weight && sorted_rows && block_expert && num_padded && group_ptr && out_rows);
-  SSB_CHECK_ARG(padded_len % BM == 0);
+  SSB_CHECK_ARG(padded_len % TM == 0);
   GemmArgs g{};
   g.a = h_buf;
   g.lda = inter;
   g.a_rows = sorted ? padded_len : rows;     // sorted: h rows at their sorted positions
-  g.a_box_rows = sorted ? BM : 1;
+  g.a_box_rows = sorted ? TM : 1;
   g.sorted_rows = sorted_rows;
   g.block_expert = block_expert;
   g.num_padded = num_padded;
@@ -656,7 +673,7 @@ int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter
   g.out = out_rows;
   g.ldo = hidden;
   g.err = err;
-  return launch(EPI_SCALE, g, padded_len / BM, hidden / BN, (cudaStream_t)stream);
+  return launch(EPI_SCALE, g, padded_len / TM, hidden / BN, (cudaStream_t)stream);
 }
 
 }  // namespace
@@ -745,7 +762,7 @@ extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const i
   g.a = x;
   g.lda = k;
   g.a_rows = m;
-  g.a_box_rows = BM;   // identity rows: one 2-D box per k-block (the tail past m reads zeros)
+  g.a_box_rows = TM;   // identity rows: one 2-D box per k-block (the tail past m reads zeros)
   g.R = m;
   g.base0 = (const uint8_t*)q;
   g.n_groups = 1;
@@ -758,7 +775,7 @@ extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const i
   g.off_s[0] = g.off_s[1] = (int64_t)((const uint8_t*)s - (const uint8_t*)q);
   g.off_b[0] = g.off_b[1] = (int64_t)((const uint8_t*)b - (const uint8_t*)q);
   g.err = nullptr;
-  return launch(EPI_PLAIN, g, (m + BM - 1) / BM, n / BN, (cudaStream_t)stream);
+  return launch(EPI_PLAIN, g, (m + TM - 1) / TM, n / BN, (cudaStream_t)stream);
 }
 
 extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uint16_t* w, int32_t n, float* out,
@@ -771,7 +788,7 @@ extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uin
   g.a = x;
   g.lda = k;
   g.a_rows = m;
-  g.a_box_rows = BM;   // identity rows: one 2-D box per k-block (the tail past m reads zeros)
+  g.a_box_rows = TM;   // identity rows: one 2-D box per k-block (the tail past m reads zeros)
   g.R = m;
   g.base0 = (const uint8_t*)w;
   g.n_groups = 1;
@@ -783,5 +800,5 @@ extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uin
   g.out = out;
   g.ldo = ldo;
   g.err = nullptr;
-  return launch(EPI_PLAIN, g, (m + BM - 1) / BM, n / BN, (cudaStream_t)stream);
+  return launch(EPI_PLAIN, g, (m + TM - 1) / TM, n / BN, (cudaStream_t)stream);
 }

@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(RL_WARPS * 32) k_router_logits(const uint16_t*
 
 // ------------------------------------------------------------------ select (softmax + top-k + renorm)
 constexpr int RS_WARPS = 4;
+// warps (tokens) per select CTA: the per-warp scratch of 1024 experts allows two within 48 KB
+constexpr int rs_warps(int epl) { return epl > 16 ? 2 : RS_WARPS; }
 constexpr int RS_MAXE = 32;  // experts per lane: experts <= 1024
 
 struct SelectArgs {
@@ -129,18 +131,17 @@ SSB_DEV void select_tail(const SelectArgs& a, int64_t t, int lane, unsigned long
 
 template <int EPL>
 __global__ void __launch_bounds__(RS_WARPS * 32) k_router_select(SelectArgs a) {
-  __shared__ unsigned long long s_cand[RS_WARPS][RS_CAND];
-  __shared__ unsigned long long s_top[RS_WARPS][16];
+  __shared__ SelectScratch<EPL> s_sel[rs_warps(EPL)];
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t t = (int64_t)blockIdx.x * RS_WARPS + warp;
+  const int64_t t = (int64_t)blockIdx.x * rs_warps(EPL) + warp;
   if (t >= a.tokens) return;
   const float* lrow = a.logits + t * a.ld;
   unsigned long long mine;
   float my_p, sum;
   warp_select<EPL>(lrow, a.experts, a.k, a.bias, a.flags, a.out_probs ? a.out_probs + t * a.experts : nullptr,
-                   s_cand[warp], s_top[warp], lane, mine, my_p, sum);
+                   s_sel[warp], lane, mine, my_p, sum);
   select_tail(a, t, lane, mine, my_p, sum, lrow);
 }
 
@@ -324,12 +325,13 @@ int launch_select(SelectArgs a, void* stream) {
   SSB_CHECK_ARG(!(a.flags & SSB_ROUTER_SHARED_GATE) || a.out_sh_gate);
   SSB_CHECK_ARG(a.prefetch_bytes % 16 == 0);
   if (a.tokens == 0) return SSB_OK;
-  dim3 grid((unsigned)((a.tokens + RS_WARPS - 1) / RS_WARPS));
   const int epl = (a.experts + 31) / 32;
+  const int nw = rs_warps(epl <= 4 ? 4 : epl <= 8 ? 8 : epl <= 16 ? 16 : 32);
+  dim3 grid((unsigned)((a.tokens + nw - 1) / nw));
   void (*kern)(SelectArgs) = epl <= 4 ? k_router_select<4> : epl <= 8 ? k_router_select<8>
                              : epl <= 16 ? k_router_select<16> : k_router_select<32>;
   ssb_note_smem("router_select", kern, 0);
-  return ssb_launch(kern, grid, dim3(RS_WARPS * 32), 0, (cudaStream_t)stream, true, a);
+  return ssb_launch(kern, grid, dim3(nw * 32), 0, (cudaStream_t)stream, true, a);
 }
 
 }  // namespace

@@ -55,108 +55,27 @@ SSB_DEV float key_value(uint32_t key) {
 
 constexpr int RS_CAND = 64;   // candidate slots per warp
 
-// One warp selects for the logits row `lrow` (experts entries; + bias; bf16-rounded first when flags has
-// SSB_ROUTER_ROUND_BF16): lane j < k ends with the rank-j composite `mine` and its probability `my_p`, every
-// lane with `sum`, the rank-order fp32 sum of the k probabilities. probs_row (nullable) gets all
-// probabilities. cand [RS_CAND] and top [16] are this warp's shared-memory scratch.
+// Shared-memory scratch of one selecting warp.
 template <int EPL>
-SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bias, int flags, float* probs_row,
-                         unsigned long long* cand, unsigned long long* top, int lane, unsigned long long& mine,
-                         float& my_p, float& sum) {
-  float v[EPL];
-  float m = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    int e = lane + 32 * i;
-    float l = -INFINITY;
-    if (e < experts) {
-      l = __ldcg(lrow + e);
-      if (bias) l = l + bias[e];
-      if (flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
-      m = fmaxf(m, l);
-    }
-    v[i] = l;
-  }
-  m = warp_max(m);
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    int e = lane + 32 * i;
-    float ex = 0.f;
-    if (e < experts) ex = expf(v[i] - m);
-    v[i] = ex;
-    s += ex;
-  }
-  s = warp_sum(s);
+struct SelectScratch {
+  float v[32 * EPL];                  // logits, then exponentials, then probabilities
+  unsigned long long c[32 * EPL];     // composites
+  unsigned long long cand[RS_CAND];
+  unsigned long long top[16];
+};
+
+// Rarely taken paths (more than RS_CAND candidates, or k > 16), kept out of line so the common path stays
+// short: this code runs once per token and per launch, so its size -- not its speed once cached -- is what the
+// instruction fetch pays for.
+template <int EPL>
+__device__ __noinline__ void warp_select_fallback(SelectScratch<EPL>& S, int experts, int k, int lane,
+                                                  unsigned long long& mine, float& my_p, float& sum) {
   unsigned long long c[EPL];
-  unsigned long long lm = 0ull;
+  float v[EPL];
 #pragma unroll
   for (int i = 0; i < EPL; ++i) {
-    int e = lane + 32 * i;
-    float p = v[i] / s;
-    v[i] = p;
-    c[i] = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
-    lm = c[i] > lm ? c[i] : lm;
-    if (probs_row && e < experts) probs_row[e] = p;
-  }
-  if (k <= 16) {
-    // Candidate filter: the k-th largest lane maximum T0 is a lower bound for the k-th largest composite (k
-    // lanes each hold an element >= T0), so only elements >= T0 can be selected. The candidates (usually a
-    // few more than k) are ranked by comparing against each other through shared memory.
-    int rk = 0;
-#pragma unroll
-    for (int d = 1; d < 32; ++d) {
-      const unsigned long long o = __shfl_sync(0xFFFFFFFFu, lm, (lane + d) & 31);
-      rk += o > lm;
-    }
-    const unsigned at = __ballot_sync(0xFFFFFFFFu, rk == k - 1 && lm != 0ull);
-    if (at) {
-      const unsigned long long T0 = __shfl_sync(0xFFFFFFFFu, lm, __ffs(at) - 1);
-      int n = 0;
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) n += c[i] >= T0;
-      int incl = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
-      if (total <= RS_CAND) {
-        int pos = incl - n;
-#pragma unroll
-        for (int i = 0; i < EPL; ++i)
-          if (c[i] >= T0) cand[pos++] = c[i];
-        __syncwarp();
-        const unsigned long long a0 = lane < total ? cand[lane] : 0ull;
-        const unsigned long long a1 = lane + 32 < total ? cand[lane + 32] : 0ull;
-        int r0 = 0, r1 = 0;
-        for (int q = 0; q < total; ++q) {
-          const unsigned long long o = cand[q];
-          r0 += o > a0;
-          r1 += o > a1;
-        }
-        if (lane < total && r0 < k) top[r0] = a0;
-        if (lane + 32 < total && r1 < k) top[r1] = a1;
-        __syncwarp();
-        sum = 0.f;   // renormalise: sequential sum in rank order
-        my_p = 0.f;
-        mine = 0ull;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j < k) {
-            const unsigned long long cj = top[j];
-            const float pj = key_value((uint32_t)(cj >> 32));
-            sum += pj;
-            if (j == lane) {
-              mine = cj;
-              my_p = pj;
-            }
-          }
-        }
-        return;
-      }
-    }
+    c[i] = S.c[lane + 32 * i];
+    v[i] = S.v[lane + 32 * i];
   }
   if (EPL <= 16 && k <= 16) {
     // Warp-wide top 16: each lane sorts its composites, then five butterfly steps merge the lanes' sorted
@@ -215,4 +134,115 @@ SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bia
   }
   sum = 0.f;  // sequential in rank order
   for (int j = 0; j < k; ++j) sum += __shfl_sync(0xFFFFFFFFu, my_p, j);
+}
+
+// One warp selects for the logits row `lrow` (experts entries; + bias; bf16-rounded first when flags has
+// SSB_ROUTER_ROUND_BF16): lane j < k ends with the rank-j composite `mine` and its probability `my_p`, every
+// lane with `sum`, the rank-order fp32 sum of the k probabilities. probs_row (nullable) gets all
+// probabilities. Lane l handles experts l, l + 32, ... in that order in every pass (so every sum has a fixed
+// order); the passes are loops over the warp's shared scratch S, the loads are issued all at once.
+template <int EPL>
+SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bias, int flags, float* probs_row,
+                         SelectScratch<EPL>& S, int lane, unsigned long long& mine, float& my_p, float& sum) {
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    S.v[e] = e < experts ? __ldcg(lrow + e) : -INFINITY;
+  }
+  float m = -INFINITY;
+#pragma unroll 1
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    if (e < experts) {
+      float l = S.v[e];
+      if (bias) l = l + bias[e];
+      if (flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
+      m = fmaxf(m, l);
+      S.v[e] = l;
+    }
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll 1
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    const float ex = e < experts ? expf(S.v[e] - m) : 0.f;
+    S.v[e] = ex;
+    s += ex;
+  }
+  s = warp_sum(s);
+  unsigned long long lm = 0ull;
+#pragma unroll 1
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    const float p = S.v[e] / s;
+    S.v[e] = p;
+    const unsigned long long c = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
+    S.c[e] = c;
+    lm = c > lm ? c : lm;
+    if (probs_row && e < experts) probs_row[e] = p;
+  }
+  if (k <= 16) {
+    // Candidate filter: the k-th largest lane maximum T0 is a lower bound for the k-th largest composite (k
+    // lanes each hold an element >= T0), so only elements >= T0 can be selected. The candidates (usually a
+    // few more than k) are ranked by comparing against each other through shared memory.
+    int rk = 0;
+#pragma unroll 1
+    for (int d = 1; d < 32; ++d) {
+      const unsigned long long o = __shfl_sync(0xFFFFFFFFu, lm, (lane + d) & 31);
+      rk += o > lm;
+    }
+    const unsigned at = __ballot_sync(0xFFFFFFFFu, rk == k - 1 && lm != 0ull);
+    if (at) {
+      const unsigned long long T0 = __shfl_sync(0xFFFFFFFFu, lm, __ffs(at) - 1);
+      int n = 0;
+#pragma unroll 1
+      for (int i = 0; i < EPL; ++i) n += S.c[lane + 32 * i] >= T0;
+      int incl = n;
+#pragma unroll 1
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+      if (total <= RS_CAND) {
+        int pos = incl - n;
+#pragma unroll 1
+        for (int i = 0; i < EPL; ++i) {
+          const unsigned long long c = S.c[lane + 32 * i];
+          if (c >= T0) S.cand[pos++] = c;
+        }
+        __syncwarp();
+        const unsigned long long a0 = lane < total ? S.cand[lane] : 0ull;
+        const unsigned long long a1 = lane + 32 < total ? S.cand[lane + 32] : 0ull;
+        int r0 = 0, r1 = 0;
+#pragma unroll 1
+        for (int q = 0; q < total; ++q) {
+          const unsigned long long o = S.cand[q];
+          r0 += o > a0;
+          r1 += o > a1;
+        }
+        if (lane < total && r0 < k) S.top[r0] = a0;
+        if (lane + 32 < total && r1 < k) S.top[r1] = a1;
+        __syncwarp();
+        sum = 0.f;   // renormalise: sequential sum in rank order
+        my_p = 0.f;
+        mine = 0ull;
+#pragma unroll 1
+        for (int j = 0; j < k; ++j) {
+          const unsigned long long cj = S.top[j];
+          const float pj = key_value((uint32_t)(cj >> 32));
+          sum += pj;
+          if (j == lane) {
+            mine = cj;
+            my_p = pj;
+          }
+        }
+        __syncwarp();
+        return;
+      }
+    }
+  }
+  __syncwarp();
+  warp_select_fallback<EPL>(S, experts, k, lane, mine, my_p, sum);
 }

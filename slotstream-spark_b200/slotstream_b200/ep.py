@@ -127,8 +127,9 @@ class CudaOps:
 
     # ---------------------------------------------------------------- helpers
     def _aligned(self, row_expert, num_local):
+        from .kernels.fused_moe_affine import BLOCK_M
         from .kernels.moe_align import moe_align
-        return moe_align(row_expert, num_local, 128)
+        return moe_align(row_expert, num_local, BLOCK_M)
 
     def _experts(self, a, tokens, row_token, row_weight, row_expert, group_ptr, n_groups, shared_local):
         n = row_token.numel()

@@ -11,7 +11,8 @@ functions of R or of the group composition, so a row's bits depend on that row a
 
 Differences from the reference, all additive: the shape comes from the tensors (hidden = x.shape[1],
 inter = h_buf.shape[1] or ``inter=``); a group may hold up to 512 experts (every expert of a layer resident at
-once); BLOCK_M is 128 (one tcgen05 M tile), so ``aligned`` must come from this module's ``align_rows``.
+once); BLOCK_M is 256 (one grouped-GEMM tile: two tcgen05 M128 halves sharing one dequantised weight tile), so
+``aligned`` must come from this module's ``align_rows``.
 """
 import torch
 
@@ -24,7 +25,7 @@ HID, INTER, TOPK = BASELINE_LAYOUT.hidden, BASELINE_LAYOUT.inter, 10
 RECORD_BYTES = BASELINE_LAYOUT.record_bytes
 (O_GATE_W, O_GATE_S, O_GATE_B, O_UP_W, O_UP_S, O_UP_B, O_DOWN_W, O_DOWN_S, O_DOWN_B) = BASELINE_LAYOUT.offsets()
 GROUP_MAX = 512
-BLOCK_M, BLOCK_N, BLOCK_K = 128, 256, 64
+BLOCK_M, BLOCK_N, BLOCK_K = 256, 128, 64
 
 
 def layout_for(hidden: int, inter: int) -> RecordLayout:
@@ -85,7 +86,7 @@ def fused_moe_affine(x, row_token, row_weight, expert_map, group_ptr, out_rows, 
     if aligned is None:
         aligned = align_rows(row_expert, expert_map, group_ptr.numel())
     elif aligned[0].numel() != padded_rows(r, group_ptr.numel(), BLOCK_M):
-        raise ValueError("aligned must come from align_rows (BLOCK_M = 128)")
+        raise ValueError(f"aligned must come from align_rows (BLOCK_M = {BLOCK_M})")
     launch_gate_up(x, row_token, aligned, group_ptr, h_buf, r, err)
     launch_down(h_buf, row_weight, aligned, group_ptr, out_rows, r, err)
 

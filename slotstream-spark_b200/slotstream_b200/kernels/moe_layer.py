@@ -76,6 +76,7 @@ def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLa
     Launches: router GEMM (tcgen05, dense bf16) + shared-gate logits, router select, align, row permute into
     expert order, gate_up + down (tcgen05 grouped GEMM, shared expert as local expert E), rank-order combine +
     shared add."""
+    from .fused_moe_affine import BLOCK_M
     from .moe_align import moe_align
     t, h = x.shape
     e = bufs.experts
@@ -94,7 +95,7 @@ def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLa
     flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0)
     _lib.check(L.ssb_router_select(_lib.ptr(lg), bufs.ld, t, e, k, _lib.ptr(bias), flags, _lib.ptr(bufs.ids),
                                    _lib.ptr(bufs.w), None, _lib.ptr(bufs.sh_gate), st), "router select")
-    aligned = moe_align(bufs.row_expert, e + 1, 128, out=(bufs.sorted_rows, bufs.block_expert, bufs.num_padded))
+    aligned = moe_align(bufs.row_expert, e + 1, BLOCK_M, out=(bufs.sorted_rows, bufs.block_expert, bufs.num_padded))
     _lib.check(L.ssb_prefill_experts(
         _lib.ptr(x), t, h, bufs.inter, _lib.ptr(bufs.row_token), _lib.ptr(bufs.row_weight), bufs.rows,
         _lib.ptr(aligned[0]), _lib.ptr(aligned[1]), _lib.ptr(aligned[2]), aligned[0].numel(), _lib.ptr(group_ptr),
