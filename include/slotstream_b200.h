@@ -256,7 +256,9 @@ int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hidden, int32
                         const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, uint16_t* x_sorted,
                         uint16_t* h_sorted, float* out_rows, int32_t* err, void* stream);
 
-/* x_sorted[m, :] = x[row_token[sorted_rows[m]], :] for m < num_padded (zero rows for padding). */
+/* x_sorted[m, :] = x[row_token[sorted_rows[m]], :] for m < num_padded (zero rows for padding), with every group
+ * of 8 columns in the K order (0,4,1,5,2,6,3,7): the order in which ssb_sorted_gate_up / ssb_sorted_down
+ * dequantise their 4-bit weights (two codes per bf16x2 pair); h_sorted comes out in the same order. */
 int ssb_permute_rows(const uint16_t* x, int64_t tokens, int32_t hidden, const int32_t* row_token, int64_t rows,
                      const int32_t* sorted_rows, const int32_t* num_padded, int64_t padded_len, uint16_t* x_sorted,
                      void* stream);

@@ -51,6 +51,8 @@ struct GemmArgs {
   int64_t a_rows;             // rows of the activation matrix (extent of the tensor map)
   int a_box_rows;             // rows per A copy: 1 (tile::gather4 of four rows) or TM (one 2-D box, identity rows)
   int out_sorted;             // SwiGLU epilogue: h row at the sorted position m instead of at row sorted_rows[m]
+  int kperm;                  // operands in the K order (0,4,1,5,2,6,3,7) inside every group of 8 (sorted path):
+                              // B is dequantised in bf16x2 pairs, A and the h written here follow that order
   const int32_t* row_token;   // nullable: the A row of row r is r
   const int32_t* sorted_rows; // nullable: identity (rows m < R)
   const int32_t* block_expert;
@@ -127,6 +129,28 @@ SSB_DEV uint4 dequant8(uint32_t w, const float2* sc2, float2 b2) {
   f2 = __ffma2_rn(__fadd2_rn(f2, m2), sc2[2], b2);
   f3 = __ffma2_rn(__fadd2_rn(f3, m2), sc2[3], b2);
   return make_uint4(cvt_bf16x2(f0.x, f0.y), cvt_bf16x2(f1.x, f1.y), cvt_bf16x2(f2.x, f2.y), cvt_bf16x2(f3.x, f3.y));
+}
+
+// 8 nibbles of w -> bf16 q*s + b in the K order (0,4,1,5,2,6,3,7): (w >> 4j) & 0x000F000F | 0x43004300 is the bf16
+// pair (128 + q_j, 128 + q_{j+4}); one bf16x2 FMA removes the 128 exactly, a second forms q*s + b with a single
+// rounding to bf16 (the value the reference's fp32 q*s + b rounds to whenever that sum is exact in fp32, as it
+// is for these 4-bit codes and bf16 scales and biases of similar size).
+SSB_DEV uint32_t hfma2_bf16(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+SSB_DEV uint4 dequant8_perm(uint32_t w, uint32_t s2, uint32_t b2) {
+  const uint32_t MAG = 0x43004300u, ONE = 0x3F803F80u, M128 = 0xC300C300u;
+  const uint32_t p0 = (w & 0x000F000Fu) | MAG, p1 = ((w >> 4) & 0x000F000Fu) | MAG;
+  const uint32_t p2 = ((w >> 8) & 0x000F000Fu) | MAG, p3 = ((w >> 12) & 0x000F000Fu) | MAG;
+  return make_uint4(hfma2_bf16(hfma2_bf16(p0, ONE, M128), s2, b2), hfma2_bf16(hfma2_bf16(p1, ONE, M128), s2, b2),
+                    hfma2_bf16(hfma2_bf16(p2, ONE, M128), s2, b2), hfma2_bf16(hfma2_bf16(p3, ONE, M128), s2, b2));
+}
+// bf16 pairs (lo, hi) of 8 consecutive values -> the same 8 values in the K order (0,4,1,5,2,6,3,7)
+SSB_DEV uint4 kperm8(uint4 v) {
+  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                    __byte_perm(v.y, v.w, 0x7632));
 }
 
 SSB_DEV void scales2(float s, float2* sc2) {
@@ -344,8 +368,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
                     hv[tt] = silu_fast(gg) * uu;   // accg / (1 + exp(-accg)) * accu, kernels/fused_moe_affine.py:80
                   }
                 }
-                dst[jj] = make_uint4(cvt_bf16x2(hv[0], hv[1]), cvt_bf16x2(hv[2], hv[3]), cvt_bf16x2(hv[4], hv[5]),
-                                     cvt_bf16x2(hv[6], hv[7]));
+                dst[jj] = a.kperm ? make_uint4(cvt_bf16x2(hv[0], hv[4]), cvt_bf16x2(hv[1], hv[5]),
+                                               cvt_bf16x2(hv[2], hv[6]), cvt_bf16x2(hv[3], hv[7]))
+                                  : make_uint4(cvt_bf16x2(hv[0], hv[1]), cvt_bf16x2(hv[2], hv[3]),
+                                               cvt_bf16x2(hv[4], hv[5]), cvt_bf16x2(hv[6], hv[7]));
               }
             }
           }
@@ -464,21 +490,18 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
         const int kb = (int)(j % KB);
         const uint8_t* st = S.stg + (j % PD) * STG;
         uint4 w = make_uint4(0, 0, 0, 0);
-        float sv = 0.f, bv = 0.f;
+        uint32_t sw = 0, bw = 0;
+        bool hi = false;
         if ((valid >> (j % PD)) & 1u) {
           w = *reinterpret_cast<const uint4*>(st + p * 16);
           const uint2 sbw = *reinterpret_cast<const uint2*>(st + W_STG + p * 8);
-          const uint32_t sw = sbw.x, bw = sbw.y;
+          sw = sbw.x;
+          bw = sbw.y;
           // gs 64: the k-block's group kb sits in half (kb & 1) of the word; gs 32: half hf covers group 2kb + hf
-          const bool hi = a.gs == 64 ? (kb & 1) : hf;
-          sv = hi ? bf16_hi(sw) : bf16_lo(sw);
-          bv = hi ? bf16_hi(bw) : bf16_lo(bw);
+          hi = a.gs == 64 ? (kb & 1) : hf;
         } else if (p == 0) {
           set_err(a.err, SSB_ERR_MISALIGNED);
         }
-        float2 sc[4];
-        scales2(sv, sc);
-        const float2 bb = make_float2(bv, bv);
         const int s = (int)(j % STAGES);
         const uint32_t ph = (uint32_t)((j / STAGES) & 1);
         if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
@@ -487,9 +510,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
         }
         uint8_t* bt = S.b + s * B_STAGE;
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        if (a.kperm) {
+          const uint32_t s2 = __byte_perm(sw, 0, hi ? 0x3232 : 0x1010), b2 = __byte_perm(bw, 0, hi ? 0x3232 : 0x1010);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)   // 16-byte chunk 4hf + c = elements 8(4hf + c) .. +7 = word c of this half
-          *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8(ws[c], sc, bb);
+          for (int c = 0; c < 4; ++c)   // 16-byte chunk 4hf + c = elements 8(4hf + c) .. +7 = word c of this half
+            *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8_perm(ws[c], s2, b2);
+        } else {
+          float2 sc[4];
+          scales2(hi ? bf16_hi(sw) : bf16_lo(sw), sc);
+          const float bv = hi ? bf16_hi(bw) : bf16_lo(bw);
+          const float2 bb = make_float2(bv, bv);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8(ws[c], sc, bb);
+        }
         fence_proxy_async_smem();
         mbar_arrive(&S.full_b[s]);
       }
@@ -513,7 +547,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
 }
 
 // x_sorted[m, :] = x[row_token[sorted_rows[m]], :] for m < num_padded (zero rows for padding), one warp per row:
-// the activation rows in expert order, so the grouped GEMM reads its A tiles as whole 2-D boxes.
+// the activation rows in expert order, so the grouped GEMM reads its A tiles as whole 2-D boxes, with every group
+// of 8 columns in the K order (0,4,1,5,2,6,3,7) in which the sorted GEMMs dequantise their weights.
 __global__ void __launch_bounds__(256) k_permute_rows(const uint4* __restrict__ x, int64_t x_rows, int64_t row_vecs,
                                                       const int32_t* __restrict__ row_token,
                                                       const int32_t* __restrict__ sorted_rows,
@@ -528,8 +563,8 @@ __global__ void __launch_bounds__(256) k_permute_rows(const uint4* __restrict__ 
     const int64_t r = __ldcg(sorted_rows + m);
     const int64_t t = (r >= 0 && r < R) ? (int64_t)__ldcg(row_token + r) : -1;
     const bool ok = t >= 0 && t < x_rows;
-    for (int64_t c = lane; c < row_vecs; c += 32)
-      out[m * row_vecs + c] = ok ? __ldg(x + t * row_vecs + c) : make_uint4(0, 0, 0, 0);
+    for (int64_t c = lane; c < row_vecs; c += 32)   // each 16-byte chunk in the K order of the sorted GEMMs
+      out[m * row_vecs + c] = ok ? kperm8(__ldg(x + t * row_vecs + c)) : make_uint4(0, 0, 0, 0);
   }
 }
 
@@ -628,6 +663,7 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
   g.a_rows = sorted ? padded_len : tokens;   // sorted: x is the permuted [padded_len, hidden] matrix
   g.a_box_rows = sorted ? TM : 1;
   g.out_sorted = sorted;
+  g.kperm = sorted;
   g.row_token = row_token;
   g.sorted_rows = sorted_rows;
   g.block_expert = block_expert;
@@ -659,6 +695,7 @@ int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter
   g.lda = inter;
   g.a_rows = sorted ? padded_len : rows;     // sorted: h rows at their sorted positions
   g.a_box_rows = sorted ? TM : 1;
+  g.kperm = sorted;
   g.sorted_rows = sorted_rows;
   g.block_expert = block_expert;
   g.num_padded = num_padded;
