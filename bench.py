@@ -58,7 +58,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "100", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                                          "-lms", "20", "-i", str(self.dev)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -88,13 +88,17 @@ class ClockSampler:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
         inside = [s for t, s in self.samples if self.t_on is not None and self.t_on <= t <= (self.t_off or t)]
-        use = inside if inside else [s for _, s in self.samples]
+        # a timed region shorter than the sampling period: the samples within 0.2 s of it (GPU still busy)
+        near = [s for t, s in self.samples
+                if self.t_on is not None and self.t_on - 0.2 <= t <= (self.t_off or t) + 0.2]
+        use = inside if inside else (near if near else [s for _, s in self.samples])
         sm = [float(s[1]) for s in use if s[1].replace(".", "").isdigit()]
         mx = [float(s[2]) for s in use if s[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for s in use for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(use), "samples_in_timed_region": len(inside)}
+                "reasons": reasons, "samples": len(use), "samples_in_timed_region": len(inside),
+                "samples_within_0.2s": len(near)}
 
 
 # ------------------------------------------------------------------ distributed plumbing

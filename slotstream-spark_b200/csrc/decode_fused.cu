@@ -57,6 +57,7 @@ struct FusedArgs {
   uint16_t* y;         // [R, H]
   uint32_t* sync;      // [2]
   int32_t* err;
+  int stage_pairs;     // gate/up row pairs one staging round of a CTA holds
 };
 
 struct __align__(16) XUnitS {
@@ -125,15 +126,25 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   __shared__ float s_w[F_MAXR][F_MAXK];
   __shared__ float s_shg[F_MAXR];
   __shared__ SelectScratch<EPL> s_sel[F_MAXR];
+  __shared__ float s_red[F_MAXR][FW];
+  __shared__ uint64_t s_bar;
+  __shared__ int s_seg_p[4], s_seg_q0[4], s_seg_n[4];
+  __shared__ uint32_t s_seg_off[4];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int R = a.R, k = a.k, H = a.H, I = a.I, E = a.E, gs = a.gs;
   const int P = R * k + R;                      // entries: routed (r, j) at r*k + j, shared of token r at R*k + r
   const int nux = H / 16, nui = I / 16;
-  // shared memory: x (bf16 raw) | x units | h units | expert bases
+  // shared memory: x (bf16 raw) | x units | expert bases | stage: the gate/up rows of phase 3, then the h units of
+  // phase 4 in the same bytes
   uint16_t* xs = reinterpret_cast<uint16_t*>(sm);
   XUnitS* xu_s = reinterpret_cast<XUnitS*>(sm + (size_t)F_MAXR * H * 2);
-  XUnitS* hx = xu_s + (size_t)F_MAXR * nux;
-  const uint8_t** bases = reinterpret_cast<const uint8_t**>(hx + (size_t)F_MAXR * (F_MAXK + 1) * nui);
+  const uint8_t** bases = reinterpret_cast<const uint8_t**>(xu_s + (size_t)F_MAXR * nux);
+  uint8_t* stage = reinterpret_cast<uint8_t*>(bases + F_MAXE);
+  XUnitS* hx = reinterpret_cast<XUnitS*>(stage);
+  if (tid == 0) {
+    mbar_init(&s_bar, 1);
+    fence_mbar_init();
+  }
 
   // ---------------- phase 1: x, router logits, expert bases
   const int nrows = E + 1;   // router rows, then the shared-expert gate row
@@ -206,12 +217,64 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   }
   if (!grid_sync(a.sync, a.err, &s_ok)) return;
 
-  // ---------------- phase 2: select (each CTA, warp per token)
+  // ---------------- phase 2: select (each CTA). The per-expert passes of warp_select run on all threads of the
+  // CTA -- element e of token t sits at index e = lane + 32 i of the token's scratch exactly as in warp_select,
+  // and the denominator is summed lane-sequentially over i by one warp per token -- so every value and the
+  // chosen experts are bit-identical to the router kernels; warp t then runs the candidate filter for token t.
+  {
+    constexpr int EW = 32 * EPL;
+    float tmax[F_MAXR];
+#pragma unroll
+    for (int t = 0; t < F_MAXR; ++t) tmax[t] = -INFINITY;
+    for (int idx = tid; idx < R * EW; idx += FT) {
+      const int t = idx / EW, e = idx - t * EW;
+      float l = -INFINITY;
+      if (e < E) {
+        l = __ldcg(a.logits + (int64_t)t * (E + 1) + e);
+        if (a.bias) l = l + __ldg(a.bias + e);
+        if (a.flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
+        tmax[t] = fmaxf(tmax[t], l);
+      }
+      s_sel[t].v[e] = l;
+    }
+#pragma unroll
+    for (int t = 0; t < F_MAXR; ++t) {
+      const float wm = warp_max(tmax[t]);
+      if (lane == 0) s_red[t][warp] = wm;
+    }
+    __syncthreads();
+    float m[F_MAXR];
+#pragma unroll
+    for (int t = 0; t < F_MAXR; ++t) {
+      m[t] = s_red[t][0];
+      for (int w = 1; w < FW; ++w) m[t] = fmaxf(m[t], s_red[t][w]);
+    }
+    for (int idx = tid; idx < R * EW; idx += FT) {
+      const int t = idx / EW, e = idx - t * EW;
+      s_sel[t].v[e] = e < E ? expf(s_sel[t].v[e] - m[t]) : 0.f;
+    }
+    __syncthreads();
+    if (warp < R) {   // the denominator in warp_select's order: lane-sequential over i, then the butterfly
+      float sl = 0.f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) sl += s_sel[warp].v[lane + 32 * i];
+      sl = warp_sum(sl);
+      if (lane == 0) s_red[warp][0] = sl;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < R * EW; idx += FT) {
+      const int t = idx / EW, e = idx - t * EW;
+      const float pv = s_sel[t].v[e] / s_red[t][0];
+      s_sel[t].v[e] = pv;
+      s_sel[t].c[e] = (e < E) ? composite(order_key(pv), (uint32_t)e) : 0ull;
+    }
+    __syncthreads();
+  }
   if (warp < R) {
     const float* lrow = a.logits + (int64_t)warp * (E + 1);
     unsigned long long mine;
     float my_p, sum;
-    warp_select<EPL>(lrow, E, k, a.bias, a.flags, nullptr, s_sel[warp], lane, mine, my_p, sum);
+    warp_select_finish<EPL>(s_sel[warp], E, k, lane, mine, my_p, sum);
     if (lane < k) {
       s_ids[warp][lane] = (int)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull));
       s_w[warp][lane] = my_p / sum;
@@ -254,62 +317,114 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
     }
   }
 
-  // ---------------- phase 3: gate_up, items (entry p, row pair q) split evenly over the grid's warps
+  // ---------------- phase 3: gate_up. CTA b owns the (entry p, row pair q) items [b*ipc, (b+1)*ipc) of the
+  // flattened list (a few contiguous row ranges of at most a few experts) and brings all of their codes, scales
+  // and biases into shared memory with one set of bulk copies per round, so the whole expert traffic of the
+  // layer is in flight at once; the warps then form h from shared memory.
   {
     const int pairs = I / 2;
-    const int64_t items = (int64_t)P * pairs;
     const int ng = H / gs;
-    for (int64_t it = (int64_t)blockIdx.x * FW + warp; it < items; it += (int64_t)gridDim.x * FW) {
-      const int p = (int)(it / pairs), q = (int)(it - (int64_t)p * pairs);
-      const int j0 = 2 * q, j1 = j0 + 1;
-      const uint8_t* base = entry_base(p);
-      float* hrow = a.h_buf + (int64_t)p * I;
-      if (!base) {
-        if (lane < 2) hrow[j0 + lane] = 0.f;
-        continue;
-      }
-      const int t = p >= R * k ? p - R * k : p / k;
-      const uint2* g0r = reinterpret_cast<const uint2*>(base + a.o.gw + (int64_t)j0 * H / 2);
-      const uint2* g1r = reinterpret_cast<const uint2*>(base + a.o.gw + (int64_t)j1 * H / 2);
-      const uint2* u0r = reinterpret_cast<const uint2*>(base + a.o.uw + (int64_t)j0 * H / 2);
-      const uint2* u1r = reinterpret_cast<const uint2*>(base + a.o.uw + (int64_t)j1 * H / 2);
-      const uint16_t* gsc = reinterpret_cast<const uint16_t*>(base + a.o.gsc);
-      const uint16_t* gbi = reinterpret_cast<const uint16_t*>(base + a.o.gb);
-      const uint16_t* usc = reinterpret_cast<const uint16_t*>(base + a.o.usc);
-      const uint16_t* ubi = reinterpret_cast<const uint16_t*>(base + a.o.ub);
-      uint2 wg0[NUX], wg1[NUX], wu0[NUX], wu1[NUX];
-#pragma unroll
-      for (int i = 0; i < NUX; ++i) {   // all of the item's weight words in flight at once
-        const int u = lane + 32 * i;
-        wg0[i] = ld_stream_u2(g0r + u);
-        wg1[i] = ld_stream_u2(g1r + u);
-        wu0[i] = ld_stream_u2(u0r + u);
-        wu1[i] = ld_stream_u2(u1r + u);
-      }
-      float ga0 = 0.f, ua0 = 0.f, ga1 = 0.f, ua1 = 0.f;
-#pragma unroll
-      for (int i = 0; i < NUX; ++i) {
-        const int u = lane + 32 * i;
-        const int g = (u * 16) / gs;
-        XUnit xu;
-        xunit_load(xu, xu_s[(size_t)t * nux + u]);
-        ga0 = unit_dot(wg0[i], bf16_bits(__ldg(gsc + j0 * ng + g)), bf16_bits(__ldg(gbi + j0 * ng + g)), xu, ga0);
-        ua0 = unit_dot(wu0[i], bf16_bits(__ldg(usc + j0 * ng + g)), bf16_bits(__ldg(ubi + j0 * ng + g)), xu, ua0);
-        ga1 = unit_dot(wg1[i], bf16_bits(__ldg(gsc + j1 * ng + g)), bf16_bits(__ldg(gbi + j1 * ng + g)), xu, ga1);
-        ua1 = unit_dot(wu1[i], bf16_bits(__ldg(usc + j1 * ng + g)), bf16_bits(__ldg(ubi + j1 * ng + g)), xu, ua1);
-      }
-      warp_sum4f(ga0, ua0, ga1, ua1);
-      if (lane < 2) {
-        const float ga = lane ? ga1 : ga0, ua = lane ? ua1 : ua0;
-        float h;
-        if (p >= R * k) {   // shared expert: lin() returns bf16, silu and the product round to bf16
-          const float gbv = round_bf16(ga), ubv = round_bf16(ua);
-          h = round_bf16(round_bf16(gbv / (1.f + expf(-gbv))) * ubv);
-        } else {
-          h = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u in fp32, kernels/moe_gemv_affine.py:76
+    const uint32_t wrow = (uint32_t)H / 2, srow = (uint32_t)ng * 2;   // bytes of one row's codes, scales
+    const int64_t items = (int64_t)P * pairs;
+    const int64_t ipc = (items + gridDim.x - 1) / gridDim.x;
+    const int64_t i_begin = (int64_t)blockIdx.x * ipc;
+    const int64_t i_end = i_begin + ipc < items ? i_begin + ipc : items;
+    int round = 0;
+    for (int64_t r0 = i_begin; r0 < i_end; r0 += a.stage_pairs, ++round) {
+      const int64_t r1 = r0 + a.stage_pairs < i_end ? r0 + a.stage_pairs : i_end;
+      if (tid == 0) {   // segments (one per entry) of this round, their copies, one completion barrier
+        int ns = 0;
+        uint32_t off = 0, bytes = 0;
+        for (int64_t it = r0; it < r1 && ns < 4;) {
+          const int pe = (int)(it / pairs), q0 = (int)(it - (int64_t)pe * pairs);
+          const int n = (int)((r1 - it) < (pairs - q0) ? (r1 - it) : (pairs - q0));
+          s_seg_p[ns] = pe;
+          s_seg_q0[ns] = q0;
+          s_seg_n[ns] = n;
+          s_seg_off[ns] = off;
+          const uint8_t* base = entry_base(pe);
+          const uint32_t rows = 2u * (uint32_t)n;
+          if (base) bytes += rows * (2 * wrow + 4 * srow);
+          off += rows * (2 * wrow + 4 * srow);
+          it += n;
+          ++ns;
         }
-        hrow[j0 + lane] = h;
+        for (int q = ns; q < 4; ++q) s_seg_n[q] = 0;
+        mbar_expect_tx(&s_bar, bytes);
+        for (int q = 0; q < ns; ++q) {
+          const uint8_t* base = entry_base(s_seg_p[q]);
+          if (!base) continue;
+          const uint32_t rows = 2u * (uint32_t)s_seg_n[q];
+          const int64_t j0 = 2 * (int64_t)s_seg_q0[q];
+          uint8_t* d = stage + s_seg_off[q];
+          bulk_g2s(d, base + a.o.gw + j0 * wrow, rows * wrow, &s_bar);
+          bulk_g2s(d + rows * wrow, base + a.o.uw + j0 * wrow, rows * wrow, &s_bar);
+          bulk_g2s(d + rows * 2 * wrow, base + a.o.gsc + j0 * srow, rows * srow, &s_bar);
+          bulk_g2s(d + rows * (2 * wrow + srow), base + a.o.gb + j0 * srow, rows * srow, &s_bar);
+          bulk_g2s(d + rows * (2 * wrow + 2 * srow), base + a.o.usc + j0 * srow, rows * srow, &s_bar);
+          bulk_g2s(d + rows * (2 * wrow + 3 * srow), base + a.o.ub + j0 * srow, rows * srow, &s_bar);
+        }
       }
+      __syncthreads();
+      // every thread waits for the copies; a CTA-wide decision to give up keeps the barrier below reachable
+      if (__syncthreads_or(!mbar_wait(&s_bar, (uint32_t)(round & 1), SSB_WAIT_LIMIT))) {
+        if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
+        mbar_wait(&s_bar, (uint32_t)(round & 1), SSB_WAIT_LIMIT);   // let the copies land before leaving
+        return;
+      }
+      for (int64_t it = r0 + warp; it < r1; it += FW) {
+        // locate the segment of item `it`: segments are consecutive runs of the round's items
+        int64_t first = r0;
+        int q = 0;
+        while (q < 3 && s_seg_n[q + 1] > 0 && it >= first + s_seg_n[q]) {
+          first += s_seg_n[q];
+          ++q;
+        }
+        const int pe = s_seg_p[q];
+        const int lq = (int)(it - first);              // pair within the segment
+        const int j0 = 2 * (s_seg_q0[q] + lq);
+        float* hrow = a.h_buf + (int64_t)pe * I;
+        if (!entry_base(pe)) {
+          if (lane < 2) hrow[j0 + lane] = 0.f;
+          continue;
+        }
+        const uint32_t rows = 2u * (uint32_t)s_seg_n[q];
+        const uint8_t* d = stage + s_seg_off[q];
+        const uint2* g0r = reinterpret_cast<const uint2*>(d + (2 * lq) * wrow);
+        const uint2* g1r = reinterpret_cast<const uint2*>(d + (2 * lq + 1) * wrow);
+        const uint2* u0r = reinterpret_cast<const uint2*>(d + rows * wrow + (2 * lq) * wrow);
+        const uint2* u1r = reinterpret_cast<const uint2*>(d + rows * wrow + (2 * lq + 1) * wrow);
+        const uint16_t* gsc = reinterpret_cast<const uint16_t*>(d + rows * 2 * wrow) + 2 * lq * ng;
+        const uint16_t* gbi = reinterpret_cast<const uint16_t*>(d + rows * (2 * wrow + srow)) + 2 * lq * ng;
+        const uint16_t* usc = reinterpret_cast<const uint16_t*>(d + rows * (2 * wrow + 2 * srow)) + 2 * lq * ng;
+        const uint16_t* ubi = reinterpret_cast<const uint16_t*>(d + rows * (2 * wrow + 3 * srow)) + 2 * lq * ng;
+        const int t = pe >= R * k ? pe - R * k : pe / k;
+        float ga0 = 0.f, ua0 = 0.f, ga1 = 0.f, ua1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < NUX; ++i) {
+          const int u = lane + 32 * i;
+          const int g = (u * 16) / gs;
+          XUnit xu;
+          xunit_load(xu, xu_s[(size_t)t * nux + u]);
+          ga0 = unit_dot(g0r[u], bf16_bits(gsc[g]), bf16_bits(gbi[g]), xu, ga0);
+          ua0 = unit_dot(u0r[u], bf16_bits(usc[g]), bf16_bits(ubi[g]), xu, ua0);
+          ga1 = unit_dot(g1r[u], bf16_bits(gsc[ng + g]), bf16_bits(gbi[ng + g]), xu, ga1);
+          ua1 = unit_dot(u1r[u], bf16_bits(usc[ng + g]), bf16_bits(ubi[ng + g]), xu, ua1);
+        }
+        warp_sum4f(ga0, ua0, ga1, ua1);
+        if (lane < 2) {
+          const float ga = lane ? ga1 : ga0, ua = lane ? ua1 : ua0;
+          float h;
+          if (pe >= R * k) {   // shared expert: lin() returns bf16, silu and the product round to bf16
+            const float gbv = round_bf16(ga), ubv = round_bf16(ua);
+            h = round_bf16(round_bf16(gbv / (1.f + expf(-gbv))) * ubv);
+          } else {
+            h = ga / (1.f + expf(-ga)) * ua;   // silu(g) * u in fp32, kernels/moe_gemv_affine.py:76
+          }
+          hrow[j0 + lane] = h;
+        }
+      }
+      __syncthreads();   // the stage is reused by the next round (and by phase 4)
     }
   }
   if (!grid_sync(a.sync, a.err, &s_ok)) return;
@@ -401,10 +516,13 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   }
 }
 
-size_t fused_smem(int H, int I) {
-  return (size_t)F_MAXR * H * 2 + sizeof(XUnitS) * ((size_t)F_MAXR * (H / 16) + (size_t)F_MAXR * (F_MAXK + 1) * (I / 16)) +
-         (size_t)F_MAXE * sizeof(void*);
+// dynamic shared memory: x, x units, expert bases, then the stage (gate/up rows of one round, or the h units)
+size_t fused_fixed_smem(int H) {
+  return (size_t)F_MAXR * H * 2 + sizeof(XUnitS) * (size_t)F_MAXR * (H / 16) + (size_t)F_MAXE * sizeof(void*);
 }
+size_t fused_pair_bytes(int H, int gs) { return (size_t)2 * (2 * (H / 2) + 4 * (H / gs) * 2); }
+size_t fused_hx_bytes(int I) { return sizeof(XUnitS) * (size_t)F_MAXR * (F_MAXK + 1) * (I / 16); }
+constexpr size_t F_SMEM_BUDGET = 200 * 1024;
 
 template <int NUX, int NUI>
 void* pick_epl(int epl) {
@@ -449,9 +567,23 @@ extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t top
     default: break;
   }
   if (!kern) return SSB_EUNSUPPORTED;
-  const size_t smem = fused_smem(hidden, inter);
-  // per (device, kernel, smem) setup once: attribute, occupancy check, SM count (host calls that would
-  // otherwise sit between every launch)
+  // pairs of gate/up rows one staging round holds: all of the CTA's share when it fits the budget
+  int sms0 = 0, dev0 = 0;
+  cudaGetDevice(&dev0);
+  cudaDeviceGetAttribute(&sms0, cudaDevAttrMultiProcessorCount, dev0);
+  if (sms0 < 1) sms0 = 148;
+  const size_t fixed = fused_fixed_smem(hidden), pair_b = fused_pair_bytes(hidden, 64);
+  const int64_t per_cta = ((int64_t)rows * (topk + 1) * (inter / 2) + sms0 - 1) / sms0;
+  int64_t stage_pairs = (int64_t)((F_SMEM_BUDGET - fixed) / pair_b);
+  if (stage_pairs > per_cta) stage_pairs = per_cta;
+  if (stage_pairs > inter / 2) stage_pairs = inter / 2;   // a round then spans at most two entries
+  if (stage_pairs < 1) return SSB_EUNSUPPORTED;
+  size_t stage_b = (size_t)stage_pairs * pair_b;
+  if (stage_b < fused_hx_bytes(inter)) stage_b = fused_hx_bytes(inter);
+  const size_t smem = fixed + stage_b;
+  if (smem > 212 * 1024) return SSB_EUNSUPPORTED;   // with the static scratch, one CTA per SM must still fit
+  // per (device, kernel) setup once: the dynamic shared-memory attribute (raised when a call needs more), an
+  // occupancy check, the SM count (host calls that would otherwise sit between every launch)
   struct Prepared {
     int dev;
     void* kern;
@@ -463,20 +595,22 @@ extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t top
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
-  int sms = 0;
+  Prepared* pp = nullptr;
   for (int i = 0; i < n_prep; ++i)
-    if (prep[i].dev == dev && prep[i].kern == kern && prep[i].smem == smem) sms = prep[i].sms;
-  if (!sms) {
+    if (prep[i].dev == dev && prep[i].kern == kern) pp = &prep[i];
+  if (!pp || pp->smem < smem) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
     ssb_note_smem("moe_decode_fused", (void (*)(FusedArgs))kern, smem);
-    int per_sm = 0;
+    int per_sm = 0, sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FT, smem);
     if (e != cudaSuccess) return (int)e;
     if (per_sm < 1 || sms < 1) return SSB_EUNSUPPORTED;
-    if (n_prep < 16) prep[n_prep++] = Prepared{dev, kern, smem, sms};
+    if (!pp && n_prep < 16) pp = &prep[n_prep++];
+    if (pp) *pp = Prepared{dev, kern, smem, sms};
   }
+  const int sms = pp ? pp->sms : sms0;
   FusedArgs a{};
   a.x = x;
   a.R = (int)rows;
@@ -507,6 +641,7 @@ extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t top
   a.y = y;
   a.sync = sync;
   a.err = err;
+  a.stage_pairs = (int)stage_pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sms);   // one CTA per SM: all resident (the launch fails otherwise)
   cfg.blockDim = dim3(FT);

@@ -136,58 +136,24 @@ __device__ __noinline__ void warp_select_fallback(SelectScratch<EPL>& S, int exp
   for (int j = 0; j < k; ++j) sum += __shfl_sync(0xFFFFFFFFu, my_p, j);
 }
 
-// One warp selects for the logits row `lrow` (experts entries; + bias; bf16-rounded first when flags has
-// SSB_ROUTER_ROUND_BF16): lane j < k ends with the rank-j composite `mine` and its probability `my_p`, every
-// lane with `sum`, the rank-order fp32 sum of the k probabilities. probs_row (nullable) gets all
-// probabilities. Lane l handles experts l, l + 32, ... in that order in every pass (so every sum has a fixed
-// order); the passes are loops over the warp's shared scratch S, the loads are issued all at once.
+// Candidate filter and renormalisation over a filled scratch (S.c composites, S.v probabilities, expert e at
+// index e = lane + 32 i): lane j < k ends with the rank-j composite `mine` and its probability `my_p`, every
+// lane with `sum`, the rank-order fp32 sum of the k probabilities. The k-th largest lane maximum T0 bounds the
+// k-th largest composite from below (k lanes each hold an element >= T0), so only elements >= T0 can be chosen;
+// those candidates (usually a few more than k) are ranked against each other through shared memory.
 template <int EPL>
-SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bias, int flags, float* probs_row,
-                         SelectScratch<EPL>& S, int lane, unsigned long long& mine, float& my_p, float& sum) {
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const int e = lane + 32 * i;
-    S.v[e] = e < experts ? __ldcg(lrow + e) : -INFINITY;
-  }
-  float m = -INFINITY;
-#pragma unroll 1
-  for (int i = 0; i < EPL; ++i) {
-    const int e = lane + 32 * i;
-    if (e < experts) {
-      float l = S.v[e];
-      if (bias) l = l + bias[e];
-      if (flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
-      m = fmaxf(m, l);
-      S.v[e] = l;
-    }
-  }
-  m = warp_max(m);
-  float s = 0.f;
-#pragma unroll 1
-  for (int i = 0; i < EPL; ++i) {
-    const int e = lane + 32 * i;
-    const float ex = e < experts ? expf(S.v[e] - m) : 0.f;
-    S.v[e] = ex;
-    s += ex;
-  }
-  s = warp_sum(s);
-  unsigned long long lm = 0ull;
-#pragma unroll 1
-  for (int i = 0; i < EPL; ++i) {
-    const int e = lane + 32 * i;
-    const float p = S.v[e] / s;
-    S.v[e] = p;
-    const unsigned long long c = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
-    S.c[e] = c;
-    lm = c > lm ? c : lm;
-    if (probs_row && e < experts) probs_row[e] = p;
-  }
+SSB_DEV void warp_select_finish(SelectScratch<EPL>& S, int experts, int k, int lane, unsigned long long& mine,
+                                float& my_p, float& sum) {
   if (k <= 16) {
-    // Candidate filter: the k-th largest lane maximum T0 is a lower bound for the k-th largest composite (k
-    // lanes each hold an element >= T0), so only elements >= T0 can be selected. The candidates (usually a
-    // few more than k) are ranked by comparing against each other through shared memory.
+    unsigned long long c[EPL];
+    unsigned long long lm = 0ull;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      c[i] = S.c[lane + 32 * i];
+      lm = c[i] > lm ? c[i] : lm;
+    }
     int rk = 0;
-#pragma unroll 1
+#pragma unroll
     for (int d = 1; d < 32; ++d) {
       const unsigned long long o = __shfl_sync(0xFFFFFFFFu, lm, (lane + d) & 31);
       rk += o > lm;
@@ -196,10 +162,10 @@ SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bia
     if (at) {
       const unsigned long long T0 = __shfl_sync(0xFFFFFFFFu, lm, __ffs(at) - 1);
       int n = 0;
-#pragma unroll 1
-      for (int i = 0; i < EPL; ++i) n += S.c[lane + 32 * i] >= T0;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) n += c[i] >= T0;
       int incl = n;
-#pragma unroll 1
+#pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
         if (lane >= o) incl += y;
@@ -207,16 +173,14 @@ SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bia
       const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
       if (total <= RS_CAND) {
         int pos = incl - n;
-#pragma unroll 1
-        for (int i = 0; i < EPL; ++i) {
-          const unsigned long long c = S.c[lane + 32 * i];
-          if (c >= T0) S.cand[pos++] = c;
-        }
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+          if (c[i] >= T0) S.cand[pos++] = c[i];
         __syncwarp();
         const unsigned long long a0 = lane < total ? S.cand[lane] : 0ull;
         const unsigned long long a1 = lane + 32 < total ? S.cand[lane + 32] : 0ull;
         int r0 = 0, r1 = 0;
-#pragma unroll 1
+#pragma unroll 4
         for (int q = 0; q < total; ++q) {
           const unsigned long long o = S.cand[q];
           r0 += o > a0;
@@ -228,14 +192,16 @@ SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bia
         sum = 0.f;   // renormalise: sequential sum in rank order
         my_p = 0.f;
         mine = 0ull;
-#pragma unroll 1
-        for (int j = 0; j < k; ++j) {
-          const unsigned long long cj = S.top[j];
-          const float pj = key_value((uint32_t)(cj >> 32));
-          sum += pj;
-          if (j == lane) {
-            mine = cj;
-            my_p = pj;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (j < k) {
+            const unsigned long long cj = S.top[j];
+            const float pj = key_value((uint32_t)(cj >> 32));
+            sum += pj;
+            if (j == lane) {
+              mine = cj;
+              my_p = pj;
+            }
           }
         }
         __syncwarp();
@@ -245,4 +211,46 @@ SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bia
   }
   __syncwarp();
   warp_select_fallback<EPL>(S, experts, k, lane, mine, my_p, sum);
+}
+
+// One warp selects for the logits row `lrow` (experts entries; + bias; bf16-rounded first when flags has
+// SSB_ROUTER_ROUND_BF16), results as warp_select_finish. probs_row (nullable) gets all probabilities. Lane l
+// handles experts l, l + 32, ... in that order in every pass, so every sum has a fixed order.
+template <int EPL>
+SSB_DEV void warp_select(const float* lrow, int experts, int k, const float* bias, int flags, float* probs_row,
+                         SelectScratch<EPL>& S, int lane, unsigned long long& mine, float& my_p, float& sum) {
+  float v[EPL];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {   // all loads in flight at once
+    const int e = lane + 32 * i;
+    float l = -INFINITY;
+    if (e < experts) {
+      l = __ldcg(lrow + e);
+      if (bias) l = l + __ldg(bias + e);
+      if (flags & SSB_ROUTER_ROUND_BF16) l = round_bf16(l);
+      m = fmaxf(m, l);
+    }
+    v[i] = l;
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    const float ex = e < experts ? expf(v[i] - m) : 0.f;
+    v[i] = ex;
+    s += ex;
+  }
+  s = warp_sum(s);
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    const float p = v[i] / s;
+    S.v[e] = p;
+    S.c[e] = (e < experts) ? composite(order_key(p), (uint32_t)e) : 0ull;
+    if (probs_row && e < experts) probs_row[e] = p;
+  }
+  __syncwarp();
+  warp_select_finish<EPL>(S, experts, k, lane, mine, my_p, sum);
 }
