@@ -149,11 +149,11 @@ def timed_steps(run, k, flush_buf, world, clocks=None):
 
 
 # ------------------------------------------------------------------ decode workload
-def bench_decode(args, world, rank):
+def decode_world(args, rank):
+    """Resident records (layers x 512 routed + one shared per layer), router weights and slot tables."""
     from slotstream_b200 import synth
-    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
     from slotstream_b200.records import BASELINE_LAYOUT as LAY, MAP_LAYERS
-    NL, E, K, b = args.layers, 512, 10, args.batch
+    NL, E = args.layers, 512
     dev = torch.device("cuda")
     rb = LAY.record_bytes
     seed = 1000 + rank
@@ -169,6 +169,20 @@ def bench_decode(args, world, rank):
     map_t = torch.full((MAP_LAYERS * E,), -1, dtype=torch.int32, device=dev)
     map_t[:NL * E] = torch.arange(NL * E, dtype=torch.int32, device=dev)
     slot_ptr = recs.data_ptr() + torch.arange(NL * E, dtype=torch.int64, device=dev) * rb
+    return dict(recs=recs, shared=shared, router_w=router_w, sh_gate_w=sh_gate_w, bias=bias, map_t=map_t,
+                slot_ptr=slot_ptr, gen=g)
+
+
+def bench_decode(args, world, rank, batch=None, W=None):
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    from slotstream_b200.records import BASELINE_LAYOUT as LAY
+    NL, E, K = args.layers, 512, 10
+    b = batch or args.batch
+    dev = torch.device("cuda")
+    rb = LAY.record_bytes
+    W = W or decode_world(args, rank)
+    recs, shared, router_w, sh_gate_w = W["recs"], W["shared"], W["router_w"], W["sh_gate_w"]
+    bias, map_t, slot_ptr, g = W["bias"], W["map_t"], W["slot_ptr"], W["gen"]
     x = torch.randn(NL, b, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
     bufs = [DecodeLayerBuffers(b, K, LAY.hidden, LAY.inter, E, dev) for _ in range(NL)]
 
@@ -501,9 +515,19 @@ def main():
         res = bench_prefill(args, world, rank)
         torch.cuda.empty_cache()
         if world == 1 and not args.no_decode:
-            d = bench_decode(args, world, rank)
+            W = decode_world(args, rank)
+            d = bench_decode(args, world, rank, 1, W)
             res["decode"] = {k: d[k] for k in ("value", "unit", "ms_per_step", "config", "hbm_gbs_per_step",
                                                "bytes_per_step", "roofline", "e2e", "clocks")}
+            # configs[1] also names batch 2 (speculative verify) and 16: same records, same step
+            res["decode"]["other_batches"] = {}
+            for bb in (2, 16):
+                e = bench_decode(args, world, rank, bb, W)
+                res["decode"]["other_batches"][str(bb)] = {
+                    "value": e["value"], "unit": e["unit"], "ms_per_step": e["ms_per_step"],
+                    "hbm_gbs_per_step": e["hbm_gbs_per_step"], "bytes_per_step": e["bytes_per_step"],
+                    "roofline_frac": e["roofline"]["frac"], "kernel": e["roofline"]["kernel"]}
+            del W
             torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_baseline import time_prefill

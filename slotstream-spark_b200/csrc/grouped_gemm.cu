@@ -31,16 +31,17 @@
 namespace {
 
 constexpr int BM = 128, MT = 2, TM = BM * MT, BK = 64, BN = 128;
-constexpr int STAGES = 4;        // A/B operand stages
-constexpr int PD = 3;            // weight staging depth of each producer thread
+constexpr int STAGES = 3;        // A/B operand stages
+constexpr int SS = 4;            // k-blocks of one weight super-step (one coalesced load of the codes): 4, or 2
+                                 // when the k-block count is not a multiple of 4
 constexpr int THREADS = 512;
 constexpr int A_WARP = 0, MMA_WARP = 1, EPI_WARP0 = 4, PROD_WARP0 = 8, N_PROD = 256;
 constexpr uint32_t A_STAGE = TM * 128;           // 32 KB: two 128-row halves
 constexpr uint32_t A_HALF = BM * 128;
 constexpr uint32_t B_STAGE = BN * 128;           // 16 KB
-constexpr uint32_t W_STG = N_PROD * 16;          // packed nibbles of one k-block, 16 B per producer thread
-constexpr uint32_t SB_STG = N_PROD * 8;          // per producer thread: the words holding its scale and bias
-constexpr uint32_t STG = W_STG + SB_STG;
+constexpr uint32_t W_STG = BN * SS * 32;         // codes of a super-step: 128 rows x 128 B, 16-byte pieces swizzled
+constexpr uint32_t SB_STG = N_PROD * 32;         // per producer thread: its row's scales (16 B) and biases (16 B)
+constexpr uint32_t STG = W_STG + SB_STG;         // one staging slot; two slots alternate
 constexpr uint32_t TMEM_COLS = 512;              // 2 buffers x 2 halves of M128 x N128 fp32 accumulators
 
 enum { EPI_SWIGLU = 0, EPI_SCALE = 1, EPI_PLAIN = 2 };
@@ -86,7 +87,7 @@ struct Smem {
   uint32_t* tmem;
 };
 
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + PD * STG + 8 * (3 * STAGES + 4) + 16;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 2 * STG + 8 * (3 * STAGES + 4) + 16;
 
 SSB_DEV Smem carve(uint8_t* raw) {
   Smem s;
@@ -96,7 +97,7 @@ SSB_DEV Smem carve(uint8_t* raw) {
   s.b = p;
   p += STAGES * B_STAGE;
   s.stg = p;
-  p += PD * STG;
+  p += 2 * STG;
   s.full_a = (uint64_t*)p;
   s.full_b = s.full_a + STAGES;
   s.empty = s.full_b + STAGES;
@@ -459,73 +460,122 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       }
       asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
-      uint32_t valid = 0;   // bit (j % PD): staging slot of step j holds a real weight row
-      auto issue = [&](int64_t j) {
-        const int kb = (int)(j % KB);
-        tile_info(j);
-        uint8_t* st = S.stg + (j % PD) * STG;
-        const uint32_t bit = 1u << (j % PD);
-        valid = t_base ? (valid | bit) : (valid & ~bit);
-        if (!t_base) return;
-        // this thread's 16 bytes of codes (consecutive threads, consecutive 16-byte slots: no bank conflicts)
-        cp_async16(smem_u32(st + p * 16), t_base + a.off_w[piece] + t_nrow * (a.K / 2) + kb * 32 + hf * 16, 16);
-        // the 4-byte-aligned words that hold the k-block's scale and bias: group kb (gs 64) or groups 2kb, 2kb+1
-        // (gs 32); both threads of a B-row fetch them, so each waits on its own copies only
-        const int g0 = a.gs == 64 ? kb : 2 * kb;
-        const uint16_t* sr = (const uint16_t*)(t_base + a.off_s[piece]) + t_nrow * ng;
-        const uint16_t* bsrc = (const uint16_t*)(t_base + a.off_b[piece]) + t_nrow * ng;
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + p * 8)),
-                     "l"(sr + (g0 & ~1)) : "memory");
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(st + W_STG + p * 8 + 4)),
-                     "l"(bsrc + (g0 & ~1)) : "memory");
-      };
-      for (int64_t j = 0; j < PD - 1 && j < steps; ++j) {
-        issue(j);
-        asm volatile("cp.async.commit_group;" ::: "memory");
-      }
-      for (int64_t j = 0; j < steps; ++j) {
-        if (j + PD - 1 < steps) issue(j + PD - 1);
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group %0;" ::"n"(PD - 1) : "memory");
-        const int kb = (int)(j % KB);
-        const uint8_t* st = S.stg + (j % PD) * STG;
-        uint4 w = make_uint4(0, 0, 0, 0);
-        uint32_t sw = 0, bw = 0;
-        bool hi = false;
-        if ((valid >> (j % PD)) & 1u) {
-          w = *reinterpret_cast<const uint4*>(st + p * 16);
-          const uint2 sbw = *reinterpret_cast<const uint2*>(st + W_STG + p * 8);
-          sw = sbw.x;
-          bw = sbw.y;
-          // gs 64: the k-block's group kb sits in half (kb & 1) of the word; gs 32: half hf covers group 2kb + hf
-          hi = a.gs == 64 ? (kb & 1) : hf;
-        } else if (p == 0) {
-          set_err(a.err, SSB_ERR_MISALIGNED);
-        }
-        const int s = (int)(j % STAGES);
-        const uint32_t ph = (uint32_t)((j / STAGES) & 1);
-        if (!mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
-          s_fail = 1;
-          break;
-        }
-        uint8_t* bt = S.b + s * B_STAGE;
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        if (a.kperm) {
-          const uint32_t s2 = __byte_perm(sw, 0, hi ? 0x3232 : 0x1010), b2 = __byte_perm(bw, 0, hi ? 0x3232 : 0x1010);
+      // Affine 4-bit weights, one super-step of SS k-blocks at a time. The 256 producers copy the tile's codes for
+      // the super-step with coalesced 16-byte pieces (thread t: pieces t + 256i of the 128 rows x 128 B; a warp
+      // covers four whole lines) into a staging slot whose pieces are XOR-swizzled by row, and each thread its
+      // row's SS scales and biases. Named barriers over the producers order the two slots; every producer passes
+      // every barrier, and a failed wait only raises this thread's flag, OR-reduced by the barrier that starts the
+      // next super-step, so all producers leave together.
+      const int ss = KB % SS == 0 ? SS : 2;   // k-blocks per super-step (KB is even)
+      const int n_ss = (int)(steps / ss);
+      const int gsb = (a.gs == 64 ? 2 : 4) * ss;   // bytes of scales (or biases) of a super-step per row
+      const void* dummy = a.a;                // valid address for zero-byte copies (rows of an unusable expert)
+      uint32_t slot_ok = 0;                   // bit (n & 1): super-step n's expert has a usable record
+      int my_fail = 0;
+      auto issue_ss = [&](int n) {
+        const int64_t j0 = (int64_t)n * ss;
+        tile_info(j0);
+        const int kb0 = (int)(j0 % KB);
+        uint8_t* st = S.stg + (n & 1) * STG;
+        const int64_t t = tile_of((int)(j0 / KB));
+        const int nb = (int)(t % NB);
 #pragma unroll
-          for (int c = 0; c < 4; ++c)   // 16-byte chunk 4hf + c = elements 8(4hf + c) .. +7 = word c of this half
-            *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8_perm(ws[c], s2, b2);
+        for (int i = 0; i < SS; ++i) {
+          if (i >= ss) break;
+          const int pc = p + N_PROD * i, row = pc / (2 * ss), c16 = pc - row * (2 * ss);
+          const int pce = (EPI == EPI_SWIGLU) ? (row >> 6) : 0;
+          const int64_t nr = (EPI == EPI_SWIGLU) ? (int64_t)nb * (BN / 2) + (row & (BN / 2 - 1)) : (int64_t)nb * BN + row;
+          const void* src = t_base ? (const void*)(t_base + a.off_w[pce] + nr * (a.K / 2) + kb0 * 32 + c16 * 16) : dummy;
+          cp_async16(smem_u32(st + row * 128 + ((c16 ^ (row & 7)) << 4)), src, t_base ? 16u : 0u);
+        }
+        const int g0 = a.gs == 64 ? kb0 : 2 * kb0;   // first group of the super-step (gsb-byte aligned)
+        const uint16_t* sr = t_base ? (const uint16_t*)(t_base + a.off_s[piece]) + t_nrow * ng + g0 : nullptr;
+        const uint16_t* bsrc = t_base ? (const uint16_t*)(t_base + a.off_b[piece]) + t_nrow * ng + g0 : nullptr;
+        const uint32_t ds = smem_u32(st + W_STG + p * 32);
+        if (gsb == 4) {
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(ds), "l"(sr ? (const void*)sr : dummy),
+                       "r"(sr ? 4 : 0) : "memory");
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(ds + 16),
+                       "l"(bsrc ? (const void*)bsrc : dummy), "r"(bsrc ? 4 : 0) : "memory");
+        } else if (gsb == 8) {
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(ds), "l"(sr ? (const void*)sr : dummy),
+                       "r"(sr ? 8 : 0) : "memory");
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(ds + 16),
+                       "l"(bsrc ? (const void*)bsrc : dummy), "r"(bsrc ? 8 : 0) : "memory");
         } else {
-          float2 sc[4];
-          scales2(hi ? bf16_hi(sw) : bf16_lo(sw), sc);
-          const float bv = hi ? bf16_hi(bw) : bf16_lo(bw);
-          const float2 bb = make_float2(bv, bv);
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8(ws[c], sc, bb);
+          cp_async16(ds, sr ? (const void*)sr : dummy, sr ? 16u : 0u);
+          cp_async16(ds + 16, bsrc ? (const void*)bsrc : dummy, bsrc ? 16u : 0u);
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&S.full_b[s]);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const uint32_t bit = 1u << (n & 1);
+        slot_ok = t_base ? (slot_ok | bit) : (slot_ok & ~bit);
+      };
+      auto prod_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(N_PROD) : "memory"); };
+      // barrier over the producers that also ORs every producer's failure flag (the same answer for all)
+      auto prod_sync_any = [&](int flag) -> bool {
+        uint32_t r;
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred p, 1, %2, p;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(r)
+            : "r"(flag), "n"(N_PROD)
+            : "memory");
+        return r != 0;
+      };
+      if (n_ss > 0) issue_ss(0);
+      for (int n = 0; n < n_ss; ++n) {
+        // every producer is done reading slot (n + 1) & 1 (super-step n - 1); stop together after any failure
+        if (prod_sync_any(my_fail)) break;
+        if (n + 1 < n_ss) {
+          issue_ss(n + 1);
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+          asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        prod_sync();   // every producer's copies of super-step n have landed
+        const uint8_t* st = S.stg + (n & 1) * STG;
+        const int64_t j0 = (int64_t)n * ss;
+        const bool ok_row = (slot_ok >> (n & 1)) & 1u;
+        if (!ok_row && p == 0) set_err(a.err, SSB_ERR_MISALIGNED);
+        const uint4 sbq = *reinterpret_cast<const uint4*>(st + W_STG + p * 32);        // scales
+        const uint4 bbq = *reinterpret_cast<const uint4*>(st + W_STG + p * 32 + 16);   // biases
+        const uint32_t sq[4] = {sbq.x, sbq.y, sbq.z, sbq.w}, bq[4] = {bbq.x, bbq.y, bbq.z, bbq.w};
+#pragma unroll
+        for (int u = 0; u < SS; ++u) {
+          if (u >= ss) break;
+          const int64_t j = j0 + u;
+          const uint4 w = ok_row ? *reinterpret_cast<const uint4*>(st + br * 128 + (((2 * u + hf) ^ (br & 7)) << 4))
+                                 : make_uint4(0, 0, 0, 0);
+          // the scale / bias of this thread's 32 elements: group u of the super-step (gs 64), or 2u + hf (gs 32)
+          const int gi = a.gs == 64 ? u : 2 * u + hf;
+          const uint32_t sw = sq[gi >> 1], bw = bq[gi >> 1];
+          const bool hi = gi & 1;
+          const int s = (int)(j % STAGES);
+          const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+          if (my_fail || !mbar_wait_ns(&S.empty[s], ph ^ 1, SSB_WAIT_NS)) {
+            my_fail = 1;   // keep passing the producer barriers; the loop ends at the next super-step
+            s_fail = 1;
+            continue;
+          }
+          uint8_t* bt = S.b + s * B_STAGE;
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+          if (a.kperm) {
+            const uint32_t s2 = ok_row ? __byte_perm(sw, 0, hi ? 0x3232 : 0x1010) : 0u;
+            const uint32_t b2 = ok_row ? __byte_perm(bw, 0, hi ? 0x3232 : 0x1010) : 0u;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)   // 16-byte chunk 4hf + c = elements 8(4hf + c) .. +7 = word c of this half
+              *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8_perm(ws[c], s2, b2);
+          } else {
+            float2 sc[4];
+            scales2(ok_row ? (hi ? bf16_hi(sw) : bf16_lo(sw)) : 0.f, sc);
+            const float bv = ok_row ? (hi ? bf16_hi(bw) : bf16_lo(bw)) : 0.f;
+            const float2 bb = make_float2(bv, bv);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4*>(bt + swz128(br, 4 * hf + c)) = dequant8(ws[c], sc, bb);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&S.full_b[s]);
+        }
       }
       asm volatile("cp.async.wait_all;" ::: "memory");
     }
@@ -653,7 +703,7 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
                  int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, int32_t shared_local,
                  uint16_t* h_buf, int32_t* err, void* stream, bool sorted = false) {
   SSB_CHECK_ARG(rows >= 0 && padded_len >= 0 && n_groups >= 1);
-  if (hidden % BK || hidden <= 0 || inter % (BN / 2) || inter <= 0 || (hidden / 64) % 2) return SSB_EUNSUPPORTED;
+  if (hidden % (2 * BK) || hidden <= 0 || inter % (BN / 2) || inter <= 0) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
   SSB_CHECK_ARG(x && row_token && sorted_rows && block_expert && num_padded && group_ptr && h_buf);
   SSB_CHECK_ARG(padded_len % TM == 0);
@@ -686,7 +736,7 @@ int down_impl(const uint16_t* h_buf, int64_t rows, int32_t hidden, int32_t inter
               const int64_t* group_ptr, int32_t n_groups, int32_t shared_local, float* out_rows, int32_t* err,
               void* stream, bool sorted = false) {
   SSB_CHECK_ARG(rows >= 0 && padded_len >= 0 && n_groups >= 1);
-  if (inter % BK || inter <= 0 || hidden % BN || hidden <= 0 || (inter / 64) % 2) return SSB_EUNSUPPORTED;
+  if (inter % (2 * BK) || inter <= 0 || hidden % BN || hidden <= 0) return SSB_EUNSUPPORTED;
   if (padded_len == 0 || rows == 0) return SSB_OK;
   SSB_CHECK_ARG(h_buf && row_weight && sorted_rows && block_expert && num_padded && group_ptr && out_rows);
   SSB_CHECK_ARG(padded_len % TM == 0);
@@ -790,7 +840,7 @@ extern "C" int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hi
 extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const int32_t* q, const uint16_t* s,
                                 const uint16_t* b, int32_t n, int32_t gs, float* out, void* stream) {
   SSB_CHECK_ARG(m >= 0 && k >= 1 && n >= 1 && (gs == 32 || gs == 64));
-  if (k % BK || n % BN || (k / gs) % 2) return SSB_EUNSUPPORTED;
+  if (k % (2 * BK) || n % BN) return SSB_EUNSUPPORTED;
   if (m == 0) return SSB_OK;
   SSB_CHECK_ARG(x && q && s && b && out);
   SSB_CHECK_ARG((((uintptr_t)q | (uintptr_t)s | (uintptr_t)b) & 3) == 0 && ((uintptr_t)q & 15) == 0);
