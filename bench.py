@@ -1,6 +1,6 @@
 """Benchmark of the B200 MoE hot path; prints ONE JSON line (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload prefill|decode|slotpool] [--impl reference]
 
 Workloads (synthetic data with the distributions BASELINE.json names):
 * ``decode``  (configs[1]): one decode step = 48 stacked config[0] MoE layers at batch b (default 1), Zipf(1.1)
@@ -8,6 +8,9 @@ Workloads (synthetic data with the distributions BASELINE
   its own resident N(0,1) hidden state (the attention / hyper-connection segments between MoE layers, which
   renormalise the residual stream in the real model, are not part of this path).
 * ``prefill`` (configs[2]/[3]): one step = one config[0] layer over a chunk of tokens per GPU.
+* ``slotpool``: one step = one fresh token through 48 layers whose routed experts stream through an
+  HBM slot pool of 1 GiB chunks holding 70% of the records (misses copied from pinned host memory on a side
+  stream); metric = MoE-path ms per token. The default run reports it as the ``slotpool`` sub-measurement.
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the launching stream with an
 L2 flush (256 MiB write) before it, barrier + synchronize on both sides, max over ranks. The JSON line carries
@@ -243,7 +246,7 @@ def bench_decode(args, world, rank, batch=None, W=None):
         kname = "moe_decode_fused (whole layer: router, select, gate_up, down, combine)"
     else:
         launch_bytes = (sum(u * rb for u in uniq) + NL * (rb + b * LAY.hidden * 2 * 2)) / NL
-        kname = "moe_decode_layer (gate_up + down)"
+        kname = "moe_decode_layer (grouped gate_up + down + rank_sum)"
     pk = peaks()
     achieved = launch_bytes / (launch_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
@@ -281,10 +284,137 @@ def bench_decode(args, world, rank, batch=None, W=None):
         "roofline": roofline,
         "e2e": {"value": round(world * b / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y_host.numel() * 2)},
-        "gpu_launches": (1 if b <= FUSED_MAX_ROWS else 4) * NL * args.steps,
+        "gpu_launches": (1 if b <= FUSED_MAX_ROWS else 5) * NL * args.steps,
         "clocks": clocks.summary(),
         "device_errors": errs,
     }
+    return res
+
+
+# ------------------------------------------------------------------ slot-pool streaming decode
+def bench_slotpool(args, world, rank):
+    """48-layer b=1 decode whose routed experts stream through an HBM slot pool of 1 GiB chunks holding 70% of
+    the 48 x 512 records (random initial slot table, CLOCK replacement); every step is a fresh token with uniform
+    routing, so about 30% of the experts it needs are absent and are copied from pinned host records on a side
+    stream while the layer waits on an event. Metric: MoE-path time per token."""
+    from slotstream_b200 import synth
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers
+    from slotstream_b200.records import BASELINE_LAYOUT as LAY
+    from slotstream_b200.slot_pool import SlotPool, decode_layer_streaming, host_table
+    NL, E, K = args.layers, 512, 10
+    dev = torch.device("cuda")
+    rb = LAY.record_bytes
+    seed = 4000 + rank
+    # host store: 512 distinct pinned records, expert e of every layer reads record e
+    store_dev = torch.empty((E, rb), dtype=torch.uint8, device=dev)
+    synth.fill_records_device(LAY, store_dev, seed)
+    store = torch.empty((E, rb), dtype=torch.uint8).pin_memory()
+    store.copy_(store_dev)
+    del store_dev
+    shared = torch.empty((NL, rb), dtype=torch.uint8, device=dev)
+    synth.fill_records_device(LAY, shared, seed + 7)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    router_w = (torch.randn(NL, E, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    sh_gate_w = (torch.randn(NL, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    n_tok = args.warmup + 2 * args.steps + 4
+    xs = torch.randn(n_tok, NL, 1, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
+    table = host_table(store.data_ptr(), rb, NL, E, per_layer=False)
+    capacity = int(round(args.pool_fraction * NL * E))
+    pool = SlotPool(rb, NL, E, chunk_bytes=1 << 30)
+    pool.resize(capacity)
+    copy = torch.cuda.Stream()
+    # random initial slot table: a random 70% of the (layer, expert) pairs, filled in random order
+    rng = np.random.default_rng(seed)
+    pick = rng.permutation(NL * E)[:capacity]
+    for l in range(NL):
+        ex = pick[pick // E == l] % E
+        if ex.size:
+            pool.ensure(l, ex, table, copy, torch.cuda.current_stream())
+    pool.release()
+    torch.cuda.synchronize()
+    bufs = [DecodeLayerBuffers(1, K, LAY.hidden, LAY.inter, E, dev) for _ in range(NL)]
+    ids_host = torch.empty((1, K), dtype=torch.int32).pin_memory()
+    tok = [0]
+    launches = [0]
+
+    def step():
+        t = tok[0] % n_tok
+        tok[0] += 1
+        for l in range(NL):
+            _, st_ = decode_layer_streaming(pool, table, xs[t, l], router_w[l], l, shared[l], sh_gate_w[l], K, bufs[l],
+                                            copy_stream=copy, ids_host=ids_host)
+            launches[0] += 4 + (1 if st_[1] else 0)
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    h0, m0, b0 = pool.counters()
+    launches[0] = 0
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    times = timed_steps(step, args.steps, flush, world, clocks)
+    clocks.stop()
+    h1, m1, b1 = pool.counters()
+    n_launch = launches[0]
+    ms = max_over_ranks(sum(times) / len(times), world)
+    errs = sum(int(bf.err.item()) for bf in bufs)
+    miss_frac = (m1 - m0) / max(1, (h1 - h0) + (m1 - m0))
+    h2d_per_step = (b1 - b0) / args.steps
+
+    # the copy engine's own H2D rate for record-sized pinned copies (the bound of this workload)
+    dst = torch.empty((64, rb), dtype=torch.uint8, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(copy):
+        for rep in range(2):
+            e0.record(copy)
+            for i in range(64):
+                dst[i].copy_(store[(7 * i + rep) % E], non_blocking=True)
+            e1.record(copy)
+    torch.cuda.synchronize()
+    h2d_gbs = 64 * rb / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    del dst
+    achieved = h2d_per_step / (ms * 1e-3) / 1e9
+
+    # e2e: the token's hidden states from pinned host memory and the layers' outputs back, inside the step
+    n_e2e = max(3, args.steps // 4)
+    tok0 = tok[0]
+    x_host = xs[tok0:tok0 + n_e2e].cpu().pin_memory()   # tokens no step has used yet
+    y_host = torch.empty((NL, 1, LAY.hidden), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        t = tok[0]
+        xs[t].copy_(x_host[t - tok0], non_blocking=True)
+        step()
+        y_host.copy_(torch.stack([bf.y for bf in bufs]), non_blocking=True)
+
+    e2e_times = timed_steps(e2e_step, n_e2e, flush, world)
+    e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
+    res = {
+        "metric": "MoE-path time per token (slot-pool streaming decode)", "value": round(ms, 4), "unit": "ms/token",
+        "higher_is_better": False, "tokens_per_s": round(1e3 / ms, 2), "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"slotpool_decode_{NL}layer_b1", "layers": NL, "batch": 1, "experts": E, "topk": K,
+                   "routing": "uniform (fresh token every step)", "pool_slots": capacity,
+                   "pool_fraction_of_records": args.pool_fraction, "chunk_bytes": 1 << 30,
+                   "pool_chunks": pool.chunks, "host_store": "512 pinned records shared by the layers",
+                   "l2": "flushed before every step (256 MiB write)", "cuda_graph": False},
+        "miss_fraction": round(miss_frac, 4), "misses_per_layer": round((m1 - m0) / (args.steps * NL), 3),
+        "h2d_bytes_per_step": int(h2d_per_step),
+        "roofline": {"bound": "h2d", "kernel": "host-to-device record copies (copy engine)",
+                     "achieved": round(achieved, 2), "peak": round(h2d_gbs, 2), "unit": "GB/s",
+                     "frac": round(achieved / h2d_gbs, 4), "peak_source": "measured in this run: 64 pinned "
+                     "record copies back to back on the copy stream", "traffic": None},
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms/token", "h2d_bytes_per_step": int(h2d_per_step + x_host[0].numel() * 2),
+                "d2h_bytes_per_step": int(y_host.numel() * 2 + NL * K * 4)},
+        "gpu_launches": n_launch,
+        "clocks": clocks.summary(),
+        "device_errors": errs,
+    }
+    pool.close()
     return res
 
 
@@ -485,7 +615,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
+    ap.add_argument("--workload", choices=["prefill", "decode", "slotpool"], default="prefill")
+    ap.add_argument("--pool-fraction", type=float, default=0.7,
+                    help="slotpool: share of the layers x 512 records the HBM pool holds")
+    ap.add_argument("--no-slotpool", action="store_true", help="skip the slot-pool sub-measurement at N=1")
     ap.add_argument("--tokens", type=int, default=32768, help="prefill tokens per GPU")
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
     ap.add_argument("--batch", type=int, default=1, help="decode batch")
@@ -509,6 +642,8 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_baseline import time_decode
             res["cpu_baseline"] = time_decode(BASELINE_LAYOUT, seconds=args.cpu_seconds)
+    elif args.workload == "slotpool":
+        res = bench_slotpool(args, world, rank)
     elif world > 1 and not args.replicas:
         res = bench_prefill_ep(args, world, rank)
     else:
@@ -528,6 +663,12 @@ def main():
                     "hbm_gbs_per_step": e["hbm_gbs_per_step"], "bytes_per_step": e["bytes_per_step"],
                     "roofline_frac": e["roofline"]["frac"], "kernel": e["roofline"]["kernel"]}
             del W
+            torch.cuda.empty_cache()
+        if world == 1 and not args.no_slotpool:
+            s = bench_slotpool(args, world, rank)
+            res["slotpool"] = {k: s[k] for k in ("metric", "value", "unit", "tokens_per_s", "ms_per_step", "config",
+                                                 "miss_fraction", "misses_per_layer", "h2d_bytes_per_step",
+                                                 "roofline", "e2e", "gpu_launches", "clocks", "device_errors")}
             torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             from oracle.cpu_baseline import time_prefill

@@ -3,7 +3,8 @@
  *
  * Every entry point takes raw device pointers, element counts and a cudaStream_t passed as void*; none
  * allocates device memory, none synchronises the host, and every launch goes to the given stream, so
- * the calls can be captured in a CUDA graph. Each returns SSB_OK (0), a negative SSB_E* code for a bad
+ * the calls can be captured in a CUDA graph -- except the ssb_pool_* calls of the slot pool, which own
+ * device memory (create / resize allocate it, destroy synchronises) and are host-side. Each returns SSB_OK (0), a negative SSB_E* code for a bad
  * argument (checked before any launch), or a positive cudaError_t from the launch.
  *
  * Conventions: bf16 tensors are passed as uint16_t* bit patterns; 4-bit affine weights follow MLX
@@ -28,7 +29,7 @@ extern "C" {
 #define SSB_EINVAL (-1)       /* null pointer, count or size out of range */
 #define SSB_EUNSUPPORTED (-2) /* a shape these kernels do not handle (see each entry point) */
 #define SSB_ENODEVICE (-3)    /* current device is not sm_100 */
-#define SSB_ETOOBIG (-4)      /* request larger than the fixed static scratch of ssb_router_topk_static */
+#define SSB_ETOOBIG (-4)      /* request larger than a fixed capacity (static scratch, slot pool) */
 
 /* ---- bits of the device error word (int32, caller-owned, OR-ed by kernels; never cleared by them) */
 #define SSB_ERR_EXPERT_RANGE 1 /* an expert id outside [0, 512) */
@@ -99,8 +100,10 @@ int ssb_moe_align(const int32_t* row_expert, int64_t rows, const int32_t* expert
  *   o[r, j, :] = w[r, j] * (D h[r, j, :])               (fp32)
  *   out[r, :]  = o[r, 0] + o[r, 1] + ... in rank order  (sequential fp32)
  * x bf16|fp32 [rows, hidden] (x_dtype SSB_BF16 / SSB_F32); h_buf fp32 [rows, topk, inter];
- * o_buf fp32 [rows, topk, hidden]; out fp32 [rows, hidden]. hidden % 512 == 0, inter % 512 == 0 or
- * inter % 16 == 0 with inter <= 8192, gs 64. err (int32, nullable) gets SSB_ERR_* bits; a bad expert
+ * o_buf fp32 [rows, topk, hidden] (nullable); out fp32 [rows, hidden]. hidden % 512 == 0 and <= 4096,
+ * inter % 64 == 0 and <= 2048 (other shapes: SSB_EUNSUPPORTED), gs 64. With o_buf and rows >= 3 (rows * topk
+ * <= 1024) the (row, rank) entries are grouped by expert, so a record chosen by several rows is read once;
+ * the results are the same bits either way. err (int32, nullable) gets SSB_ERR_* bits; a bad expert
  * contributes zero. Row-invariant and placement-invariant bit for bit.
  * Replaces: slotstream_spark/kernels/moe_gemv_affine.py:113-147 (kernels :55-110). */
 int ssb_moe_decode(const void* x, int32_t x_dtype, const int32_t* expert_ids, const float* weights,
@@ -173,6 +176,35 @@ int ssb_ep_combine(const float* ret, const int32_t* tok_slot, const int32_t* tok
                    const int32_t* ids, int64_t tokens, int32_t k, int32_t experts_per_rank, int32_t n_ranks,
                    int32_t strided, int32_t exact, int32_t hidden, const float* sh, float* out, uint16_t* y,
                    void* stream);
+
+/* ---- HBM expert slot pool for streaming decode (additive; the B200 side of slotio's Pool + Ensurer,
+ * slotio/include/slotio/pool.hpp:23-160 and slotio/src/ensure.cpp). Unlike the kernel entry points, the pool
+ * owns device memory: ssb_pool_create allocates the device tables map (int32 [layers * experts], -1 = absent)
+ * and slot_ptr (int64 [max_slots]) on the current device, ssb_pool_resize the 1 GiB chunks that hold the slots.
+ * The decode entry points read experts through these two tables (ssb_pool_tables). Not thread-safe across
+ * pools; calls on one pool are serialised by its lock. */
+typedef struct ssb_pool ssb_pool;
+ssb_pool* ssb_pool_create(int64_t record_bytes, int64_t chunk_bytes, int32_t layers, int32_t experts,
+                          int32_t max_slots);
+void ssb_pool_destroy(ssb_pool* pool);
+/* Grow to n_slots slots (allocating whole chunks); shrinking is not supported. */
+int ssb_pool_resize(ssb_pool* pool, int32_t n_slots);
+int ssb_pool_tables(ssb_pool* pool, int32_t** map_dev, int64_t** slot_ptr_dev, int64_t* map_len, int32_t* n_slots,
+                    int32_t* chunks);
+/* Make experts[0..n) of `layer` resident before the layer's kernels run on compute_stream. Duplicates are
+ * allowed; hits are marked referenced; each miss takes a CLOCK victim (never a slot this call needs), is copied
+ * from host_table[layer * experts + e] (pinned host record) on copy_stream after the victim's last reader
+ * (see ssb_pool_release) has finished, and is published in map on copy_stream; compute_stream then waits for
+ * the copies (either stream may be 0, the default stream). out_slots[i] (host, nullable) = slot of experts[i];
+ * stats (host int64 [3], nullable) = hits,
+ * misses, bytes copied by this call. SSB_ETOOBIG when the misses do not fit (nothing changed).
+ * Replaces: Ensurer::ensure, slotio/include/slotio/pool.hpp:141-160 (slotio/src/ensure.cpp). */
+int ssb_pool_ensure(ssb_pool* pool, int32_t layer, const int32_t* experts, int32_t n, const void* const* host_table,
+                    void* copy_stream, void* compute_stream, int32_t* out_slots, int64_t* stats);
+/* Record, on compute_stream after the kernels of the last ensured layer, the event that every slot that
+ * layer used waits for before it can be overwritten. */
+int ssb_pool_release(ssb_pool* pool, void* compute_stream);
+int ssb_pool_counters(ssb_pool* pool, int64_t* hits, int64_t* misses, int64_t* bytes);
 
 /* Router logits + select (as ssb_router_logits then ssb_router_select) with the logits held in a fixed
  * device array that comes with the library's device code, so the call needs no workspace and allocates nothing:

@@ -354,7 +354,381 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
   }
 }
 
+// ------------------------------------------------------------------ grouped path (rows >= 3)
+// Routed entries that chose the same expert form a group (the shared expert's rows form one more); a group's
+// entries are cut, in entry order, into runs of GRP_TOK, and the CTA of entry p computes the run that starts
+// at p against ONE staged copy of the expert's slice (CTAs of other entries exit at once). The weights of an
+// expert chosen by several rows are read once per layer instead of once per row. Every (entry, output) value
+// is the op sequence of the per-row kernels above, and the rank-order sum moves to its own small kernel
+// (the reference's _rank_sum), so the grouped path equals the per-row path bit for bit.
+constexpr int GRP_TOK = 8;      // entries one grouped CTA computes
+constexpr int GRP_MAX = 1024;   // routed entries (rows * topk) the grouped path takes
+constexpr int GD_ROWS = 64;     // hidden rows per grouped down CTA (eight per warp)
+
+// Warp-wide: the entries of the run that starts at routed entry p (none when p does not start a run), in
+// entry order, into s_list; returns their count.
+SSB_DEV int group_run(const int32_t* s_ids, int n_routed, int p, int* s_list, int lane) {
+  const int e = s_ids[p];
+  int occ = 0;
+  for (int q0 = 0; q0 < p; q0 += 32) {
+    const int q = q0 + lane;
+    occ += __popc(__ballot_sync(0xFFFFFFFFu, q < p && s_ids[q] == e));
+  }
+  if (occ % GRP_TOK) return 0;
+  int n = 0;
+  for (int q0 = p; q0 < n_routed && n < GRP_TOK; q0 += 32) {
+    const int q = q0 + lane;
+    const bool m = q < n_routed && s_ids[q] == e;
+    const unsigned b = __ballot_sync(0xFFFFFFFFu, m);
+    const int before = __popc(b & ((1u << lane) - 1u));
+    if (m && n + before < GRP_TOK) s_list[n + before] = q;
+    n += __popc(b);
+  }
+  return n < GRP_TOK ? n : GRP_TOK;
+}
+
+template <int NUX>
+__global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up_g(DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ const uint8_t* s_base;
+  __shared__ int s_list[GRP_TOK];
+  __shared__ int s_n;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_routed = (int)(a.R * a.topk);
+  const int p = blockIdx.y;
+  const int n0 = blockIdx.x * GU_ROWS;
+  const int H = a.H, gs = a.gs;
+  const uint32_t wbytes = (uint32_t)GU_ROWS * H / 2, sbytes = (uint32_t)GU_ROWS * (H / gs) * 2;
+  uint8_t* gw = sm;
+  uint8_t* uw = gw + wbytes;
+  uint8_t* gsc = uw + wbytes;
+  uint8_t* gb = gsc + sbytes;
+  uint8_t* usc = gb + sbytes;
+  uint8_t* ub = usc + sbytes;
+  int32_t* s_ids = reinterpret_cast<int32_t*>(ub + sbytes);
+  const bool is_shared = p >= n_routed;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    s_n = 0;
+    s_base = nullptr;
+  }
+  __syncthreads();
+  auto issue = [&](const uint8_t* base) {
+    mbar_expect_tx(&bar, 2 * wbytes + 4 * sbytes);
+    bulk_g2s(gw, base + a.o.gw + (int64_t)n0 * H / 2, wbytes, &bar);
+    bulk_g2s(uw, base + a.o.uw + (int64_t)n0 * H / 2, wbytes, &bar);
+    bulk_g2s(gsc, base + a.o.gsc + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+    bulk_g2s(gb, base + a.o.gb + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+    bulk_g2s(usc, base + a.o.usc + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+    bulk_g2s(ub, base + a.o.ub + (int64_t)n0 * (H / gs) * 2, sbytes, &bar);
+  };
+  if (is_shared) {
+    const int occ = p - n_routed;
+    if (occ % GRP_TOK) return;
+    if (tid == 0) {   // the shared record is static: start its copies before the wait
+      const int n = (int)(a.R - occ) < GRP_TOK ? (int)(a.R - occ) : GRP_TOK;
+      for (int i = 0; i < n; ++i) s_list[i] = p + i;
+      s_n = n;
+      s_base = a.shared_rec;
+      issue(a.shared_rec);
+    }
+    pdl_wait();
+    pdl_trigger();
+  } else {
+    pdl_wait();
+    pdl_trigger();
+    for (int q = tid; q < n_routed; q += blockDim.x) s_ids[q] = ld_cg_i32(a.ids + q);
+    __syncthreads();
+    if (warp == 0) {
+      const int n = group_run(s_ids, n_routed, p, s_list, lane);
+      if (lane == 0 && n) {
+        const uint8_t* base = a.bases ? (const uint8_t*)ld_cg_i64(a.bases + p)
+                                      : resolve_expert(s_ids[p], a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots,
+                                                       a.err);
+        s_base = base;
+        s_n = n;
+        if (base) issue(base);
+      }
+    }
+  }
+  __syncthreads();
+  const int n = s_n;
+  if (n == 0) return;
+  const uint8_t* base = s_base;
+  if (!base) {
+    for (int idx = tid; idx < n * GU_ROWS; idx += blockDim.x)
+      a.h_buf[(int64_t)s_list[idx / GU_ROWS] * a.I + n0 + idx % GU_ROWS] = 0.f;
+    return;
+  }
+  if (!mbar_wait(&bar, 0, SSB_WAIT_LIMIT)) {
+    set_err(a.err, SSB_ERR_TIMEOUT);
+    mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
+    return;
+  }
+  const int ng = H / gs, nunits = H / 16;
+  const int j0 = 2 * warp, j1 = j0 + 1;
+  const uint2* g0r = reinterpret_cast<const uint2*>(gw + (size_t)j0 * H / 2);
+  const uint2* u0r = reinterpret_cast<const uint2*>(uw + (size_t)j0 * H / 2);
+  const uint2* g1r = reinterpret_cast<const uint2*>(gw + (size_t)j1 * H / 2);
+  const uint2* u1r = reinterpret_cast<const uint2*>(uw + (size_t)j1 * H / 2);
+  const uint16_t* gs16 = reinterpret_cast<const uint16_t*>(gsc);
+  const uint16_t* gb16 = reinterpret_cast<const uint16_t*>(gb);
+  const uint16_t* us16 = reinterpret_cast<const uint16_t*>(usc);
+  const uint16_t* ub16 = reinterpret_cast<const uint16_t*>(ub);
+  for (int t = 0; t < n; ++t) {
+    const int q = s_list[t];
+    const int64_t r = is_shared ? q - n_routed : q / a.topk;
+    float ga0 = 0.f, ua0 = 0.f, ga1 = 0.f, ua1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NUX; ++i) {
+      const int u = lane + 32 * i;
+      if (u < nunits) {
+        float x16[16];
+        load_x16(a, r, u, x16);
+        XUnit xu;
+        xunit_from_f32(xu, x16);
+        const int g = (u * 16) / gs;
+        ga0 = unit_dot(g0r[u], bf16_bits(gs16[j0 * ng + g]), bf16_bits(gb16[j0 * ng + g]), xu, ga0);
+        ua0 = unit_dot(u0r[u], bf16_bits(us16[j0 * ng + g]), bf16_bits(ub16[j0 * ng + g]), xu, ua0);
+        ga1 = unit_dot(g1r[u], bf16_bits(gs16[j1 * ng + g]), bf16_bits(gb16[j1 * ng + g]), xu, ga1);
+        ua1 = unit_dot(u1r[u], bf16_bits(us16[j1 * ng + g]), bf16_bits(ub16[j1 * ng + g]), xu, ua1);
+      }
+    }
+    warp_sum4(ga0, ua0, ga1, ua1);
+    if (lane < 2) {
+      const float ga = lane ? ga1 : ga0, ua = lane ? ua1 : ua0;
+      float h;
+      if (is_shared) {
+        const float gbv = round_bf16(ga), ubv = round_bf16(ua);
+        h = round_bf16(round_bf16(gbv / (1.f + expf(-gbv))) * ubv);
+      } else {
+        h = ga / (1.f + expf(-ga)) * ua;
+      }
+      a.h_buf[(int64_t)q * a.I + n0 + j0 + lane] = h;
+    }
+  }
+}
+
+// o[entry, m] = w * (D h) for the run's entries over GD_ROWS hidden rows; the shared expert's gated value
+// bf16(sh_gate * bf16(D_s h_s)) goes to out[r, m], which k_dec_rank_sum reads before overwriting it.
+template <int NUI>
+__global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down_g(DecodeArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ const uint8_t* s_base;
+  __shared__ int s_list[GRP_TOK];
+  __shared__ int s_n;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_routed = (int)(a.R * a.topk);
+  const int p = blockIdx.y;
+  const int m0 = blockIdx.x * GD_ROWS;
+  const int I = a.I, gs = a.gs, H = a.H;
+  const int nunits = I / 16, ng = I / gs;
+  const uint32_t wbytes = (uint32_t)GD_ROWS * I / 2, sbytes = (uint32_t)GD_ROWS * ng * 2;
+  uint8_t* dw = sm;
+  uint8_t* dsc = dw + wbytes;
+  uint8_t* db = dsc + sbytes;
+  XUnitS* hx = reinterpret_cast<XUnitS*>(db + sbytes);   // [GRP_TOK][nunits]
+  int32_t* s_ids = reinterpret_cast<int32_t*>(hx + GRP_TOK * nunits);
+  const bool is_shared = p >= n_routed;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    s_n = 0;
+    s_base = nullptr;
+  }
+  __syncthreads();
+  auto issue = [&](const uint8_t* base) {
+    mbar_expect_tx(&bar, wbytes + 2 * sbytes);
+    bulk_g2s(dw, base + a.o.dw + (int64_t)m0 * I / 2, wbytes, &bar);
+    bulk_g2s(dsc, base + a.o.dsc + (int64_t)m0 * ng * 2, sbytes, &bar);
+    bulk_g2s(db, base + a.o.db + (int64_t)m0 * ng * 2, sbytes, &bar);
+  };
+  // The weights are staged before the wait on the gate_up grid: the expert ids were written before that grid
+  // started, and every grid here triggers its dependents only after its own wait, so they are visible now.
+  if (is_shared) {
+    const int occ = p - n_routed;
+    if (occ % GRP_TOK) return;
+    if (tid == 0) {
+      const int n = (int)(a.R - occ) < GRP_TOK ? (int)(a.R - occ) : GRP_TOK;
+      for (int i = 0; i < n; ++i) s_list[i] = p + i;
+      s_n = n;
+      s_base = a.shared_rec;
+      issue(a.shared_rec);
+    }
+  } else {
+    for (int q = tid; q < n_routed; q += blockDim.x) s_ids[q] = ld_cg_i32(a.ids + q);
+    __syncthreads();
+    if (warp == 0) {
+      const int n = group_run(s_ids, n_routed, p, s_list, lane);
+      if (lane == 0 && n) {
+        const uint8_t* base = a.bases ? (const uint8_t*)ld_cg_i64(a.bases + p)
+                                      : resolve_expert(s_ids[p], a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots,
+                                                       nullptr);
+        s_base = base;
+        s_n = n;
+        if (base) issue(base);
+      }
+    }
+  }
+  __syncthreads();
+  const int n = s_n;
+  if (n == 0) return;
+  pdl_wait();
+  pdl_trigger();
+  const uint8_t* base = s_base;
+  if (!base) {   // an unmapped routed expert contributes zero
+    for (int idx = tid; idx < n * GD_ROWS; idx += blockDim.x)
+      a.o_buf[(int64_t)s_list[idx / GD_ROWS] * H + m0 + idx % GD_ROWS] = 0.f;
+    return;
+  }
+  // the run's activations h in the pre-scaled per-unit form (h was written by the gate_up grid)
+  for (int idx = tid; idx < n * nunits; idx += DN_WARPS * 32) {
+    const int t = idx / nunits, u = idx - t * nunits;
+    const float4* hp = reinterpret_cast<const float4*>(a.h_buf + (int64_t)s_list[t] * I + u * 16);
+    float h16[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = __ldcg(hp + q);
+      h16[4 * q] = v.x;
+      h16[4 * q + 1] = v.y;
+      h16[4 * q + 2] = v.z;
+      h16[4 * q + 3] = v.w;
+    }
+    XUnit xu;
+    xunit_from_f32(xu, h16);
+    XUnitS& d = hx[idx];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d.v[q] = xu.v[q];
+    d.sum = xu.sum;
+  }
+  __syncthreads();
+  if (!mbar_wait(&bar, 0, SSB_WAIT_LIMIT)) {
+    if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
+    mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
+    return;
+  }
+  constexpr int RPW = GD_ROWS / DN_WARPS;
+  for (int rr = 0; rr < RPW; ++rr) {
+    const int row = warp * RPW + rr;
+    const int m = m0 + row;
+    const uint2* wr = reinterpret_cast<const uint2*>(dw + (size_t)row * I / 2);
+    const uint16_t* sr = reinterpret_cast<const uint16_t*>(dsc) + row * ng;
+    const uint16_t* br = reinterpret_cast<const uint16_t*>(db) + row * ng;
+    float d[GRP_TOK];
+#pragma unroll
+    for (int t = 0; t < GRP_TOK; ++t) {
+      d[t] = 0.f;
+      if (t < n) {
+#pragma unroll
+        for (int i = 0; i < NUI; ++i) {
+          const int u = lane + 32 * i;
+          if (u < nunits) {
+            const XUnitS& xs = hx[t * nunits + u];
+            XUnit xu;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) xu.v[q] = xs.v[q];
+            xu.sum = xs.sum;
+            const int g = (u * 16) / gs;
+            d[t] = unit_dot(wr[u], bf16_bits(sr[g]), bf16_bits(br[g]), xu, d[t]);
+          }
+        }
+      }
+    }
+    warp_sum4(d[0], d[1], d[2], d[3]);
+    warp_sum4(d[4], d[5], d[6], d[7]);
+    float v = d[0];
+#pragma unroll
+    for (int t = 1; t < GRP_TOK; ++t) v = lane == t ? d[t] : v;
+    if (lane < n) {
+      const int q = s_list[lane];
+      if (is_shared) {
+        const int64_t r = q - n_routed;
+        a.out[r * H + m] = round_bf16(a.sh_gate[r] * round_bf16(v));
+      } else {
+        a.o_buf[(int64_t)q * H + m] = v * a.wts[q];   // acc * w, kernels/moe_gemv_affine.py:96-97
+      }
+    }
+  }
+}
+
+// out[r, :] = o[r, 0, :] + o[r, 1, :] + ... in rank order (kernels/moe_gemv_affine.py:100-110); with the
+// shared expert, y = bf16(bf16(out) + sh) where sh is the value k_dec_down_g left in out.
+__global__ void __launch_bounds__(256) k_dec_rank_sum(DecodeArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i4 = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i4 * 4 >= a.R * a.H) return;
+  const int64_t r = i4 * 4 / a.H, m = i4 * 4 - r * a.H;
+  const float4* o = reinterpret_cast<const float4*>(a.o_buf + r * a.topk * a.H + m);
+  const int64_t st4 = a.H / 4;
+  float4 acc = __ldcg(o);
+  for (int j = 1; j < a.topk; ++j) {
+    const float4 v = __ldcg(o + j * st4);
+    acc.x = acc.x + v.x;
+    acc.y = acc.y + v.y;
+    acc.z = acc.z + v.z;
+    acc.w = acc.w + v.w;
+  }
+  float4* out = reinterpret_cast<float4*>(a.out + r * a.H + m);
+  if (a.y) {
+    const float4 sh = __ldcg(out);
+    uint2 yv;
+    yv.x = (uint32_t)f32_to_bf16(round_bf16(acc.x) + sh.x) | ((uint32_t)f32_to_bf16(round_bf16(acc.y) + sh.y) << 16);
+    yv.y = (uint32_t)f32_to_bf16(round_bf16(acc.z) + sh.z) | ((uint32_t)f32_to_bf16(round_bf16(acc.w) + sh.w) << 16);
+    *reinterpret_cast<uint2*>(a.y + r * a.H + m) = yv;
+  }
+  *out = acc;
+}
+
+int launch_decode_grouped(DecodeArgs a, cudaStream_t st, bool pdl) {
+  const int nux = (a.H / 16 + 31) / 32;
+  const int nui = (a.I / 16 + 31) / 32;
+  const int64_t n_routed = a.R * a.topk;
+  const int64_t pairs = n_routed + (a.shared_rec ? a.R : 0);
+  const size_t ids_bytes = (size_t)n_routed * 4;
+  const size_t gu_smem = (size_t)2 * GU_ROWS * a.H / 2 + (size_t)4 * GU_ROWS * (a.H / a.gs) * 2 + ids_bytes;
+  const size_t dn_smem = (size_t)GD_ROWS * a.I / 2 + (size_t)2 * GD_ROWS * (a.I / a.gs) * 2 +
+                         (size_t)GRP_TOK * (a.I / 16) * sizeof(XUnitS) + ids_bytes;
+  if (gu_smem > 200 * 1024 || dn_smem > 200 * 1024) return SSB_EUNSUPPORTED;
+  void (*gu)(DecodeArgs) = nullptr;
+  void (*dn)(DecodeArgs) = nullptr;
+  switch (nux) {
+    case 1: gu = k_dec_gate_up_g<1>; break;
+    case 2: gu = k_dec_gate_up_g<2>; break;
+    case 3: gu = k_dec_gate_up_g<3>; break;
+    case 4: gu = k_dec_gate_up_g<4>; break;
+    case 5: gu = k_dec_gate_up_g<5>; break;
+    case 6: gu = k_dec_gate_up_g<6>; break;
+    case 8: gu = k_dec_gate_up_g<8>; break;
+    default: return SSB_EUNSUPPORTED;
+  }
+  switch (nui) {
+    case 1: dn = k_dec_down_g<1>; break;
+    case 2: dn = k_dec_down_g<2>; break;
+    case 3: dn = k_dec_down_g<3>; break;
+    case 4: dn = k_dec_down_g<4>; break;
+    default: return SSB_EUNSUPPORTED;
+  }
+  cudaFuncSetAttribute(gu, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gu_smem);
+  cudaFuncSetAttribute(dn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem);
+  ssb_note_smem("moe_gate_up_grouped", gu, gu_smem);
+  ssb_note_smem("moe_down_grouped", dn, dn_smem);
+  int rc = ssb_launch(gu, dim3(a.I / GU_ROWS, (unsigned)pairs), dim3(GU_WARPS * 32), gu_smem, st, pdl, a);
+  if (rc) return rc;
+  rc = ssb_launch(dn, dim3(a.H / GD_ROWS, (unsigned)pairs), dim3(DN_WARPS * 32), dn_smem, st, true, a);
+  if (rc) return rc;
+  const int64_t n4 = a.R * a.H / 4;
+  return ssb_launch(k_dec_rank_sum, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, st, true, a);
+}
+
 int launch_decode(DecodeArgs a, cudaStream_t st, bool pdl) {
+  if (a.R >= 3 && a.o_buf && a.R * a.topk <= GRP_MAX && a.H % GD_ROWS == 0 && a.I % 16 == 0) {
+    const int rc = launch_decode_grouped(a, st, pdl);
+    if (rc != SSB_EUNSUPPORTED) return rc;
+  }
   const int nux = (a.H / 16 + 31) / 32;
   const int nui = (a.I / 16 + 31) / 32;
   const int nexp = a.topk + (a.shared_rec ? 1 : 0);

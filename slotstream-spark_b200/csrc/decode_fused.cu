@@ -58,6 +58,8 @@ struct FusedArgs {
   uint32_t* sync;      // [2]
   int32_t* err;
   int stage_pairs;     // gate/up row pairs one staging round of a CTA holds
+  int down_stage;      // 1: this CTA's down rows of every entry are bulk-copied into shared memory after select
+  uint32_t dstage_off; // their offset in the dynamic shared memory
 };
 
 struct __align__(16) XUnitS {
@@ -127,7 +129,7 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   __shared__ float s_shg[F_MAXR];
   __shared__ SelectScratch<EPL> s_sel[F_MAXR];
   __shared__ float s_red[F_MAXR][FW];
-  __shared__ uint64_t s_bar;
+  __shared__ uint64_t s_bar, s_bar_d;
   __shared__ int s_seg_p[4], s_seg_q0[4], s_seg_n[4];
   __shared__ uint32_t s_seg_off[4];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -141,8 +143,10 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   const uint8_t** bases = reinterpret_cast<const uint8_t**>(xu_s + (size_t)F_MAXR * nux);
   uint8_t* stage = reinterpret_cast<uint8_t*>(bases + F_MAXE);
   XUnitS* hx = reinterpret_cast<XUnitS*>(stage);
+  uint8_t* dstage = sm + a.dstage_off;
   if (tid == 0) {
     mbar_init(&s_bar, 1);
+    mbar_init(&s_bar_d, 1);
     fence_mbar_init();
   }
 
@@ -302,7 +306,25 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
   if (blockIdx.x == 0 && tid < R) a.out_sh_gate[tid] = s_shg[tid];
   // this CTA's output columns, and L2 prefetches of their down rows (needed after the next barrier)
   const int c0 = (int)((int64_t)blockIdx.x * H / gridDim.x), c1 = (int)((int64_t)(blockIdx.x + 1) * H / gridDim.x);
-  for (int pe = lane; warp == FW - 1 && pe < P && c1 > c0; pe += 32) {
+  const int ncol = c1 - c0;
+  const int ngd = I / gs;
+  const uint32_t d_ebytes = (uint32_t)ncol * ((uint32_t)I / 2 + 2u * (uint32_t)ngd * 2u);   // one entry's down rows
+  if (a.down_stage && tid == 32) {   // every entry's rows c0 .. c1-1 of D (codes, scales, biases) into dstage
+    uint32_t bytes = 0;
+    for (int pe = 0; pe < P; ++pe)
+      if (entry_base(pe) && ncol > 0) bytes += d_ebytes;
+    mbar_expect_tx(&s_bar_d, bytes);
+    for (int pe = 0; pe < P && ncol > 0; ++pe) {
+      const uint8_t* base = entry_base(pe);
+      if (!base) continue;
+      uint8_t* d = dstage + (size_t)pe * d_ebytes;
+      bulk_g2s(d, base + a.o.dw + (int64_t)c0 * I / 2, (uint32_t)ncol * I / 2, &s_bar_d);
+      bulk_g2s(d + ncol * I / 2, base + a.o.dsc + (int64_t)c0 * ngd * 2, (uint32_t)ncol * ngd * 2, &s_bar_d);
+      bulk_g2s(d + ncol * I / 2 + ncol * ngd * 2, base + a.o.db + (int64_t)c0 * ngd * 2, (uint32_t)ncol * ngd * 2,
+               &s_bar_d);
+    }
+  }
+  for (int pe = lane; !a.down_stage && warp == FW - 1 && pe < P && c1 > c0; pe += 32) {
     const uint8_t* base = entry_base(pe);
     if (base) {
       const int ng = I / gs;
@@ -367,9 +389,10 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
       }
       __syncthreads();
       // every thread waits for the copies; a CTA-wide decision to give up keeps the barrier below reachable
-      if (__syncthreads_or(!mbar_wait(&s_bar, (uint32_t)(round & 1), SSB_WAIT_LIMIT))) {
+      if (__syncthreads_or(!mbar_wait_spin(&s_bar, (uint32_t)(round & 1), SSB_WAIT_NS))) {
         if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
-        mbar_wait(&s_bar, (uint32_t)(round & 1), SSB_WAIT_LIMIT);   // let the copies land before leaving
+        mbar_wait_spin(&s_bar, (uint32_t)(round & 1), SSB_WAIT_NS);   // let the copies land before leaving
+        if (a.down_stage) mbar_wait_spin(&s_bar_d, 0, SSB_WAIT_NS);
         return;
       }
       for (int64_t it = r0 + warp; it < r1; it += FW) {
@@ -444,6 +467,11 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
     }
     xunit_store(hx[idx], v16);
   }
+  if (a.down_stage && __syncthreads_or(!mbar_wait_spin(&s_bar_d, 0, SSB_WAIT_NS))) {
+    if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
+    mbar_wait_spin(&s_bar_d, 0, SSB_WAIT_NS);
+    return;
+  }
   __syncthreads();
   const int ng4 = I / gs;
   for (int m = c0 + warp; m < c1; m += FW) {
@@ -469,9 +497,20 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
             wv[jj][i] = make_uint2(0u, 0u);
             sc[jj][i] = bi[jj][i] = 0.f;
             if (eb[jj] && u < nui) {
-              wv[jj][i] = __ldcg(reinterpret_cast<const uint2*>(eb[jj] + a.o.dw + (int64_t)m * I / 2) + u);
-              sc[jj][i] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(eb[jj] + a.o.dsc) + (int64_t)m * ng4 + g));
-              bi[jj][i] = bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(eb[jj] + a.o.db) + (int64_t)m * ng4 + g));
+              if (a.down_stage) {   // row m - c0 of the entry's staged codes, scales and biases
+                const uint8_t* d = dstage + (size_t)p * d_ebytes;
+                const int mi = m - c0;
+                wv[jj][i] = reinterpret_cast<const uint2*>(d + (size_t)mi * I / 2)[u];
+                sc[jj][i] = bf16_bits(reinterpret_cast<const uint16_t*>(d + (size_t)ncol * I / 2)[mi * ng4 + g]);
+                bi[jj][i] = bf16_bits(
+                    reinterpret_cast<const uint16_t*>(d + (size_t)ncol * I / 2 + (size_t)ncol * ng4 * 2)[mi * ng4 + g]);
+              } else {
+                wv[jj][i] = __ldcg(reinterpret_cast<const uint2*>(eb[jj] + a.o.dw + (int64_t)m * I / 2) + u);
+                sc[jj][i] =
+                    bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(eb[jj] + a.o.dsc) + (int64_t)m * ng4 + g));
+                bi[jj][i] =
+                    bf16_bits(__ldcg(reinterpret_cast<const uint16_t*>(eb[jj] + a.o.db) + (int64_t)m * ng4 + g));
+              }
             }
           }
         }
@@ -580,8 +619,14 @@ extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t top
   if (stage_pairs < 1) return SSB_EUNSUPPORTED;
   size_t stage_b = (size_t)stage_pairs * pair_b;
   if (stage_b < fused_hx_bytes(inter)) stage_b = fused_hx_bytes(inter);
-  const size_t smem = fixed + stage_b;
+  size_t smem = fixed + stage_b;
   if (smem > 212 * 1024) return SSB_EUNSUPPORTED;   // with the static scratch, one CTA per SM must still fit
+  // the down rows of every entry for this CTA's output columns, when they fit beside the stage
+  const int max_cols = (hidden + sms0 - 1) / sms0;
+  const size_t dstage_b = (size_t)rows * (topk + 1) * max_cols * ((size_t)inter / 2 + 2 * (size_t)(inter / 64) * 2);
+  const int down_stage = fixed + stage_b + dstage_b <= 212 * 1024 ? 1 : 0;
+  const uint32_t dstage_off = (uint32_t)(fixed + stage_b);
+  if (down_stage) smem += dstage_b;
   // per (device, kernel) setup once: the dynamic shared-memory attribute (raised when a call needs more), an
   // occupancy check, the SM count (host calls that would otherwise sit between every launch)
   struct Prepared {
@@ -642,6 +687,8 @@ extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t top
   a.sync = sync;
   a.err = err;
   a.stage_pairs = (int)stage_pairs;
+  a.down_stage = down_stage;
+  a.dstage_off = dstage_off;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sms);   // one CTA per SM: all resident (the launch fails otherwise)
   cfg.blockDim = dim3(FT);

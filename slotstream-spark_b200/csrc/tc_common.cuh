@@ -139,3 +139,25 @@ SSB_DEV bool mbar_wait_ns(uint64_t* bar, uint32_t parity, uint64_t ns) {
   }
 }
 constexpr uint64_t SSB_WAIT_NS = 250ull * 1000 * 1000;   // 250 ms: far above any stage time
+
+// As mbar_wait_ns, polling with test_wait (no suspension): for one-shot waits on a latency-critical path, where
+// a suspended thread's wake-up would add to the critical path.
+SSB_DEV bool mbar_wait_spin(uint64_t* bar, uint32_t parity, uint64_t ns) {
+  const uint32_t a = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 1023u) == 0u) {
+      uint64_t t = globaltimer_ns();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > ns) return false;
+    }
+  }
+}

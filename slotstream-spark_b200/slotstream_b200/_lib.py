@@ -41,6 +41,13 @@ SIGNATURES = {
     "ssb_ep_combine": [_P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
     "ssb_moe_decode_fused": [_P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _P,
                              _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    "ssb_pool_create": [_I64, _I64, _I32, _I32, _I32],
+    "ssb_pool_destroy": [_P],
+    "ssb_pool_resize": [_P, _I32],
+    "ssb_pool_tables": [_P, _P, _P, _P, _P, _P],
+    "ssb_pool_ensure": [_P, _I32, _P, _I32, _P, _P, _P, _P, _P],
+    "ssb_pool_release": [_P, _P],
+    "ssb_pool_counters": [_P, _P, _P, _P],
     "ssb_router_topk_static": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P],
     "ssb_combine_rank_order": [_P, _I64, _I32, _I32, _P, _P],
     "ssb_combine_layer": [_P, _I64, _I32, _I32, _P, _P, _P, _P],
@@ -73,6 +80,8 @@ def lib():
             f.restype = ctypes.c_int
         h.ssb_version.argtypes = []
         h.ssb_version.restype = ctypes.c_char_p
+        h.ssb_pool_create.restype = ctypes.c_void_p
+        h.ssb_pool_destroy.restype = None
         _lib = h
     return _lib
 
@@ -92,7 +101,7 @@ def stream():
 
 _NAMES = {SSB_EINVAL: "SSB_EINVAL (bad argument)", SSB_EUNSUPPORTED: "SSB_EUNSUPPORTED (shape not handled)",
           SSB_ENODEVICE: "SSB_ENODEVICE (not an sm_100 device)",
-          SSB_ETOOBIG: "SSB_ETOOBIG (request exceeds the fixed static scratch of the entry point)"}
+          SSB_ETOOBIG: "SSB_ETOOBIG (request exceeds a fixed capacity: static scratch or slot pool)"}
 
 
 def check(rc, what):

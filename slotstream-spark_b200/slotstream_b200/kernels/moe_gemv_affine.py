@@ -61,8 +61,8 @@ def moe_decode(x, expert_ids, weights, layer: int, map_t, slot_ptr_t, h_buf, o_b
         r, topk, hid, inter, int(layer), _lib.ptr(map_t), map_t.numel(), _lib.ptr(slot_ptr_t), slot_ptr_t.numel(),
         _lib.ptr(h_buf), _lib.ptr(o_buf), _lib.ptr(out), _lib.ptr(err), _lib.stream())
     _lib.check(rc, "moe_decode")
-    _note("moe_gate_up")
-    _note("moe_down")
+    for name in ("moe_gate_up", "moe_down", "moe_gate_up_grouped", "moe_down_grouped"):
+        _note(name)
     return out
 
 

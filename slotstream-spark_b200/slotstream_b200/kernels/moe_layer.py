@@ -162,6 +162,6 @@ def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, 
         _lib.ptr(bufs.bases), _lib.ptr(bufs.h), _lib.ptr(bufs.o), _lib.ptr(bufs.out), _lib.ptr(bufs.y),
         _lib.DECODE_PDL if pdl else 0, _lib.ptr(bufs.err), st)
     _lib.check(rc, "moe_decode_layer")
-    _note("moe_gate_up")
-    _note("moe_down")
+    for name in ("moe_gate_up", "moe_down", "moe_gate_up_grouped", "moe_down_grouped"):
+        _note(name)
     return bufs.y

@@ -112,6 +112,29 @@ def test_row_invariance_and_duplicates():
         assert torch.equal(one[0], out[r])
 
 
+def test_grouped_runs_equal_single_rows():
+    """20 rows: experts 0..4 chosen by every row (runs of 8, 8, 4 entries), an unmapped id in two rows, the
+    rest random. Each row equals its own one-row call bit for bit, and the unmapped choice sets the error."""
+    lay = BASELINE_LAYOUT
+    recs = _experts(lay, 16)
+    pool = DevicePool(lay, recs, range(16), list(range(16)), 16, LAYER)
+    R = 20
+    x, ids, w = _inputs(lay, R, 8, 16)
+    rng = np.random.default_rng(8)
+    ids_np = np.stack([np.concatenate([np.arange(5), 5 + rng.permutation(11)[:5]]) for _ in range(R)]).astype(np.int32)
+    ids_np[3, 7] = ids_np[11, 2] = 300
+    ids = torch.from_numpy(ids_np).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out, o = _run(pool, x, ids, w, err=err)
+    assert int(err.item()) & 2
+    for r in range(R):
+        e1 = torch.zeros(1, dtype=torch.int32, device="cuda")
+        one, o1 = _run(pool, x[r:r + 1].contiguous(), ids[r:r + 1].contiguous(), w[r:r + 1].contiguous(), err=e1)
+        assert torch.equal(one[0], out[r]), r
+        assert torch.equal(o1[0], o[r]), r
+    assert torch.all(o[3, 7] == 0) and torch.all(o[11, 2] == 0)
+
+
 def test_config_errors():
     lay = BASELINE_LAYOUT
     recs = _experts(lay, 16)
