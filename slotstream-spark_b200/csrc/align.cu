@@ -14,6 +14,7 @@ namespace {
 constexpr int AL_WARPS = 32;
 constexpr int AL_THREADS = AL_WARPS * 32;
 constexpr int AL_MAX_LOCAL = 1280;
+constexpr int AL_UNR = 16;      // 32-row batches whose loads one warp keeps in flight
 
 SSB_DEV int local_of(const int32_t* __restrict__ row_expert, const int32_t* __restrict__ emap, int map_len,
                      int64_t i) {
@@ -40,10 +41,17 @@ __global__ void __launch_bounds__(AL_THREADS) k_moe_align(const int32_t* __restr
   const int64_t lo0 = (int64_t)warp * chunk;
   const int64_t lo = lo0 < R ? lo0 : R, hi = lo + chunk < R ? lo + chunk : R;
   int* mycnt = cnt + warp * NL;
-  for (int64_t base = lo; base < hi; base += 32) {
-    int64_t i = base + lane;
-    int v = i < hi ? local_of(row_expert, emap, map_len, i) : -1;
-    if (v >= 0 && v < NL) atomicAdd(&mycnt[v], 1);
+  // AL_UNR batches of 32 rows per step: their loads are issued together, then the batches are used in order
+  for (int64_t base = lo; base < hi; base += 32 * AL_UNR) {
+    int v[AL_UNR];
+#pragma unroll
+    for (int j = 0; j < AL_UNR; ++j) {
+      const int64_t i = base + 32 * j + lane;
+      v[j] = i < hi ? local_of(row_expert, emap, map_len, i) : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < AL_UNR; ++j)
+      if (v[j] >= 0 && v[j] < NL) atomicAdd(&mycnt[v[j]], 1);
   }
   __syncthreads();
   for (int e = tid; e < NL; e += AL_THREADS) {
@@ -80,17 +88,26 @@ __global__ void __launch_bounds__(AL_THREADS) k_moe_align(const int32_t* __restr
     cnt[i] += pend[e] - padded;
   }
   __syncthreads();
-  for (int64_t base = lo; base < hi; base += 32) {
-    int64_t i = base + lane;
-    int v = i < hi ? local_of(row_expert, emap, map_len, i) : -1;
-    bool valid = v >= 0 && v < NL;
-    int key = valid ? v : -1 - lane;  // invalid lanes never match anyone
-    unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
-    unsigned below = peers & lanemask_lt();
-    if (valid) sorted_rows[mycnt[v] + __popc(below)] = (int32_t)i;
-    __syncwarp();
-    if (valid && below == 0) mycnt[v] += __popc(peers);
-    __syncwarp();
+  for (int64_t base = lo; base < hi; base += 32 * AL_UNR) {
+    int vv[AL_UNR];
+#pragma unroll
+    for (int j = 0; j < AL_UNR; ++j) {
+      const int64_t i = base + 32 * j + lane;
+      vv[j] = i < hi ? local_of(row_expert, emap, map_len, i) : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < AL_UNR; ++j) {   // batches in row order, rows in lane order: the sort stays stable
+      const int64_t i = base + 32 * j + lane;
+      const int v = vv[j];
+      bool valid = v >= 0 && v < NL;
+      int key = valid ? v : -1 - lane;  // invalid lanes never match anyone
+      unsigned peers = __match_any_sync(0xFFFFFFFFu, key);
+      unsigned below = peers & lanemask_lt();
+      if (valid) sorted_rows[mycnt[v] + __popc(below)] = (int32_t)i;
+      __syncwarp();
+      if (valid && below == 0) mycnt[v] += __popc(peers);
+      __syncwarp();
+    }
   }
   // padding inside each expert's span, then the tail past num_padded
   for (int e = tid; e < NL; e += AL_THREADS) {

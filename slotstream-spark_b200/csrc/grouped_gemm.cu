@@ -42,6 +42,8 @@ constexpr uint32_t B_STAGE = BN * 128;           // 16 KB
 constexpr uint32_t W_STG = BN * SS * 32;         // codes of a super-step: 128 rows x 128 B, 16-byte pieces swizzled
 constexpr uint32_t SB_STG = N_PROD * 32;         // per producer thread: its row's scales (16 B) and biases (16 B)
 constexpr uint32_t STG = W_STG + SB_STG;         // one staging slot; two slots alternate
+constexpr int EPI_LD = 36;                        // fp32 epilogue transpose buffer: 32 rows of 32 (+4) floats
+constexpr uint32_t EPI_BYTES = 4 * 32 * EPI_LD * 4;   // one buffer per epilogue warp
 constexpr uint32_t TMEM_COLS = 512;              // 2 buffers x 2 halves of M128 x N128 fp32 accumulators
 
 enum { EPI_SWIGLU = 0, EPI_SCALE = 1, EPI_PLAIN = 2 };
@@ -79,6 +81,7 @@ struct Smem {
   uint8_t* a;
   uint8_t* b;
   uint8_t* stg;
+  float* epi;
   uint64_t* full_a;
   uint64_t* full_b;
   uint64_t* empty;
@@ -87,7 +90,7 @@ struct Smem {
   uint32_t* tmem;
 };
 
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 2 * STG + 8 * (3 * STAGES + 4) + 16;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + 2 * STG + EPI_BYTES + 8 * (3 * STAGES + 4) + 16;
 
 SSB_DEV Smem carve(uint8_t* raw) {
   Smem s;
@@ -98,6 +101,8 @@ SSB_DEV Smem carve(uint8_t* raw) {
   p += STAGES * B_STAGE;
   s.stg = p;
   p += 2 * STG;
+  s.epi = (float*)p;
+  p += EPI_BYTES;
   s.full_a = (uint64_t*)p;
   s.full_b = s.full_a + STAGES;
   s.empty = s.full_b + STAGES;
@@ -377,29 +382,39 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
             }
           }
         } else {
+          // fp32 rows: each 32-row x 32-column chunk goes through this warp's transpose buffer so that eight
+          // lanes store one row's 128 contiguous bytes (four rows per store instruction) instead of every lane
+          // storing 16 bytes of its own row
           float* out = (float*)a.out;
+          float* tb = S.epi + q * (32 * EPI_LD);
 #pragma unroll 1
           for (int cc = 0; cc < BN / 32; ++cc) {
             const int col = 32 * cc;
             float v[32];
             tmem_ld32(taddr + col, v);
-            if (valid) {
-              float4* dst = reinterpret_cast<float4*>(out + row * a.ldo + (int64_t)nb * BN + col);
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                float4 o;
-                if (EPI == EPI_SCALE && shared_e) {   // bf16(sigmoid gate * bf16(h D^T))
-                  o = make_float4(round_bf16(wt * round_bf16(v[4 * jj])), round_bf16(wt * round_bf16(v[4 * jj + 1])),
-                                  round_bf16(wt * round_bf16(v[4 * jj + 2])),
-                                  round_bf16(wt * round_bf16(v[4 * jj + 3])));
-                } else if (EPI == EPI_SCALE) {
-                  o = make_float4(v[4 * jj] * wt, v[4 * jj + 1] * wt, v[4 * jj + 2] * wt, v[4 * jj + 3] * wt);
-                } else {
-                  o = make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
-                }
-                dst[jj] = o;
+            for (int jj = 0; jj < 8; ++jj) {
+              float4 o;
+              if (EPI == EPI_SCALE && shared_e) {   // bf16(sigmoid gate * bf16(h D^T))
+                o = make_float4(round_bf16(wt * round_bf16(v[4 * jj])), round_bf16(wt * round_bf16(v[4 * jj + 1])),
+                                round_bf16(wt * round_bf16(v[4 * jj + 2])), round_bf16(wt * round_bf16(v[4 * jj + 3])));
+              } else if (EPI == EPI_SCALE) {
+                o = make_float4(v[4 * jj] * wt, v[4 * jj + 1] * wt, v[4 * jj + 2] * wt, v[4 * jj + 3] * wt);
+              } else {
+                o = make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
               }
+              *reinterpret_cast<float4*>(tb + lane * EPI_LD + 4 * jj) = o;
             }
+            __syncwarp();
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int rr = 4 * it + (lane >> 3), c4 = 4 * (lane & 7);
+              const int64_t rrow = __shfl_sync(0xFFFFFFFFu, row, rr);
+              const float4 o = *reinterpret_cast<const float4*>(tb + rr * EPI_LD + c4);
+              if (rrow >= 0 && rrow < a.R)
+                *reinterpret_cast<float4*>(out + rrow * a.ldo + (int64_t)nb * BN + col + c4) = o;
+            }
+            __syncwarp();
           }
         }
       }
@@ -599,6 +614,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
 // x_sorted[m, :] = x[row_token[sorted_rows[m]], :] for m < num_padded (zero rows for padding), one warp per row:
 // the activation rows in expert order, so the grouped GEMM reads its A tiles as whole 2-D boxes, with every group
 // of 8 columns in the K order (0,4,1,5,2,6,3,7) in which the sorted GEMMs dequantise their weights.
+constexpr int PERM_UNR = 8;   // 16-byte chunks per lane in flight in k_permute_rows
+
 __global__ void __launch_bounds__(256) k_permute_rows(const uint4* __restrict__ x, int64_t x_rows, int64_t row_vecs,
                                                       const int32_t* __restrict__ row_token,
                                                       const int32_t* __restrict__ sorted_rows,
@@ -609,12 +626,33 @@ __global__ void __launch_bounds__(256) k_permute_rows(const uint4* __restrict__ 
   const int lane = threadIdx.x & 31;
   const int64_t np = __ldcg(num_padded);
   const int64_t n = np < padded_len ? np : padded_len;
-  for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < n; m += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+  const int64_t step = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  // the source token of a sorted row (-1: padding or a bad row)
+  auto token_of = [&](int64_t m) -> int64_t {
+    if (m >= n) return -1;
     const int64_t r = __ldcg(sorted_rows + m);
     const int64_t t = (r >= 0 && r < R) ? (int64_t)__ldcg(row_token + r) : -1;
-    const bool ok = t >= 0 && t < x_rows;
-    for (int64_t c = lane; c < row_vecs; c += 32)   // each 16-byte chunk in the K order of the sorted GEMMs
-      out[m * row_vecs + c] = ok ? kperm8(__ldg(x + t * row_vecs + c)) : make_uint4(0, 0, 0, 0);
+    return t < x_rows ? t : -1;
+  };
+  int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t t = token_of(m);
+  for (; m < n; m += step) {
+    const int64_t t_next = token_of(m + step);   // the next row's index loads overlap this row's copy
+    // each 16-byte chunk in the K order of the sorted GEMMs; eight chunks per lane in flight at once
+    for (int64_t c0 = 0; c0 < row_vecs; c0 += 32 * PERM_UNR) {
+      uint4 v[PERM_UNR];
+#pragma unroll
+      for (int j = 0; j < PERM_UNR; ++j) {
+        const int64_t c = c0 + lane + 32 * j;
+        v[j] = (t >= 0 && c < row_vecs) ? __ldg(x + t * row_vecs + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < PERM_UNR; ++j) {
+        const int64_t c = c0 + lane + 32 * j;
+        if (c < row_vecs) out[m * row_vecs + c] = t >= 0 ? kperm8(v[j]) : make_uint4(0, 0, 0, 0);
+      }
+    }
+    t = t_next;
   }
 }
 

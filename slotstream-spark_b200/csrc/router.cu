@@ -74,6 +74,50 @@ __global__ void __launch_bounds__(RL_WARPS * 32) k_router_logits(const uint16_t*
   }
 }
 
+// One weight row (the shared-expert gate of a prefill chunk): a warp per token, x read straight from global
+// memory with all of a lane's chunks in flight at once; the same per-lane order and butterfly as above.
+constexpr int RL1_WARPS = 8;
+constexpr int RL1_TPW = 4;   // tokens per warp
+
+__global__ void __launch_bounds__(RL1_WARPS * 32) k_router_logits_row(const uint16_t* __restrict__ x,
+                                                                      const uint16_t* __restrict__ w, int64_t tokens,
+                                                                      int hidden, int ld, float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cpl = (hidden >> 3) >> 5;
+  uint4 wr[RL_MAXC];
+#pragma unroll
+  for (int i = 0; i < RL_MAXC; ++i)
+    if (i < cpl) wr[i] = ld_stream_u4(w + (size_t)(lane + 32 * i) * 8);
+  pdl_wait();
+  pdl_trigger();
+  const int64_t t0 = ((int64_t)blockIdx.x * RL1_WARPS + warp) * RL1_TPW;
+  for (int tt = 0; tt < RL1_TPW; ++tt) {
+    const int64_t t = t0 + tt;
+    if (t >= tokens) break;
+    uint4 xv[RL_MAXC];
+#pragma unroll
+    for (int i = 0; i < RL_MAXC; ++i)
+      if (i < cpl) xv[i] = __ldg(reinterpret_cast<const uint4*>(x + t * hidden) + lane + 32 * i);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < RL_MAXC; ++i) {
+      if (i < cpl) {
+        const uint4 a = xv[i], b = wr[i];
+        acc = fmaf(bf16_lo(b.x), bf16_lo(a.x), acc);
+        acc = fmaf(bf16_hi(b.x), bf16_hi(a.x), acc);
+        acc = fmaf(bf16_lo(b.y), bf16_lo(a.y), acc);
+        acc = fmaf(bf16_hi(b.y), bf16_hi(a.y), acc);
+        acc = fmaf(bf16_lo(b.z), bf16_lo(a.z), acc);
+        acc = fmaf(bf16_hi(b.z), bf16_hi(a.z), acc);
+        acc = fmaf(bf16_lo(b.w), bf16_lo(a.w), acc);
+        acc = fmaf(bf16_hi(b.w), bf16_hi(a.w), acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[t * ld] = acc;
+  }
+}
+
 // ------------------------------------------------------------------ select (softmax + top-k + renorm)
 constexpr int RS_WARPS = 4;
 // warps (tokens) per select CTA: the per-warp scratch of 1024 experts allows two within 48 KB
@@ -296,6 +340,12 @@ extern "C" int ssb_router_logits(const uint16_t* x, const uint16_t* w, const uin
   SSB_CHECK_ARG(ld >= n_rows + (w_extra ? 1 : 0));
   if (tokens == 0) return SSB_OK;
   const int n_total = n_rows + (w_extra ? 1 : 0);
+  if (n_total == 1 && tokens >= 1024) {   // one row over many tokens: no staging of x, a warp per token
+    const int64_t per_cta = (int64_t)RL1_WARPS * RL1_TPW;
+    ssb_note_smem("router_logits", k_router_logits_row, 0);
+    return ssb_launch(k_router_logits_row, dim3((unsigned)((tokens + per_cta - 1) / per_cta)), dim3(RL1_WARPS * 32), 0,
+                      (cudaStream_t)stream, true, x, w_extra ? w_extra : w, tokens, hidden, ld, logits);
+  }
   dim3 grid((n_total + RL_WARPS - 1) / RL_WARPS, (unsigned)((tokens + RL_TT - 1) / RL_TT));
   SSB_CHECK_ARG(grid.y <= 65535u);
   size_t smem = (size_t)RL_TT * hidden * 2;

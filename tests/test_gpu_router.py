@@ -80,6 +80,28 @@ def test_router_logits_are_fp32_exact_sums():
     assert np.max(np.abs(got - ref)) < 2e-5
 
 
+def test_single_row_logits_equal_staged_kernel():
+    """One weight row over >= 1024 tokens (the prefill shared gate) takes the warp-per-token kernel; its sums are
+    the bits of the staged kernel that shorter calls use."""
+    from slotstream_b200 import _lib
+    T = 2048
+    x, _, sg = _router_inputs(T, seed=3)
+    xt, sgt = bf16_tensor(x), bf16_tensor(sg)
+    ld = 5
+    big = torch.full((T * ld,), -1.0, dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().ssb_router_logits(xt.data_ptr(), sgt.data_ptr(), None, T, 2048, 1, ld, big.data_ptr(),
+                                            _lib.stream()), "router_logits")
+    small = torch.full((T * ld,), -1.0, dtype=torch.float32, device="cuda")
+    for t0 in range(0, T, 512):
+        _lib.check(_lib.lib().ssb_router_logits(xt[t0:].data_ptr(), sgt.data_ptr(), None, 512, 2048, 1, ld,
+                                                small[t0 * ld:].data_ptr(), _lib.stream()), "router_logits")
+    torch.cuda.synchronize()
+    assert torch.equal(big.view(T, ld)[:, 0], small.view(T, ld)[:, 0])
+    assert torch.all(big.view(T, ld)[:, 1:] == -1.0)
+    ref = O.bf16_to_f32(x).astype(np.float64) @ O.bf16_to_f32(sg).astype(np.float64).reshape(-1)
+    assert np.max(np.abs(big.view(T, ld)[:, 0].cpu().numpy() - ref)) < 2e-5
+
+
 @pytest.mark.parametrize("zipf", [False, True])
 @pytest.mark.parametrize("round_bf16", [False, True])
 def test_router_topk_matches_oracle(zipf, round_bf16):
