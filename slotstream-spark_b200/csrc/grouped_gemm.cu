@@ -656,6 +656,62 @@ __global__ void __launch_bounds__(256) k_permute_rows(const uint4* __restrict__ 
   }
 }
 
+// Row-order variant used inside ssb_prefill_experts: pos[r] = sorted position of row r (-1: dropped), then one
+// warp per row r in row order copies x[row_token[r]] to x_sorted[pos[r]]. Rows of one token are neighbours in
+// row order, so each activation row comes from DRAM about once instead of once per expert; padding rows of
+// x_sorted are not written (the GEMMs never store the results of padding rows).
+__global__ void __launch_bounds__(256) k_row_pos(const int32_t* __restrict__ sorted_rows,
+                                                 const int32_t* __restrict__ num_padded, int64_t R,
+                                                 int64_t padded_len, int32_t* __restrict__ pos) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t np = __ldcg(num_padded);
+  const int64_t n = np < padded_len ? np : padded_len;
+  for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < n; m += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = __ldcg(sorted_rows + m);
+    if (r >= 0 && r < R) pos[r] = (int32_t)m;
+  }
+}
+
+__global__ void __launch_bounds__(256) k_permute_by_row(const uint4* __restrict__ x, int64_t x_rows, int64_t row_vecs,
+                                                        const int32_t* __restrict__ row_token,
+                                                        const int32_t* __restrict__ pos, int64_t R,
+                                                        uint4* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t step = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  auto dest_of = [&](int64_t r, int64_t& t) -> int64_t {
+    if (r >= R) return -1;
+    const int64_t m = __ldcg(pos + r);
+    t = __ldg(row_token + r);
+    return (m >= 0 && t >= 0 && t < x_rows) ? m : -1;
+  };
+  int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t t = -1, m = dest_of(r, t);
+  for (; r < R; r += step) {
+    int64_t t_next = -1;
+    const int64_t m_next = dest_of(r + step, t_next);   // the next row's index loads overlap this row's copy
+    if (m >= 0) {
+      for (int64_t c0 = 0; c0 < row_vecs; c0 += 32 * PERM_UNR) {
+        uint4 v[PERM_UNR];
+#pragma unroll
+        for (int j = 0; j < PERM_UNR; ++j) {
+          const int64_t c = c0 + lane + 32 * j;
+          if (c < row_vecs) v[j] = __ldg(x + t * row_vecs + c);
+        }
+#pragma unroll
+        for (int j = 0; j < PERM_UNR; ++j) {
+          const int64_t c = c0 + lane + 32 * j;
+          if (c < row_vecs) out[m * row_vecs + c] = kperm8(v[j]);
+        }
+      }
+    }
+    m = m_next;
+    t = t_next;
+  }
+}
+
 int num_sms() {
   static int sms = 0;
   if (!sms) {
@@ -834,6 +890,26 @@ int permute_impl(const uint16_t* x, int64_t tokens, int32_t hidden, const int32_
                     (uint4*)x_sorted);
 }
 
+// x_sorted through the row-order path; pos_ws (int32 [rows]) is scratch
+int permute_by_row_impl(const uint16_t* x, int64_t tokens, int32_t hidden, const int32_t* row_token, int64_t rows,
+                        const int32_t* sorted_rows, const int32_t* num_padded, int64_t padded_len, uint16_t* x_sorted,
+                        int32_t* pos_ws, cudaStream_t st) {
+  SSB_CHECK_ARG(tokens >= 0 && rows >= 0 && padded_len >= 0 && hidden > 0 && hidden % 8 == 0);
+  if (padded_len == 0 || rows == 0) return SSB_OK;
+  SSB_CHECK_ARG(x && row_token && sorted_rows && num_padded && x_sorted && pos_ws);
+  SSB_CHECK_ARG((((uintptr_t)x | (uintptr_t)x_sorted) & 15) == 0);
+  cudaError_t e = cudaMemsetAsync(pos_ws, 0xFF, (size_t)rows * 4, st);
+  if (e != cudaSuccess) return (int)e;
+  const int64_t pb = (padded_len + 255) / 256;
+  int rc = ssb_launch(k_row_pos, dim3((unsigned)(pb < 148 * 8 ? pb : 148 * 8)), dim3(256), 0, st, false, sorted_rows,
+                      num_padded, rows, padded_len, pos_ws);
+  if (rc) return rc;
+  const int64_t blocks = (rows + 7) / 8;
+  return ssb_launch(k_permute_by_row, dim3((unsigned)(blocks < 148 * 8 ? blocks : 148 * 8)), dim3(256), 0, st, true,
+                    (const uint4*)x, tokens, (int64_t)hidden / 8, row_token, (const int32_t*)pos_ws, rows,
+                    (uint4*)x_sorted);
+}
+
 extern "C" int ssb_permute_rows(const uint16_t* x, int64_t tokens, int32_t hidden, const int32_t* row_token,
                                 int64_t rows, const int32_t* sorted_rows, const int32_t* num_padded,
                                 int64_t padded_len, uint16_t* x_sorted, void* stream) {
@@ -865,8 +941,10 @@ extern "C" int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hi
                                    int32_t shared_local, uint16_t* x_sorted, uint16_t* h_sorted, float* out_rows,
                                    int32_t* err, void* stream) {
   SSB_CHECK_ARG(tokens >= 0);
-  int rc = permute_impl(x, tokens, hidden, row_token, rows, sorted_rows, num_padded, padded_len, x_sorted,
-                        (cudaStream_t)stream);
+  SSB_CHECK_ARG((int64_t)padded_len * inter * 2 >= rows * 4);
+  // h_sorted is written by gate_up only after the permute: until then it holds the rows' sorted positions
+  int rc = permute_by_row_impl(x, tokens, hidden, row_token, rows, sorted_rows, num_padded, padded_len, x_sorted,
+                               reinterpret_cast<int32_t*>(h_sorted), (cudaStream_t)stream);
   if (rc) return rc;
   rc = ssb_sorted_gate_up(x_sorted, hidden, inter, row_token, rows, sorted_rows, block_expert, num_padded, padded_len,
                           group_ptr, n_groups, shared_local, h_sorted, err, stream);

@@ -40,9 +40,10 @@ def test_align_large_vs_oracle(r, nl, bm):
     assert np.array_equal(be, rb)
 
 
-def test_align_with_expert_map_equals_gather_then_align():
+@pytest.mark.parametrize("n", [20000, 70000])   # one CTA; a cluster of CTAs (32768 rows and more)
+def test_align_with_expert_map_equals_gather_then_align(n):
     rng = np.random.default_rng(1)
-    ids = rng.integers(-2, 514, 20000).astype(np.int32)
+    ids = rng.integers(-2, 514, n).astype(np.int32)
     emap = np.full(512, -1, dtype=np.int32)
     group = rng.permutation(512)[:32]
     emap[group] = np.arange(32)
