@@ -206,6 +206,20 @@ int ssb_pool_ensure(ssb_pool* pool, int32_t layer, const int32_t* experts, int32
 int ssb_pool_release(ssb_pool* pool, void* compute_stream);
 int ssb_pool_counters(ssb_pool* pool, int64_t* hits, int64_t* misses, int64_t* bytes);
 
+/* One decode MoE layer streaming its experts through the pool (host-side; it waits for the router): router
+ * logits and select with the shared gate (as ssb_router_logits + ssb_router_select: logits_ws fp32
+ * [rows, experts + 1], ids int32 / w fp32 [rows, topk], sh_gate fp32 [rows]), the ids copied to ids_host
+ * (pinned int32 [rows, topk]), ssb_pool_ensure for them (stats as there), ssb_moe_decode_layer through the
+ * pool's tables on compute_stream (h_buf, o_buf, out, y, err as there), then ssb_pool_release.
+ * Replaces: the per-layer sequence of slotstream_spark/model/layers.py:372-385 (seg_moe: router ids to the host,
+ * pool.ensure, the MoE kernels through the pool's tables) and runtime/graphs.py:316-323. */
+int ssb_pool_decode_layer(ssb_pool* pool, int32_t layer, const uint16_t* x, int64_t rows, int32_t topk,
+                          int32_t hidden, int32_t inter, int32_t experts, const uint16_t* w_router,
+                          const uint16_t* sh_gate_w, const float* bias, const void* const* host_table,
+                          const void* shared_record, float* logits_ws, int32_t* ids, float* w, float* sh_gate,
+                          int32_t* ids_host, float* h_buf, float* o_buf, float* out, uint16_t* y, int32_t* err,
+                          void* copy_stream, void* compute_stream, int64_t* stats);
+
 /* Router logits + select (as ssb_router_logits then ssb_router_select) with the logits held in a fixed
  * device array that comes with the library's device code, so the call needs no workspace and allocates nothing:
  * for callers that cannot allocate on their call path (a host binding without a caching allocator, a
@@ -273,13 +287,16 @@ int ssb_fused_moe_down(const uint16_t* h_buf, int64_t rows, int32_t hidden, int3
                        void* stream);
 
 /* Both prefill expert GEMMs of a fused MoE layer (additive), on activation rows permuted into expert order:
- * ssb_permute_rows, then ssb_sorted_gate_up, then ssb_sorted_down below, so the grouped GEMMs read whole
- * 256-row 2-D tiles instead of gathering rows (align with block_m = 256). Local expert `shared_local` (-1: none) is the shared expert --
+ * the rows of x copied into expert order (as ssb_permute_rows, but in row order through their sorted positions,
+ * and without writing the padding rows, whose results no GEMM stores), then ssb_sorted_gate_up, then
+ * ssb_sorted_down below, so the grouped GEMMs read whole 256-row 2-D tiles instead of gathering rows (align
+ * with block_m = 256). Local expert `shared_local` (-1: none) is the shared expert --
  * its h is bf16(bf16(silu(bf16 g)) * bf16 u) and its down rows bf16(row_weight * bf16(h D^T)), the
  * reference's bf16 rounding between the shared expert's ops (model/moe_sweep.py:37-43) -- so it rides in the
  * same grouped launch as the routed experts with its rows weighted by the sigmoid gate. x holds `tokens` rows
  * (row_token < tokens); x_sorted bf16 [padded_len, hidden] and h_sorted bf16 [padded_len, inter] are scratch
- * (h in sorted order); out_rows fp32 [rows, hidden] indexed by row as ssb_fused_moe_down.
+ * (h in sorted order; h_sorted first holds the rows' sorted positions); out_rows fp32 [rows, hidden] indexed by
+ * row as ssb_fused_moe_down.
  * Replaces: the per-group fused_moe_affine calls of model/moe_sweep.py:163-176 plus shared_expert
  * (:37-43) for a layer whose experts are all resident. */
 int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inter,

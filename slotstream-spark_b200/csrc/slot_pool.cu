@@ -264,3 +264,41 @@ extern "C" int ssb_pool_counters(ssb_pool* p, int64_t* hits, int64_t* misses, in
   if (bytes) *bytes = p->bytes;
   return SSB_OK;
 }
+
+// One streaming decode layer with the host side in native code: router logits + select on the compute stream,
+// the chosen ids to the host (the only synchronisation), ensure, the expert kernels through the pool's tables,
+// release. Every kernel is the one the separate entry points launch, so the results are theirs bit for bit.
+extern "C" int ssb_pool_decode_layer(ssb_pool* p, int32_t layer, const uint16_t* x, int64_t rows, int32_t topk,
+                                     int32_t hidden, int32_t inter, int32_t experts, const uint16_t* w_router,
+                                     const uint16_t* sh_gate_w, const float* bias, const void* const* host_table,
+                                     const void* shared_record, float* logits_ws, int32_t* ids, float* w,
+                                     float* sh_gate, int32_t* ids_host, float* h_buf, float* o_buf, float* out,
+                                     uint16_t* y, int32_t* err, void* copy_stream, void* compute_stream,
+                                     int64_t* stats) {
+  if (!p || !x || !w_router || !sh_gate_w || !host_table || !logits_ws || !ids || !w || !sh_gate || !ids_host)
+    return SSB_EINVAL;
+  if (rows < 0 || topk < 1 || experts != p->experts || layer < 0 || layer >= p->layers) return SSB_EINVAL;
+  if (rows == 0) return SSB_OK;
+  const cudaStream_t ks = (cudaStream_t)compute_stream;
+  int rc = ssb_router_logits(x, w_router, sh_gate_w, rows, hidden, experts, experts + 1, logits_ws, compute_stream);
+  if (rc) return rc;
+  rc = ssb_router_select(logits_ws, experts + 1, rows, experts, topk, bias, SSB_ROUTER_SHARED_GATE, ids, w, nullptr,
+                         sh_gate, compute_stream);
+  if (rc) return rc;
+  cudaError_t e = cudaMemcpyAsync(ids_host, ids, (size_t)rows * topk * 4, cudaMemcpyDeviceToHost, ks);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ks);
+  if (e != cudaSuccess) return (int)e;
+  rc = ssb_pool_ensure(p, layer, ids_host, (int32_t)(rows * topk), host_table, copy_stream, compute_stream, nullptr,
+                       stats);
+  if (rc) return rc;
+  int32_t* map_dev = nullptr;
+  int64_t* slot_ptr_dev = nullptr;
+  int64_t map_len = 0;
+  int32_t n_slots = 0;
+  rc = ssb_pool_tables(p, &map_dev, &slot_ptr_dev, &map_len, &n_slots, nullptr);
+  if (rc) return rc;
+  rc = ssb_moe_decode_layer(x, ids, w, rows, topk, hidden, inter, layer, map_dev, map_len, slot_ptr_dev, n_slots,
+                            shared_record, sh_gate, nullptr, h_buf, o_buf, out, y, 0, err, compute_stream);
+  if (rc) return rc;
+  return ssb_pool_release(p, compute_stream);
+}

@@ -96,28 +96,26 @@ def host_table(records_ptr: int, record_bytes: int, layers: int, experts: int, p
 
 def decode_layer_streaming(pool: SlotPool, table, x, w_router, layer: int, shared_record, sh_gate_w, k: int, bufs,
                            *, bias=None, copy_stream=None, ids_host=None):
-    """One decode MoE layer whose routed experts stream through the pool: router (logits + select), the chosen
-    ids to the host, ensure (misses copied on ``copy_stream``), then gate_up / down / combine through the pool's
-    tables on the current stream, and release. ``ids_host``: optional pinned int32 [rows, k] buffer for the
-    ids' readback. Returns (y, (hits, misses, bytes))."""
+    """One decode MoE layer whose routed experts stream through the pool (ssb_pool_decode_layer): router (logits
+    + select), the chosen ids to the host, ensure (misses copied on ``copy_stream``), then gate_up / down /
+    combine through the pool's tables on the current stream, and release, with the host side in native code.
+    ``ids_host``: pinned int32 [rows, k] buffer for the ids' readback (allocated when None).
+    Returns (y, (hits, misses, bytes))."""
     from .kernels.moe_layer import _addr
     r, h = x.shape
-    e = bufs.experts
-    L, P, st = _lib.lib(), _lib.ptr, _lib.stream()
-    _lib.check(L.ssb_router_logits(P(x), P(w_router), P(sh_gate_w), r, h, e, e + 1, P(bufs.ws), st), "router_logits")
-    _lib.check(L.ssb_router_select(P(bufs.ws), e + 1, r, e, k, P(bias), _lib.ROUTER_SHARED_GATE, P(bufs.ids), P(bufs.w),
-                                   None, P(bufs.sh_gate), st), "router_select")
-    # the host must know the routing to fill the misses
+    if x.dtype != torch.bfloat16 or not x.is_contiguous() or (r, k, h) != (bufs.rows, bufs.topk, bufs.hidden):
+        raise ValueError("x must be contiguous bf16 [rows, hidden] matching the buffers")
     if ids_host is None:
-        ids = bufs.ids.cpu().numpy()
-    else:
-        ids_host.copy_(bufs.ids, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        ids = ids_host.numpy()
-    _, stats = pool.ensure(layer, ids, table, copy_stream, torch.cuda.current_stream())
-    _lib.check(L.ssb_moe_decode_layer(P(x), P(bufs.ids), P(bufs.w), r, k, h, bufs.inter, int(layer), P(pool.map),
-                                      pool.map.numel(), P(pool.slot_ptr), pool.slots, _addr(shared_record),
-                                      P(bufs.sh_gate), None, P(bufs.h), P(bufs.o), P(bufs.out), P(bufs.y), 0,
-                                      P(bufs.err), st), "moe_decode_layer")
-    pool.release(torch.cuda.current_stream())
-    return bufs.y, stats
+        ids_host = torch.empty((r, k), dtype=torch.int32).pin_memory()
+    st = np.zeros(3, dtype=np.int64)
+    P = _lib.ptr
+    cs = copy_stream.cuda_stream if copy_stream is not None else _lib.stream()
+    rc = _lib.lib().ssb_pool_decode_layer(
+        pool.h, int(layer), P(x), r, k, h, bufs.inter, bufs.experts, P(w_router), P(sh_gate_w), P(bias),
+        ctypes.cast(table, ctypes.c_void_p), _addr(shared_record), P(bufs.ws), P(bufs.ids), P(bufs.w),
+        P(bufs.sh_gate), ids_host.data_ptr(), P(bufs.h), P(bufs.o), P(bufs.out), P(bufs.y), P(bufs.err), cs,
+        _lib.stream(), st.ctypes.data)
+    if rc == _lib.SSB_ETOOBIG:
+        raise RuntimeError("pool exhausted: the misses of this layer do not fit in the unpinned slots")
+    _lib.check(rc, "pool_decode_layer")
+    return bufs.y, tuple(int(v) for v in st)
