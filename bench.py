@@ -35,6 +35,12 @@ import torch  # noqa: E402
 
 METRIC = "MoE-layer tokens/s (decode b=1 HBM GB/s; prefill TFLOPS) at 1/2/4/8 B200"
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) per launch of the dominant kernel, from ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum, one pass) on the bench's own workloads; commands and figures under profiles/
+TRAFFIC_BYTES = {
+    "prefill_gate_up_32768": 2_360_000_000 + 357_240_000,   # full 32,768-token layer, profiles/grouped_gemm_traffic_32k.md
+    "decode_fused_b1": 21_685_760,                          # one b = 1 layer, profiles/decode_fused_b1.md
+}
 
 
 def peaks():
@@ -287,7 +293,8 @@ def bench_decode(args, world, rank, batch=None, W=None):
     achieved = launch_bytes / (launch_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                "peak_source": pk["source"], "traffic": None,
+                "peak_source": pk["source"],
+                "traffic": TRAFFIC_BYTES["decode_fused_b1"] if (fused and b == 1) else None,
                 "bytes_per_launch": int(launch_bytes), "launch_us": round(launch_ms * 1e3, 2)}
 
     # e2e: host inputs (pinned) -> device, graph step, outputs -> host, all inside the timed region
@@ -533,7 +540,8 @@ def bench_prefill(args, world, rank):
     roofline = {"bound": "tensor", "kernel": "fused_moe gate_up (tcgen05 grouped GEMM, SwiGLU epilogue)",
                 "achieved": round(gu_tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(gu_tf / pk["bf16_tflops"], 4), "peak_source": pk["source"] + " (burst)",
-                "traffic": None, "flop_per_launch": gu_flop, "launch_ms": round(gu_ms, 4),
+                "traffic": TRAFFIC_BYTES.get(f"prefill_gate_up_{T}") if args.routing == "zipf" else None,
+                "flop_per_launch": gu_flop, "launch_ms": round(gu_ms, 4),
                 "padded_rows": n_padded, "rows": bufs.rows,
                 "down": {"achieved": round(dn_flop / (dn_ms * 1e-3) / 1e12, 1), "launch_ms": round(dn_ms, 4)}}
 
