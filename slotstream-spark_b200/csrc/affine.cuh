@@ -66,6 +66,33 @@ SSB_DEV float unit_dot(uint2 wv, float s, float b, const XUnit& x, float acc) {
   return fmaf(s, qx, fmaf(b, x.sum, acc));
 }
 
+// The same dot product with the unit's codes decoded once (q_j * 16^j' as float pairs, in dot_word's order), for a
+// unit that several activations meet: unit_dot_dec(unit_decode(wv), s, b, x, acc) == unit_dot(wv, s, b, x, acc).
+struct WUnit {
+  float2 v[8];
+};
+SSB_DEV WUnit unit_decode(uint2 wv) {
+  const uint32_t M = 0x4B000000u;
+  const float2 m = make_float2(-8388608.f, -8388608.f);
+  WUnit d;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t w = h ? wv.y : wv.x, w5 = w >> 12;
+    d.v[4 * h + 0] = __fadd2_rn(make_float2(__uint_as_float((w & 0xFu) | M), __uint_as_float((w & 0xF0u) | M)), m);
+    d.v[4 * h + 1] = __fadd2_rn(make_float2(__uint_as_float((w & 0xF00u) | M), __uint_as_float((w & 0xF000u) | M)), m);
+    d.v[4 * h + 2] = __fadd2_rn(make_float2(__uint_as_float((w & 0xF0000u) | M), __uint_as_float((w5 & 0xF00u) | M)), m);
+    d.v[4 * h + 3] = __fadd2_rn(make_float2(__uint_as_float((w5 & 0xF000u) | M), __uint_as_float((w5 & 0xF0000u) | M)), m);
+  }
+  return d;
+}
+SSB_DEV float unit_dot_dec(const WUnit& d, float s, float b, const XUnit& x, float acc) {
+  float2 a2 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) a2 = __ffma2_rn(d.v[q], x.v[q], a2);
+  float qx = a2.x + a2.y;
+  return fmaf(s, qx, fmaf(b, x.sum, acc));
+}
+
 // ---------------------------------------------------------------- mbarrier + bulk copies (async proxy)
 SSB_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

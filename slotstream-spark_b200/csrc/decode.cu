@@ -48,6 +48,7 @@ struct DecodeArgs {
   float* out;
   uint16_t* y;
   int32_t* err;
+  int run;   // grouped gate_up: entries per run (<= GU_RUN), sized so the run's staged activations fit
 };
 
 // XUnit as stored in shared memory: 16-byte aligned, 80 bytes.
@@ -361,30 +362,31 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down(DecodeArgs a) {
 // expert chosen by several rows are read once per layer instead of once per row. Every (entry, output) value
 // is the op sequence of the per-row kernels above, and the rank-order sum moves to its own small kernel
 // (the reference's _rank_sum), so the grouped path equals the per-row path bit for bit.
-constexpr int GRP_TOK = 8;      // entries one grouped CTA computes
+constexpr int GRP_TOK = 8;      // entries one grouped down CTA computes
+constexpr int GU_RUN = 4;       // entries one grouped gate_up CTA computes (their activations staged per CTA)
 constexpr int GRP_MAX = 1024;   // routed entries (rows * topk) the grouped path takes
 constexpr int GD_ROWS = 64;     // hidden rows per grouped down CTA (eight per warp)
 
 // Warp-wide: the entries of the run that starts at routed entry p (none when p does not start a run), in
 // entry order, into s_list; returns their count.
-SSB_DEV int group_run(const int32_t* s_ids, int n_routed, int p, int* s_list, int lane) {
+SSB_DEV int group_run(const int32_t* s_ids, int n_routed, int p, int* s_list, int lane, int run) {
   const int e = s_ids[p];
   int occ = 0;
   for (int q0 = 0; q0 < p; q0 += 32) {
     const int q = q0 + lane;
     occ += __popc(__ballot_sync(0xFFFFFFFFu, q < p && s_ids[q] == e));
   }
-  if (occ % GRP_TOK) return 0;
+  if (occ % run) return 0;
   int n = 0;
-  for (int q0 = p; q0 < n_routed && n < GRP_TOK; q0 += 32) {
+  for (int q0 = p; q0 < n_routed && n < run; q0 += 32) {
     const int q = q0 + lane;
     const bool m = q < n_routed && s_ids[q] == e;
     const unsigned b = __ballot_sync(0xFFFFFFFFu, m);
     const int before = __popc(b & ((1u << lane) - 1u));
-    if (m && n + before < GRP_TOK) s_list[n + before] = q;
+    if (m && n + before < run) s_list[n + before] = q;
     n += __popc(b);
   }
-  return n < GRP_TOK ? n : GRP_TOK;
+  return n < run ? n : run;
 }
 
 template <int NUX>
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up_g(DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ uint64_t bar;
   __shared__ const uint8_t* s_base;
-  __shared__ int s_list[GRP_TOK];
+  __shared__ int s_list[GU_RUN];
   __shared__ int s_n;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n_routed = (int)(a.R * a.topk);
@@ -407,6 +409,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up_g(DecodeArgs a) {
   uint8_t* usc = gb + sbytes;
   uint8_t* ub = usc + sbytes;
   int32_t* s_ids = reinterpret_cast<int32_t*>(ub + sbytes);
+  XUnitS* xs = reinterpret_cast<XUnitS*>(ub + sbytes + (((size_t)n_routed * 4 + 15) & ~(size_t)15));   // [run][H/16]
   const bool is_shared = p >= n_routed;
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -426,9 +429,9 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up_g(DecodeArgs a) {
   };
   if (is_shared) {
     const int occ = p - n_routed;
-    if (occ % GRP_TOK) return;
+    if (occ % a.run) return;
     if (tid == 0) {   // the shared record is static: start its copies before the wait
-      const int n = (int)(a.R - occ) < GRP_TOK ? (int)(a.R - occ) : GRP_TOK;
+      const int n = (int)(a.R - occ) < a.run ? (int)(a.R - occ) : a.run;
       for (int i = 0; i < n; ++i) s_list[i] = p + i;
       s_n = n;
       s_base = a.shared_rec;
@@ -442,7 +445,7 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up_g(DecodeArgs a) {
     for (int q = tid; q < n_routed; q += blockDim.x) s_ids[q] = ld_cg_i32(a.ids + q);
     __syncthreads();
     if (warp == 0) {
-      const int n = group_run(s_ids, n_routed, p, s_list, lane);
+      const int n = group_run(s_ids, n_routed, p, s_list, lane, a.run);
       if (lane == 0 && n) {
         const uint8_t* base = a.bases ? (const uint8_t*)ld_cg_i64(a.bases + p)
                                       : resolve_expert(s_ids[p], a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots,
@@ -462,12 +465,26 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up_g(DecodeArgs a) {
       a.h_buf[(int64_t)s_list[idx / GU_ROWS] * a.I + n0 + idx % GU_ROWS] = 0.f;
     return;
   }
+  const int ng = H / gs, nunits = H / 16;
+  // the run's activations in the pre-scaled per-unit form, once per CTA (every warp reads every token's units)
+  for (int idx = tid; idx < n * nunits; idx += blockDim.x) {
+    const int t = idx / nunits, u = idx - t * nunits;
+    const int q = s_list[t];
+    float x16[16];
+    load_x16(a, is_shared ? q - n_routed : q / a.topk, u, x16);
+    XUnit xu;
+    xunit_from_f32(xu, x16);
+    XUnitS& d = xs[idx];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) d.v[c] = xu.v[c];
+    d.sum = xu.sum;
+  }
+  __syncthreads();
   if (!mbar_wait(&bar, 0, SSB_WAIT_LIMIT)) {
     set_err(a.err, SSB_ERR_TIMEOUT);
     mbar_wait(&bar, 0, SSB_WAIT_LIMIT);
     return;
   }
-  const int ng = H / gs, nunits = H / 16;
   const int j0 = 2 * warp, j1 = j0 + 1;
   const uint2* g0r = reinterpret_cast<const uint2*>(gw + (size_t)j0 * H / 2);
   const uint2* u0r = reinterpret_cast<const uint2*>(uw + (size_t)j0 * H / 2);
@@ -477,36 +494,54 @@ __global__ void __launch_bounds__(GU_WARPS * 32) k_dec_gate_up_g(DecodeArgs a) {
   const uint16_t* gb16 = reinterpret_cast<const uint16_t*>(gb);
   const uint16_t* us16 = reinterpret_cast<const uint16_t*>(usc);
   const uint16_t* ub16 = reinterpret_cast<const uint16_t*>(ub);
-  for (int t = 0; t < n; ++t) {
-    const int q = s_list[t];
-    const int64_t r = is_shared ? q - n_routed : q / a.topk;
-    float ga0 = 0.f, ua0 = 0.f, ga1 = 0.f, ua1 = 0.f;
+  // each unit's codes are decoded once and met by every token of the run; per (row, token) the units are
+  // accumulated in the order of the per-row kernel, so the bits are the same
+  float acc[4][GU_RUN];
 #pragma unroll
-    for (int i = 0; i < NUX; ++i) {
-      const int u = lane + 32 * i;
-      if (u < nunits) {
-        float x16[16];
-        load_x16(a, r, u, x16);
-        XUnit xu;
-        xunit_from_f32(xu, x16);
-        const int g = (u * 16) / gs;
-        ga0 = unit_dot(g0r[u], bf16_bits(gs16[j0 * ng + g]), bf16_bits(gb16[j0 * ng + g]), xu, ga0);
-        ua0 = unit_dot(u0r[u], bf16_bits(us16[j0 * ng + g]), bf16_bits(ub16[j0 * ng + g]), xu, ua0);
-        ga1 = unit_dot(g1r[u], bf16_bits(gs16[j1 * ng + g]), bf16_bits(gb16[j1 * ng + g]), xu, ga1);
-        ua1 = unit_dot(u1r[u], bf16_bits(us16[j1 * ng + g]), bf16_bits(ub16[j1 * ng + g]), xu, ua1);
+  for (int t = 0; t < GU_RUN; ++t) acc[0][t] = acc[1][t] = acc[2][t] = acc[3][t] = 0.f;
+#pragma unroll
+  for (int i = 0; i < NUX; ++i) {
+    const int u = lane + 32 * i;
+    if (u < nunits) {
+      const int g = (u * 16) / gs;
+      const WUnit dg0 = unit_decode(g0r[u]), du0 = unit_decode(u0r[u]), dg1 = unit_decode(g1r[u]),
+                  du1 = unit_decode(u1r[u]);
+      const float sg0 = bf16_bits(gs16[j0 * ng + g]), bg0 = bf16_bits(gb16[j0 * ng + g]);
+      const float su0 = bf16_bits(us16[j0 * ng + g]), bu0 = bf16_bits(ub16[j0 * ng + g]);
+      const float sg1 = bf16_bits(gs16[j1 * ng + g]), bg1 = bf16_bits(gb16[j1 * ng + g]);
+      const float su1 = bf16_bits(us16[j1 * ng + g]), bu1 = bf16_bits(ub16[j1 * ng + g]);
+#pragma unroll
+      for (int t = 0; t < GU_RUN; ++t) {
+        if (t < n) {
+          const XUnitS& xt = xs[t * nunits + u];
+          XUnit xu;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) xu.v[c] = xt.v[c];
+          xu.sum = xt.sum;
+          acc[0][t] = unit_dot_dec(dg0, sg0, bg0, xu, acc[0][t]);
+          acc[1][t] = unit_dot_dec(du0, su0, bu0, xu, acc[1][t]);
+          acc[2][t] = unit_dot_dec(dg1, sg1, bg1, xu, acc[2][t]);
+          acc[3][t] = unit_dot_dec(du1, su1, bu1, xu, acc[3][t]);
+        }
       }
     }
-    warp_sum4(ga0, ua0, ga1, ua1);
-    if (lane < 2) {
-      const float ga = lane ? ga1 : ga0, ua = lane ? ua1 : ua0;
-      float h;
-      if (is_shared) {
-        const float gbv = round_bf16(ga), ubv = round_bf16(ua);
-        h = round_bf16(round_bf16(gbv / (1.f + expf(-gbv))) * ubv);
-      } else {
-        h = ga / (1.f + expf(-ga)) * ua;
+  }
+#pragma unroll
+  for (int t = 0; t < GU_RUN; ++t) {
+    if (t < n) {
+      float ga0 = acc[0][t], ua0 = acc[1][t], ga1 = acc[2][t], ua1 = acc[3][t];
+      warp_sum4(ga0, ua0, ga1, ua1);
+      if (lane < 2) {
+        const float ga = lane ? ga1 : ga0, ua = lane ? ua1 : ua0;
+        float h;
+        if (is_shared) {
+          const float gbv = round_bf16(ga), ubv = round_bf16(ua);
+          h = round_bf16(round_bf16(gbv / (1.f + expf(-gbv))) * ubv);
+        } else {
+          h = ga / (1.f + expf(-ga)) * ua;
+        }
+        a.h_buf[(int64_t)s_list[t] * a.I + n0 + j0 + lane] = h;
       }
-      a.h_buf[(int64_t)q * a.I + n0 + j0 + lane] = h;
     }
   }
 }
@@ -562,7 +597,7 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down_g(DecodeArgs a) {
     for (int q = tid; q < n_routed; q += blockDim.x) s_ids[q] = ld_cg_i32(a.ids + q);
     __syncthreads();
     if (warp == 0) {
-      const int n = group_run(s_ids, n_routed, p, s_list, lane);
+      const int n = group_run(s_ids, n_routed, p, s_list, lane, GRP_TOK);
       if (lane == 0 && n) {
         const uint8_t* base = a.bases ? (const uint8_t*)ld_cg_i64(a.bases + p)
                                       : resolve_expert(s_ids[p], a.layer, a.map, a.map_len, a.slot_ptr, a.n_slots,
@@ -617,22 +652,26 @@ __global__ void __launch_bounds__(DN_WARPS * 32) k_dec_down_g(DecodeArgs a) {
     const uint2* wr = reinterpret_cast<const uint2*>(dw + (size_t)row * I / 2);
     const uint16_t* sr = reinterpret_cast<const uint16_t*>(dsc) + row * ng;
     const uint16_t* br = reinterpret_cast<const uint16_t*>(db) + row * ng;
+    // each unit's codes decoded once for all of the run's tokens; per token the units keep their order
     float d[GRP_TOK];
 #pragma unroll
-    for (int t = 0; t < GRP_TOK; ++t) {
-      d[t] = 0.f;
-      if (t < n) {
+    for (int t = 0; t < GRP_TOK; ++t) d[t] = 0.f;
 #pragma unroll
-        for (int i = 0; i < NUI; ++i) {
-          const int u = lane + 32 * i;
-          if (u < nunits) {
+    for (int i = 0; i < NUI; ++i) {
+      const int u = lane + 32 * i;
+      if (u < nunits) {
+        const int g = (u * 16) / gs;
+        const WUnit dw = unit_decode(wr[u]);
+        const float sv = bf16_bits(sr[g]), bv = bf16_bits(br[g]);
+#pragma unroll
+        for (int t = 0; t < GRP_TOK; ++t) {
+          if (t < n) {
             const XUnitS& xs = hx[t * nunits + u];
             XUnit xu;
 #pragma unroll
             for (int q = 0; q < 8; ++q) xu.v[q] = xs.v[q];
             xu.sum = xs.sum;
-            const int g = (u * 16) / gs;
-            d[t] = unit_dot(wr[u], bf16_bits(sr[g]), bf16_bits(br[g]), xu, d[t]);
+            d[t] = unit_dot_dec(dw, sv, bv, xu, d[t]);
           }
         }
       }
@@ -688,8 +727,13 @@ int launch_decode_grouped(DecodeArgs a, cudaStream_t st, bool pdl) {
   const int nui = (a.I / 16 + 31) / 32;
   const int64_t n_routed = a.R * a.topk;
   const int64_t pairs = n_routed + (a.shared_rec ? a.R : 0);
-  const size_t ids_bytes = (size_t)n_routed * 4;
-  const size_t gu_smem = (size_t)2 * GU_ROWS * a.H / 2 + (size_t)4 * GU_ROWS * (a.H / a.gs) * 2 + ids_bytes;
+  const size_t ids_bytes = ((size_t)n_routed * 4 + 15) & ~(size_t)15;
+  const size_t gu_fixed = (size_t)2 * GU_ROWS * a.H / 2 + (size_t)4 * GU_ROWS * (a.H / a.gs) * 2 + ids_bytes;
+  // entries per gate_up run: as many as fit with their activations staged in shared memory
+  const size_t xs_unit = (size_t)(a.H / 16) * sizeof(XUnitS);
+  a.run = GU_RUN;
+  while (a.run > 1 && gu_fixed + (size_t)a.run * xs_unit > 100 * 1024) a.run /= 2;   // two CTAs per SM
+  const size_t gu_smem = gu_fixed + (size_t)a.run * xs_unit;
   const size_t dn_smem = (size_t)GD_ROWS * a.I / 2 + (size_t)2 * GD_ROWS * (a.I / a.gs) * 2 +
                          (size_t)GRP_TOK * (a.I / 16) * sizeof(XUnitS) + ids_bytes;
   if (gu_smem > 200 * 1024 || dn_smem > 200 * 1024) return SSB_EUNSUPPORTED;
