@@ -7,9 +7,12 @@
 // entries in rank-k order or (exact mode) the k per-entry rows, so that the home rank can sum every token's
 // expert outputs in router-rank order bit for bit like the one-GPU layer (kernels/fused_moe_affine.py:164-172).
 //
-// Send order: rows for destination 0 first, then 1, ...; inside a destination by ascending token. The plan is
-// one CTA: each thread owns a contiguous token chunk, per-destination counts are block-scanned, and a second
-// pass writes every row to its final position, so the order is deterministic.
+// Send order: rows for destination 0 first, then 1, ...; inside a destination by ascending token. The plan runs
+// on a cluster of CTAs (one CTA when clusters are unavailable): each CTA owns a contiguous token range and each
+// of its threads a contiguous chunk of it (the next token's choices loaded while the current one is handled);
+// per-destination counts are block-scanned, the CTAs exchange their totals through distributed shared memory,
+// and a second pass writes every row to its final position, so the order is deterministic.
+#include <cooperative_groups.h>
 #include <cub/block/block_scan.cuh>
 
 #include "common.cuh"
@@ -40,25 +43,40 @@ struct CountsSum {
   }
 };
 
-// Per-destination entry counts of token t (4 bits each; k <= 15 entries per destination fit) and the mask.
-SSB_DEV uint32_t token_dests(const int32_t* ids, int64_t t, int k, const Placement& pl, uint64_t* ecnt,
-                             int32_t* err) {
+// One token's choices in registers (k <= 15): the ids, and (with_w) the weights.
+struct TokChoices {
+  int e[16];
+  float w[16];
+};
+template <bool WITH_W>
+SSB_DEV void load_choices(const int32_t* ids, const float* w, int64_t t, int k, TokChoices& c) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    c.e[j] = j < k ? __ldcg(ids + t * k + j) : -1;
+    if (WITH_W) c.w[j] = j < k ? __ldcg(w + t * k + j) : 0.f;
+  }
+}
+// Per-destination entry counts (4 bits each; k <= 15 entries per destination fit) and the destination mask.
+SSB_DEV uint32_t choice_dests(const TokChoices& c, int k, const Placement& pl, uint64_t* ecnt, int32_t* err) {
   uint32_t m = 0;
-  uint64_t c = 0;
-  for (int j = 0; j < k; ++j) {
-    const int e = __ldcg(ids + t * k + j);
+  uint64_t n = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j >= k) break;
+    const int e = c.e[j];
     if (!pl.valid(e)) {
       set_err(err, SSB_ERR_EXPERT_RANGE);
       continue;
     }
     const int d = pl.rank(e);
     m |= 1u << d;
-    c += 1ull << (4 * d);
+    n += 1ull << (4 * d);
   }
-  *ecnt = c;
+  *ecnt = n;
   return m;
 }
 
+// Both passes walk a thread's token chunk with the next token's choices loaded while the current one is handled.
 __global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(const int32_t* __restrict__ ids,
                                                           const float* __restrict__ w, int64_t T, int k,
                                                           Placement pl, int32_t* __restrict__ dest_count,
@@ -66,25 +84,38 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(const int32_t* __restr
                                                           int32_t* __restrict__ send_meta,
                                                           int32_t* __restrict__ tok_slot,
                                                           int32_t* __restrict__ tok_entry, int32_t* err) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   using Scan = cub::BlockScan<Counts, PLAN_THREADS>;
   __shared__ typename Scan::TempStorage tmp;
   __shared__ int s_off[EP_MAXG];
+  __shared__ int s_tot[2 * EP_MAXG], s_before[2 * EP_MAXG], s_grand[2 * EP_MAXG];
   pdl_wait();
   pdl_trigger();
   const int tid = threadIdx.x, G = pl.G;
+  const int crank = (int)cluster.block_rank(), csize = (int)cluster.num_blocks();
   const int mw = 2 * k + 2;
-  const int64_t chunk = (T + PLAN_THREADS - 1) / PLAN_THREADS;
-  const int64_t t0 = tid * chunk, t1 = t0 + chunk < T ? t0 + chunk : T;
+  const int64_t cchunk = (T + csize - 1) / csize;
+  const int64_t c0 = (int64_t)crank * cchunk < T ? (int64_t)crank * cchunk : T;
+  const int64_t c1 = c0 + cchunk < T ? c0 + cchunk : T;
+  const int64_t chunk = (c1 - c0 + PLAN_THREADS - 1) / PLAN_THREADS;
+  const int64_t t0 = c0 + tid * chunk < c1 ? c0 + tid * chunk : c1, t1 = t0 + chunk < c1 ? t0 + chunk : c1;
   Counts mine;
 #pragma unroll
   for (int d = 0; d < 2 * EP_MAXG; ++d) mine.c[d] = 0;
-  for (int64_t t = t0; t < t1; ++t) {
-    uint64_t ec;
-    const uint32_t m = token_dests(ids, t, k, pl, &ec, nullptr);
+  {
+    TokChoices cur, nxt;
+    if (t0 < t1) load_choices<false>(ids, w, t0, k, cur);
+    for (int64_t t = t0; t < t1; ++t) {
+      if (t + 1 < t1) load_choices<false>(ids, w, t + 1, k, nxt);
+      uint64_t ec;
+      const uint32_t m = choice_dests(cur, k, pl, &ec, nullptr);
 #pragma unroll
-    for (int d = 0; d < EP_MAXG; ++d) {
-      mine.c[d] += (m >> d) & 1u;
-      mine.c[EP_MAXG + d] += (int)((ec >> (4 * d)) & 15u);
+      for (int d = 0; d < EP_MAXG; ++d) {
+        mine.c[d] += (m >> d) & 1u;
+        mine.c[EP_MAXG + d] += (int)((ec >> (4 * d)) & 15u);
+      }
+      cur = nxt;
     }
   }
   Counts excl, total, zero;
@@ -92,24 +123,45 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(const int32_t* __restr
   for (int d = 0; d < 2 * EP_MAXG; ++d) zero.c[d] = 0;
   Scan(tmp).ExclusiveScan(mine, excl, zero, CountsSum(), total);
   if (tid == 0) {
+#pragma unroll
+    for (int d = 0; d < 2 * EP_MAXG; ++d) s_tot[d] = total.c[d];
+  }
+  cluster.sync();   // every CTA's totals are complete
+  if (tid < 2 * EP_MAXG) {   // rows and entries of the earlier CTAs, and of all of them
+    int b = 0, g = 0;
+    for (int c = 0; c < csize; ++c) {
+      const int v = *cluster.map_shared_rank(s_tot + tid, c);
+      b += c < crank ? v : 0;
+      g += v;
+    }
+    s_before[tid] = b;
+    s_grand[tid] = g;
+  }
+  cluster.sync();   // no CTA leaves while another may still read its totals
+  if (tid == 0) {
     int off = 0;
     for (int d = 0; d < G; ++d) {
       s_off[d] = off;
-      dest_count[2 * d] = total.c[d];
-      dest_count[2 * d + 1] = total.c[EP_MAXG + d];
-      off += total.c[d];
+      if (crank == 0) {
+        dest_count[2 * d] = s_grand[d];
+        dest_count[2 * d + 1] = s_grand[EP_MAXG + d];
+      }
+      off += s_grand[d];
     }
   }
   __syncthreads();
   int pos[EP_MAXG], epos[EP_MAXG];
 #pragma unroll
   for (int d = 0; d < EP_MAXG; ++d) {
-    pos[d] = d < G ? s_off[d] + excl.c[d] : 0;
-    epos[d] = excl.c[EP_MAXG + d];
+    pos[d] = d < G ? s_off[d] + s_before[d] + excl.c[d] : 0;
+    epos[d] = s_before[EP_MAXG + d] + excl.c[EP_MAXG + d];
   }
+  TokChoices cur, nxt;
+  if (t0 < t1) load_choices<true>(ids, w, t0, k, cur);
   for (int64_t t = t0; t < t1; ++t) {
+    if (t + 1 < t1) load_choices<true>(ids, w, t + 1, k, nxt);
     uint64_t ec;
-    const uint32_t m = token_dests(ids, t, k, pl, &ec, err);
+    const uint32_t m = choice_dests(cur, k, pl, &ec, err);
 #pragma unroll
     for (int d = 0; d < EP_MAXG; ++d) {
       if (d >= G) break;
@@ -124,17 +176,48 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_ep_plan(const int32_t* __restr
       tok_entry[t * G + d] = epos[d];
       send_token[p] = (int32_t)t;
       int32_t* meta = send_meta + (int64_t)p * mw;
-      for (int j = 0; j < k; ++j) {
-        const int e = __ldcg(ids + t * k + j);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= k) break;
+        const int e = cur.e[j];
         const bool here = pl.valid(e) && pl.rank(e) == d;
         meta[j] = here ? pl.local(e) : -1;
-        meta[k + j] = here ? __float_as_int(__ldcg(w + t * k + j)) : 0;
+        meta[k + j] = here ? __float_as_int(cur.w[j]) : 0;
       }
       meta[2 * k] = epos[d];
       meta[2 * k + 1] = n;
       epos[d] += n;
     }
+    cur = nxt;
   }
+}
+
+int plan_cluster_size() {   // 16 CTAs when the device runs such clusters, else 8, else 1
+  static int cl = -1;
+  if (cl < 0) {
+    cl = 1;
+    if (cudaFuncSetAttribute(k_ep_plan, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      (void)cudaGetLastError();
+    for (int want : {16, 8}) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(want);
+      cfg.blockDim = dim3(PLAN_THREADS);
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = want;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, k_ep_plan, &cfg) == cudaSuccess && n >= 1) {
+        cl = want;
+        break;
+      }
+      (void)cudaGetLastError();
+    }
+  }
+  return cl;
 }
 
 // dst[i, :] = src[idx[i], :] for rows of `row_bytes` (a multiple of 16) bytes.
@@ -286,9 +369,29 @@ extern "C" int ssb_ep_plan(const int32_t* ids, const float* w, int64_t tokens, i
   SSB_CHECK_ARG(ids && w && dest_count && send_token && send_meta && tok_slot && tok_entry);
   SSB_CHECK_ARG(tokens <= 0x7fffffffLL / k);
   ssb_note_smem("ep_plan", k_ep_plan, 0);
-  return ssb_launch(k_ep_plan, dim3(1), dim3(PLAN_THREADS), 0, (cudaStream_t)stream, true, ids, w, tokens, k,
-                    Placement{experts_per_rank, n_ranks, strided}, dest_count, send_token, send_meta, tok_slot,
-                    tok_entry, err);
+  const Placement pl{experts_per_rank, n_ranks, strided};
+  const int cl = tokens >= 4096 ? plan_cluster_size() : 1;
+  if (cl > 1) {   // one CTA per 1/cl of the tokens
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl);
+    cfg.blockDim = dim3(PLAN_THREADS);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_ep_plan, ids, w, tokens, k, pl, dest_count, send_token, send_meta,
+                                       tok_slot, tok_entry, err);
+    if (e == cudaSuccess) return SSB_OK;
+    (void)cudaGetLastError();   // fall back to one CTA
+  }
+  return ssb_launch(k_ep_plan, dim3(1), dim3(PLAN_THREADS), 0, (cudaStream_t)stream, true, ids, w, tokens, k, pl,
+                    dest_count, send_token, send_meta, tok_slot, tok_entry, err);
 }
 
 extern "C" int ssb_gather_rows(const void* src, int64_t src_rows, const int32_t* idx, int64_t n, int64_t row_bytes,

@@ -79,13 +79,16 @@ def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bo
     ids, w, sh_gate = ops.route(x)
     sh = ops.shared(x, sh_gate)
     plan = ops.plan(ids, w)
-    send_x = ops.gather(x, plan.send_token)
     recv_count = torch.empty_like(plan.dest_count)
     dist.all_to_all_single(recv_count.view(-1), plan.dest_count.view(-1), group=group)
-    sc = plan.dest_count.cpu().tolist()
-    rc = recv_count.cpu().tolist()
+    both = torch.cat([plan.dest_count.view(-1), recv_count.view(-1)]).cpu().tolist()   # the one host sync
+    sc = [both[2 * d:2 * d + 2] for d in range(G)]
+    rc = [both[2 * G + 2 * d:2 * G + 2 * d + 2] for d in range(G)]
     send_rows, send_ent = [c[0] for c in sc], [c[1] for c in sc]
     recv_rows, recv_ent = [c[0] for c in rc], [c[1] for c in rc]
+    n_send = sum(send_rows)
+    plan.send_token, plan.send_meta = plan.send_token[:n_send], plan.send_meta[:n_send]
+    send_x = ops.gather(x, plan.send_token)
     n_recv = sum(recv_rows)
     recv_x = x.new_empty((n_recv, x.shape[1]))
     dist.all_to_all_single(recv_x, send_x, recv_rows, send_rows, group=group)
@@ -124,6 +127,7 @@ class CudaOps:
         self.shared_ptr = torch.tensor([int(shared_ptr)], dtype=torch.int64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self._static = {}
+        self._side, self._sh_ready = None, None
 
     # ---------------------------------------------------------------- helpers
     def _aligned(self, row_expert, num_local):
@@ -164,13 +168,25 @@ class CudaOps:
         return ids, w, sh_gate
 
     def shared(self, x, sh_gate):
+        """The shared expert of this rank's tokens, on a side stream: it overlaps the exchange and is joined
+        in ``combine``."""
         t = x.shape[0]
         key = ("shared", t)
         if key not in self._static:
             self._static[key] = (torch.arange(t, dtype=torch.int32, device=x.device),
                                  torch.zeros(t, dtype=torch.int32, device=x.device))
         tok, zero = self._static[key]
-        return self._experts(x, t, tok, sh_gate, zero, self.shared_ptr, 1, 0)
+        main = torch.cuda.current_stream()
+        if self._side is None:
+            self._side = torch.cuda.Stream()
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            out = self._experts(x, t, tok, sh_gate, zero, self.shared_ptr, 1, 0)
+        sh_gate.record_stream(self._side)
+        out.record_stream(main)
+        self._sh_ready = torch.cuda.Event()
+        self._sh_ready.record(self._side)
+        return out
 
     def plan(self, ids, w):
         t, k, G = ids.shape[0], self.k, self.G
@@ -183,9 +199,7 @@ class CudaOps:
         _lib.check(_lib.lib().ssb_ep_plan(P(ids), P(w), t, k, self.epr, G, int(self.strided), P(p.dest_count),
                                           P(p.send_token), P(p.send_meta), P(p.tok_slot), P(p.tok_entry), P(self.err),
                                           _lib.stream()), "ep plan")
-        n = int(p.dest_count[:, 0].sum())   # rows actually used (the buffers were sized for the worst case)
-        p.send_token, p.send_meta = p.send_token[:n], p.send_meta[:n]
-        return p
+        return p   # sized for the worst case; ep_forward trims to the counts it reads back
 
     def gather(self, x, idx):
         out = x.new_empty((idx.numel(), x.shape[1]))
@@ -227,6 +241,8 @@ class CudaOps:
         y = torch.empty((t, self.hidden), dtype=torch.bfloat16, device=dev)
         reo = (torch.tensor(ret_entry_off, dtype=torch.int64).to(dev, non_blocking=True)
                if ret_entry_off is not None else None)
+        if self._sh_ready is not None:
+            torch.cuda.current_stream().wait_event(self._sh_ready)   # the shared expert's rows (side stream)
         P = _lib.ptr
         _lib.check(_lib.lib().ssb_ep_combine(P(ret), P(plan.tok_slot), P(plan.tok_entry), P(reo), P(ids), t, self.k,
                                              self.epr, self.G, int(self.strided), int(exact), self.hidden, P(sh),
