@@ -73,6 +73,10 @@ class ClockSampler:
             self.proc = None
             return
         threading.Thread(target=self._read, daemon=True).start()
+        # nvidia-smi takes a moment to start: wait for its first sample so that the timed region is covered
+        t0 = time.monotonic()
+        while not self.samples and time.monotonic() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
