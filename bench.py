@@ -39,7 +39,7 @@ L2_FLUSH_BYTES = 256 << 20
 # dram__bytes_write.sum, one pass) on the bench's own workloads; commands and figures under profiles/
 TRAFFIC_BYTES = {
     "prefill_gate_up_32768": 2_360_000_000 + 357_240_000,   # full 32,768-token layer, profiles/grouped_gemm_traffic_32k.md
-    "decode_fused_b1": 21_685_760,                          # one b = 1 layer, profiles/decode_fused_b1.md
+    "decode_fused_b1": 21_684_736,                          # one b = 1 layer, profiles/decode_fused_b1.md
 }
 
 
