@@ -629,7 +629,7 @@ def bench_prefill_ep(args, world, rank):
                   strided=True, bias=bias)
 
     def step():
-        return ep_forward(ops, x, K, world)
+        return ep_forward(ops, x, K, world, micro_batches=args.micro_batches)
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
@@ -670,6 +670,7 @@ def bench_prefill_ep(args, world, rank):
                    "inter": LAY.inter, "experts": E, "experts_per_gpu": len(owned), "placement": "strided (e % G)",
                    "topk": K, "shared_experts": 1, "routing": "zipf_s1.1" if args.routing == "zipf" else "uniform",
                    "exchange": "NCCL all-to-all-v (dispatch rows + metadata, fp32 partial sums back)",
+                   "micro_batches": args.micro_batches,
                    "l2": "flushed before every step (256 MiB write); inputs > L2", "parallelism": f"ep{world}"},
         "tflops_per_gpu": round(tf, 1), "roofline": roofline,
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
@@ -697,6 +698,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
+    ap.add_argument("--micro-batches", type=int, default=1,
+                    help="N > 1: token parts whose exchanges overlap the expert GEMMs of their neighbours")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

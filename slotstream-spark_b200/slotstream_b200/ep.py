@@ -72,38 +72,72 @@ def _prefix(v: list[int]) -> list[int]:
     return out
 
 
-def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bool = False):
+def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bool = False,
+               micro_batches: int = 1):
     """One expert-parallel MoE layer over this rank's tokens x [T, H] -> y bf16 [T, H].
-    ``ops`` supplies the per-rank compute (``CudaOps`` on B200); the exchange is the same for every backend."""
+    ``ops`` supplies the per-rank compute (``CudaOps`` on B200); the exchange is the same for every backend.
+
+    ``micro_batches`` = m > 1 splits the tokens into m contiguous parts with their own plans: the counts of
+    all parts go in one all-to-all (still one host sync), every exchange is asynchronous, and part i's expert
+    GEMMs are issued after part i+1's dispatch and before part i-1's return, so on NCCL the transfers of one
+    part overlap the math of its neighbour. Every token's arithmetic is the same as with m = 1."""
     G = n_ranks
+    t_all = x.shape[0]
+    m = max(1, min(int(micro_batches), t_all)) if t_all else 1
     ids, w, sh_gate = ops.route(x)
     sh = ops.shared(x, sh_gate)
-    plan = ops.plan(ids, w)
-    recv_count = torch.empty_like(plan.dest_count)
-    dist.all_to_all_single(recv_count.view(-1), plan.dest_count.view(-1), group=group)
-    both = torch.cat([plan.dest_count.view(-1), recv_count.view(-1)]).cpu().tolist()   # the one host sync
-    sc = [both[2 * d:2 * d + 2] for d in range(G)]
-    rc = [both[2 * G + 2 * d:2 * G + 2 * d + 2] for d in range(G)]
-    send_rows, send_ent = [c[0] for c in sc], [c[1] for c in sc]
-    recv_rows, recv_ent = [c[0] for c in rc], [c[1] for c in rc]
-    n_send = sum(send_rows)
-    plan.send_token, plan.send_meta = plan.send_token[:n_send], plan.send_meta[:n_send]
-    send_x = ops.gather(x, plan.send_token)
-    n_recv = sum(recv_rows)
-    recv_x = x.new_empty((n_recv, x.shape[1]))
-    dist.all_to_all_single(recv_x, send_x, recv_rows, send_rows, group=group)
-    recv_meta = plan.send_meta.new_empty((n_recv, plan.send_meta.shape[1]))
-    dist.all_to_all_single(recv_meta, plan.send_meta, recv_rows, send_rows, group=group)
-    entries = ops.unpack(recv_meta, _prefix(recv_rows), _prefix(recv_ent), sum(recv_ent))
-    out_rows = ops.experts(recv_x, entries)
-    if exact:
-        ret = out_rows.new_empty((sum(send_ent), out_rows.shape[1]))
-        dist.all_to_all_single(ret, out_rows, send_ent, recv_ent, group=group)
-        return ops.combine(ret, plan, ids, _prefix(send_ent)[:G], sh, exact=True)
-    partial = ops.combine_rows(out_rows, entries)
-    ret = partial.new_empty((sum(send_rows), partial.shape[1]))
-    dist.all_to_all_single(ret, partial, send_rows, recv_rows, group=group)
-    return ops.combine(ret, plan, ids, None, sh, exact=False)
+    bounds = [t_all * i // m for i in range(m + 1)]
+    parts = [(bounds[i], bounds[i + 1]) for i in range(m)]
+    plans = [ops.plan(ids[a:b], w[a:b]) for a, b in parts]
+    send_counts = torch.stack([p.dest_count for p in plans], dim=1).contiguous()   # [G, m, 2]: per destination
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts.view(-1), send_counts.view(-1), group=group)
+    both = torch.cat([send_counts.view(-1), recv_counts.view(-1)]).cpu().tolist()   # the one host sync
+    half = G * m * 2
+    sc = [[both[(d * m + i) * 2:(d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
+    rc = [[both[half + (d * m + i) * 2:half + (d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
+    # dispatch every part (asynchronous: the math below waits only for its own part)
+    sent = []
+    for i, ((a, b), plan) in enumerate(zip(parts, plans)):
+        send_rows, send_ent = [c[0] for c in sc[i]], [c[1] for c in sc[i]]
+        recv_rows, recv_ent = [c[0] for c in rc[i]], [c[1] for c in rc[i]]
+        n_send, n_recv = sum(send_rows), sum(recv_rows)
+        plan.send_token, plan.send_meta = plan.send_token[:n_send], plan.send_meta[:n_send]
+        send_x = ops.gather(x[a:b], plan.send_token)
+        recv_x = x.new_empty((n_recv, x.shape[1]))
+        recv_meta = plan.send_meta.new_empty((n_recv, plan.send_meta.shape[1]))
+        works = [dist.all_to_all_single(recv_x, send_x, recv_rows, send_rows, group=group, async_op=True),
+                 dist.all_to_all_single(recv_meta, plan.send_meta, recv_rows, send_rows, group=group,
+                                        async_op=True)]
+        sent.append((send_x, recv_x, recv_meta, works, send_rows, send_ent, recv_rows, recv_ent))
+    # experts of each part as soon as its rows are in; its results go back asynchronously
+    returned = []
+    for i, (send_x, recv_x, recv_meta, works, send_rows, send_ent, recv_rows, recv_ent) in enumerate(sent):
+        for wk in works:
+            wk.wait()
+        entries = ops.unpack(recv_meta, _prefix(recv_rows), _prefix(recv_ent), sum(recv_ent))
+        out_rows = ops.experts(recv_x, entries)
+        if exact:
+            back = out_rows
+            ret = out_rows.new_empty((sum(send_ent), out_rows.shape[1]))
+            work = dist.all_to_all_single(ret, back, send_ent, recv_ent, group=group, async_op=True)
+        else:
+            back = ops.combine_rows(out_rows, entries)
+            ret = back.new_empty((sum(send_rows), back.shape[1]))
+            work = dist.all_to_all_single(ret, back, send_rows, recv_rows, group=group, async_op=True)
+        returned.append((ret, back, work))
+    ys, routed = [], []
+    for i, ((a, b), plan) in enumerate(zip(parts, plans)):
+        ret, _, work = returned[i]
+        work.wait()
+        send_ent = sent[i][5]
+        off = _prefix(send_ent)[:G] if exact else None
+        ys.append(ops.combine(ret, plan, ids[a:b], off, sh[a:b], exact=exact))
+        routed.append(ops.routed)
+    if m == 1:
+        return ys[0]
+    ops.routed = torch.cat(routed)
+    return torch.cat(ys)
 
 
 class CudaOps:

@@ -37,7 +37,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir, strided, exact, zipf):
+def _rank_main(rank, world, port, out_dir, strided, exact, zipf, mb=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -45,17 +45,19 @@ def _rank_main(rank, world, port, out_dir, strided, exact, zipf):
         recs, shared, rw, sg = _world(5)
         bias = synth.zipf_bias(E) * 4 if zipf else None
         ops = CpuOps(LAY, recs, shared, rw, sg, K, E, world, rank, strided=strided, bias=bias)
-        y = ep_forward(ops, bits_to_bf16(_tokens(rank)), K, world, exact=exact)
+        y = ep_forward(ops, bits_to_bf16(_tokens(rank)), K, world, exact=exact, micro_batches=mb)
         np.save(os.path.join(out_dir, f"routed{rank}.npy"), ops.routed.numpy())
         np.save(os.path.join(out_dir, f"y{rank}.npy"), y.view(torch.int16).numpy())
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("strided,exact,zipf", [(True, True, False), (False, True, True), (True, False, True)])
-def test_ep_exchange_matches_single_rank(tmp_path, strided, exact, zipf):
+@pytest.mark.parametrize("strided,exact,zipf,mb", [(True, True, False, 1), (False, True, True, 1), (True, False, True, 1),
+                                                   (True, True, True, 2), (False, False, False, 3)])
+def test_ep_exchange_matches_single_rank(tmp_path, strided, exact, zipf, mb):
+    """mb > 1: the tokens split into micro-batches with overlapped exchanges; the sums stay the same."""
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), strided, exact, zipf), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), strided, exact, zipf, mb), nprocs=world,
                        join=True, start_method="spawn")
     recs, shared, rw, sg = _world(5)
     bias = synth.zipf_bias(E) * 4 if zipf else None

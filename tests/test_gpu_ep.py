@@ -137,7 +137,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world_size, port, out_dir):
+def _nccl_rank(rank, world_size, port, out_dir, mb=1):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -154,7 +154,7 @@ def _nccl_rank(rank, world_size, port, out_dir):
         x = bf16_tensor(synth.activations(90 + rank, 300, lay.hidden))
         ops = CudaOps(W["rw"], W["sg"], base[owned_experts(rank, E, world_size, True)].cuda(), int(base[E]), K,
                       lay.inter, world_size, True, bias=W["bias"])
-        y = ep_forward(ops, x, K, world_size, exact=True)
+        y = ep_forward(ops, x, K, world_size, exact=True, micro_batches=mb)
         y1, _ = _one_gpu(W, x)
         torch.cuda.synchronize()
         ok = bool(torch.equal(y, y1)) and int(ops.err.item()) == 0
@@ -166,8 +166,11 @@ def _nccl_rank(rank, world_size, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_ranks_over_nccl_match_one_gpu(tmp_path):
+@pytest.mark.parametrize("mb", [1, 2])
+def test_two_ranks_over_nccl_match_one_gpu(tmp_path, mb):
+    """mb = 2: micro-batched exchange, the expert GEMMs of one part overlapping the transfers of the other."""
     import torch.multiprocessing as mp
-    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path), mb), nprocs=2, join=True,
+                       start_method="spawn")
     for r in range(2):
         assert (tmp_path / f"ok{r}").read_text() == "1"
