@@ -626,7 +626,7 @@ def bench_prefill_ep(args, world, rank):
     g.manual_seed(2100 + rank)                # each rank its own tokens
     x = torch.randn(T, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
     ops = CudaOps(router_w, sh_gate_w, group_ptr, recs.data_ptr() + len(owned) * rb, K, LAY.inter, world,
-                  strided=True, bias=bias)
+                  strided=True, bias=bias, sm_reserve=args.sm_reserve)
 
     def step():
         return ep_forward(ops, x, K, world, micro_batches=args.micro_batches)
@@ -670,7 +670,7 @@ def bench_prefill_ep(args, world, rank):
                    "inter": LAY.inter, "experts": E, "experts_per_gpu": len(owned), "placement": "strided (e % G)",
                    "topk": K, "shared_experts": 1, "routing": "zipf_s1.1" if args.routing == "zipf" else "uniform",
                    "exchange": "NCCL all-to-all-v (dispatch rows + metadata, fp32 partial sums back)",
-                   "micro_batches": args.micro_batches,
+                   "micro_batches": args.micro_batches, "gemm_sm_reserve": args.sm_reserve,
                    "l2": "flushed before every step (256 MiB write); inputs > L2", "parallelism": f"ep{world}"},
         "tflops_per_gpu": round(tf, 1), "roofline": roofline,
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
@@ -700,6 +700,8 @@ def main():
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="N > 1: token parts whose exchanges overlap the expert GEMMs of their neighbours")
+    ap.add_argument("--sm-reserve", type=int, default=0,
+                    help="N > 1 with micro-batches: SMs the persistent GEMMs leave to the overlapped all-to-alls")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

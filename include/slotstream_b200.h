@@ -53,6 +53,12 @@ int ssb_device_check(void);
  * (slotstream_spark/kernels/gemv_affine.py:15-25). */
 int ssb_kernel_smem(const char* name);
 
+/* Number of SMs the persistent grouped GEMMs (ssb_prefill_experts, ssb_fused_moe_*, ssb_gemm_dense) leave
+ * free at their next launches (default 0: one CTA on every SM), so that kernels on another stream -- the
+ * all-to-all of an expert-parallel exchange -- can run beside them. A process-wide setting read at each launch.
+ * No counterpart in the reference (it runs on one GPU with no collective to overlap). */
+int ssb_set_gemm_sm_reserve(int32_t sms);
+
 /* Stable top-k of each row of fp32 scores [rows, n] (n <= 65536, 1 <= k <= n): order-preserving uint32
  * keys (NaN lowest), ties to the lower index; k <= 16 sorted by (value desc, index asc), larger k by
  * index asc; rows with fewer than k valid entries pad with index -1 / value -inf. n_valid (int32 [rows])

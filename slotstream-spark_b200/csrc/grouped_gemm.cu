@@ -712,6 +712,10 @@ __global__ void __launch_bounds__(256) k_permute_by_row(const uint4* __restrict_
   }
 }
 
+// SMs the persistent GEMM leaves free for kernels that run beside it (collectives on another stream); set by
+// ssb_set_gemm_sm_reserve, read at each launch.
+int g_sm_reserve = 0;
+
 int num_sms() {
   static int sms = 0;
   if (!sms) {
@@ -771,7 +775,9 @@ int launch(int epi, GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t s
   a.n_mblocks = n_mblocks;
   a.n_nblocks = n_nblocks;
   const int64_t tiles = n_mblocks * n_nblocks;
-  const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+  int ctas = num_sms() - g_sm_reserve;
+  if (ctas < 1) ctas = 1;
+  const int grid = (int)(tiles < ctas ? tiles : ctas);
   return ssb_launch(k, dim3(grid), dim3(THREADS), SMEM_BYTES, st, true, tm, a);
 }
 
@@ -1004,4 +1010,10 @@ extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uin
   g.ldo = ldo;
   g.err = nullptr;
   return launch(EPI_PLAIN, g, (m + TM - 1) / TM, n / BN, (cudaStream_t)stream);
+}
+
+extern "C" int ssb_set_gemm_sm_reserve(int32_t sms) {
+  SSB_CHECK_ARG(sms >= 0 && sms < 1024);
+  g_sm_reserve = sms;
+  return SSB_OK;
 }

@@ -84,6 +84,18 @@ def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bo
     G = n_ranks
     t_all = x.shape[0]
     m = max(1, min(int(micro_batches), t_all)) if t_all else 1
+    reserve = getattr(ops, "sm_reserve", 0) if m > 1 and G > 1 else 0
+    if reserve:
+        ops.reserve_sms(reserve)   # the overlapped all-to-alls need SMs beside the persistent GEMMs
+    try:
+        return _ep_forward(ops, x, k, G, group, exact, m)
+    finally:
+        if reserve:
+            ops.reserve_sms(0)
+
+
+def _ep_forward(ops, x, k, G, group, exact, m):
+    t_all = x.shape[0]
     ids, w, sh_gate = ops.route(x)
     sh = ops.shared(x, sh_gate)
     bounds = [t_all * i // m for i in range(m + 1)]
@@ -147,7 +159,7 @@ class CudaOps:
     base of the shared expert; w_router bf16 [E, H] and sh_gate_w bf16 [H] are replicated on every rank."""
 
     def __init__(self, w_router, sh_gate_w, group_ptr, shared_ptr: int, k: int, inter: int, n_ranks: int,
-                 strided: bool = True, bias=None, logits_round_bf16: bool = False):
+                 strided: bool = True, bias=None, logits_round_bf16: bool = False, sm_reserve: int = 0):
         e, h = w_router.shape
         if n_ranks < 1 or n_ranks > MAX_RANKS or e % n_ranks:
             raise ValueError(f"need 1 <= n_ranks <= {MAX_RANKS} dividing the expert count")
@@ -162,6 +174,10 @@ class CudaOps:
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self._static = {}
         self._side, self._sh_ready = None, None
+        self.sm_reserve = int(sm_reserve)   # SMs left to the collectives while micro-batches overlap
+
+    def reserve_sms(self, n: int):
+        _lib.check(_lib.lib().ssb_set_gemm_sm_reserve(int(n)), "set gemm sm reserve")
 
     # ---------------------------------------------------------------- helpers
     def _aligned(self, row_expert, num_local):
