@@ -694,6 +694,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="decode batch")
     ap.add_argument("--layers", type=int, default=48, help="decode layers per step (48 = configs[1])")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement at N=1")
+    ap.add_argument("--no-chunks", action="store_true", help="skip the 2K / 8K-token prefill sub-measurements")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -723,6 +724,18 @@ def main():
     else:
         res = bench_prefill(args, world, rank)
         torch.cuda.empty_cache()
+        if world == 1 and not args.no_chunks:
+            # configs[2] also names 2,048- and 8,192-token chunks: the same layer, measured the same way
+            res["chunks"] = {}
+            for tk in (2048, 8192, 32768):
+                if tk == args.tokens:
+                    continue
+                a2 = argparse.Namespace(**vars(args))
+                a2.tokens = tk
+                c = bench_prefill(a2, world, rank)
+                res["chunks"][str(tk)] = {k: c[k] for k in ("value", "unit", "ms_per_step", "tflops", "roofline",
+                                                            "e2e", "clocks", "device_errors")}
+                torch.cuda.empty_cache()
         if world == 1 and not args.no_decode:
             W = decode_world(args, rank)
             d = bench_decode(args, world, rank, 1, W)
