@@ -114,3 +114,22 @@ def test_prefill_layer_matches_decode_layer_routing(layer):
     O.ids_match(pb.ids.cpu().numpy(), db.ids.cpu().numpy(), logits)
     same = (pb.ids == db.ids).all(dim=1).cpu().numpy()
     np.testing.assert_allclose(pb.w.cpu().numpy()[same], db.w.cpu().numpy()[same], rtol=2e-5, atol=1e-7)
+
+
+def test_prefill_layer_same_bits_with_sms_reserved(layer):
+    """ssb_set_gemm_sm_reserve shrinks the persistent GEMMs' grid (SMs left to collectives on another stream);
+    a row's result depends only on its row and expert, never on which CTA computed its tile."""
+    from slotstream_b200 import _lib
+    L = layer
+    x = synth.activations(23, 2500, L["lay"].hidden)
+    bias = synth.zipf_bias(E)
+    y0, b0 = _run(L, x, bias)
+    try:
+        _lib.check(_lib.lib().ssb_set_gemm_sm_reserve(120), "set reserve")
+        y1, b1 = _run(L, x, bias)
+    finally:
+        _lib.check(_lib.lib().ssb_set_gemm_sm_reserve(0), "clear reserve")
+    assert torch.equal(b0.ids, b1.ids)
+    assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+    assert torch.equal(b0.out_rows, b1.out_rows)
+    assert _lib.lib().ssb_set_gemm_sm_reserve(-1) == _lib.SSB_EINVAL
