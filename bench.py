@@ -39,6 +39,7 @@ L2_FLUSH_BYTES = 256 << 20
 # dram__bytes_write.sum, one pass) on the bench's own workloads; commands and figures under profiles/
 TRAFFIC_BYTES = {
     "prefill_gate_up_32768": 2_360_000_000 + 357_240_000,   # full 32,768-token layer, profiles/grouped_gemm_traffic_32k.md
+    "prefill_gate_up_8192": 745_336_832 + 84_327_424,       # 8,192-token layer, profiles/prefill_layer_8k_launches.md
     "decode_fused_b1": 21_684_736,                          # one b = 1 layer, profiles/decode_fused_b1.md
 }
 
