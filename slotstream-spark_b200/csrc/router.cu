@@ -335,10 +335,11 @@ int launch_select(SelectArgs a, void* stream);
 
 extern "C" int ssb_router_logits(const uint16_t* x, const uint16_t* w, const uint16_t* w_extra, int64_t tokens,
                                  int32_t hidden, int32_t n_rows, int32_t ld, float* logits, void* stream) {
-  SSB_CHECK_ARG(x && w && logits && tokens >= 0 && n_rows >= 1);
+  SSB_CHECK_ARG(tokens >= 0 && n_rows >= 1);
   if (hidden % 256 || hidden <= 0 || hidden > 4096) return SSB_EUNSUPPORTED;
   SSB_CHECK_ARG(ld >= n_rows + (w_extra ? 1 : 0));
-  if (tokens == 0) return SSB_OK;
+  if (tokens == 0) return SSB_OK;   // empty tensors may come with null pointers
+  SSB_CHECK_ARG(x && w && logits);
   const int n_total = n_rows + (w_extra ? 1 : 0);
   if (n_total == 1 && tokens >= 1024) {   // one row over many tokens: no staging of x, a warp per token
     const int64_t per_cta = (int64_t)RL1_WARPS * RL1_TPW;
@@ -358,8 +359,9 @@ extern "C" int ssb_router_logits(const uint16_t* x, const uint16_t* w, const uin
 
 extern "C" int ssb_topk_stable(const float* scores, const int32_t* n_valid, int64_t rows, int32_t n, int32_t k,
                                int32_t* out_idx, float* out_val, void* stream) {
-  SSB_CHECK_ARG(scores && out_idx && rows >= 0 && n >= 1 && n <= 65536 && k >= 1 && k <= n);
-  if (rows == 0) return SSB_OK;
+  SSB_CHECK_ARG(rows >= 0 && n >= 1 && n <= 65536 && k >= 1 && k <= n);
+  if (rows == 0) return SSB_OK;   // empty tensors may come with null pointers
+  SSB_CHECK_ARG(scores && out_idx);
   SSB_CHECK_ARG(rows <= 2147483647LL);
   ssb_note_smem("topk_stable", k_topk_stable, 0);
   return ssb_launch(k_topk_stable, dim3((unsigned)rows), dim3(TK_THREADS), 0, (cudaStream_t)stream, true, scores,
@@ -369,12 +371,13 @@ extern "C" int ssb_topk_stable(const float* scores, const int32_t* n_valid, int6
 namespace {
 
 int launch_select(SelectArgs a, void* stream) {
-  SSB_CHECK_ARG(a.logits && a.out_idx && a.out_w && a.tokens >= 0);
+  SSB_CHECK_ARG(a.tokens >= 0);
   SSB_CHECK_ARG(a.experts >= 1 && a.experts <= 32 * RS_MAXE && a.k >= 1 && a.k <= 32 && a.k <= a.experts);
   SSB_CHECK_ARG(a.ld >= a.experts + ((a.flags & SSB_ROUTER_SHARED_GATE) ? 1 : 0));
-  SSB_CHECK_ARG(!(a.flags & SSB_ROUTER_SHARED_GATE) || a.out_sh_gate);
   SSB_CHECK_ARG(a.prefetch_bytes % 16 == 0);
-  if (a.tokens == 0) return SSB_OK;
+  if (a.tokens == 0) return SSB_OK;   // empty tensors may come with null pointers
+  SSB_CHECK_ARG(a.logits && a.out_idx && a.out_w);
+  SSB_CHECK_ARG(!(a.flags & SSB_ROUTER_SHARED_GATE) || a.out_sh_gate);
   const int epl = (a.experts + 31) / 32;
   const int nw = rs_warps(epl <= 4 ? 4 : epl <= 8 ? 8 : epl <= 16 ? 16 : 32);
   dim3 grid((unsigned)((a.tokens + nw - 1) / nw));
@@ -457,12 +460,13 @@ extern "C" int ssb_router_topk_static(const uint16_t* x, const uint16_t* w, cons
                                       int64_t tokens, int32_t hidden, int32_t experts, int32_t k,
                                       const float* bias, int32_t flags, int32_t* out_idx, float* out_w,
                                       float* out_sh_gate, void* stream) {
-  SSB_CHECK_ARG(x && w && out_idx && out_w && tokens >= 0 && experts >= 1 && k >= 1);
+  SSB_CHECK_ARG(tokens >= 0 && experts >= 1 && k >= 1);
   SSB_CHECK_ARG(k <= 32 && k <= experts && experts <= 32 * RS_MAXE && (flags & ~SSB_ROUTER_ROUND_BF16) == 0);
-  SSB_CHECK_ARG(!w_shared_gate || out_sh_gate);
   const int32_t ld = experts + (w_shared_gate ? 1 : 0);
   if (tokens > ROUTER_STATIC_LOGITS / ld) return SSB_ETOOBIG;
-  if (tokens == 0) return SSB_OK;
+  if (tokens == 0) return SSB_OK;   // empty tensors may come with null pointers
+  SSB_CHECK_ARG(x && w && out_idx && out_w);
+  SSB_CHECK_ARG(!w_shared_gate || out_sh_gate);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
