@@ -630,7 +630,7 @@ def bench_prefill_ep(args, world, rank):
                   strided=True, bias=bias, sm_reserve=args.sm_reserve)
 
     def step():
-        return ep_forward(ops, x, K, world, micro_batches=args.micro_batches)
+        return ep_forward(ops, x, K, world, micro_batches=args.micro_batches, partials_bf16=args.partials == "bf16")
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
@@ -670,7 +670,7 @@ def bench_prefill_ep(args, world, rank):
         "config": {"workload": f"ep_prefill_layer_{T}tok_per_gpu", "tokens_per_gpu": T, "hidden": LAY.hidden,
                    "inter": LAY.inter, "experts": E, "experts_per_gpu": len(owned), "placement": "strided (e % G)",
                    "topk": K, "shared_experts": 1, "routing": "zipf_s1.1" if args.routing == "zipf" else "uniform",
-                   "exchange": "NCCL all-to-all-v (dispatch rows + metadata, fp32 partial sums back)",
+                   "exchange": f"NCCL all-to-all-v (dispatch rows + metadata, {args.partials} partial sums back)",
                    "micro_batches": args.micro_batches, "gemm_sm_reserve": args.sm_reserve,
                    "l2": "flushed before every step (256 MiB write); inputs > L2", "parallelism": f"ep{world}"},
         "tflops_per_gpu": round(tf, 1), "roofline": roofline,
@@ -702,6 +702,8 @@ def main():
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="N > 1: token parts whose exchanges overlap the expert GEMMs of their neighbours")
+    ap.add_argument("--partials", choices=["fp32", "bf16"], default="fp32",
+                    help="N > 1: precision of the per-(token, destination) partial sums sent back")
     ap.add_argument("--sm-reserve", type=int, default=0,
                     help="N > 1 with micro-batches: SMs the persistent GEMMs leave to the overlapped all-to-alls")
     args = ap.parse_args()

@@ -174,6 +174,10 @@ int ssb_ep_unpack(const int32_t* meta, int64_t rows, int32_t k, const int32_t* s
 int ssb_combine_rows(const float* rows, const int64_t* row_e0, const int32_t* row_cnt, int64_t n, int32_t hidden,
                      float* partial, void* stream);
 
+/* The same sums rounded to bf16 (round to nearest even): a half-size partial-sum return for the exchange. */
+int ssb_combine_rows_bf16(const float* rows, const int64_t* row_e0, const int32_t* row_cnt, int64_t n,
+                          int32_t hidden, uint16_t* partial, void* stream);
+
 /* Home combine of the returned rows: exact = 0 sums the partial rows ret[tok_slot[t, d]] over d ascending;
  * exact = 1 sums the entry rows ret[ret_entry_off[d] + tok_entry[t, d] + i] in router-rank order (bit-equal
  * to the one-GPU layer). out fp32 [tokens, hidden] (nullable); y bf16 = bf16(bf16(routed) + bf16(sh))
@@ -182,6 +186,12 @@ int ssb_ep_combine(const float* ret, const int32_t* tok_slot, const int32_t* tok
                    const int32_t* ids, int64_t tokens, int32_t k, int32_t experts_per_rank, int32_t n_ranks,
                    int32_t strided, int32_t exact, int32_t hidden, const float* sh, float* out, uint16_t* y,
                    void* stream);
+
+/* Home combine of bf16 partial rows (ssb_combine_rows_bf16 on the destinations): routed[t] = sum over d ascending
+ * of float(ret[tok_slot[t, d]]) in fp32; out / y as ssb_ep_combine. */
+int ssb_ep_combine_bf16(const uint16_t* ret, const int32_t* tok_slot, const int32_t* ids, int64_t tokens, int32_t k,
+                        int32_t experts_per_rank, int32_t n_ranks, int32_t strided, int32_t hidden, const float* sh,
+                        float* out, uint16_t* y, void* stream);
 
 /* ---- HBM expert slot pool for streaming decode (additive; the B200 side of slotio's Pool + Ensurer,
  * slotio/include/slotio/pool.hpp:23-160 and slotio/src/ensure.cpp). Unlike the kernel entry points, the pool

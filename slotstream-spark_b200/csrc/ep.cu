@@ -274,10 +274,23 @@ __global__ void k_ep_unpack(const int32_t* __restrict__ meta, int64_t n, int k, 
   }
 }
 
-// partial[r, :] = rows[e0] + rows[e0 + 1] + ... + rows[e0 + cnt - 1] (e0 = row_e0[r]), sequential fp32.
+// partial[r, :] = rows[e0] + rows[e0 + 1] + ... + rows[e0 + cnt - 1] (e0 = row_e0[r]), sequential fp32; stored as
+// fp32 (float4) or rounded to bf16 (uint2: four bf16, round to nearest even) for a half-size return.
+SSB_DEV void store4(float4* p, float4 v) { *p = v; }
+SSB_DEV void store4(uint2* p, float4 v) {
+  *p = make_uint2((uint32_t)f32_to_bf16(v.x) | ((uint32_t)f32_to_bf16(v.y) << 16),
+                  (uint32_t)f32_to_bf16(v.z) | ((uint32_t)f32_to_bf16(v.w) << 16));
+}
+SSB_DEV float4 load4(const float4* p) { return __ldcs(p); }
+SSB_DEV float4 load4(const uint2* p) {
+  const uint2 b = __ldcs(p);
+  return make_float4(bf16_lo(b.x), bf16_hi(b.x), bf16_lo(b.y), bf16_hi(b.y));
+}
+
+template <typename P4>
 __global__ void __launch_bounds__(256) k_combine_rows(const float4* __restrict__ rows, const int64_t* __restrict__ row_e0,
                                                       const int32_t* __restrict__ row_cnt, int64_t n, int64_t h4,
-                                                      float4* __restrict__ partial) {
+                                                      P4* __restrict__ partial) {
   pdl_wait();
   pdl_trigger();
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < n * h4; v += (int64_t)gridDim.x * blockDim.x) {
@@ -292,7 +305,7 @@ __global__ void __launch_bounds__(256) k_combine_rows(const float4* __restrict__
       acc.z += x.z;
       acc.w += x.w;
     }
-    partial[v] = acc;
+    store4(partial + v, acc);
   }
 }
 
@@ -300,7 +313,8 @@ __global__ void __launch_bounds__(256) k_combine_rows(const float4* __restrict__
 // (the partial row that d returned for t); exact != 0: routed[t] = sum over j (router rank order) of the entry
 // row ret[ret_entry_off[d] + tok_entry[t, d] + i], d the rank of ids[t, j] and i the count of t's earlier
 // choices on d. out (fp32 [T, H], nullable) gets routed; y (nullable) = bf16(bf16(routed) + bf16(sh)).
-__global__ void __launch_bounds__(256) k_ep_combine(const float4* __restrict__ ret, const int32_t* __restrict__ tok_slot,
+template <typename R4>
+__global__ void __launch_bounds__(256) k_ep_combine(const R4* __restrict__ ret, const int32_t* __restrict__ tok_slot,
                                                     const int32_t* __restrict__ tok_entry,
                                                     const int64_t* __restrict__ ret_entry_off,
                                                     const int32_t* __restrict__ ids, int64_t T, int k, Placement pl,
@@ -321,7 +335,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const float4* __restrict__ r
         const int i = (int)((seen >> (4 * d)) & 15u);
         seen += 1ull << (4 * d);
         const int64_t row = __ldg(ret_entry_off + d) + __ldcg(tok_entry + t * G + d) + i;
-        const float4 x = __ldcs(ret + row * h4 + c);
+        const float4 x = load4(ret + row * h4 + c);
         acc.x += x.x;
         acc.y += x.y;
         acc.z += x.z;
@@ -331,7 +345,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const float4* __restrict__ r
       for (int d = 0; d < G; ++d) {
         const int sl = __ldcg(tok_slot + t * G + d);
         if (sl < 0) continue;
-        const float4 x = __ldcs(ret + (int64_t)sl * h4 + c);
+        const float4 x = load4(ret + (int64_t)sl * h4 + c);
         acc.x += x.x;
         acc.y += x.y;
         acc.z += x.z;
@@ -422,8 +436,18 @@ extern "C" int ssb_combine_rows(const float* rows, const int64_t* row_e0, const 
   if (n == 0) return SSB_OK;
   SSB_CHECK_ARG(rows && row_e0 && row_cnt && partial && ((((uintptr_t)rows) | ((uintptr_t)partial)) & 15) == 0);
   const int64_t h4 = hidden / 4;
-  return ssb_launch(k_combine_rows, dim3(grid_for(n * h4, 256)), dim3(256), 0, (cudaStream_t)stream, true,
+  return ssb_launch(k_combine_rows<float4>, dim3(grid_for(n * h4, 256)), dim3(256), 0, (cudaStream_t)stream, true,
                     (const float4*)rows, row_e0, row_cnt, n, h4, (float4*)partial);
+}
+
+extern "C" int ssb_combine_rows_bf16(const float* rows, const int64_t* row_e0, const int32_t* row_cnt, int64_t n,
+                                     int32_t hidden, uint16_t* partial, void* stream) {
+  SSB_CHECK_ARG(n >= 0 && hidden > 0 && hidden % 4 == 0);
+  if (n == 0) return SSB_OK;
+  SSB_CHECK_ARG(rows && row_e0 && row_cnt && partial && ((uintptr_t)rows & 15) == 0 && ((uintptr_t)partial & 7) == 0);
+  const int64_t h4 = hidden / 4;
+  return ssb_launch(k_combine_rows<uint2>, dim3(grid_for(n * h4, 256)), dim3(256), 0, (cudaStream_t)stream, true,
+                    (const float4*)rows, row_e0, row_cnt, n, h4, (uint2*)partial);
 }
 
 extern "C" int ssb_ep_combine(const float* ret, const int32_t* tok_slot, const int32_t* tok_entry,
@@ -436,8 +460,22 @@ extern "C" int ssb_ep_combine(const float* ret, const int32_t* tok_slot, const i
   SSB_CHECK_ARG(ret && ids && (exact ? (tok_entry && ret_entry_off) : tok_slot != nullptr));
   SSB_CHECK_ARG((((uintptr_t)ret | (uintptr_t)sh | (uintptr_t)out) & 15) == 0 && ((uintptr_t)y & 7) == 0);
   const int64_t h4 = hidden / 4;
-  return ssb_launch(k_ep_combine, dim3(grid_for(tokens * h4, 256)), dim3(256), 0, (cudaStream_t)stream, true,
+  return ssb_launch(k_ep_combine<float4>, dim3(grid_for(tokens * h4, 256)), dim3(256), 0, (cudaStream_t)stream, true,
                     (const float4*)ret, tok_slot, tok_entry, ret_entry_off, ids, tokens, k,
                     Placement{experts_per_rank, n_ranks, strided}, exact, h4, (const float4*)sh, (float4*)out,
                     (uint2*)y);
+}
+
+extern "C" int ssb_ep_combine_bf16(const uint16_t* ret, const int32_t* tok_slot, const int32_t* ids, int64_t tokens,
+                                   int32_t k, int32_t experts_per_rank, int32_t n_ranks, int32_t strided,
+                                   int32_t hidden, const float* sh, float* out, uint16_t* y, void* stream) {
+  SSB_CHECK_ARG(tokens >= 0 && k >= 1 && k <= 15 && placement_ok(experts_per_rank, n_ranks, strided));
+  SSB_CHECK_ARG(hidden > 0 && hidden % 4 == 0);
+  if (tokens == 0) return SSB_OK;
+  SSB_CHECK_ARG(ret && ids && tok_slot && (out || y));
+  SSB_CHECK_ARG((((uintptr_t)ret & 7) | (((uintptr_t)sh | (uintptr_t)out) & 15)) == 0 && ((uintptr_t)y & 7) == 0);
+  const int64_t h4 = hidden / 4;
+  return ssb_launch(k_ep_combine<uint2>, dim3(grid_for(tokens * h4, 256)), dim3(256), 0, (cudaStream_t)stream, true,
+                    (const uint2*)ret, tok_slot, (const int32_t*)nullptr, (const int64_t*)nullptr, ids, tokens, k,
+                    Placement{experts_per_rank, n_ranks, strided}, 0, h4, (const float4*)sh, (float4*)out, (uint2*)y);
 }

@@ -39,7 +39,9 @@ SIGNATURES = {
     "ssb_gather_rows": [_P, _I64, _P, _I64, _I64, _P, _P, _P],
     "ssb_ep_unpack": [_P, _I64, _I32, _P, _P, _I32, _I64, _P, _P, _P, _P, _P, _P, _P],
     "ssb_combine_rows": [_P, _P, _P, _I64, _I32, _P, _P],
+    "ssb_combine_rows_bf16": [_P, _P, _P, _I64, _I32, _P, _P],
     "ssb_ep_combine": [_P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+    "ssb_ep_combine_bf16": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
     "ssb_moe_decode_fused": [_P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _P,
                              _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "ssb_pool_create": [_I64, _I64, _I32, _I32, _I32],

@@ -73,14 +73,18 @@ def _prefix(v: list[int]) -> list[int]:
 
 
 def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bool = False,
-               micro_batches: int = 1):
+               micro_batches: int = 1, partials_bf16: bool = False):
     """One expert-parallel MoE layer over this rank's tokens x [T, H] -> y bf16 [T, H].
     ``ops`` supplies the per-rank compute (``CudaOps`` on B200); the exchange is the same for every backend.
 
     ``micro_batches`` = m > 1 splits the tokens into m contiguous parts with their own plans: the counts of
     all parts go in one all-to-all (still one host sync), every exchange is asynchronous, and part i's expert
     GEMMs are issued after part i+1's dispatch and before part i-1's return, so on NCCL the transfers of one
-    part overlap the math of its neighbour. Every token's arithmetic is the same as with m = 1."""
+    part overlap the math of its neighbour. Every token's arithmetic is the same as with m = 1.
+
+    ``partials_bf16`` (default mode only): the per-(token, destination) partial sums are rounded to bf16 before
+    they go back, halving the return bytes; routed then differs from the fp32 return by the partials'
+    rounding (a relative 2^-9 each)."""
     G = n_ranks
     t_all = x.shape[0]
     m = max(1, min(int(micro_batches), t_all)) if t_all else 1
@@ -88,13 +92,13 @@ def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bo
     if reserve:
         ops.reserve_sms(reserve)   # the overlapped all-to-alls need SMs beside the persistent GEMMs
     try:
-        return _ep_forward(ops, x, k, G, group, exact, m)
+        return _ep_forward(ops, x, k, G, group, exact, m, bool(partials_bf16) and not exact)
     finally:
         if reserve:
             ops.reserve_sms(0)
 
 
-def _ep_forward(ops, x, k, G, group, exact, m):
+def _ep_forward(ops, x, k, G, group, exact, m, bf16):
     t_all = x.shape[0]
     ids, w, sh_gate = ops.route(x)
     sh = ops.shared(x, sh_gate)
@@ -134,7 +138,7 @@ def _ep_forward(ops, x, k, G, group, exact, m):
             ret = out_rows.new_empty((sum(send_ent), out_rows.shape[1]))
             work = dist.all_to_all_single(ret, back, send_ent, recv_ent, group=group, async_op=True)
         else:
-            back = ops.combine_rows(out_rows, entries)
+            back = ops.combine_rows(out_rows, entries, bf16=bf16)
             ret = back.new_empty((sum(send_rows), back.shape[1]))
             work = dist.all_to_all_single(ret, back, send_rows, recv_rows, group=group, async_op=True)
         returned.append((ret, back, work))
@@ -144,7 +148,7 @@ def _ep_forward(ops, x, k, G, group, exact, m):
         work.wait()
         send_ent = sent[i][5]
         off = _prefix(send_ent)[:G] if exact else None
-        ys.append(ops.combine(ret, plan, ids[a:b], off, sh[a:b], exact=exact))
+        ys.append(ops.combine(ret, plan, ids[a:b], off, sh[a:b], exact=exact, bf16=bf16))
         routed.append(ops.routed)
     if m == 1:
         return ys[0]
@@ -276,15 +280,17 @@ class CudaOps:
         return self._experts(recv_x, recv_x.shape[0], ent.row_token, ent.row_weight, ent.row_expert, self.group_ptr,
                              self.epr, -1)
 
-    def combine_rows(self, out_rows, ent):
+    def combine_rows(self, out_rows, ent, bf16: bool = False):
         n = ent.row_e0.numel()
-        partial = torch.empty((n, self.hidden), dtype=torch.float32, device=out_rows.device)
+        partial = torch.empty((n, self.hidden), dtype=torch.bfloat16 if bf16 else torch.float32,
+                              device=out_rows.device)
         P = _lib.ptr
-        _lib.check(_lib.lib().ssb_combine_rows(P(out_rows), P(ent.row_e0), P(ent.row_cnt), n, self.hidden, P(partial),
-                                               _lib.stream()), "combine rows")
+        fn = _lib.lib().ssb_combine_rows_bf16 if bf16 else _lib.lib().ssb_combine_rows
+        _lib.check(fn(P(out_rows), P(ent.row_e0), P(ent.row_cnt), n, self.hidden, P(partial), _lib.stream()),
+                   "combine rows")
         return partial
 
-    def combine(self, ret, plan, ids, ret_entry_off, sh, exact):
+    def combine(self, ret, plan, ids, ret_entry_off, sh, exact, bf16: bool = False):
         t = ids.shape[0]
         dev = ids.device
         self.routed = torch.empty((t, self.hidden), dtype=torch.float32, device=dev)
@@ -294,6 +300,11 @@ class CudaOps:
         if self._sh_ready is not None:
             torch.cuda.current_stream().wait_event(self._sh_ready)   # the shared expert's rows (side stream)
         P = _lib.ptr
+        if bf16 and not exact:   # bf16 partial rows
+            _lib.check(_lib.lib().ssb_ep_combine_bf16(P(ret), P(plan.tok_slot), P(ids), t, self.k, self.epr, self.G,
+                                                      int(self.strided), self.hidden, P(sh), P(self.routed), P(y),
+                                                      _lib.stream()), "ep combine")
+            return y
         _lib.check(_lib.lib().ssb_ep_combine(P(ret), P(plan.tok_slot), P(plan.tok_entry), P(reo), P(ids), t, self.k,
                                              self.epr, self.G, int(self.strided), int(exact), self.hidden, P(sh),
                                              P(self.routed), P(y), _lib.stream()), "ep combine")

@@ -65,10 +65,13 @@ class CpuOps:
                 for le, r, w in zip(ent.row_expert.numpy(), ent.row_token.numpy(), ent.row_weight.numpy())]
         return torch.from_numpy(np.array(rows, np.float32).reshape(-1, self.layout.hidden))
 
-    def combine_rows(self, out_rows, ent):
-        return torch.from_numpy(EO.combine_rows(out_rows.numpy(), ent.row_e0.numpy(), ent.row_cnt.numpy()))
+    def combine_rows(self, out_rows, ent, bf16=False):
+        part = EO.combine_rows(out_rows.numpy(), ent.row_e0.numpy(), ent.row_cnt.numpy())
+        if bf16:   # the bf16 return, carried as bf16-valued fp32 (gloo moves fp32)
+            part = O.round_bf16(part).astype(np.float32)
+        return torch.from_numpy(part)
 
-    def combine(self, ret, plan, ids, ret_entry_off, sh, exact):
+    def combine(self, ret, plan, ids, ret_entry_off, sh, exact, bf16=False):
         routed = EO.combine(ret.numpy(), plan.tok_slot.numpy(), plan.tok_entry.numpy(), ret_entry_off, ids.numpy(),
                             self.n_experts, self.G, self.strided, exact)
         self.routed = torch.from_numpy(routed)

@@ -37,7 +37,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir, strided, exact, zipf, mb=1):
+def _rank_main(rank, world, port, out_dir, strided, exact, zipf, mb=1, bf16=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -45,7 +45,7 @@ def _rank_main(rank, world, port, out_dir, strided, exact, zipf, mb=1):
         recs, shared, rw, sg = _world(5)
         bias = synth.zipf_bias(E) * 4 if zipf else None
         ops = CpuOps(LAY, recs, shared, rw, sg, K, E, world, rank, strided=strided, bias=bias)
-        y = ep_forward(ops, bits_to_bf16(_tokens(rank)), K, world, exact=exact, micro_batches=mb)
+        y = ep_forward(ops, bits_to_bf16(_tokens(rank)), K, world, exact=exact, micro_batches=mb, partials_bf16=bf16)
         np.save(os.path.join(out_dir, f"routed{rank}.npy"), ops.routed.numpy())
         np.save(os.path.join(out_dir, f"y{rank}.npy"), y.view(torch.int16).numpy())
     finally:
@@ -86,3 +86,18 @@ def test_plan_orders_rows_by_destination_then_token():
             assert sm[r, 2 * K + 1] == len(mine)
             assert [sm[r, j] for j in mine] == [ids[t, j] // 4 for j in mine]
     assert np.all((ts >= 0) == (te >= 0))
+
+
+def test_ep_exchange_with_bf16_partials(tmp_path):
+    """Default mode with the partial sums rounded to bf16 for the return: routed within the partials' rounding
+    (relative L2 under 2^-8) of the one-rank layer."""
+    world = 2
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), True, False, True, 2, True),
+                       nprocs=world, join=True, start_method="spawn")
+    recs, shared, rw, sg = _world(5)
+    for rank in range(world):
+        got = np.load(tmp_path / f"routed{rank}.npy").astype(np.float64)
+        ref = single_rank_reference(LAY, recs, shared, rw, sg, K, _tokens(rank), bias=synth.zipf_bias(E) * 4)
+        ref = ref.astype(np.float64)
+        assert np.linalg.norm(got - ref) <= 2.0 ** -8 * np.linalg.norm(ref)
+        assert not np.array_equal(got, ref)   # the rounding did happen

@@ -137,7 +137,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world_size, port, out_dir, mb=1):
+def _nccl_rank(rank, world_size, port, out_dir, mb=1, bf16=False):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -154,10 +154,15 @@ def _nccl_rank(rank, world_size, port, out_dir, mb=1):
         x = bf16_tensor(synth.activations(90 + rank, 300, lay.hidden))
         ops = CudaOps(W["rw"], W["sg"], base[owned_experts(rank, E, world_size, True)].cuda(), int(base[E]), K,
                       lay.inter, world_size, True, bias=W["bias"])
-        y = ep_forward(ops, x, K, world_size, exact=True, micro_batches=mb)
+        y = ep_forward(ops, x, K, world_size, exact=not bf16, micro_batches=mb, partials_bf16=bf16)
         y1, _ = _one_gpu(W, x)
         torch.cuda.synchronize()
-        ok = bool(torch.equal(y, y1)) and int(ops.err.item()) == 0
+        if bf16:   # partial sums rounded to bf16 on the return: within the layer tolerance of one GPU
+            d, r = (y.float() - y1.float()), y1.float()
+            ok = bool(d.norm() <= 5e-3 * r.norm()) and bool(d.abs().max() <= 2e-2 * r.abs().max())
+        else:
+            ok = bool(torch.equal(y, y1))
+        ok = ok and int(ops.err.item()) == 0
         with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
             f.write("1" if ok else "0")
         dist.barrier()
@@ -166,11 +171,12 @@ def _nccl_rank(rank, world_size, port, out_dir, mb=1):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mb", [1, 2])
-def test_two_ranks_over_nccl_match_one_gpu(tmp_path, mb):
-    """mb = 2: micro-batched exchange, the expert GEMMs of one part overlapping the transfers of the other."""
+@pytest.mark.parametrize("mb,bf16", [(1, False), (2, False), (1, True)])
+def test_two_ranks_over_nccl_match_one_gpu(tmp_path, mb, bf16):
+    """mb = 2: micro-batched exchange, the expert GEMMs of one part overlapping the transfers of the other;
+    bf16: partial sums returned in bf16 (default mode), compared within the layer tolerance."""
     import torch.multiprocessing as mp
-    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path), mb), nprocs=2, join=True,
+    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path), mb, bf16), nprocs=2, join=True,
                        start_method="spawn")
     for r in range(2):
         assert (tmp_path / f"ok{r}").read_text() == "1"
