@@ -702,7 +702,7 @@ def main():
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="N > 1: token parts whose exchanges overlap the expert GEMMs of their neighbours")
-    ap.add_argument("--partials", choices=["fp32", "bf16"], default="fp32",
+    ap.add_argument("--partials", choices=["fp32", "bf16"], default="bf16",
                     help="N > 1: precision of the per-(token, destination) partial sums sent back")
     ap.add_argument("--sm-reserve", type=int, default=0,
                     help="N > 1 with micro-batches: SMs the persistent GEMMs leave to the overlapped all-to-alls")
