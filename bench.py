@@ -35,13 +35,15 @@ import torch  # noqa: E402
 
 METRIC = "MoE-layer tokens/s (decode b=1 HBM GB/s; prefill TFLOPS) at 1/2/4/8 B200"
 L2_FLUSH_BYTES = 256 << 20
-# DRAM bytes (read + write) per launch of the dominant kernel, from ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum, one pass) on the bench's own workloads; commands and figures under profiles/
+# DRAM bytes (read + write) per launch of the dominant kernel: constants measured by ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum, one replay pass) on earlier runs of these same workloads, not in this run
 TRAFFIC_BYTES = {
-    "prefill_gate_up_32768": 2_360_000_000 + 357_240_000,   # full 32,768-token layer, profiles/grouped_gemm_traffic_32k.md
-    "prefill_gate_up_8192": 745_336_832 + 84_327_424,       # 8,192-token layer, profiles/prefill_layer_8k_launches.md
-    "decode_fused_b1": 21_684_736,                          # one b = 1 layer, profiles/decode_fused_b1.md
+    "prefill_gate_up_32768": 2_360_000_000 + 357_240_000,   # one gate_up launch of the 32,768-token layer
+    "prefill_gate_up_8192": 745_336_832 + 84_327_424,       # one gate_up launch of the 8,192-token layer
+    "decode_fused_b1": 21_684_736,                          # one fused b = 1 decode layer launch
 }
+TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, measured on an earlier run of " \
+                 "this workload (a constant of this file, not measured in this run)"
 
 
 def peaks():
@@ -198,6 +200,37 @@ def pipelined_steps(x_dev, graphs, y_dev, x_host, k, world):
     return t0.elapsed_time(t1) / k
 
 
+# ------------------------------------------------------------------ CPU leg (cpu_baseline + parity of this run)
+def cpu_leg_prefill(LAY, recs, router_w, sh_gate_w, bias, x, y_dev, ids_dev, passes):
+    """The reference's CPU path (oracle/cpu_baseline.py) over this run's own prefill chunk: the records, router
+    and tokens copied back from the GPU, `passes` timed passes over the whole chunk (0: one untimed pass), and the
+    GPU layer output of the timed step compared with the CPU result on the same bytes."""
+    from oracle.cpu_baseline import CpuLayer, parity, time_prefill_chunks
+    L = CpuLayer.from_tensors(LAY, recs.cpu(), router_w.cpu(), sh_gate_w.cpu(), None if bias is None else bias.cpu())
+    rec, y_cpu, ids_cpu = time_prefill_chunks(L, x.cpu(), n_chunks=max(1, passes))
+    par = parity(y_dev.cpu(), ids_dev.cpu(), y_cpu, ids_cpu)
+    par["reference"] = "CPU path of the reference (oracle/cpu_baseline.py) on the same records and tokens"
+    return (rec if passes else None), par
+
+
+def cpu_leg_decode(LAY, W, x0, y0, ids0, seconds):
+    """Decode layer 0 of this run on the CPU (its 512 records and shared record copied back): parity of the GPU
+    layer-0 output for the b tokens of the timed step, and, when seconds > 0, the CPU decode rate."""
+    from oracle.cpu_baseline import CpuLayer, decode_token_layer, parity, time_decode
+    E = 512
+    recs = torch.cat([W["recs"][:E], W["shared"][:1]]).cpu()
+    L = CpuLayer.from_tensors(LAY, recs, W["router_w"][0].cpu(), W["sh_gate_w"][0].cpu(), W["bias"].cpu())
+    ys, ids = [], []
+    with torch.no_grad():
+        for t in range(x0.shape[0]):
+            y, i = decode_token_layer(L, x0[t:t + 1].cpu().float())
+            ys.append(y)
+            ids.append(i)
+    par = parity(y0.cpu(), ids0.cpu(), torch.cat(ys), torch.cat(ids))
+    par["reference"] = "CPU path of the reference (oracle/cpu_baseline.py), layer 0 of this run's step"
+    return (time_decode(L, seconds=seconds) if seconds > 0 else None), par
+
+
 # ------------------------------------------------------------------ decode workload (configs[1])
 def decode_world(args, rank):
     """Resident records (layers x 512 routed + one shared per layer), router weights and slot tables."""
@@ -223,7 +256,7 @@ def decode_world(args, rank):
                 slot_ptr=slot_ptr, gen=g)
 
 
-def bench_decode(args, world, rank, batch=None, W=None):
+def bench_decode(args, world, rank, batch=None, W=None, cpu_seconds=None):
     from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
     from slotstream_b200.records import BASELINE_LAYOUT as LAY
     NL, E, K = args.layers, 512, 10
@@ -300,6 +333,7 @@ def bench_decode(args, world, rank, batch=None, W=None):
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                 "peak_source": pk["source"],
                 "traffic": TRAFFIC_BYTES["decode_fused_b1"] if (fused and b == 1) else None,
+                "traffic_source": TRAFFIC_SOURCE,
                 "bytes_per_launch": int(launch_bytes), "launch_us": round(launch_ms * 1e3, 2)}
 
     # e2e: host inputs (pinned) -> device, graph step, outputs -> host, all inside the timed region
@@ -336,6 +370,11 @@ def bench_decode(args, world, rank, batch=None, W=None):
         "clocks": clocks.summary(),
         "device_errors": errs,
     }
+    if cpu_seconds is not None:
+        cb, par = cpu_leg_decode(LAY, W, x[0], bufs[0].y, bufs[0].ids, cpu_seconds)
+        res["parity"] = par
+        if cb is not None:
+            res["cpu_baseline"] = cb
     return res
 
 
@@ -468,9 +507,12 @@ def bench_slotpool(args, world, rank):
 
 # ------------------------------------------------------------------ prefill workload (configs[2], configs[3] per GPU)
 FLOP_PER_TOKEN = 10 * 6_291_456 + 6_291_456 + 2 * 2048 * 512 + 4096   # routed + shared + router + shared gate
+# kernels of one prefill layer step: router GEMM, shared-gate logits, select, align, row positions, row permute,
+# gate_up GEMM, down GEMM, combine (the position reset before the permute is a memset, not a kernel)
+PREFILL_LAUNCHES = 9
 
 
-def bench_prefill(args, world, rank):
+def bench_prefill(args, world, rank, cpu_passes=None):
     from slotstream_b200 import _lib, synth
     from slotstream_b200.kernels.moe_layer import PrefillLayerBuffers, moe_layer_prefill
     from slotstream_b200.records import BASELINE_LAYOUT as LAY
@@ -546,6 +588,7 @@ def bench_prefill(args, world, rank):
                 "achieved": round(gu_tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(gu_tf / pk["bf16_tflops"], 4), "peak_source": pk["source"] + " (burst)",
                 "traffic": TRAFFIC_BYTES.get(f"prefill_gate_up_{T}") if args.routing == "zipf" else None,
+                "traffic_source": TRAFFIC_SOURCE,
                 "flop_per_launch": gu_flop, "launch_ms": round(gu_ms, 4),
                 "padded_rows": n_padded, "rows": bufs.rows,
                 "down": {"achieved": round(dn_flop / (dn_ms * 1e-3) / 1e12, 1), "launch_ms": round(dn_ms, 4)}}
@@ -581,7 +624,7 @@ def bench_prefill(args, world, rank):
     del graph2, bufs2, x2
 
     value = world * T / (ms * 1e-3)
-    return {
+    res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -601,24 +644,78 @@ def bench_prefill(args, world, rank):
                             "steps' compute",
                 "serial": {"value": round(world * T / (e2e_serial_ms * 1e-3), 1), "ms_per_step": round(e2e_serial_ms, 4),
                            "schedule": "H2D, layer, D2H one after the other on one stream"}},
-        "gpu_launches": 8 * args.steps,
+        "gpu_launches": PREFILL_LAUNCHES * args.steps,
         "clocks": clocks.summary(),
         "device_errors": errs,
     }
+    if cpu_passes is not None:
+        cb, par = cpu_leg_prefill(LAY, recs, router_w, sh_gate_w, bias, x, bufs.y, bufs.ids, cpu_passes)
+        res["parity"] = par
+        if cb is not None:
+            res["cpu_baseline"] = cb
+    return res
 
 
 # ------------------------------------------------------------------ expert-parallel prefill (configs[3], N > 1)
+def pipelined_eager(x_dev, run, x_host, k, world):
+    """ms per step of k eager steps over two buffer sets, as ``pipelined_steps`` but with ``run(b) -> y`` (a layer
+    call that may synchronise the host, like the expert-parallel exchange) instead of a graph replay: step i's x
+    H2D goes on a copy stream ahead of its compute and its y D2H on another, overlapping the neighbouring steps."""
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    y_host = [None, None]
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    ev_in, ev_c, ev_out = [ev() for _ in range(k + 1)], [ev() for _ in range(k)], [ev() for _ in range(k)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    t0.record(comp)
+    h2d.wait_event(t0)
+
+    def copy_in(i):
+        if i >= 2:
+            h2d.wait_event(ev_c[i - 2])          # x_dev[b] is free once step i-2 computed
+        with torch.cuda.stream(h2d):
+            x_dev[i % 2].copy_(x_host[i % 2], non_blocking=True)
+        ev_in[i].record(h2d)
+
+    copy_in(0)
+    for i in range(k):
+        b = i % 2
+        if i + 1 < k:
+            copy_in(i + 1)                        # the next step's input crosses while this one computes
+        comp.wait_event(ev_in[i])
+        y = run(b)
+        ev_c[i].record(comp)
+        if y_host[b] is None:
+            y_host[b] = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        if i >= 2:
+            d2h.wait_event(ev_out[i - 2])
+        d2h.wait_event(ev_c[i])
+        with torch.cuda.stream(d2h):
+            y_host[b].copy_(y, non_blocking=True)
+            y.record_stream(d2h)
+        ev_out[i].record(d2h)
+    comp.wait_event(ev_out[k - 1])
+    t1.record(comp)
+    barrier(world)
+    return t0.elapsed_time(t1) / k
+
+
 def bench_prefill_ep(args, world, rank):
     from slotstream_b200 import synth
     from slotstream_b200.ep import CudaOps, ep_forward, owned_experts
+    from slotstream_b200.kernels.moe_layer import PrefillLayerBuffers, moe_layer_prefill
     from slotstream_b200.records import BASELINE_LAYOUT as LAY
     E, K, T = 512, 10, args.tokens
     dev = torch.device("cuda")
     rb = LAY.record_bytes
     owned = owned_experts(rank, E, world, strided=True)
-    recs = torch.empty((len(owned) + 1, rb), dtype=torch.uint8, device=dev)   # this rank's experts + the shared one
-    synth.fill_records_device(LAY, recs, 3000 + rank)
-    group_ptr = recs.data_ptr() + torch.arange(len(owned), dtype=torch.int64, device=dev) * rb
+    # every rank generates the same 513 records (same seed) and owns the strided share of them; the others stay
+    # so that each rank can run the one-GPU layer on its own tokens for the parity check below
+    recs = torch.empty((E + 1, rb), dtype=torch.uint8, device=dev)
+    synth.fill_records_device(LAY, recs, 3000)
+    base = recs.data_ptr() + torch.arange(E + 1, dtype=torch.int64, device=dev) * rb
+    group_ptr = base[torch.tensor(owned, device=dev)].contiguous()
     g = torch.Generator(device=dev)
     g.manual_seed(2000)                       # router and shared gate replicated: same on every rank
     router_w = (torch.randn(E, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
@@ -626,44 +723,99 @@ def bench_prefill_ep(args, world, rank):
     bias = torch.from_numpy(synth.zipf_bias(E)).to(dev) if args.routing == "zipf" else None
     g.manual_seed(2100 + rank)                # each rank its own tokens
     x = torch.randn(T, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
-    ops = CudaOps(router_w, sh_gate_w, group_ptr, recs.data_ptr() + len(owned) * rb, K, LAY.inter, world,
-                  strided=True, bias=bias, sm_reserve=args.sm_reserve)
-
-    def step():
-        return ep_forward(ops, x, K, world, micro_batches=args.micro_batches, partials_bf16=args.partials == "bf16")
-
+    ops = CudaOps(router_w, sh_gate_w, group_ptr, int(base[E]), K, LAY.inter, world, strided=True, bias=bias,
+                  sm_reserve=args.sm_reserve)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    for _ in range(args.warmup):
+
+    def measure(partials, phases_out=None):
+        def step():
+            return ep_forward(ops, x, K, world, micro_batches=args.micro_batches, partials_bf16=partials == "bf16")
+        for _ in range(args.warmup):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(torch.cuda.current_device())
+        clocks.start()
+        times = timed_steps(step, args.steps, flush, world, clocks)
+        clocks.stop()
+        ms = max_over_ranks(sum(times) / len(times), world)
+        # one more step, instrumented: phase times (max over ranks) and this rank's received rows
+        ph = []
+        barrier(world)
         flush.zero_()
-        step()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(torch.cuda.current_device())
-    clocks.start()
-    times = timed_steps(step, args.steps, flush, world, clocks)
-    clocks.stop()
-    ms = max_over_ranks(sum(times) / len(times), world)
+        y = ep_forward(ops, x, K, world, micro_batches=args.micro_batches, partials_bf16=partials == "bf16",
+                       phases=ph)
+        torch.cuda.synchronize()
+        evs = [(n, e) for n, *e in ph if n != "rows"]
+        rows = [r for r in ph if r[0] == "rows"][0]
+        phase_ms = {}
+        for (n0, e0), (n1, e1) in zip(evs, evs[1:]):
+            phase_ms[n1] = max_over_ranks(e0[0].elapsed_time(e1[0]), world)
+        step_ms = max_over_ranks(evs[0][1][0].elapsed_time(evs[-1][1][0]), world)
+        load = torch.tensor([rows[1], rows[2]], dtype=torch.float64, device=dev)
+        if world > 1:
+            allv = [torch.empty_like(load) for _ in range(world)]
+            torch.distributed.all_gather(allv, load)
+        else:
+            allv = [load]
+        recv_rows = [int(v[0].item()) for v in allv]
+        recv_ent = [int(v[1].item()) for v in allv]
+        return ms, y.clone(), clocks.summary(), {
+            "ms": {k: round(v, 4) for k, v in phase_ms.items()}, "instrumented_step_ms": round(step_ms, 4),
+            "received_rows_per_rank": {"min": min(recv_rows), "max": max(recv_rows)},
+            "received_entries_per_rank": {"min": min(recv_ent), "max": max(recv_ent), "mean": sum(recv_ent) / world},
+            "note": "CUDA events on the launching stream at the phase borders of one extra step, max over ranks; "
+                    "the shared expert runs on a side stream inside these phases"}
+
+    def parity_vs_one_gpu(y_ep):
+        """This rank's tokens through the one-GPU layer (all 513 records on this rank): the EP output must match it
+        within the layer tolerance (fp32 partial sums differ from the one-GPU rank-order sum by reassociation)."""
+        bufs = PrefillLayerBuffers(T, K, LAY.hidden, LAY.inter, E, dev)
+        y1 = moe_layer_prefill(x, router_w, base, sh_gate_w, K, bufs, bias=bias)
+        torch.cuda.synchronize()
+        d = (y_ep.double() - y1.double())
+        stats = torch.tensor([float(d.norm() / y1.double().norm()), float(d.abs().max()),
+                              float((y_ep.view(torch.int16) != y1.view(torch.int16)).double().mean())],
+                             dtype=torch.float64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
+        del bufs
+        return {"rel_l2": round(float(stats[0]), 7), "max_abs": round(float(stats[1]), 5),
+                "bf16_outputs_differing_frac": round(float(stats[2]), 6),
+                "reference": "the one-GPU layer (moe_layer_prefill, all records resident) on each rank's own tokens; "
+                             "max over ranks", "bar": "rel_l2 <= 1e-2"}
+
+    ms, y_ep, clocks, phases = measure(args.partials)
     value = world * T / (ms * 1e-3)
     errs = int(ops.err.item())
+    parity = parity_vs_one_gpu(y_ep)
+    alt = None
+    if not args.no_partials_alt:
+        other = "bf16" if args.partials == "fp32" else "fp32"
+        ms2, y2, clocks2, phases2 = measure(other)
+        alt = {"partials": other, "value": round(world * T / (ms2 * 1e-3), 1), "ms_per_step": round(ms2, 4),
+               "phases": phases2, "parity": parity_vs_one_gpu(y2), "clocks": clocks2}
 
-    # e2e: this rank's tokens from pinned host memory, the layer, y back to the host
-    x_host = x.cpu().pin_memory()
-    y_host = torch.empty((T, LAY.hidden), dtype=torch.bfloat16).pin_memory()
+    # e2e: this rank's tokens from pinned host memory, the layer, y back to the host, double-buffered like N=1
+    x2 = x.clone()
+    x_host = [x.cpu().pin_memory(), x2.cpu().pin_memory()]
 
-    def e2e_step():
-        x.copy_(x_host, non_blocking=True)
-        y = step()
-        y_host.copy_(y, non_blocking=True)
+    def run(b):
+        return ep_forward(ops, (x, x2)[b], K, world, micro_batches=args.micro_batches,
+                          partials_bf16=args.partials == "bf16")
 
-    e2e_step()
-    e2e_times = timed_steps(e2e_step, args.steps, flush, world)
-    e2e_ms = max_over_ranks(sum(e2e_times) / len(e2e_times), world)
+    pipelined_eager([x, x2], run, x_host, 2, world)   # warm-up of the two-stream schedule
+    e2e_ms = max_over_ranks(pipelined_eager([x, x2], run, x_host, args.steps, world), world)
     pk = peaks()
     tf = T * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12      # per GPU: each rank's share of the layer's FLOPs
     roofline = {"bound": "tensor", "kernel": "whole expert-parallel layer step per GPU (FLOPs of its tokens)",
                 "achieved": round(tf, 1), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": round(tf / pk["bf16_tflops_sustained"], 4), "peak_source": pk["source"] + " (sustained)",
                 "traffic": None}
-    return {
+    # route (router GEMM, shared-gate logits, select) 3 + shared expert (align + 4) 5 + per part: plan, gather,
+    # unpack, experts (align + 4), partial sums, combine = 10
+    launches = 8 + 10 * args.micro_batches
+    res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -671,13 +823,18 @@ def bench_prefill_ep(args, world, rank):
                    "inter": LAY.inter, "experts": E, "experts_per_gpu": len(owned), "placement": "strided (e % G)",
                    "topk": K, "shared_experts": 1, "routing": "zipf_s1.1" if args.routing == "zipf" else "uniform",
                    "exchange": f"NCCL all-to-all-v (dispatch rows + metadata, {args.partials} partial sums back)",
-                   "micro_batches": args.micro_batches, "gemm_sm_reserve": args.sm_reserve,
+                   "partials": args.partials, "micro_batches": args.micro_batches, "gemm_sm_reserve": args.sm_reserve,
                    "l2": "flushed before every step (256 MiB write); inputs > L2", "parallelism": f"ep{world}"},
-        "tflops_per_gpu": round(tf, 1), "roofline": roofline,
-        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": T * LAY.hidden * 2, "d2h_bytes_per_step": T * LAY.hidden * 2},
-        "gpu_launches": 16 * args.steps, "clocks": clocks.summary(), "device_errors": errs,
+        "tflops_per_gpu": round(tf, 1), "roofline": roofline, "phases": phases, "parity": parity,
+        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": T * LAY.hidden * 2, "d2h_bytes_per_step": T * LAY.hidden * 2,
+                "schedule": "double-buffered: each step's x H2D and y D2H on copy streams beside the neighbouring "
+                            "steps' compute (per rank)"},
+        "gpu_launches": launches * args.steps, "clocks": clocks, "device_errors": errs,
     }
+    if alt is not None:
+        res["partials_alt"] = alt
+    return res
 
 
 # ------------------------------------------------------------------ main
@@ -697,13 +854,16 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement at N=1")
     ap.add_argument("--no-chunks", action="store_true", help="skip the 2K / 8K-token prefill sub-measurements")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="decode CPU baseline sample length")
+    ap.add_argument("--cpu-passes", type=int, default=2, help="prefill CPU baseline: timed passes over the chunk")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU leg (baseline and parity)")
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="N > 1: token parts whose exchanges overlap the expert GEMMs of their neighbours")
-    ap.add_argument("--partials", choices=["fp32", "bf16"], default="bf16",
-                    help="N > 1: precision of the per-(token, destination) partial sums sent back")
+    ap.add_argument("--partials", choices=["fp32", "bf16"], default="fp32",
+                    help="N > 1: precision of the per-(token, destination) partial sums sent back (the line also "
+                         "reports the other precision as a sub-measurement unless --no-partials-alt)")
+    ap.add_argument("--no-partials-alt", action="store_true")
     ap.add_argument("--sm-reserve", type=int, default=0,
                     help="N > 1 with micro-batches: SMs the persistent GEMMs leave to the overlapped all-to-alls")
     args = ap.parse_args()
@@ -714,18 +874,15 @@ def main():
             print(json.dumps(reference_arm(args, int(os.environ.get("WORLD_SIZE", "1")))), flush=True)
         return
     world, rank, _ = dist_setup()
-    from slotstream_b200.records import BASELINE_LAYOUT
+    cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
     if args.workload == "decode":
-        res = bench_decode(args, world, rank)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            from oracle.cpu_baseline import time_decode
-            res["cpu_baseline"] = time_decode(BASELINE_LAYOUT, seconds=args.cpu_seconds)
+        res = bench_decode(args, world, rank, cpu_seconds=args.cpu_seconds if cpu else None)
     elif args.workload == "slotpool":
         res = bench_slotpool(args, world, rank)
     elif world > 1 and not args.replicas:
         res = bench_prefill_ep(args, world, rank)
     else:
-        res = bench_prefill(args, world, rank)
+        res = bench_prefill(args, world, rank, cpu_passes=args.cpu_passes if cpu else None)
         torch.cuda.empty_cache()
         if world == 1 and not args.no_chunks:
             # configs[2] also names 2,048- and 8,192-token chunks: the same layer, measured the same way
@@ -735,23 +892,25 @@ def main():
                     continue
                 a2 = argparse.Namespace(**vars(args))
                 a2.tokens = tk
-                c = bench_prefill(a2, world, rank)
+                c = bench_prefill(a2, world, rank, cpu_passes=0 if cpu else None)
                 res["chunks"][str(tk)] = {k: c[k] for k in ("value", "unit", "ms_per_step", "tflops", "roofline",
-                                                            "e2e", "clocks", "device_errors")}
+                                                            "e2e", "clocks", "device_errors", "parity") if k in c}
                 torch.cuda.empty_cache()
         if world == 1 and not args.no_decode:
             W = decode_world(args, rank)
-            d = bench_decode(args, world, rank, 1, W)
+            d = bench_decode(args, world, rank, 1, W, cpu_seconds=args.cpu_seconds if cpu else None)
             res["decode"] = {k: d[k] for k in ("value", "unit", "ms_per_step", "config", "hbm_gbs_per_step",
-                                               "bytes_per_step", "roofline", "e2e", "clocks")}
+                                               "bytes_per_step", "roofline", "e2e", "clocks", "parity",
+                                               "cpu_baseline") if k in d}
             # configs[1] also names batch 2 (speculative verify) and 16: same records, same step
             res["decode"]["other_batches"] = {}
             for bb in (2, 16):
-                e = bench_decode(args, world, rank, bb, W)
+                e = bench_decode(args, world, rank, bb, W, cpu_seconds=0 if cpu else None)
                 res["decode"]["other_batches"][str(bb)] = {
                     "value": e["value"], "unit": e["unit"], "ms_per_step": e["ms_per_step"],
                     "hbm_gbs_per_step": e["hbm_gbs_per_step"], "bytes_per_step": e["bytes_per_step"],
-                    "roofline_frac": e["roofline"]["frac"], "kernel": e["roofline"]["kernel"]}
+                    "roofline_frac": e["roofline"]["frac"], "kernel": e["roofline"]["kernel"],
+                    "parity": e.get("parity")}
             del W
             torch.cuda.empty_cache()
         if world == 1 and not args.no_slotpool:
@@ -760,9 +919,6 @@ def main():
                                                  "miss_fraction", "misses_per_layer", "h2d_bytes_per_step",
                                                  "roofline", "e2e", "gpu_launches", "clocks", "device_errors")}
             torch.cuda.empty_cache()
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            from oracle.cpu_baseline import time_prefill
-            res["cpu_baseline"] = time_prefill(BASELINE_LAYOUT, args.tokens, seconds=args.cpu_seconds)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
@@ -770,35 +926,56 @@ def main():
 
 
 def reference_arm(args, world):
-    """The reference's own CPU path (oracle torch port of moe_ref / affine_ref) on all host cores, same
-    metric and config; each step is a bounded sample."""
+    """The reference's own CPU path for this workload (oracle/cpu_baseline.py, the torch restatement of moe_ref /
+    affine_ref / stable top-k) on all host cores, on the GPU arm's config: prefill steps are whole chunks of
+    args.tokens tokens (each routed expert dequantised once per chunk, as the GPU arm's layer reads each record once);
+    decode steps are one token through 48 layers (dequantisation inside, as the reference's CPU branch)."""
     sys.path.insert(0, str(ROOT))
-    from oracle.cpu_baseline import CpuLayer, time_decode, time_prefill
-    from slotstream_b200.records import BASELINE_LAYOUT
-    per_step = max(1.0, min(10.0, 60.0 / max(args.steps, 1)))
-    vals = []
-    b = args.batch
-    if args.workload == "decode":
-        run = lambda s: time_decode(BASELINE_LAYOUT, seconds=s)  # noqa: E731
-        config = {"workload": f"decode_step_48layer_b{b}", "layers": 48, "batch": b, "hidden": 2048, "inter": 512,
-                  "experts": 512, "topk": 10, "routing": "zipf_s1.1"}
-        dtype = "f32"
-    else:
-        layer = CpuLayer(BASELINE_LAYOUT, 0)
-        run = lambda s: time_prefill(BASELINE_LAYOUT, args.tokens, seconds=s, layer=layer)  # noqa: E731
-        config = {"workload": f"prefill_layer_{args.tokens}tok_per_gpu", "tokens_per_gpu": args.tokens,
-                  "hidden": 2048, "inter": 512, "experts": 512, "topk": 10,
-                  "routing": args.routing + ("_s1.1" if args.routing == "zipf" else "")}
-        dtype = "bf16"
-    for _ in range(min(args.warmup, 1)):
-        run(0.5)
-    for _ in range(args.steps):
-        vals.append(run(per_step))
-    v = statistics.mean(r["value"] for r in vals)
-    cb = dict(vals[-1])
-    cb["value"] = v
+    from oracle.cpu_baseline import CpuLayer, decode_token_layer, host_info, prefill_chunk
+    from slotstream_b200.records import BASELINE_LAYOUT as LAY
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    layer = CpuLayer.from_seed(LAY, 0)
+    if args.routing == "uniform":
+        layer.bias = None
+    g = torch.Generator().manual_seed(0)
+    times = []
+    with torch.no_grad():
+        if args.workload == "decode":
+            b = args.batch
+            xs = torch.randn(args.steps + 1, b, LAY.hidden, generator=g).bfloat16().float()
+
+            def step(i):
+                for _ in range(args.layers):
+                    for t in range(b):
+                        decode_token_layer(layer, xs[i, t:t + 1])
+            config = {"workload": f"decode_step_{args.layers}layer_b{b}", "layers": args.layers, "batch": b,
+                      "hidden": LAY.hidden, "inter": LAY.inter, "experts": 512, "topk": 10, "routing": "zipf_s1.1"}
+            units, dtype, sample = b, "f32", f"{args.layers} layers x {b} token(s) per step, dequantisation inside"
+        else:
+            x = torch.randn(args.tokens, LAY.hidden, generator=g).bfloat16().float()
+
+            def step(i):
+                prefill_chunk(layer, x)
+            wl = (f"ep_prefill_layer_{args.tokens}tok_per_gpu" if world > 1 and not args.replicas
+                  else f"prefill_layer_{args.tokens}tok_per_gpu")
+            config = {"workload": wl, "tokens_per_gpu": args.tokens, "hidden": LAY.hidden, "inter": LAY.inter,
+                      "experts": 512, "topk": 10, "shared_experts": 1,
+                      "routing": args.routing + ("_s1.1" if args.routing == "zipf" else "")}
+            units, dtype = args.tokens, "f32"
+            sample = f"whole {args.tokens}-token chunks, each routed expert dequantised once per chunk"
+        for i in range(min(args.warmup, 1)):
+            step(i)
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            step(i)
+            times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    v = units / (ms * 1e-3)
+    cb = {"value": v, "unit": "tokens/s", "kind": "port", "sample": sample, "steps_timed": len(times)}
+    cb.update(host_info(threads))
     return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak",
+            "warmup": min(args.warmup, 1), "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": dtype, "data": "synthetic", "impl": "reference", "config": config,
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}

@@ -152,7 +152,8 @@ int ssb_router_select_resolve(const float* logits, int32_t ld, int64_t tokens, i
 /* Dispatch plan of one rank's routed tokens ids/w [tokens, k]: dest_count int32 [n_ranks, 2] (rows, entries
  * per destination); send_token int32 [>= tokens * min(n_ranks, k)] (rows ordered by destination, then
  * token); send_meta int32 [same, 2k + 2] (local expert or -1 per choice, weight bits, entry base, entry
- * count); tok_slot / tok_entry int32 [tokens, n_ranks] (send row and entry base of (t, d), -1 if none). */
+ * count); tok_slot / tok_entry int32 [tokens, n_ranks] (send row and entry base of (t, d), -1 if none).
+ * tokens = 0 only zeroes dest_count (the other pointers may be NULL). */
 int ssb_ep_plan(const int32_t* ids, const float* w, int64_t tokens, int32_t k, int32_t experts_per_rank,
                 int32_t n_ranks, int32_t strided, int32_t* dest_count, int32_t* send_token, int32_t* send_meta,
                 int32_t* tok_slot, int32_t* tok_entry, int32_t* err, void* stream);
@@ -238,13 +239,14 @@ int ssb_pool_decode_layer(ssb_pool* pool, int32_t layer, const uint16_t* x, int6
 
 /* Router logits + select (as ssb_router_logits then ssb_router_select) with the logits held in a fixed
  * device array that comes with the library's device code, so the call needs no workspace and allocates nothing:
- * for callers that cannot allocate on their call path (a host binding without a caching allocator, a
- * process whose slot pool holds nearly all HBM, a stream under graph capture). Capacity: 65536 floats
+ * for callers that cannot allocate on their call path (a host binding without a caching allocator, which would
+ * need a device-synchronising cudaMalloc per step; a process whose slot pool holds nearly all HBM). Capacity: 65536 floats
  * (256 KiB); tokens * (experts + 1 when w_shared_gate is given, else experts) above it returns SSB_ETOOBIG
  * before any launch. flags: 0 or SSB_ROUTER_ROUND_BF16; a non-null w_shared_gate (bf16 [hidden]) adds the
  * shared gate into out_sh_gate. The array is shared by every call on a device: calls that overlap on one
- * device (other streams or host threads) race. The first call on each device looks up the array's address;
- * make one call before capturing a stream. Other limits as ssb_router_logits and ssb_router_select.
+ * device (other streams or host threads) race. The first call on each device looks up the array's address and
+ * keeps it for the life of the process: make that first call before any stream capture, and do not reset the
+ * device (cudaDeviceReset) while the library is loaded. Other limits as ssb_router_logits and ssb_router_select.
  * Replaces: no counterpart in the reference. */
 int ssb_router_topk_static(const uint16_t* x, const uint16_t* w, const uint16_t* w_shared_gate, int64_t tokens,
                            int32_t hidden, int32_t experts, int32_t k, const float* bias, int32_t flags,
@@ -341,14 +343,15 @@ int ssb_sorted_down(const uint16_t* h_sorted, int64_t rows, int32_t hidden, int3
                     int64_t padded_len, const int64_t* group_ptr, int32_t n_groups, int32_t shared_local,
                     float* out_rows, int32_t* err, void* stream);
 
-/* Dense bf16 GEMM on tcgen05 (router logits of a prefill chunk): out[m, n] = sum_k x[m, k] * w[n, k],
- * fp32 into rows of `ldo` floats (ldo % 4 == 0). k % 64 == 0, n % 128 == 0; row-invariant.
- * Replaces: the router lin() of model/layers.py:339 inside the prefill GEMM scope (kernels/gemm_affine.py:40-59). */
+/* Dense bf16 GEMM on tcgen05: out[m, n] = sum_k x[m, k] * w[n, k], fp32 into rows of `ldo` floats (ldo >= n).
+ * k % 64 == 0, any n >= 1 (the last 128-column block is partial); row-invariant (fixed k order per output).
+ * Replaces: gemm(x, DenseWeight), slotstream_spark/kernels/gemm_affine.py:40-59, 62-98 -- the dense lin() calls of
+ * model/layers.py:62-76 inside prefill_gemm(), the router logits of a prefill chunk among them. */
 int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uint16_t* w, int32_t n, float* out, int64_t ldo,
                    void* stream);
 
 /* Dense prefill GEMM with an affine 4-bit weight on tcgen05: out[m, n] = sum_k x[m, k] * bf16(q*s + b)[n, k],
- * fp32 out. k % 64 == 0, (k/gs) even, n % 128 == 0; row-invariant (fixed k order per output).
+ * fp32 out [m, n]. k % 128 == 0, gs 32 or 64, any n >= 1; row-invariant (fixed k order per output).
  * Replaces: gemm(x, AffineWeight), slotstream_spark/kernels/gemm_affine.py:62-98 (kernel :19-37). */
 int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const int32_t* q, const uint16_t* s, const uint16_t* b,
                      int32_t n, int32_t gs, float* out, void* stream);

@@ -308,6 +308,31 @@ def moe_layer_prefill(layout, x_bf16, router_w_bf16, k, expert_f32, sh_f32, sh_g
     return out, routed, sh, ids, w, logits
 
 
+def moe_layer_grouped(layout, x_bf16, router_w_bf16, k, expert_dense, sh_f32, sh_gate_bf16, bias=None,
+                      logits_round_bf16=False):
+    """``moe_layer`` with the routed rows batched per expert, for chunks of thousands of tokens: the same fp64
+    arithmetic (exact dequant, y = w * D(silu(G x) * U x) per (token, rank), rank-order fp64 sum,
+    model/reference_torch.py:118-134), the same shared expert and bf16 final add. ``expert_dense(e)`` -> fp64
+    (G, U, D). Returns (out bf16-valued fp32 [T, H], routed fp64 [T, H], ids, weights, logits)."""
+    ids, w, logits = router(x_bf16, router_w_bf16, k, bias=bias, logits_round_bf16=logits_round_bf16)
+    t = ids.shape[0]
+    x = bf16_to_f32(x_bf16).astype(np.float64)
+    rows = np.zeros((t * k, layout.hidden), dtype=np.float64)
+    flat = ids.reshape(-1)
+    for e in np.unique(flat):
+        sel = np.nonzero(flat == e)[0]
+        g, u, d = expert_dense(int(e))
+        xe = x[sel // k]
+        rows[sel] = ((silu64(xe @ g.T) * (xe @ u.T)) @ d.T) * w.reshape(-1)[sel, None].astype(np.float64)
+    v = rows.reshape(t, k, -1)
+    routed = v[:, 0].copy()
+    for j in range(1, k):
+        routed = routed + v[:, j]
+    sh = shared_expert(x_bf16, *sh_f32, sh_gate_bf16)
+    out = round_bf16(round_bf16(routed).astype(np.float64) + sh)
+    return out, routed, ids, w, logits
+
+
 def rel_l2(a, b):
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)

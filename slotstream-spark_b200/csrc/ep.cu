@@ -380,6 +380,10 @@ extern "C" int ssb_ep_plan(const int32_t* ids, const float* w, int64_t tokens, i
                            int32_t n_ranks, int32_t strided, int32_t* dest_count, int32_t* send_token,
                            int32_t* send_meta, int32_t* tok_slot, int32_t* tok_entry, int32_t* err, void* stream) {
   SSB_CHECK_ARG(tokens >= 0 && k >= 1 && k <= 15 && placement_ok(experts_per_rank, n_ranks, strided));
+  if (tokens == 0) {   // an empty part still reports its (zero) counts; its other outputs are empty
+    SSB_CHECK_ARG(dest_count);
+    return (int)cudaMemsetAsync(dest_count, 0, sizeof(int32_t) * 2 * (size_t)n_ranks, (cudaStream_t)stream);
+  }
   SSB_CHECK_ARG(ids && w && dest_count && send_token && send_meta && tok_slot && tok_entry);
   SSB_CHECK_ARG(tokens <= 0x7fffffffLL / k);
   ssb_note_smem("ep_plan", k_ep_plan, 0);

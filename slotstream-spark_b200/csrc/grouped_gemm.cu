@@ -74,6 +74,8 @@ struct GemmArgs {
   const float* row_weight;
   void* out;
   int64_t ldo;
+  int64_t n_valid;            // plain epilogue: output columns (B rows) that exist; the last n-block is partial
+  int out_vec;                // plain epilogue: out and ldo allow 16-byte stores
   int32_t* err;
 };
 
@@ -411,8 +413,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
               const int rr = 4 * it + (lane >> 3), c4 = 4 * (lane & 7);
               const int64_t rrow = __shfl_sync(0xFFFFFFFFu, row, rr);
               const float4 o = *reinterpret_cast<const float4*>(tb + rr * EPI_LD + c4);
-              if (rrow >= 0 && rrow < a.R)
-                *reinterpret_cast<float4*>(out + rrow * a.ldo + (int64_t)nb * BN + col + c4) = o;
+              const int64_t c0 = (int64_t)nb * BN + col + c4;
+              if (rrow >= 0 && rrow < a.R) {
+                if (EPI != EPI_PLAIN || (a.out_vec && c0 + 4 <= a.n_valid)) {
+                  *reinterpret_cast<float4*>(out + rrow * a.ldo + c0) = o;
+                } else {   // a partial last n-block, or rows that 16-byte stores cannot address
+                  const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    if (c0 + e < a.n_valid) out[rrow * a.ldo + c0 + e] = ov[e];
+                }
+              }
             }
             __syncwarp();
           }
@@ -459,10 +470,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
             fail = true;
           } else {
             const uint32_t bt = smem_u32(S.b + s * B_STAGE);
+            const bool row_ok = t_base && (EPI != EPI_PLAIN || t_nrow < a.n_valid);   // rows past n read zeros
             const uint16_t* drow =
-                t_base ? (const uint16_t*)t_base + t_nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
+                row_ok ? (const uint16_t*)t_base + t_nrow * a.ldb + kb * BK : (const uint16_t*)a.base0;
 #pragma unroll
-            for (int c = 4 * hf; c < 4 * hf + 4; ++c) cp_async16(bt + swz128(br, c), drow + c * 8, t_base ? 16u : 0u);
+            for (int c = 4 * hf; c < 4 * hf + 4; ++c) cp_async16(bt + swz128(br, c), drow + c * 8, row_ok ? 16u : 0u);
           }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
@@ -500,12 +512,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
           const int pc = p + N_PROD * i, row = pc / (2 * ss), c16 = pc - row * (2 * ss);
           const int pce = (EPI == EPI_SWIGLU) ? (row >> 6) : 0;
           const int64_t nr = (EPI == EPI_SWIGLU) ? (int64_t)nb * (BN / 2) + (row & (BN / 2 - 1)) : (int64_t)nb * BN + row;
-          const void* src = t_base ? (const void*)(t_base + a.off_w[pce] + nr * (a.K / 2) + kb0 * 32 + c16 * 16) : dummy;
-          cp_async16(smem_u32(st + row * 128 + ((c16 ^ (row & 7)) << 4)), src, t_base ? 16u : 0u);
+          const bool row_ok = t_base && (EPI != EPI_PLAIN || nr < a.n_valid);   // rows past n read zero codes
+          const void* src = row_ok ? (const void*)(t_base + a.off_w[pce] + nr * (a.K / 2) + kb0 * 32 + c16 * 16) : dummy;
+          cp_async16(smem_u32(st + row * 128 + ((c16 ^ (row & 7)) << 4)), src, row_ok ? 16u : 0u);
         }
         const int g0 = a.gs == 64 ? kb0 : 2 * kb0;   // first group of the super-step (gsb-byte aligned)
-        const uint16_t* sr = t_base ? (const uint16_t*)(t_base + a.off_s[piece]) + t_nrow * ng + g0 : nullptr;
-        const uint16_t* bsrc = t_base ? (const uint16_t*)(t_base + a.off_b[piece]) + t_nrow * ng + g0 : nullptr;
+        const bool sb_ok = t_base && (EPI != EPI_PLAIN || t_nrow < a.n_valid);   // rows past n: zero scale and bias
+        const uint16_t* sr = sb_ok ? (const uint16_t*)(t_base + a.off_s[piece]) + t_nrow * ng + g0 : nullptr;
+        const uint16_t* bsrc = sb_ok ? (const uint16_t*)(t_base + a.off_b[piece]) + t_nrow * ng + g0 : nullptr;
         const uint32_t ds = smem_u32(st + W_STG + p * 32);
         if (gsb == 4) {
           asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(ds), "l"(sr ? (const void*)sr : dummy),
@@ -962,7 +976,7 @@ extern "C" int ssb_prefill_experts(const uint16_t* x, int64_t tokens, int32_t hi
 extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const int32_t* q, const uint16_t* s,
                                 const uint16_t* b, int32_t n, int32_t gs, float* out, void* stream) {
   SSB_CHECK_ARG(m >= 0 && k >= 1 && n >= 1 && (gs == 32 || gs == 64));
-  if (k % (2 * BK) || n % BN) return SSB_EUNSUPPORTED;
+  if (k % (2 * BK)) return SSB_EUNSUPPORTED;
   if (m == 0) return SSB_OK;
   SSB_CHECK_ARG(x && q && s && b && out);
   SSB_CHECK_ARG((((uintptr_t)q | (uintptr_t)s | (uintptr_t)b) & 3) == 0 && ((uintptr_t)q & 15) == 0);
@@ -980,17 +994,19 @@ extern "C" int ssb_gemm_affine4(const uint16_t* x, int64_t m, int32_t k, const i
   g.shared_local = -1;
   g.out = out;
   g.ldo = n;
+  g.n_valid = n;
+  g.out_vec = (n % 4 == 0) && ((uintptr_t)out & 15) == 0;
   g.off_w[0] = g.off_w[1] = 0;
   g.off_s[0] = g.off_s[1] = (int64_t)((const uint8_t*)s - (const uint8_t*)q);
   g.off_b[0] = g.off_b[1] = (int64_t)((const uint8_t*)b - (const uint8_t*)q);
   g.err = nullptr;
-  return launch(EPI_PLAIN, g, (m + TM - 1) / TM, n / BN, (cudaStream_t)stream);
+  return launch(EPI_PLAIN, g, (m + TM - 1) / TM, (n + BN - 1) / BN, (cudaStream_t)stream);
 }
 
 extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uint16_t* w, int32_t n, float* out,
                               int64_t ldo, void* stream) {
-  SSB_CHECK_ARG(m >= 0 && k >= 1 && n >= 1 && ldo >= n && ldo % 4 == 0);
-  if (k % BK || n % BN) return SSB_EUNSUPPORTED;
+  SSB_CHECK_ARG(m >= 0 && k >= 1 && n >= 1 && ldo >= n);
+  if (k % BK) return SSB_EUNSUPPORTED;
   if (m == 0) return SSB_OK;
   SSB_CHECK_ARG(x && w && out && ((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0);
   GemmArgs g{};
@@ -1008,8 +1024,10 @@ extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uin
   g.shared_local = -1;
   g.out = out;
   g.ldo = ldo;
+  g.n_valid = n;
+  g.out_vec = (ldo % 4 == 0) && ((uintptr_t)out & 15) == 0;
   g.err = nullptr;
-  return launch(EPI_PLAIN, g, (m + TM - 1) / TM, n / BN, (cudaStream_t)stream);
+  return launch(EPI_PLAIN, g, (m + TM - 1) / TM, (n + BN - 1) / BN, (cudaStream_t)stream);
 }
 
 extern "C" int ssb_set_gemm_sm_reserve(int32_t sms) {

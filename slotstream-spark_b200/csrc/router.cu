@@ -440,15 +440,17 @@ extern "C" int ssb_router_select_resolve(const float* logits, int32_t ld, int64_
 //
 // Some callers cannot allocate device memory on their call path. A host binding without a caching
 // allocator (cgo, JNI, plain C over this ABI) would have to call cudaMalloc, which synchronises the whole
-// device, on every decode step; a process whose expert slot pool reserved nearly all of HBM up front has no
-// headroom left to hand out; and a stream that is being captured into a graph may not allocate at all.
+// device, on every decode step; and a process whose expert slot pool reserved nearly all of HBM up front has
+// no headroom left to hand out.
 // For those callers the logits live in a file-scope __device__ array of ROUTER_STATIC_LOGITS floats
 // (256 KiB): a call whose tokens * (experts + 1 with a shared gate, else experts) exceeds it is refused with
 // SSB_ETOOBIG before anything is launched. The logits kernel writes every element the select kernel reads,
 // earlier on the same stream, so nothing in the array has to start at zero. There is one array per device
 // in the process: calls that overlap on one device (other streams, other host threads) overwrite each
 // other's logits and race. The first call on a device looks the array's address up with
-// cudaGetSymbolAddress (with that device current), so make one call before capturing a stream.
+// cudaGetSymbolAddress (with that device current) and keeps it for the life of the process, so that first
+// call should come before any stream capture, and resetting the device (cudaDeviceReset) while this library
+// is loaded is not supported: the address kept for it would be stale.
 namespace {
 constexpr int64_t ROUTER_STATIC_LOGITS = 65536;
 constexpr int ROUTER_STATIC_MAX_DEVICES = 64;

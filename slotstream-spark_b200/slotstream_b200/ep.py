@@ -73,38 +73,54 @@ def _prefix(v: list[int]) -> list[int]:
 
 
 def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bool = False,
-               micro_batches: int = 1, partials_bf16: bool = False):
+               micro_batches: int = 1, partials_bf16: bool = False, phases: list | None = None):
     """One expert-parallel MoE layer over this rank's tokens x [T, H] -> y bf16 [T, H].
     ``ops`` supplies the per-rank compute (``CudaOps`` on B200); the exchange is the same for every backend.
 
     ``micro_batches`` = m > 1 splits the tokens into m contiguous parts with their own plans: the counts of
     all parts go in one all-to-all (still one host sync), every exchange is asynchronous, and part i's expert
     GEMMs are issued after part i+1's dispatch and before part i-1's return, so on NCCL the transfers of one
-    part overlap the math of its neighbour. Every token's arithmetic is the same as with m = 1.
+    part overlap the math of its neighbour. Every token's arithmetic is the same as with m = 1. Every rank must
+    pass the same m; parts may be empty (a rank with fewer than m tokens, or none).
 
     ``partials_bf16`` (default mode only): the per-(token, destination) partial sums are rounded to bf16 before
     they go back, halving the return bytes; routed then differs from the fp32 return by the partials'
-    rounding (a relative 2^-9 each)."""
+    rounding (a relative 2^-9 each).
+
+    ``phases`` (a list, CUDA only) receives (name, event) pairs recorded on the current stream at the phase
+    borders -- after routing, the plan, the count exchange and its host read, each part's dispatch, expert GEMMs,
+    partial sums, return and combine -- so a caller can time the phases of one call; it also receives
+    ("rows", received rows, received entries) of this rank."""
     G = n_ranks
-    t_all = x.shape[0]
-    m = max(1, min(int(micro_batches), t_all)) if t_all else 1
+    # every rank must post the same collectives: m depends only on the argument, never on this rank's token count
+    # (a rank with fewer tokens than m, or none, sends empty parts)
+    m = max(1, int(micro_batches))
     reserve = getattr(ops, "sm_reserve", 0) if m > 1 and G > 1 else 0
     if reserve:
         ops.reserve_sms(reserve)   # the overlapped all-to-alls need SMs beside the persistent GEMMs
     try:
-        return _ep_forward(ops, x, k, G, group, exact, m, bool(partials_bf16) and not exact)
+        return _ep_forward(ops, x, k, G, group, exact, m, bool(partials_bf16) and not exact, phases)
     finally:
         if reserve:
             ops.reserve_sms(0)
 
 
-def _ep_forward(ops, x, k, G, group, exact, m, bf16):
+def _ep_forward(ops, x, k, G, group, exact, m, bf16, phases=None):
+    def mark(name):
+        if phases is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            phases.append((name, ev))
+
+    mark("start")
     t_all = x.shape[0]
     ids, w, sh_gate = ops.route(x)
+    mark("route")
     sh = ops.shared(x, sh_gate)
     bounds = [t_all * i // m for i in range(m + 1)]
     parts = [(bounds[i], bounds[i + 1]) for i in range(m)]
     plans = [ops.plan(ids[a:b], w[a:b]) for a, b in parts]
+    mark("plan")
     send_counts = torch.stack([p.dest_count for p in plans], dim=1).contiguous()   # [G, m, 2]: per destination
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts.view(-1), send_counts.view(-1), group=group)
@@ -112,6 +128,9 @@ def _ep_forward(ops, x, k, G, group, exact, m, bf16):
     half = G * m * 2
     sc = [[both[(d * m + i) * 2:(d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
     rc = [[both[half + (d * m + i) * 2:half + (d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
+    mark("counts_exchange_and_host_read")
+    if phases is not None:
+        phases.append(("rows", sum(c[0] for r in rc for c in r), sum(c[1] for r in rc for c in r)))
     # dispatch every part (asynchronous: the math below waits only for its own part)
     sent = []
     for i, ((a, b), plan) in enumerate(zip(parts, plans)):
@@ -131,14 +150,17 @@ def _ep_forward(ops, x, k, G, group, exact, m, bf16):
     for i, (send_x, recv_x, recv_meta, works, send_rows, send_ent, recv_rows, recv_ent) in enumerate(sent):
         for wk in works:
             wk.wait()
+        mark(f"dispatch{i}")
         entries = ops.unpack(recv_meta, _prefix(recv_rows), _prefix(recv_ent), sum(recv_ent))
         out_rows = ops.experts(recv_x, entries)
+        mark(f"experts{i}")
         if exact:
             back = out_rows
             ret = out_rows.new_empty((sum(send_ent), out_rows.shape[1]))
             work = dist.all_to_all_single(ret, back, send_ent, recv_ent, group=group, async_op=True)
         else:
             back = ops.combine_rows(out_rows, entries, bf16=bf16)
+            mark(f"partial_sums{i}")
             ret = back.new_empty((sum(send_rows), back.shape[1]))
             work = dist.all_to_all_single(ret, back, send_rows, recv_rows, group=group, async_op=True)
         returned.append((ret, back, work))
@@ -146,9 +168,11 @@ def _ep_forward(ops, x, k, G, group, exact, m, bf16):
     for i, ((a, b), plan) in enumerate(zip(parts, plans)):
         ret, _, work = returned[i]
         work.wait()
+        mark(f"return{i}")
         send_ent = sent[i][5]
         off = _prefix(send_ent)[:G] if exact else None
         ys.append(ops.combine(ret, plan, ids[a:b], off, sh[a:b], exact=exact, bf16=bf16))
+        mark(f"combine{i}")
         routed.append(ops.routed)
     if m == 1:
         return ys[0]

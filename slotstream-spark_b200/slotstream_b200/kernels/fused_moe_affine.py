@@ -9,21 +9,23 @@ Rounding path, as the reference: the dequantised gate, up and down tiles are rou
 first), products accumulate in fp32, h is stored bf16. Tiles and the k order are constants of the shape, never
 functions of R or of the group composition, so a row's bits depend on that row and that record only.
 
-Differences from the reference, all additive: the shape comes from the tensors (hidden = x.shape[1],
-inter = h_buf.shape[1] or ``inter=``); a group may hold up to 512 experts (every expert of a layer resident at
-once); BLOCK_M is 256 (one grouped-GEMM tile: two tcgen05 M128 halves sharing one dequantised weight tile), so
-``aligned`` must come from this module's ``align_rows``.
+Differences from the reference, all additive: the kernels take the shape from the tensors (hidden = x.shape[1],
+inter = h_buf.shape[1] or ``inter=``); the module constants HID / INTER / TOPK / RECORD_BYTES / O_* describe the
+shape set by ``slotstream_b200.kernels.configure`` (the reference model's 2560 / 640 until then), and a call
+without h_buf whose x does not have HID columns raises instead of guessing I; a group may hold up to 512 experts
+(every expert of a layer resident at once); BLOCK_M is 256 (one grouped-GEMM tile: two tcgen05 M128 halves
+sharing one dequantised weight tile), so ``aligned`` must come from this module's ``align_rows``.
 """
 import torch
 
 from .. import _lib
-from ..records import BASELINE_LAYOUT, RecordLayout
+from ..records import RecordLayout
+from . import shape as _shape
 from .gemv_affine import _note
 from .moe_align import moe_align, padded_rows
 
-HID, INTER, TOPK = BASELINE_LAYOUT.hidden, BASELINE_LAYOUT.inter, 10
-RECORD_BYTES = BASELINE_LAYOUT.record_bytes
-(O_GATE_W, O_GATE_S, O_GATE_B, O_UP_W, O_UP_S, O_UP_B, O_DOWN_W, O_DOWN_S, O_DOWN_B) = BASELINE_LAYOUT.offsets()
+# HID, INTER, TOPK, RECORD_BYTES and O_GATE_W .. O_DOWN_B: the configured model shape (kernels/shape.py)
+_shape.install(globals())
 GROUP_MAX = 512
 BLOCK_M, BLOCK_N, BLOCK_K = 256, 128, 64
 
@@ -64,7 +66,8 @@ def fused_moe_affine(x, row_token, row_weight, expert_map, group_ptr, out_rows, 
     group_ptr int64 [G <= GROUP_MAX] record base addresses · out_rows fp32 [R, H] (rows outside the group are
     left alone) -> None (kernels/fused_moe_affine.py:136-161, same argument checks). ``row_expert`` int32 [R]
     is the global expert of each row; ``aligned`` may carry a precomputed ``align_rows`` result and ``h_buf``
-    a bf16 [R, I] buffer; ``inter`` gives I when no h_buf is passed (default: this module's INTER)."""
+    a bf16 [R, I] buffer; ``inter`` gives I when no h_buf is passed, else I is the configured INTER, which needs
+    x to have the configured HID columns (the record offsets follow from both)."""
     r = row_token.numel()
     if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
         raise ValueError("x must be a contiguous bf16 [T, H] tensor")
@@ -80,7 +83,12 @@ def fused_moe_affine(x, row_token, row_weight, expert_map, group_ptr, out_rows, 
     if tuple(out_rows.shape) != (r, hid) or out_rows.dtype != torch.float32 or not out_rows.is_contiguous():
         raise ValueError(f"out_rows must be contiguous fp32 [R, {hid}]")
     if h_buf is None:
-        h_buf = torch.empty((r, inter or INTER), dtype=torch.bfloat16, device=x.device)
+        if inter is None:
+            if hid != HID:
+                raise ValueError(f"x has {hid} columns but the configured shape is {HID}/{INTER}: call "
+                                 "slotstream_b200.kernels.configure(hidden, inter) or pass h_buf or inter")
+            inter = INTER
+        h_buf = torch.empty((r, inter), dtype=torch.bfloat16, device=x.device)
     elif h_buf.dim() != 2 or h_buf.shape[0] != r or h_buf.dtype != torch.bfloat16 or not h_buf.is_contiguous():
         raise ValueError("h_buf must be bf16 [R, I]")
     if aligned is None:
@@ -91,9 +99,10 @@ def fused_moe_affine(x, row_token, row_weight, expert_map, group_ptr, out_rows, 
     launch_down(h_buf, row_weight, aligned, group_ptr, out_rows, r, err)
 
 
-def combine_rank_order(out_rows, T, K=TOPK, out=None):
+def combine_rank_order(out_rows, T, K=None, out=None):
     """out_rows fp32 [T*K, H], row = token*K + rank -> fp32 [T, H], summed in router rank order (sequential
-    fp32), bit-equal to kernels/fused_moe_affine.py:164-172."""
+    fp32), bit-equal to kernels/fused_moe_affine.py:164-172. K defaults to the configured TOPK."""
+    K = TOPK if K is None else K
     if out_rows.shape[0] != T * K:
         raise ValueError("out_rows must have T*K rows")
     if out_rows.dtype != torch.float32 or out_rows.dim() != 2 or not out_rows.is_contiguous():

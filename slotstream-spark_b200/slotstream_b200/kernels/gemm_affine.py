@@ -1,9 +1,11 @@
 """Tensor-core GEMM for the dense prefill rows -- drop-in for slotstream_spark/kernels/gemm_affine.py.
 
 y[m, n] = sum_k x[m, k] * w[n, k], fp32 accumulate (kernels/gemm_affine.py:1-8). The affine 4-bit weight is
-dequantised as q*s + b in fp32, rounded to bf16 once, and fed to tcgen05 MMAs (M128 N256 K16) with the
-accumulator in TMEM. Tiles and the k order depend only on (n, k), never on M, so each output row depends only on
-its own x row: rows i..j of an M-row call equal a (j - i)-row call bit for bit.
+dequantised as q*s + b in fp32, rounded to bf16 once, and fed to tcgen05 MMAs (256-row tiles of two M128 N128
+halves) with the accumulator in TMEM; a bf16 ``DenseWeight`` goes to the same tensor-core kernel with its rows
+copied straight into the operand tiles. Any N (the last 128-column block is partial). Tiles and the k order depend
+only on (n, k), never on M, so each output row depends only on its own x row: rows i..j of an M-row call equal a
+(j - i)-row call bit for bit.
 """
 import torch
 
@@ -24,7 +26,7 @@ def gemm(x: torch.Tensor, w, out: torch.Tensor | None = None, cfg: dict | None =
             raise ValueError(f"gemm supports 4-bit affine weights only, got bits={w.bits}")
         n = w.n
     elif isinstance(w, DenseWeight):
-        raise ValueError("dense bf16 weights take gemv() or the router kernels in this build")
+        n = w.n
     else:
         raise TypeError("w must be AffineWeight or DenseWeight")
     if k != w.k:
@@ -37,10 +39,17 @@ def gemm(x: torch.Tensor, w, out: torch.Tensor | None = None, cfg: dict | None =
           or not out.is_contiguous()):
         raise ValueError(f"out must be a contiguous fp32 [{m}, {n}] tensor on {x.device}, got "
                          f"{tuple(out.shape)} {out.dtype} {out.device}")
-    rc = _lib.lib().ssb_gemm_affine4(_lib.ptr(x), m, k, _lib.ptr(w.q), _lib.ptr(w.s), _lib.ptr(w.b), n, w.gs,
-                                     _lib.ptr(out), _lib.stream())
-    _lib.check(rc, "gemm_affine4")
-    _note("gemm_affine4")
+    if isinstance(w, DenseWeight):
+        if not w.w.is_contiguous():
+            raise ValueError("the dense weight must be contiguous")
+        rc = _lib.lib().ssb_gemm_dense(_lib.ptr(x), m, k, _lib.ptr(w.w), n, _lib.ptr(out), n, _lib.stream())
+        _lib.check(rc, "gemm_dense")
+        _note("gemm_tc")
+    else:
+        rc = _lib.lib().ssb_gemm_affine4(_lib.ptr(x), m, k, _lib.ptr(w.q), _lib.ptr(w.s), _lib.ptr(w.b), n, w.gs,
+                                         _lib.ptr(out), _lib.stream())
+        _lib.check(rc, "gemm_affine4")
+        _note("gemm_affine4")
     STATS["calls"] += 1
     STATS["rows"] += m
     return out

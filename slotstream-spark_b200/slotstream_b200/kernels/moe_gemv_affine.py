@@ -8,17 +8,18 @@ down (o_k = w_k * D h_k, fp32) with the rank-order sum out = o_0 + o_1 + ... fus
 
 The reference hard-codes 2560/640; here the shape comes from the tensors (hidden = x.shape[1],
 inter = h_buf.shape[2], top-k = expert_ids.shape[1]) and the record offsets from
-``slotstream_b200.records.RecordLayout``. The module constants describe the BASELINE shape (2048/512).
+``slotstream_b200.records.RecordLayout``. The module constants (HID, INTER, TOPK, RECORD_BYTES, O_*) describe the
+shape set by ``slotstream_b200.kernels.configure``: the reference model's 2560 / 640 until then.
 """
 import torch
 
 from .. import _lib
-from ..records import BASELINE_LAYOUT, EXPERTS_PER_LAYER, RecordLayout
+from ..records import EXPERTS_PER_LAYER, RecordLayout
+from . import shape as _shape
 from .gemv_affine import _note
 
-HID, INTER, TOPK = BASELINE_LAYOUT.hidden, BASELINE_LAYOUT.inter, 10
-RECORD_BYTES = BASELINE_LAYOUT.record_bytes
-(O_GATE_W, O_GATE_S, O_GATE_B, O_UP_W, O_UP_S, O_UP_B, O_DOWN_W, O_DOWN_S, O_DOWN_B) = BASELINE_LAYOUT.offsets()
+# HID, INTER, TOPK, RECORD_BYTES and O_GATE_W .. O_DOWN_B: the configured model shape (kernels/shape.py)
+_shape.install(globals())
 GS = 64
 MOE_DEFAULT = {"bn": 4, "br": 32, "bk": 512, "bkd": 128, "num_warps": 4}   # accepted for API parity
 

@@ -27,8 +27,8 @@ def _world(seed):
     return recs, shared, rw, sg
 
 
-def _tokens(rank):
-    return synth.activations(70 + rank, T, LAY.hidden)
+def _tokens(rank, counts=None):
+    return synth.activations(70 + rank, T if counts is None else counts[rank], LAY.hidden)
 
 
 def _free_port():
@@ -37,7 +37,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir, strided, exact, zipf, mb=1, bf16=False):
+def _rank_main(rank, world, port, out_dir, strided, exact, zipf, mb=1, bf16=False, counts=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -45,7 +45,8 @@ def _rank_main(rank, world, port, out_dir, strided, exact, zipf, mb=1, bf16=Fals
         recs, shared, rw, sg = _world(5)
         bias = synth.zipf_bias(E) * 4 if zipf else None
         ops = CpuOps(LAY, recs, shared, rw, sg, K, E, world, rank, strided=strided, bias=bias)
-        y = ep_forward(ops, bits_to_bf16(_tokens(rank)), K, world, exact=exact, micro_batches=mb, partials_bf16=bf16)
+        y = ep_forward(ops, bits_to_bf16(_tokens(rank, counts)), K, world, exact=exact, micro_batches=mb,
+                       partials_bf16=bf16)
         np.save(os.path.join(out_dir, f"routed{rank}.npy"), ops.routed.numpy())
         np.save(os.path.join(out_dir, f"y{rank}.npy"), y.view(torch.int16).numpy())
     finally:
@@ -101,3 +102,24 @@ def test_ep_exchange_with_bf16_partials(tmp_path):
         ref = ref.astype(np.float64)
         assert np.linalg.norm(got - ref) <= 2.0 ** -8 * np.linalg.norm(ref)
         assert not np.array_equal(got, ref)   # the rounding did happen
+
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_ep_exchange_with_uneven_and_empty_ranks(tmp_path, exact):
+    """Four ranks holding 0, 2, 12 and 5 tokens with micro_batches = 3: every rank posts the same collectives (the
+    part count does not depend on the token count), empty parts exchange zero rows, and each rank's sums equal the
+    one-rank layer on its own tokens."""
+    world, counts = 4, (0, 2, 12, 5)
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), True, exact, True, 3, False, counts),
+                       nprocs=world, join=True, start_method="spawn")
+    recs, shared, rw, sg = _world(5)
+    for rank in range(world):
+        got = np.load(tmp_path / f"routed{rank}.npy")
+        assert got.shape == (counts[rank], LAY.hidden)
+        if counts[rank] == 0:
+            continue
+        ref = single_rank_reference(LAY, recs, shared, rw, sg, K, _tokens(rank, counts), bias=synth.zipf_bias(E) * 4)
+        if exact:
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        else:
+            np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)

@@ -137,7 +137,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world_size, port, out_dir, mb=1, bf16=False):
+def _nccl_rank(rank, world_size, port, out_dir, mb=1, bf16=False, tokens=300, zipf=True, exact=None):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -150,33 +150,53 @@ def _nccl_rank(rank, world_size, port, out_dir, mb=1, bf16=False):
         base = recs.data_ptr() + torch.arange(E + 1, dtype=torch.int64) * lay.record_bytes
         W = dict(lay=lay, recs=recs, base=base, rw=bf16_tensor(synth.router_weight(0, E, lay.hidden, 0)),
                  sg=bf16_tensor(synth.shared_gate_weight(0, lay.hidden, 0)),
-                 bias=torch.from_numpy(synth.zipf_bias(E)).cuda())
-        x = bf16_tensor(synth.activations(90 + rank, 300, lay.hidden))
+                 bias=torch.from_numpy(synth.zipf_bias(E)).cuda() if zipf else None)
+        x = bf16_tensor(synth.activations(90 + rank, tokens, lay.hidden, tag=tokens))
         ops = CudaOps(W["rw"], W["sg"], base[owned_experts(rank, E, world_size, True)].cuda(), int(base[E]), K,
                       lay.inter, world_size, True, bias=W["bias"])
-        y = ep_forward(ops, x, K, world_size, exact=not bf16, micro_batches=mb, partials_bf16=bf16)
-        y1, _ = _one_gpu(W, x)
+        exact = (not bf16) if exact is None else exact
+        y = ep_forward(ops, x, K, world_size, exact=exact, micro_batches=mb, partials_bf16=bf16)
+        y1, routed1 = _one_gpu(W, x)
         torch.cuda.synchronize()
-        if bf16:   # partial sums rounded to bf16 on the return: within the layer tolerance of one GPU
-            d, r = (y.float() - y1.float()), y1.float()
+        d, r = (y.float() - y1.float()), y1.float()
+        if exact:
+            ok = bool(torch.equal(y, y1)) and bool(torch.equal(ops.routed.view(torch.int32), routed1.view(torch.int32)))
+        elif bf16:   # partial sums rounded to bf16 on the return: within the layer tolerance of one GPU
             ok = bool(d.norm() <= 5e-3 * r.norm()) and bool(d.abs().max() <= 2e-2 * r.abs().max())
-        else:
-            ok = bool(torch.equal(y, y1))
+        else:        # fp32 partial sums: the one-GPU rank-order sum reassociated per destination
+            dr = ops.routed - routed1
+            ok = bool(dr.norm() <= 1e-5 * routed1.norm()) and bool(d.norm() <= 1e-3 * r.norm())
         ok = ok and int(ops.err.item()) == 0
         with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
-            f.write("1" if ok else "0")
+            f.write("1" if ok else f"0 rel {float(d.norm() / r.norm()):.3e} max {float(d.abs().max()):.3e}")
         dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+def _spawn(tmp_path, n, **kw):
+    import torch.multiprocessing as mp
+    args = (n, _free_port(), str(tmp_path), kw.get("mb", 1), kw.get("bf16", False), kw.get("tokens", 300),
+            kw.get("zipf", True), kw.get("exact"))
+    mp.start_processes(_nccl_rank, args=args, nprocs=n, join=True, start_method="spawn")
+    for r in range(n):
+        assert (tmp_path / f"ok{r}").read_text() == "1", (r, (tmp_path / f"ok{r}").read_text())
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("mb,bf16", [(1, False), (2, False), (1, True)])
 def test_two_ranks_over_nccl_match_one_gpu(tmp_path, mb, bf16):
     """mb = 2: micro-batched exchange, the expert GEMMs of one part overlapping the transfers of the other;
-    bf16: partial sums returned in bf16 (default mode), compared within the layer tolerance."""
-    import torch.multiprocessing as mp
-    mp.start_processes(_nccl_rank, args=(2, _free_port(), str(tmp_path), mb, bf16), nprocs=2, join=True,
-                       start_method="spawn")
-    for r in range(2):
-        assert (tmp_path / f"ok{r}").read_text() == "1"
+    bf16: partial sums returned in bf16, compared within the layer tolerance."""
+    _spawn(tmp_path, 2, mb=mb, bf16=bf16)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+@pytest.mark.parametrize("zipf", [True, False])
+@pytest.mark.parametrize("mode", ["exact", "fp32", "bf16"])
+def test_all_ranks_over_nccl_32k_tokens_match_one_gpu(tmp_path, zipf, mode):
+    """Every visible GPU a rank (4 or 8), 32,768 tokens per rank, Zipf-skewed and uniform routing: each rank's
+    expert-parallel output against the one-GPU layer on the same tokens -- bit for bit in exact mode, within fp32
+    reassociation with fp32 partial sums, within the layer tolerance with bf16 partial sums."""
+    n = 8 if torch.cuda.device_count() >= 8 else 4
+    _spawn(tmp_path, n, tokens=32768, zipf=zipf, bf16=mode == "bf16", exact=mode == "exact")

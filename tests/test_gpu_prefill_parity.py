@@ -1,0 +1,122 @@
+"""The prefill MoE layer at the chunk sizes the benchmark times (2,048, 8,192 and 32,768 tokens, Zipf(1.1) routing)
+against the oracle, on the bars of the layer contract as written:
+
+* top-k ids bit-exact, except positions whose two candidates' router logits tie within 1e-6;
+* the bf16 layer output within relative L2 1e-2 of the exact oracle (fp64 routed experts);
+* max-abs 2e-2, in absolute terms, on the routed fp32 rank-order sum: the layer's output before it is rounded to
+  bf16, compared with the oracle that follows the reference's prefill rounding path (dequantised tiles and h in bf16,
+  fp32 accumulation, kernels/fused_moe_affine.py:14-16) under the kernel's own routing;
+* the bf16 output equal to that oracle's up to rounding flips: one bf16 ulp of the routed sum and of the output, plus
+  the shared expert's difference (its chain rounds to bf16 between ops, model/moe_sweep.py:37-43).
+
+The output itself is bf16 with values up to about 25 (RMS about 5 for these synthetic experts), where one bf16 ulp is
+0.0625-0.125: an absolute 2e-2 bar on the rounded output would only hold if every rounding landed on the same side as
+the oracle's, so the absolute bar is applied to the fp32 sum before rounding, and the rounded output is checked for
+rounding flips only. The test prints the literal max-abs of the bf16 output beside the others.
+
+At 2,048 tokens every token is checked; at 8,192 and 32,768 tokens (experts with thousands of rows spanning many
+256-row tiles, the align on its 16-CTA cluster) a seeded sample of 64 tokens, whose rows the oracle computes from the
+same records.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import bf16_tensor, record, to_np_bf16_bits
+from oracle import moe_oracle as O
+from slotstream_b200 import synth
+from slotstream_b200.records import BASELINE_LAYOUT
+
+pytestmark = pytest.mark.gpu
+E, K = 512, 10
+SEED = 0
+
+
+@pytest.fixture(scope="module")
+def layer():
+    lay = BASELINE_LAYOUT
+    recs = [record(lay, SEED, 0, e) for e in range(E + 1)]
+    pool = torch.from_numpy(np.stack(recs)).cuda()
+    gp = (pool.data_ptr() + torch.arange(E + 1, dtype=torch.int64) * lay.record_bytes).cuda()
+    rw = synth.router_weight(SEED, E, lay.hidden, 0)
+    sg = synth.shared_gate_weight(SEED, lay.hidden, 0)
+    return dict(lay=lay, recs=recs, pool=pool, gp=gp, rw=rw, sg=sg, bias=synth.zipf_bias(E))
+
+
+def _run(L, x_bits):
+    from slotstream_b200.kernels.moe_layer import PrefillLayerBuffers, moe_layer_prefill
+    t = x_bits.shape[0]
+    bufs = PrefillLayerBuffers(t, K, L["lay"].hidden, L["lay"].inter, E)
+    y = moe_layer_prefill(bf16_tensor(x_bits), bf16_tensor(L["rw"]), L["gp"], bf16_tensor(L["sg"]), K, bufs,
+                          bias=torch.from_numpy(L["bias"]).cuda())
+    torch.cuda.synchronize()
+    assert int(bufs.err.item()) == 0
+    return y, bufs
+
+
+def _check(L, x_bits, y_bits, ids_k, w_k, routed_k, sh_k, label):
+    """Every bar of the contract for the tokens in x_bits, given the kernel's outputs for them: y (bf16 bits), ids,
+    weights, the routed fp32 rank-order sum and the shared expert's rows (bf16-valued fp32)."""
+    lay = L["lay"]
+    # each oracle pass dequantises an expert once (its rows are batched), so nothing is cached: 513 records in fp64
+    # would hold 13 GB of host memory
+    ex32 = lambda e: O.record_dense(lay, L["recs"][e], np.float32)  # noqa: E731
+    ex64 = lambda e: O.record_dense(lay, L["recs"][e])  # noqa: E731
+    sh32 = ex32(E)
+
+    # routing: the oracle's own router; positions whose candidates' logits tie within 1e-6 are exempt
+    ids_ref, w_ref, logits = O.router(x_bits, L["rw"], K, bias=L["bias"])
+    exempt = O.ids_match(ids_k, ids_ref, logits)
+    same = np.all(ids_k == ids_ref, axis=1)
+    np.testing.assert_allclose(w_k[same], w_ref[same], rtol=2e-5, atol=1e-7)
+    # the exact oracle (fp64 routed experts, its own routing): relative L2 of the bf16 output
+    exact, *_ = O.moe_layer_grouped(lay, x_bits, L["rw"], K, ex64, sh32, L["sg"], bias=L["bias"])
+    got = O.bf16_to_f32(y_bits).astype(np.float64)
+    rel = O.rel_l2(got, exact)
+    assert rel <= 1e-2, f"{label}: rel-L2 {rel:.3e} vs the exact oracle"
+    # the reference's prefill rounding path under the kernel's routing: absolute max-abs 2e-2 on the routed fp32 sum
+    ref_y, ref_routed, ref_sh, *_ = O.moe_layer_prefill(lay, x_bits, L["rw"], K, ex32, sh32, L["sg"],
+                                                         bias=L["bias"], routing=(ids_k, w_k))
+    d_routed = float(np.max(np.abs(routed_k.astype(np.float64) - ref_routed)))
+    assert d_routed <= 2e-2, f"{label}: routed fp32 max-abs {d_routed:.3e}"
+    # the shared expert: its bf16 chain may round one intermediate the other way (2^-8 of its size each)
+    d_sh = np.abs(sh_k.astype(np.float64) - ref_sh)
+    assert float(np.max(d_sh)) <= 2.0 ** -6 * float(np.max(np.abs(ref_sh))), f"{label}: shared expert"
+    # the bf16 output: rounding flips only (routed.to(bf16), the shared difference, the final bf16 add)
+    bound = O.bf16_ulp(ref_routed) + d_sh + O.bf16_ulp(ref_y)
+    flips = np.abs(got - ref_y)
+    assert np.all(flips <= bound), f"{label}: output differs beyond rounding flips ({float(np.max(flips - bound)):.3e})"
+    lit = float(np.max(np.abs(got - exact)))
+    print(f"\n{label}: tokens {x_bits.shape[0]}, tie exemptions {exempt}, rel-L2 {rel:.2e}, routed fp32 max-abs "
+          f"{d_routed:.2e}, bf16 output max-abs vs exact {lit:.3e} (vs the same-rounding oracle "
+          f"{float(np.max(flips)):.3e}; outputs that differ {int(np.count_nonzero(flips))}/{flips.size})")
+    return exempt
+
+
+def test_prefill_2048_tokens_every_token(layer):
+    L = layer
+    t = 2048
+    x = synth.activations(SEED, t, L["lay"].hidden, tag=2048)
+    y, bufs = _run(L, x)
+    rows = bufs.out_rows.cpu().numpy()
+    routed = O.combine_rank_order(rows[:t * K], t, K)
+    _check(L, x, to_np_bf16_bits(y), bufs.ids.cpu().numpy(), bufs.w.cpu().numpy(), routed, rows[t * K:],
+           "2048 tokens")
+
+
+@pytest.mark.parametrize("t", [8192, 32768])
+def test_prefill_large_chunks_sampled(layer, t):
+    L = layer
+    x = synth.activations(SEED, t, L["lay"].hidden, tag=t)
+    y, bufs = _run(L, x)
+    # the cluster align runs from 32,768 rows on; experts then hold thousands of rows
+    counts = np.bincount(bufs.ids.cpu().numpy().reshape(-1), minlength=E)
+    assert counts.max() > 1024
+    rng = np.random.default_rng(t)
+    tok = np.unique(np.concatenate([[0, t - 1], rng.choice(t, 62, replace=False)]))
+    sel = torch.from_numpy(tok).cuda()
+    rows = bufs.out_rows[:t * K].view(t, K, -1)[sel].cpu().numpy().reshape(tok.size * K, -1)
+    routed = O.combine_rank_order(rows, tok.size, K)
+    sh = bufs.out_rows[t * K:][sel].cpu().numpy()
+    _check(L, x[tok], to_np_bf16_bits(y[sel]), bufs.ids[sel].cpu().numpy(), bufs.w[sel].cpu().numpy(), routed, sh,
+           f"{t} tokens (sample of {tok.size})")

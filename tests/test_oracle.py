@@ -130,3 +130,25 @@ def test_fused_rows_match_reference_helpers():
     # nibble-swap control far outside
     assert O.rel_l2(bf, exact) < 1e-2
     assert O.rel_l2(g["swap"], exact) > 10 * 1e-2
+
+
+def test_grouped_layer_equals_per_token_layer():
+    """moe_layer_grouped (rows batched per expert, used for chunks of thousands of tokens) is the same fp64
+    arithmetic as moe_layer's per-(token, rank) loop: equal up to fp64 summation order."""
+    lay, E, K = BASELINE_LAYOUT, 512, 10
+    x = synth.activations(5, 6, lay.hidden, tag=6)
+    rw = synth.router_weight(5, E, lay.hidden)
+    sg = synth.shared_gate_weight(5, lay.hidden)
+    bias = synth.zipf_bias(E)
+    dense = {}
+
+    def expert(e):
+        if e not in dense:
+            dense[e] = O.record_dense(lay, synth.expert_record(lay, 5, 0, e))
+        return dense[e]
+    sh = O.record_dense(lay, synth.expert_record(lay, 5, 0, E), np.float32)
+    out1, routed1, _, ids1, w1, _ = O.moe_layer(lay, x, rw, K, expert, sh, sg, bias=bias)
+    out2, routed2, ids2, w2, _ = O.moe_layer_grouped(lay, x, rw, K, expert, sh, sg, bias=bias)
+    assert np.array_equal(ids1, ids2) and np.array_equal(w1, w2)
+    assert O.rel_l2(routed2, routed1) < 1e-13
+    assert np.array_equal(out1, out2)

@@ -49,6 +49,30 @@ def test_static_router_matches_workspace_router_twice(tokens):
         torch.testing.assert_close(sh, rsh, rtol=1e-6, atol=0.0)
 
 
+def test_static_router_allocates_nothing():
+    """With its outputs allocated up front, a call leaves torch's allocator and the device's free memory as
+    they were: the logits live in the library's own device array."""
+    rw = bf16_tensor(synth.router_weight(0, E, H, 0))
+    sg = bf16_tensor(synth.shared_gate_weight(0, H, 0))
+    x = bf16_tensor(synth.activations(70, 64, H))
+    idx = torch.empty((64, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((64, K), dtype=torch.float32, device="cuda")
+    sh = torch.empty((64,), dtype=torch.float32, device="cuda")
+
+    def call():
+        _lib.check(_lib.lib().ssb_router_topk_static(_lib.ptr(x), _lib.ptr(rw), _lib.ptr(sg), 64, H, E, K, None, 0,
+                                                     _lib.ptr(idx), _lib.ptr(w), _lib.ptr(sh), _lib.stream()),
+                   "router_topk_static")
+        torch.cuda.synchronize()
+
+    call()                                   # the first call on the device looks the array's address up
+    alloc0, free0 = torch.cuda.memory_allocated(), torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        call()
+    assert torch.cuda.memory_allocated() == alloc0
+    assert torch.cuda.mem_get_info()[0] == free0
+
+
 def test_static_router_without_shared_gate_and_bf16_logits():
     rw = bf16_tensor(synth.router_weight(0, E, H, 0))
     x = bf16_tensor(synth.activations(60, 8, H))
