@@ -254,15 +254,25 @@ int ssb_router_topk_static(const uint16_t* x, const uint16_t* w, const uint16_t*
 
 /* Whole decode MoE layer for rows <= 2 tokens in ONE cooperative launch (one CTA per SM, two grid barriers):
  * router logits (x . w_router^T and the shared gate x . sh_gate_w, fp32), select as ssb_router_select (bias,
- * flags 0 or SSB_ROUTER_ROUND_BF16), expert resolution through the slot tables as ssb_moe_decode, then
- * ssb_moe_decode_layer's gate_up / down / rank-order sum / shared add. Outputs and their bits equal the
- * separate calls: out_idx / out_w [rows, topk], out_sh_gate [rows], out_base [rows, topk] (nullable), h_buf
- * [rows * (topk + 1), inter], o_buf [rows, topk, hidden] (nullable), out fp32 / y bf16 [rows, hidden].
- * logits_ws: fp32 [rows, experts + 1]. sync: two uint32 words, zero before the first call and after a call
- * that reported SSB_ERR_TIMEOUT; calls sharing sync must not overlap. Limits: hidden % 512 == 0 and <= 4096,
- * inter in {512, 1024, 2048}, experts <= 512, topk <= 16, gs 64; other shapes return SSB_EUNSUPPORTED.
+ * flags SSB_ROUTER_ROUND_BF16), expert resolution through the slot tables as ssb_moe_decode, then gate_up / down /
+ * rank-order sum / shared add. Two kernels: on CUDA cores (exact fp32 dequantisation algebra; h, out and y equal
+ * ssb_moe_decode_layer's bit for bit), and on the tensor cores (4-bit codes dequantised exactly to bf16, fp32
+ * accumulation, the affine scale and bias applied per 64-element group in fp32, h kept in fp32 as a bf16 hi + lo
+ * pair; each distinct chosen expert read once for both tokens; h, out and y within the exact path's tolerance,
+ * relative L2 1e-4). Both give out_idx / out_w / out_sh_gate / out_base equal to the separate calls bit for bit.
+ * flags SSB_DECODE_FUSED_CUDA_CORES / SSB_DECODE_FUSED_TENSOR_CORES pick one; by default one token runs on CUDA
+ * cores and two on the tensor cores (the faster of the two for each, measured on B200). The tensor-core kernel
+ * falls back to the CUDA-core one for a shape it does not take (hidden other than 2048 / 2560 / 4096, inter not a
+ * multiple of 128, or more resident weight rows per SM than its shared memory holds). Outputs: out_idx / out_w [rows, topk], out_sh_gate [rows], out_base
+ * [rows, topk] (nullable), h_buf [rows * (topk + 1), inter] (16-byte aligned), o_buf [rows, topk, hidden]
+ * (nullable), out fp32 / y bf16 [rows, hidden]. logits_ws: fp32 [rows, experts + 1]. sync: two uint32 words,
+ * zero before the first call and after a call that reported SSB_ERR_TIMEOUT; calls sharing sync must not overlap.
+ * Limits: hidden % 512 == 0 and <= 4096, inter in {512, 1024, 2048} (tensor cores: any multiple of 128 up to
+ * 2048), experts <= 512, topk <= 16, gs 64; other shapes return SSB_EUNSUPPORTED.
  * Replaces: the router of model/layers.py:336-347 plus the decode MoE call site of
  * slotstream_spark/runtime/graphs.py:160-169, for callers that opt in. */
+#define SSB_DECODE_FUSED_CUDA_CORES 4
+#define SSB_DECODE_FUSED_TENSOR_CORES 8
 int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t topk, int32_t hidden, int32_t inter, int32_t experts,
                          const uint16_t* w_router, const uint16_t* sh_gate_w, const float* bias, int32_t flags,
                          int32_t layer, const int32_t* map_t, int64_t map_len, const int64_t* slot_ptr_t,

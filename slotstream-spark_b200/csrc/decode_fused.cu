@@ -23,6 +23,7 @@
 // then a butterfly), so the fused layer reproduces router_logits + router_select + moe_decode_layer bit for
 // bit. Grid barriers spin with a bounded wait on a caller-owned counter word and give up with
 // SSB_ERR_TIMEOUT; the word must be zero before the first call and again after a timeout.
+#include "decode_internal.h"
 #include "registry.h"
 #include "select.cuh"
 #include "tc_common.cuh"
@@ -643,13 +644,12 @@ constexpr size_t F_SMEM_MAX = 227 * 1024;   // opt-in shared memory per CTA on s
 
 }  // namespace
 
-extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t topk, int32_t hidden, int32_t inter,
-                                    int32_t experts, const uint16_t* w_router, const uint16_t* sh_gate_w,
-                                    const float* bias, int32_t flags, int32_t layer, const int32_t* map_t,
-                                    int64_t map_len, const int64_t* slot_ptr_t, int64_t n_slots,
-                                    const void* shared_record, float* logits_ws, int32_t* out_idx, float* out_w,
-                                    float* out_sh_gate, int64_t* out_base, float* h_buf, float* o_buf, float* out,
-                                    uint16_t* y, uint32_t* sync, int32_t* err, void* stream) {
+int decode_fused_cuda_cores(const uint16_t* x, int64_t rows, int32_t topk, int32_t hidden, int32_t inter,
+                            int32_t experts, const uint16_t* w_router, const uint16_t* sh_gate_w, const float* bias,
+                            int32_t flags, int32_t layer, const int32_t* map_t, int64_t map_len,
+                            const int64_t* slot_ptr_t, int64_t n_slots, const void* shared_record, float* logits_ws,
+                            int32_t* out_idx, float* out_w, float* out_sh_gate, int64_t* out_base, float* h_buf,
+                            float* o_buf, float* out, uint16_t* y, uint32_t* sync, int32_t* err, void* stream) {
   SSB_CHECK_ARG(rows >= 0 && topk >= 1 && topk <= F_MAXK && topk <= experts && experts >= 1 && layer >= 0);
   if (rows > F_MAXR || experts > F_MAXE || hidden % 512 || hidden <= 0 || hidden > 4096 || inter % 512 ||
       inter <= 0 || inter > 2048 || inter == 1536)
@@ -735,7 +735,7 @@ extern "C" int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t top
     if (per_sm < 1) return SSB_EUNSUPPORTED;
     pp->smem = smem;
   }
-  ssb_note_smem_bytes("moe_decode_fused", (int)(pp->static_smem + smem));
+  ssb_note_smem_bytes("moe_decode_fused_cc", (int)(pp->static_smem + smem));
   FusedArgs a{};
   a.x = x;
   a.R = R;

@@ -16,6 +16,8 @@ ERR_EXPERT_RANGE, ERR_UNMAPPED, ERR_SLOT_RANGE, ERR_MISALIGNED, ERR_TIMEOUT = 1,
 BF16, F32 = 0, 1
 ROUTER_ROUND_BF16, ROUTER_SHARED_GATE = 1, 2
 DECODE_PDL = 1
+DECODE_FUSED_CUDA_CORES = 4
+DECODE_FUSED_TENSOR_CORES = 8
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32

@@ -119,10 +119,13 @@ def _addr(rec) -> int:
 
 def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, sh_gate_w, k: int,
                      bufs: DecodeLayerBuffers, *, bias=None, logits_round_bf16: bool = False, pdl: bool = True,
-                     prefetch_bytes: int = 0, fused: bool = True):
+                     prefetch_bytes: int = 0, fused: bool = True, cuda_cores: bool = False,
+                     tensor_cores: bool = False):
     """x bf16 [R, H] -> bufs.y bf16 [R, H] (also fills bufs.ids, bufs.w, bufs.out = routed fp32 sum).
-    ``fused`` (R <= 2): the whole layer in one cooperative launch (ssb_moe_decode_fused), the same bits as the
-    four-launch path router_logits -> router_select_resolve -> moe_decode_layer used otherwise.
+    ``fused`` (R <= 2): the whole layer in one cooperative launch (ssb_moe_decode_fused): the same ids and weights as
+    the four-launch path router_logits -> router_select_resolve -> moe_decode_layer used otherwise. One token runs on
+    CUDA cores (every output equal to the four-launch path bit for bit), two on the tensor cores (h and the routed sum
+    within the fp32 tolerance); ``cuda_cores`` / ``tensor_cores`` force one of the two.
     ``prefetch_bytes`` > 0 makes the four-launch router prefetch that many bytes of each chosen record into L2."""
     r, h = x.shape
     if (r, k, h) != (bufs.rows, bufs.topk, bufs.hidden) or w_router.shape[0] != bufs.experts:
@@ -141,7 +144,9 @@ def moe_layer_decode(x, w_router, layer: int, map_t, slot_ptr_t, shared_record, 
     if fused and r <= FUSED_MAX_ROWS:
         rc = L.ssb_moe_decode_fused(
             _lib.ptr(x), r, k, h, bufs.inter, e, _lib.ptr(w_router), _lib.ptr(sh_gate_w), _lib.ptr(bias),
-            _lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0, int(layer), _lib.ptr(map_t), map_t.numel(),
+            (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0) | (_lib.DECODE_FUSED_CUDA_CORES if cuda_cores else 0)
+            | (_lib.DECODE_FUSED_TENSOR_CORES if tensor_cores else 0),
+            int(layer), _lib.ptr(map_t), map_t.numel(),
             _lib.ptr(slot_ptr_t), slot_ptr_t.numel(), _addr(shared_record), _lib.ptr(bufs.ws), _lib.ptr(bufs.ids),
             _lib.ptr(bufs.w), _lib.ptr(bufs.sh_gate), _lib.ptr(bufs.bases), _lib.ptr(bufs.h), _lib.ptr(bufs.o),
             _lib.ptr(bufs.out), _lib.ptr(bufs.y), _lib.ptr(bufs.sync), _lib.ptr(bufs.err), st)

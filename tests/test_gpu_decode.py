@@ -234,18 +234,20 @@ def test_decode_layer_matches_bf16_oracle_and_is_row_invariant(layer_world):
     # intermediate moves it by 2^-8 of its size) and the output's two roundings
     assert np.max(np.abs(bufs.out.cpu().numpy() - routed)) <= 2e-2
     assert np.all(np.abs(got - out_ref) <= 2e-2 + 2.0 ** -6 * np.abs(sh_ref) + 2 * O.bf16_ulp(out_ref))
+    # row invariance of the four-launch path (the 16-row call groups entries by expert, the 1-row calls do not); the
+    # fused tensor-core layer (the 1- and 2-row default) has its own invariance test below
     one = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
     xt = bf16_tensor(x)
     for r in (0, 7, 15):
-        y1 = moe_layer_decode(xt[r:r + 1].contiguous(), *args, one, bias=torch.from_numpy(bias).cuda())
+        y1 = moe_layer_decode(xt[r:r + 1].contiguous(), *args, one, bias=torch.from_numpy(bias).cuda(), fused=False)
         assert torch.equal(y1[0], y[r])
 
 
 # ------------------------------------------------------------------ fused (one cooperative launch) decode layer
 @pytest.mark.parametrize("rows,zipf,round_bf16", [(1, True, False), (2, True, False), (1, False, True), (2, False, False)])
-def test_fused_layer_equals_four_launch_layer(layer_world, rows, zipf, round_bf16):
-    """ssb_moe_decode_fused reproduces router_logits -> router_select_resolve -> moe_decode_layer bit for bit
-    (ids, weights, shared gate, h, o, routed sum and the bf16 output), on three calls in a row."""
+def test_fused_cuda_core_layer_equals_four_launch_layer(layer_world, rows, zipf, round_bf16):
+    """ssb_moe_decode_fused on CUDA cores reproduces router_logits -> router_select_resolve -> moe_decode_layer bit
+    for bit (ids, weights, shared gate, h, o, routed sum and the bf16 output), on three calls in a row."""
     from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
     lay, recs, pool, shared = layer_world
     rw = bf16_tensor(synth.router_weight(0, 512, lay.hidden, 0))
@@ -256,7 +258,7 @@ def test_fused_layer_equals_four_launch_layer(layer_world, rows, zipf, round_bf1
     for call in range(3):
         x = bf16_tensor(synth.activations(200 + call, rows, lay.hidden))
         args = (x, rw, 0, pool.map, pool.slot_ptr, shared, sg, 10)
-        moe_layer_decode(*args, fb, bias=bias, logits_round_bf16=round_bf16, fused=True)
+        moe_layer_decode(*args, fb, bias=bias, logits_round_bf16=round_bf16, fused=True, cuda_cores=True)
         moe_layer_decode(*args, sb, bias=bias, logits_round_bf16=round_bf16, fused=False)
         torch.cuda.synchronize()
         assert int(fb.err.item()) == 0 and int(sb.err.item()) == 0
@@ -281,8 +283,73 @@ def test_fused_layer_reports_unmapped_choice(layer_world):
     holes[gone] = -1
     fb = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
     sb = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
-    moe_layer_decode(x, rw, 0, holes, pool.slot_ptr, shared, sg, 10, fb, fused=True)
+    cb = DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
+    moe_layer_decode(x, rw, 0, holes, pool.slot_ptr, shared, sg, 10, fb, fused=True, tensor_cores=True)
+    moe_layer_decode(x, rw, 0, holes, pool.slot_ptr, shared, sg, 10, cb, fused=True, cuda_cores=True)
     moe_layer_decode(x, rw, 0, holes, pool.slot_ptr, shared, sg, 10, sb, fused=False)
     torch.cuda.synchronize()
-    assert int(fb.err.item()) & 2 and int(sb.err.item()) & 2
-    assert torch.equal(fb.out, sb.out) and torch.equal(fb.y, sb.y)
+    assert int(fb.err.item()) & 2 and int(cb.err.item()) & 2 and int(sb.err.item()) & 2
+    assert torch.equal(cb.out, sb.out) and torch.equal(cb.y, sb.y)
+    assert torch.equal(fb.ids, sb.ids)
+    assert float((fb.out - sb.out).norm() / sb.out.norm()) <= 1e-5   # the missing expert contributes zero in both
+
+
+@pytest.mark.parametrize("rows,zipf,round_bf16", [(1, True, False), (2, True, False), (1, False, True), (2, False, False)])
+def test_fused_tensor_core_layer_matches_four_launch_layer(layer_world, rows, zipf, round_bf16):
+    """The tensor-core fused layer (the default) against the exact-fp32 four-launch path on three calls in a row:
+    ids, weights, shared gate and resolved bases bit for bit; h, o and the routed sum within the fp32 decode
+    tolerance (relative L2 1e-4 -- and the routed sum against the fp64 oracle too); the bf16 output within rounding
+    flips of the four-launch output."""
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    lay, recs, pool, shared = layer_world
+    rw = bf16_tensor(synth.router_weight(0, 512, lay.hidden, 0))
+    sg = bf16_tensor(synth.shared_gate_weight(0, lay.hidden, 0))
+    bias = torch.from_numpy(synth.zipf_bias(512)).cuda() if zipf else None
+    fb = DecodeLayerBuffers(rows, 10, lay.hidden, lay.inter)
+    sb = DecodeLayerBuffers(rows, 10, lay.hidden, lay.inter)
+    dense = {}
+
+    def ex(e):
+        if e not in dense:
+            dense[e] = O.record_dense(lay, recs[e])
+        return dense[e]
+    for call in range(3):
+        xb = synth.activations(200 + call, rows, lay.hidden)
+        x = bf16_tensor(xb)
+        args = (x, rw, 0, pool.map, pool.slot_ptr, shared, sg, 10)
+        moe_layer_decode(*args, fb, bias=bias, logits_round_bf16=round_bf16, fused=True, tensor_cores=True)
+        moe_layer_decode(*args, sb, bias=bias, logits_round_bf16=round_bf16, fused=False)
+        torch.cuda.synchronize()
+        assert int(fb.err.item()) == 0 and int(sb.err.item()) == 0
+        for name in ("ids", "w", "sh_gate", "bases"):
+            assert torch.equal(getattr(fb, name), getattr(sb, name)), (call, name)
+        n = rows * 11 * lay.inter
+        for name, a_, b_ in (("h", fb.h[:n], sb.h[:n]), ("o", fb.o, sb.o), ("out", fb.out, sb.out)):
+            rel = float((a_.double() - b_.double()).norm() / b_.double().norm())
+            assert rel <= 1e-4, (call, name, rel)
+        routed = O.moe_decode(lay, O.bf16_to_f32(xb), fb.ids.cpu().numpy(), fb.w.cpu().numpy(), ex)
+        assert O.rel_l2(fb.out.cpu().numpy(), routed) <= 1e-4
+        y_f = O.bf16_to_f32(to_np_bf16_bits(fb.y)).astype(np.float64)
+        y_s = O.bf16_to_f32(to_np_bf16_bits(sb.y)).astype(np.float64)
+        sh = np.abs(y_s - O.bf16_to_f32(O.f32_to_bf16(sb.out.cpu().numpy())).astype(np.float64))
+        bound = O.bf16_ulp(y_s) + O.bf16_ulp(sb.out.cpu().numpy()) + 2.0 ** -7 * sh + 1e-3
+        assert np.all(np.abs(y_f - y_s) <= bound), call
+
+
+def test_fused_tensor_core_layer_is_row_invariant(layer_world):
+    """A two-token call gives each token the bits of a one-token call: the tokens are separate mma columns, and
+    the routing, the fold and the combine are per token."""
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    lay, recs, pool, shared = layer_world
+    rw = bf16_tensor(synth.router_weight(0, 512, lay.hidden, 0))
+    sg = bf16_tensor(synth.shared_gate_weight(0, lay.hidden, 0))
+    bias = torch.from_numpy(synth.zipf_bias(512)).cuda()
+    x = bf16_tensor(synth.activations(400, 2, lay.hidden))
+    two, one = DecodeLayerBuffers(2, 10, lay.hidden, lay.inter), DecodeLayerBuffers(1, 10, lay.hidden, lay.inter)
+    moe_layer_decode(x, rw, 0, pool.map, pool.slot_ptr, shared, sg, 10, two, bias=bias, tensor_cores=True)
+    for r in range(2):
+        moe_layer_decode(x[r:r + 1].contiguous(), rw, 0, pool.map, pool.slot_ptr, shared, sg, 10, one, bias=bias,
+                         tensor_cores=True)
+        torch.cuda.synchronize()
+        assert torch.equal(one.ids[0], two.ids[r]) and torch.equal(one.w[0], two.w[r])
+        assert torch.equal(one.out[0], two.out[r]) and torch.equal(one.y[0], two.y[r])

@@ -102,7 +102,8 @@ def test_sweep_group_calls(shape_reset, hidden, inter):
     rows_ref = O.fused_rows_bf16_path(O.bf16_to_f32(x_bits), np.repeat(np.arange(T), K), w.reshape(-1), flat,
                                       lambda e: f32[e], range(R))
     ref = O.combine_rank_order(rows_ref.astype(np.float32), T, K)
-    assert O.rel_l2(routed, ref) <= 1e-5
+    # the same rounding points; an h element that rounds to the other bf16 neighbour moves a row by 2^-8 of one term
+    assert O.rel_l2(routed, ref) <= 1e-3
     exact = O.fused_rows_exact(O.bf16_to_f32(x_bits), np.repeat(np.arange(T), K), w.reshape(-1), flat,
                                lambda e: O.record_dense(lay, recs[e]), range(R))
     assert O.rel_l2(routed, O.combine_rank_order(exact, T, K)) <= 1e-2
