@@ -30,6 +30,7 @@ extern "C" {
 #define SSB_EUNSUPPORTED (-2) /* a shape these kernels do not handle (see each entry point) */
 #define SSB_ENODEVICE (-3)    /* current device is not sm_100 */
 #define SSB_ETOOBIG (-4)      /* request larger than a fixed capacity (static scratch, slot pool) */
+#define SSB_ETIMEDOUT (-5)    /* a bounded host-side wait gave up (ssb_wait_seq) */
 
 /* ---- bits of the device error word (int32, caller-owned, OR-ed by kernels; never cleared by them) */
 #define SSB_ERR_EXPERT_RANGE 1 /* an expert id outside [0, 512) */
@@ -58,6 +59,13 @@ int ssb_kernel_smem(const char* name);
  * all-to-all of an expert-parallel exchange -- can run beside them. A process-wide setting read at each launch.
  * No counterpart in the reference (it runs on one GPU with no collective to overlap). */
 int ssb_set_gemm_sm_reserve(int32_t sms);
+
+/* Bound, in nanoseconds, of the grid-barrier waits of the cooperative kernels (ssb_moe_decode_fused; default 250 ms):
+ * a barrier that does not complete in time gives up, the kernel sets SSB_ERR_TIMEOUT in the caller's error word
+ * and returns (its outputs are then not valid, and its sync word must be zeroed before the next call). A
+ * process-wide setting read at each launch; waits on the kernels' own copies keep their fixed bound. No
+ * counterpart in the reference (its kernels do not wait on one another). */
+int ssb_set_wait_limit_ns(int64_t ns);
 
 /* Stable top-k of each row of fp32 scores [rows, n] (n <= 65536, 1 <= k <= n): order-preserving uint32
  * keys (NaN lowest), ties to the lower index; k <= 16 sorted by (value desc, index asc), larger k by
@@ -279,6 +287,19 @@ int ssb_moe_decode_fused(const uint16_t* x, int64_t rows, int32_t topk, int32_t 
                          int64_t n_slots, const void* shared_record, float* logits_ws, int32_t* out_idx, float* out_w,
                          float* out_sh_gate, int64_t* out_base, float* h_buf, float* o_buf, float* out, uint16_t* y,
                          uint32_t* sync, int32_t* err, void* stream);
+
+/* Router readback signal (one warp, graph-capturable): copies ids int32 / w fp32 [n] (n <= 32; n = 0 publishes only)
+ * into slot `layer` of slot_ids / slot_w (32 elements per layer; pinned host buffers the device writes through their
+ * mapping), then publishes *seq = ctrl[1] + layer with a system-scope release exchange, so a host thread that observes
+ * seq >= ctrl[1] + layer with an acquire load (ssb_wait_seq) also sees that layer's ids and weights. ctrl int64 [2]
+ * (position, step base) is written by the host before the step's graph launches.
+ * Replaces: signal(), slotstream_spark/kernels/signal.py:15-37 (kernel :15-26). */
+int ssb_signal(const int32_t* ids, const float* w, int32_t n, int32_t* slot_ids, float* slot_w, int64_t* seq,
+               const int64_t* ctrl, int32_t layer, void* stream);
+
+/* Host-side: spin (acquire loads, yielding every 256 polls) until *seq >= target; SSB_ETIMEDOUT after timeout_ns.
+ * Replaces: Readback.wait / slotio.wait_seq, slotstream_spark/runtime/readback.py:40-46. */
+int ssb_wait_seq(const int64_t* seq, int64_t target, int64_t timeout_ns);
 
 /* Rank-order combine: out[t, :] = rows[t*k] + rows[t*k + 1] + ... sequentially in fp32.
  * rows fp32 [tokens * k, hidden], out fp32 [tokens, hidden]; hidden % 4 == 0.

@@ -68,6 +68,7 @@ struct FusedArgs {
   int stage_rows;      // rows one staging round holds
   int down_stage;      // 1: this CTA's columns of every entry's down rows are bulk-copied into shared memory
   uint32_t gstage_off, dstage_off;   // staged gate/up rows, later the h units; staged down rows
+  uint64_t barrier_ns;               // grid-barrier wait bound (ssb_set_wait_limit_ns)
 };
 
 struct __align__(16) XUnitS {
@@ -79,7 +80,7 @@ struct __align__(16) XUnitS {
 // Ticket barrier on one monotonically increasing word: each CTA adds 1 with release semantics and waits
 // (acquire loads) until the word reaches the end of its round, so nothing has to be reset between rounds and
 // the release costs one atomic per CTA. Wrap-around is harmless (signed difference).
-SSB_DEV bool grid_sync(uint32_t* sync, int32_t* err, int* s_ok) {
+SSB_DEV bool grid_sync(uint32_t* sync, int32_t* err, int* s_ok, uint64_t limit_ns) {
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
@@ -92,7 +93,7 @@ SSB_DEV bool grid_sync(uint32_t* sync, int32_t* err, int* s_ok) {
       uint32_t cur;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(sync) : "memory");
       if ((int32_t)(cur - target) >= 0) break;
-      if ((++polls & 255u) == 0 && globaltimer_ns() - t0 > SSB_WAIT_NS) {
+      if ((++polls & 7u) == 0 && globaltimer_ns() - t0 > limit_ns) {
         ok = 0;
         set_err(err, SSB_ERR_TIMEOUT);
         break;
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
       }
     }
   }
-  if (!grid_sync(a.sync, a.err, &s_ok)) {
+  if (!grid_sync(a.sync, a.err, &s_ok, a.barrier_ns)) {
     if (tid == 0 && a.down_stage && ncol > 0) mbar_wait_ns(&s_bar_sh, 0, SSB_WAIT_NS);
     return;
   }
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(FT, 1) k_dec_fused(FusedArgs a) {
       return;
     }
   }
-  if (!grid_sync(a.sync, a.err, &s_ok)) {
+  if (!grid_sync(a.sync, a.err, &s_ok, a.barrier_ns)) {
     if (tid == 0) {   // let this CTA's copies in flight land before it leaves
       if (down_routed) mbar_wait_ns(&s_bar_d, 0, SSB_WAIT_NS);
       if (a.down_stage && ncol > 0) mbar_wait_ns(&s_bar_sh, 0, SSB_WAIT_NS);
@@ -770,6 +771,7 @@ int decode_fused_cuda_cores(const uint16_t* x, int64_t rows, int32_t topk, int32
   a.down_stage = down_stage;
   a.gstage_off = (uint32_t)fixed;
   a.dstage_off = (uint32_t)(fixed + stage_b);
+  a.barrier_ns = ssb_barrier_wait_ns();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)G);   // one CTA per SM: all resident (the launch fails otherwise)
   cfg.blockDim = dim3(FT);

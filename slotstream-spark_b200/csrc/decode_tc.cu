@@ -76,6 +76,7 @@ struct TcArgs {
   uint32_t pitch;          // bytes of one staged weight row (H / 2 + 16)
   uint32_t stage_bytes;    // one staged unit: 16 rows + gate/up scales and biases
   uint32_t off_xp, off_xsum, off_bases, off_bias, off_part, off_stage;
+  uint64_t barrier_ns;     // grid-barrier wait bound (ssb_set_wait_limit_ns)
 };
 
 SSB_DEV void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -115,7 +116,7 @@ SSB_DEV uint4 kperm8_t(uint4 v) {
 }
 
 // Ticket grid barrier (see decode_fused.cu): false when the bounded wait gave up (SSB_ERR_TIMEOUT is set).
-SSB_DEV bool grid_sync_tc(uint32_t* sync, int32_t* err, int* s_ok) {
+SSB_DEV bool grid_sync_tc(uint32_t* sync, int32_t* err, int* s_ok, uint64_t limit_ns) {
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
@@ -128,7 +129,7 @@ SSB_DEV bool grid_sync_tc(uint32_t* sync, int32_t* err, int* s_ok) {
       uint32_t cur;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(sync) : "memory");
       if ((int32_t)(cur - target) >= 0) break;
-      if ((++polls & 255u) == 0 && globaltimer_ns() - t0 > SSB_WAIT_NS) {
+      if ((++polls & 7u) == 0 && globaltimer_ns() - t0 > limit_ns) {
         ok = 0;
         set_err(err, SSB_ERR_TIMEOUT);
         break;
@@ -399,7 +400,7 @@ __global__ void __launch_bounds__(TT, 1) k_dec_tc(TcArgs a) {
     if (tid == 0) set_err(a.err, SSB_ERR_TIMEOUT);
     return;
   }
-  if (!grid_sync_tc(a.sync, a.err, &s_ok)) return;
+  if (!grid_sync_tc(a.sync, a.err, &s_ok, a.barrier_ns)) return;
 
   // ---------------- phase 2: select (each CTA). The per-expert passes of warp_select run on all threads of the CTA --
   // element e of token t sits at index e = lane + 32 i of the token's scratch exactly as in warp_select, and the
@@ -568,7 +569,7 @@ __global__ void __launch_bounds__(TT, 1) k_dec_tc(TcArgs a) {
       a.h_buf[(int64_t)p * I + j8 * 8 + j] = s_ubase[ui] ? gs / (1.f + expf(-gs)) * us : 0.f;
     }
   }
-  if (!grid_sync_tc(a.sync, a.err, &s_ok)) return;
+  if (!grid_sync_tc(a.sync, a.err, &s_ok, a.barrier_ns)) return;
 
   // ---------------- phase 4: down for columns [c0, c1) of every distinct expert and the shared one
   {
@@ -797,6 +798,7 @@ static int decode_tc(const uint16_t* x, int64_t rows, int32_t topk, int32_t hidd
   a.off_bias = off_bias;
   a.off_part = off_part;
   a.off_stage = off_stage;
+  a.barrier_ns = ssb_barrier_wait_ns();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)G);   // one CTA per SM, all resident (the cooperative launch fails otherwise)
   cfg.blockDim = dim3(TT);

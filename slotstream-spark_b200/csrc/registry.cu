@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -11,6 +12,7 @@
 
 namespace {
 std::mutex g_mu;
+std::atomic<int64_t> g_barrier_ns{250LL * 1000 * 1000};   // grid-barrier wait bound of the cooperative kernels
 std::unordered_map<std::string, int>& table() {
   static std::unordered_map<std::string, int> t;
   return t;
@@ -41,4 +43,12 @@ extern "C" int ssb_device_check(void) {
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   return (major == 10 && minor == 0) ? SSB_OK : SSB_ENODEVICE;
+}
+
+uint64_t ssb_barrier_wait_ns() { return (uint64_t)g_barrier_ns.load(std::memory_order_relaxed); }
+
+extern "C" int ssb_set_wait_limit_ns(int64_t ns) {
+  if (ns < 0) return SSB_EINVAL;
+  g_barrier_ns.store(ns, std::memory_order_relaxed);
+  return SSB_OK;
 }

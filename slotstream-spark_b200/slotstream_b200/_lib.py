@@ -11,7 +11,7 @@ import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libslotstream_b200.so"
 
-SSB_OK, SSB_EINVAL, SSB_EUNSUPPORTED, SSB_ENODEVICE, SSB_ETOOBIG = 0, -1, -2, -3, -4
+SSB_OK, SSB_EINVAL, SSB_EUNSUPPORTED, SSB_ENODEVICE, SSB_ETOOBIG, SSB_ETIMEDOUT = 0, -1, -2, -3, -4, -5
 ERR_EXPERT_RANGE, ERR_UNMAPPED, ERR_SLOT_RANGE, ERR_MISALIGNED, ERR_TIMEOUT = 1, 2, 4, 8, 16
 BF16, F32 = 0, 1
 ROUTER_ROUND_BF16, ROUTER_SHARED_GATE = 1, 2
@@ -28,6 +28,7 @@ SIGNATURES = {
     "ssb_device_check": [],
     "ssb_kernel_smem": [ctypes.c_char_p],
     "ssb_set_gemm_sm_reserve": [_I32],
+    "ssb_set_wait_limit_ns": [_I64],
     "ssb_topk_stable": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
     "ssb_router_logits": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P],
     "ssb_router_select": [_P, _I32, _I64, _I32, _I32, _P, _I32, _P, _P, _P, _P, _P],
@@ -56,6 +57,8 @@ SIGNATURES = {
     "ssb_pool_decode_layer": [_P, _I32, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                               _P, _P, _P, _P, _P, _P, _P, _P],
     "ssb_router_topk_static": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P],
+    "ssb_signal": [_P, _P, _I32, _P, _P, _P, _P, _I32, _P],
+    "ssb_wait_seq": [_P, _I64, _I64],
     "ssb_combine_rank_order": [_P, _I64, _I32, _I32, _P, _P],
     "ssb_combine_layer": [_P, _I64, _I32, _I32, _P, _P, _P, _P],
     "ssb_gemv_affine": [_P, _I32, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P],
@@ -108,7 +111,8 @@ def stream():
 
 _NAMES = {SSB_EINVAL: "SSB_EINVAL (bad argument)", SSB_EUNSUPPORTED: "SSB_EUNSUPPORTED (shape not handled)",
           SSB_ENODEVICE: "SSB_ENODEVICE (not an sm_100 device)",
-          SSB_ETOOBIG: "SSB_ETOOBIG (request exceeds a fixed capacity: static scratch or slot pool)"}
+          SSB_ETOOBIG: "SSB_ETOOBIG (request exceeds a fixed capacity: static scratch or slot pool)",
+          SSB_ETIMEDOUT: "SSB_ETIMEDOUT (a bounded wait gave up)"}
 
 
 def check(rc, what):

@@ -72,6 +72,20 @@ def _prefix(v: list[int]) -> list[int]:
     return out
 
 
+class ExchangeError(RuntimeError):
+    """The exchanged per-destination counts are inconsistent: this rank stops before posting any transfer sized by
+    them (its peers' next collective then fails with the process group's timeout instead of hanging)."""
+
+
+def _check_counts(counts, k, direction):
+    """counts[part][rank] = (rows, entries): every sent row carries 1..k entries of its token."""
+    for i, part in enumerate(counts):
+        for d, (rows, ent) in enumerate(part):
+            if rows < 0 or ent < rows or ent > rows * k:
+                raise ExchangeError(f"part {i}: counts {direction} rank {d} are inconsistent: {rows} rows, "
+                                    f"{ent} entries (k = {k})")
+
+
 def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bool = False,
                micro_batches: int = 1, partials_bf16: bool = False, phases: list | None = None):
     """One expert-parallel MoE layer over this rank's tokens x [T, H] -> y bf16 [T, H].
@@ -128,6 +142,8 @@ def _ep_forward(ops, x, k, G, group, exact, m, bf16, phases=None):
     half = G * m * 2
     sc = [[both[(d * m + i) * 2:(d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
     rc = [[both[half + (d * m + i) * 2:half + (d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
+    _check_counts(rc, k, "received from")
+    _check_counts(sc, k, "sent to")
     mark("counts_exchange_and_host_read")
     if phases is not None:
         phases.append(("rows", sum(c[0] for r in rc for c in r), sum(c[1] for r in rc for c in r)))

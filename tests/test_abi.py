@@ -66,3 +66,25 @@ def test_no_cpu_fallback():
         pytest.skip("library not built")
     with pytest.raises(ValueError, match="CUDA"):
         topk_stable(torch.zeros(2, 8), 3)
+
+
+def test_wait_seq_is_host_side_and_bounded():
+    """ssb_wait_seq is host code (acquire loads on a pinned word): it returns when the word reaches the target and
+    gives up with SSB_ETIMEDOUT after its bound, with no GPU involved."""
+    import torch
+    from slotstream_b200 import _lib
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("library not built")
+    seq = torch.tensor([41], dtype=torch.int64)
+    L = _lib.lib()
+    assert L.ssb_wait_seq(seq.data_ptr(), 41, 10_000_000) == _lib.SSB_OK
+    assert L.ssb_wait_seq(seq.data_ptr(), 42, 5_000_000) == _lib.SSB_ETIMEDOUT
+    assert L.ssb_wait_seq(None, 1, 1) == _lib.SSB_EINVAL
+
+
+def test_signal_argument_errors_need_no_gpu():
+    import torch
+    from slotstream_b200.kernels.signal import SLOT, signal
+    with pytest.raises(ValueError):
+        signal(torch.zeros(SLOT + 1, dtype=torch.int32), torch.zeros(SLOT + 1), torch.zeros(64, dtype=torch.int32),
+               torch.zeros(64), torch.zeros(1, dtype=torch.int64), torch.zeros(2, dtype=torch.int64), 0)

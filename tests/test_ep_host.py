@@ -123,3 +123,49 @@ def test_ep_exchange_with_uneven_and_empty_ranks(tmp_path, exact):
             assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
         else:
             np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+
+
+class _CorruptOps(CpuOps):
+    """Rank 0's plan claims more entries for rank 1 than its rows can carry."""
+
+    def plan(self, ids, w):
+        p = super().plan(ids, w)
+        if self.rank == 0:
+            p.dest_count[1, 1] = p.dest_count[1, 0] * self.k + 5
+        return p
+
+
+def _corrupt_main(rank, world, port, out_dir):
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
+    outcome = "returned"
+    try:
+        from slotstream_b200.ep import ExchangeError, ep_forward
+        recs, shared, rw, sg = _world(5)
+        ops = _CorruptOps(LAY, recs, shared, rw, sg, K, E, world, rank, strided=True)
+        try:
+            ep_forward(ops, bits_to_bf16(_tokens(rank)), K, world)
+        except ExchangeError:
+            outcome = "inconsistent counts"
+        except RuntimeError:
+            outcome = "collective failed"
+    finally:
+        with open(os.path.join(out_dir, f"outcome{rank}"), "w") as f:
+            f.write(outcome)
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_corrupt_counts_end_every_rank_with_an_error(tmp_path):
+    """One rank sends a count vector that cannot be right: the rank receiving it raises before posting the dispatch,
+    and the sender's next collective ends with the process group's timeout -- every rank stops with an error, none
+    hangs and none computes on the bad sizes."""
+    world = 2
+    mp.start_processes(_corrupt_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    outcomes = [(tmp_path / f"outcome{r}").read_text() for r in range(world)]
+    assert outcomes[1] == "inconsistent counts"
+    assert outcomes[0] in ("inconsistent counts", "collective failed")
