@@ -1,6 +1,6 @@
 """Benchmark of the B200 MoE hot path; prints ONE JSON line (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload prefill|decode|slotpool] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload prefill|decode|slotpool|sweep] [--impl reference]
 
 Workloads (synthetic data with the distributions BASELINE.json names):
 * ``decode``  (configs[1]): one decode step = 48 stacked config[0] MoE layers at batch b (default 1), Zipf(1.1)
@@ -8,6 +8,8 @@ Workloads (synthetic data with the distributions BASELINE
   its own resident N(0,1) hidden state (the attention / hyper-connection segments between MoE layers, which
   renormalise the residual stream in the real model, are not part of this path).
 * ``prefill`` (configs[2]/[3]): one step = one config[0] layer over a chunk of tokens per GPU.
+* ``sweep``   (configs[2] with a partly resident layer): the prefill layer when only the hottest half of its
+  records sit in HBM; the rest are staged per 32-expert group from pinned host memory beside the compute.
 * ``slotpool``: one step = one fresh token through 48 layers whose routed experts stream through an
   HBM slot pool of 1 GiB chunks holding 70% of the records (misses copied from pinned host memory on a side
   stream); metric = MoE-path ms per token. The default run reports it as the ``slotpool`` sub-measurement.
@@ -661,6 +663,124 @@ def bench_prefill(args, world, rank, cpu_passes=None):
     return res
 
 
+# ------------------------------------------------------------------ prefill sweep with a partly resident layer
+def bench_sweep(args, world, rank):
+    """The prefill layer when only part of its 512 records sit in HBM (the prefill MoE sweep): the resident share is
+    the hottest experts of the chunk's routing (what a pool filled from the routing frequencies holds), the other
+    records are staged per 32-expert group from pinned host memory on a copy stream while earlier groups compute.
+    The bound is the slower of the all-resident layer and the staged bytes over the measured pinned H2D bandwidth."""
+    from slotstream_b200 import _lib, synth
+    from slotstream_b200.kernels.moe_layer import PrefillLayerBuffers, moe_layer_prefill
+    from slotstream_b200.records import BASELINE_LAYOUT as LAY
+    from slotstream_b200.sweep import PrefillSweep
+    E, K, T = 512, 10, args.tokens
+    dev = torch.device("cuda")
+    rb = LAY.record_bytes
+    seed = 2000 + rank
+    recs = torch.empty((E + 1, rb), dtype=torch.uint8, device=dev)
+    synth.fill_records_device(LAY, recs, seed)
+    host = recs.cpu().pin_memory()
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    router_w = (torch.randn(E, LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    sh_gate_w = (torch.randn(LAY.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.from_numpy(synth.zipf_bias(E)).to(dev) if args.routing == "zipf" else None
+    x = torch.randn(T, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
+    group_ptr = recs.data_ptr() + torch.arange(E + 1, dtype=torch.int64, device=dev) * rb
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    # the all-resident layer: the result the sweep must equal bit for bit, and the compute-side bound (eager, as the
+    # sweep runs)
+    full = PrefillLayerBuffers(T, K, LAY.hidden, LAY.inter, E, dev)
+
+    def resident_step():
+        moe_layer_prefill(x, router_w, group_ptr, sh_gate_w, K, full, bias=bias)
+
+    for _ in range(args.warmup):
+        resident_step()
+    torch.cuda.synchronize()
+    full_ms = max_over_ranks(sum(timed_steps(resident_step, args.steps, flush, world)) / args.steps, world)
+    counts = torch.bincount(full.ids.reshape(-1).long(), minlength=E).cpu().numpy()
+    n_res = int(round(args.resident_fraction * E))
+    hottest = np.lexsort((np.arange(E), -counts))[:n_res]
+    res_ptr = {int(e): recs.data_ptr() + int(e) * rb for e in hottest}
+    shared_ptr = recs.data_ptr() + E * rb
+    host_base = host.data_ptr()
+    sw = PrefillSweep(LAY.hidden, LAY.inter, K, T, rb)
+
+    def step():
+        sw.layer(x, router_w, sh_gate_w, shared_ptr, res_ptr, lambda e: host_base + e * rb, bias=bias)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    bit_equal = bool(torch.equal(sw.bufs.y.view(torch.int16), full.y.view(torch.int16)))
+    ids_equal = bool(torch.equal(sw.bufs.ids, full.ids))
+    s0 = sw.stats.as_dict()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    times = timed_steps(step, args.steps, flush, world, clocks)
+    clocks.stop()
+    ms = max_over_ranks(sum(times) / len(times), world)
+    s1 = sw.stats.as_dict()
+    per = {key: (s1[key] - s0[key]) / args.steps for key in s1}
+    staged_bytes = per["bytes_staged"]
+    groups = len(sw.last_plan.groups) + 1
+
+    # the staging link's own bandwidth: one pinned 1 GiB host-to-device copy on this box, timed with events
+    probe_h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    probe_d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    probe_d.copy_(probe_h, non_blocking=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    probe_d.copy_(probe_h, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    h2d_gbs = (1 << 30) / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    del probe_h, probe_d
+    achieved = staged_bytes / (ms * 1e-3) / 1e9
+    bound_ms = max(full_ms, staged_bytes / (h2d_gbs * 1e9) * 1e3)
+
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T, LAY.hidden), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(sw.bufs.y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = max_over_ranks(sum(timed_steps(e2e_step, args.steps, flush, world)) / args.steps, world)
+    return {
+        "metric": METRIC, "value": round(world * T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"prefill_sweep_{T}tok_resident{n_res}of{E}", "tokens_per_gpu": T,
+                   "resident_records": n_res, "staged_per_step": per["records_staged"],
+                   "resident_choice": "the hottest experts of the chunk's routing", "routing": args.routing,
+                   "group_size": sw.group_size, "staging_groups": sw.staging_groups, "inflight": sw.inflight,
+                   "l2": "flushed before every step (256 MiB write); inputs > L2", "cuda_graph": False},
+        "all_resident_ms": round(full_ms, 4),
+        "bound_ms": round(bound_ms, 4),
+        "roofline": {"bound": "h2d" if bound_ms > full_ms else "tensor",
+                     "kernel": "staging copies (pinned host -> HBM) overlapped with the grouped GEMMs",
+                     "achieved": round(achieved, 1), "peak": round(h2d_gbs, 1), "unit": "GB/s",
+                     "frac": round(achieved / h2d_gbs, 4),
+                     "peak_source": "measured in this run: one pinned 1 GiB host-to-device copy",
+                     "staged_bytes_per_step": int(staged_bytes), "frac_of_bound": round(bound_ms / ms, 4),
+                     "traffic": None},
+        "parity": {"bit_equal_to_all_resident": bit_equal, "ids_equal": ids_equal},
+        "stats_per_step": per,
+        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x.numel() * 2 + staged_bytes), "d2h_bytes_per_step": int(y_host.numel() * 2),
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": (3 + 5 * groups + 1) * args.steps,
+        "clocks": clocks.summary(),
+        "device_errors": int(sw.bufs.err.item()) + int(full.err.item()),
+    }
+
+
 # ------------------------------------------------------------------ expert-parallel prefill (configs[3], N > 1)
 def pipelined_eager(x_dev, run, x_host, k, world):
     """ms per step of k eager steps over two buffer sets, as ``pipelined_steps`` but with ``run(b) -> y`` (a layer
@@ -848,10 +968,13 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=["prefill", "decode", "slotpool"], default="prefill")
+    ap.add_argument("--workload", choices=["prefill", "decode", "slotpool", "sweep"], default="prefill")
     ap.add_argument("--pool-fraction", type=float, default=0.7,
                     help="slotpool: share of the layers x 512 records the HBM pool holds")
     ap.add_argument("--no-slotpool", action="store_true", help="skip the slot-pool sub-measurement at N=1")
+    ap.add_argument("--resident-fraction", type=float, default=0.5,
+                    help="sweep: share of the layer's 512 records resident in HBM (the rest staged from host)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the partly resident sweep sub-measurement at N=1")
     ap.add_argument("--tokens", type=int, default=32768, help="prefill tokens per GPU")
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
     ap.add_argument("--batch", type=int, default=1, help="decode batch")
@@ -884,6 +1007,8 @@ def main():
         res = bench_decode(args, world, rank, cpu_seconds=args.cpu_seconds if cpu else None)
     elif args.workload == "slotpool":
         res = bench_slotpool(args, world, rank)
+    elif args.workload == "sweep":
+        res = bench_sweep(args, world, rank)
     elif world > 1 and not args.replicas:
         res = bench_prefill_ep(args, world, rank)
     else:
@@ -923,6 +1048,11 @@ def main():
             res["slotpool"] = {k: s[k] for k in ("metric", "value", "unit", "tokens_per_s", "ms_per_step", "config",
                                                  "miss_fraction", "misses_per_layer", "h2d_bytes_per_step",
                                                  "roofline", "e2e", "gpu_launches", "clocks", "device_errors")}
+            torch.cuda.empty_cache()
+        if world == 1 and not args.no_sweep:
+            s = bench_sweep(args, world, rank)
+            res["sweep"] = {k: s[k] for k in ("value", "unit", "ms_per_step", "config", "all_resident_ms", "bound_ms",
+                                              "roofline", "parity", "e2e", "gpu_launches", "clocks", "device_errors")}
             torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps(res), flush=True)

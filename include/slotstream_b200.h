@@ -245,6 +245,12 @@ int ssb_pool_decode_layer(ssb_pool* pool, int32_t layer, const uint16_t* x, int6
                           int32_t* ids_host, float* h_buf, float* o_buf, float* out, uint16_t* y, int32_t* err,
                           void* copy_stream, void* compute_stream, int64_t* stats);
 
+/* Host-side helper: one asynchronous copy of `bytes` bytes (cudaMemcpyAsync, direction from the addresses) on
+ * `stream`, for callers that hold raw record addresses -- the prefill sweep stages non-resident records from pinned
+ * host memory with it. Replaces: the staging reads of slotio's Sweep (slotstream_spark/model/moe_sweep.py:113-121)
+ * for records already in pinned host memory. */
+int ssb_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* Router logits + select (as ssb_router_logits then ssb_router_select) with the logits held in a fixed
  * device array that comes with the library's device code, so the call needs no workspace and allocates nothing:
  * for callers that cannot allocate on their call path (a host binding without a caching allocator, which would

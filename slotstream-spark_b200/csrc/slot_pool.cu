@@ -302,3 +302,14 @@ extern "C" int ssb_pool_decode_layer(ssb_pool* p, int32_t layer, const uint16_t*
   if (rc) return rc;
   return ssb_pool_release(p, compute_stream);
 }
+
+extern "C" int ssb_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (!dst || !src || bytes < 0) return SSB_EINVAL;
+  if (bytes == 0) return SSB_OK;
+  const cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return (int)e;
+  }
+  return SSB_OK;
+}

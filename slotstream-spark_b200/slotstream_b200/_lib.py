@@ -54,6 +54,7 @@ SIGNATURES = {
     "ssb_pool_ensure": [_P, _I32, _P, _I32, _P, _P, _P, _P, _P],
     "ssb_pool_release": [_P, _P],
     "ssb_pool_counters": [_P, _P, _P, _P],
+    "ssb_copy_async": [_P, _P, _I64, _P],
     "ssb_pool_decode_layer": [_P, _I32, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                               _P, _P, _P, _P, _P, _P, _P, _P],
     "ssb_router_topk_static": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P],

@@ -68,6 +68,23 @@ class PrefillLayerBuffers:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
 
 
+def _route_into(x, w_router, sh_gate_w, k: int, bufs: PrefillLayerBuffers, *, bias=None,
+                logits_round_bf16: bool = False):
+    """Router of a prefill chunk into the buffers: tcgen05 logits GEMM, the shared-gate logit, then the select writes
+    ids / weights / shared gate straight into row_expert / row_weight."""
+    t, h = x.shape
+    e = bufs.experts
+    L = _lib.lib()
+    st = _lib.stream()
+    lg = bufs.logits
+    _lib.check(L.ssb_gemm_dense(_lib.ptr(x), t, h, _lib.ptr(w_router), e, _lib.ptr(lg), bufs.ld, st), "router gemm")
+    _lib.check(L.ssb_router_logits(_lib.ptr(x), _lib.ptr(sh_gate_w), None, t, h, 1, bufs.ld, lg.data_ptr() + 4 * e, st),
+               "shared gate logits")
+    flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0)
+    _lib.check(L.ssb_router_select(_lib.ptr(lg), bufs.ld, t, e, k, _lib.ptr(bias), flags, _lib.ptr(bufs.ids),
+                                   _lib.ptr(bufs.w), None, _lib.ptr(bufs.sh_gate), st), "router select")
+
+
 def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLayerBuffers, *, bias=None,
                       logits_round_bf16: bool = False):
     """x bf16 [T, H] -> bufs.y bf16 [T, H]: one MoE layer over a prefill chunk, every expert resident.
@@ -88,13 +105,7 @@ def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLa
         raise ValueError("x must be a contiguous bf16 [T, H] tensor")
     L = _lib.lib()
     st = _lib.stream()
-    lg = bufs.logits
-    _lib.check(L.ssb_gemm_dense(_lib.ptr(x), t, h, _lib.ptr(w_router), e, _lib.ptr(lg), bufs.ld, st), "router gemm")
-    _lib.check(L.ssb_router_logits(_lib.ptr(x), _lib.ptr(sh_gate_w), None, t, h, 1, bufs.ld, lg.data_ptr() + 4 * e, st),
-               "shared gate logits")
-    flags = _lib.ROUTER_SHARED_GATE | (_lib.ROUTER_ROUND_BF16 if logits_round_bf16 else 0)
-    _lib.check(L.ssb_router_select(_lib.ptr(lg), bufs.ld, t, e, k, _lib.ptr(bias), flags, _lib.ptr(bufs.ids),
-                                   _lib.ptr(bufs.w), None, _lib.ptr(bufs.sh_gate), st), "router select")
+    _route_into(x, w_router, sh_gate_w, k, bufs, bias=bias, logits_round_bf16=logits_round_bf16)
     aligned = moe_align(bufs.row_expert, e + 1, BLOCK_M, out=(bufs.sorted_rows, bufs.block_expert, bufs.num_padded))
     _lib.check(L.ssb_prefill_experts(
         _lib.ptr(x), t, h, bufs.inter, _lib.ptr(bufs.row_token), _lib.ptr(bufs.row_weight), bufs.rows,

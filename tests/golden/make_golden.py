@@ -18,6 +18,8 @@ What each fixture pins (reference file:line of the code that produced the expect
                          reference's own 2560/640 shape (that helper hard-codes 2560 columns).
 * ``fused_ref.npz``   -- the fp64 exact and bf16-path references of tests/gates/test_fused_moe_affine.py:68-100
                          at 2560/640, with the nibble-swap control.
+* ``sweep_plan.npz``  -- engine/sweep.py:34-58 (``plan_sweep``): row order and groups for empty, all-resident,
+                         none-resident, mixed and Zipf-skewed rows at group sizes 1, 7 and 32.
 
 Inputs come from ``slotstream_b200.synth`` (numpy PCG64, seeded), so tests regenerate them bit for bit; each
 fixture stores a SHA-256 of its inputs to catch generator drift.
@@ -220,9 +222,27 @@ def make_fused_ref(ref):
                         inputs_sha=sha(*recs))
 
 
+def make_sweep_plan(ref):
+    plan = ref["sweep"].plan_sweep
+    rng = np.random.default_rng(SEED + 77)
+    cases = [(0, 0.5, 32), (40, 1.0, 32), (40, 0.0, 32), (1000, 0.3, 7), (1000, 0.7, 1), (20480, 0.4, 32)]
+    out = {"n_cases": len(cases)}
+    for c, (r, frac, gs) in enumerate(cases):
+        ids = rng.integers(0, 512, r).astype(np.int32) if c != 5 else (rng.zipf(1.1, r) % 512).astype(np.int32)
+        res = rng.random(512) < frac
+        p = plan(ids, res, gs)
+        out[f"ids_{c}"], out[f"res_{c}"], out[f"gs_{c}"], out[f"order_{c}"] = ids, res, gs, p.order
+        out[f"groups_{c}"] = np.array([[g.row_lo, g.row_hi, int(g.resident), g.experts.size] for g in p.groups],
+                                      dtype=np.int64).reshape(-1, 4)
+        out[f"experts_{c}"] = (np.concatenate([g.experts for g in p.groups]) if p.groups
+                               else np.zeros(0, np.int32))
+    np.savez_compressed(HERE / "sweep_plan.npz", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of a slotstream-spark checkout")
+    ap.add_argument("--only", default=None, help="comma-separated fixture makers to run (e.g. make_sweep_plan)")
     a = ap.parse_args()
     refp = Path(a.reference).resolve()
     sys.path.insert(0, str(refp))
@@ -231,13 +251,19 @@ def main():
     from slotstream_spark.kernels import affine_ref, moe_align  # noqa: E402
     from slotstream_spark.kernels import fused_moe_affine as fm  # noqa: E402
     from slotstream_spark.model import reference_torch  # noqa: E402
+    from slotstream_spark.engine import sweep  # noqa: E402
     import test_topk_stable  # noqa: E402
     import test_moe_gemv_affine  # noqa: E402
     import test_fused_moe_affine  # noqa: E402
     ref = dict(affine_ref=affine_ref, moe_align=moe_align, fm=fm, reference_torch=reference_torch,
-               test_topk=test_topk_stable, test_moe=test_moe_gemv_affine, test_fused=test_fused_moe_affine)
+               test_topk=test_topk_stable, test_moe=test_moe_gemv_affine, test_fused=test_fused_moe_affine, sweep=sweep)
     torch.set_num_threads(8)
-    for f in (make_affine, make_topk, make_align, make_combine, make_moe_ref, make_decode_ref, make_fused_ref):
+    makers = (make_affine, make_topk, make_align, make_combine, make_moe_ref, make_decode_ref, make_fused_ref,
+              make_sweep_plan)
+    only = None if a.only is None else set(a.only.split(","))
+    for f in makers:
+        if only is not None and f.__name__ not in only:
+            continue
         f(ref)
         print("wrote", f.__name__)
 

@@ -88,3 +88,16 @@ def test_signal_argument_errors_need_no_gpu():
     with pytest.raises(ValueError):
         signal(torch.zeros(SLOT + 1, dtype=torch.int32), torch.zeros(SLOT + 1), torch.zeros(64, dtype=torch.int32),
                torch.zeros(64), torch.zeros(1, dtype=torch.int64), torch.zeros(2, dtype=torch.int64), 0)
+
+
+def test_copy_async_argument_errors_need_no_gpu():
+    """ssb_copy_async checks its arguments on the host before any CUDA call; a zero-byte copy is a no-op."""
+    import ctypes
+    from slotstream_b200 import _lib
+    L = _lib.lib()
+    buf = ctypes.create_string_buffer(16)
+    addr = ctypes.addressof(buf)
+    assert L.ssb_copy_async(None, addr, 16, None) == _lib.SSB_EINVAL
+    assert L.ssb_copy_async(addr, None, 16, None) == _lib.SSB_EINVAL
+    assert L.ssb_copy_async(addr, addr, -1, None) == _lib.SSB_EINVAL
+    assert L.ssb_copy_async(addr, addr, 0, None) == _lib.SSB_OK

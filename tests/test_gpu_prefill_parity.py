@@ -85,7 +85,10 @@ def _check(L, x_bits, y_bits, ids_k, w_k, routed_k, sh_k, label):
     assert float(np.max(d_sh)) <= 2.0 ** -6 * float(np.max(np.abs(ref_sh))), f"{label}: shared expert"
     # the bf16 output: the routed difference carried through routed.to(bf16) (plus one ulp where its rounding goes
     # the other way), the shared expert's difference, and one ulp of the final bf16 add
-    bound = np.abs(routed_k.astype(np.float64) - ref_routed) + O.bf16_ulp(ref_routed) + d_sh + O.bf16_ulp(ref_y)
+    # (an ulp is taken at the larger of the two values: across a power of two the kernel's side has twice the spacing)
+    rk = routed_k.astype(np.float64)
+    bound = (np.abs(rk - ref_routed) + O.bf16_ulp(np.maximum(np.abs(rk), np.abs(ref_routed))) + d_sh +
+             O.bf16_ulp(np.maximum(np.abs(got), np.abs(ref_y))))
     flips = np.abs(got - ref_y)
     assert np.all(flips <= bound), f"{label}: output differs beyond rounding flips ({float(np.max(flips - bound)):.3e})"
     lit = float(np.max(np.abs(got - exact)))
