@@ -18,6 +18,10 @@ What each fixture pins (reference file:line of the code that produced the expect
                          reference's own 2560/640 shape (that helper hard-codes 2560 columns).
 * ``fused_ref.npz``   -- the fp64 exact and bf16-path references of tests/gates/test_fused_moe_affine.py:68-100
                          at 2560/640, with the nibble-swap control.
+* ``experts_bin/``    -- tools/repack_experts.py run unmodified on the reference's own synthetic MLX checkpoint
+                         (tests/t0/synth_ckpt.py:43-92; 2 layers, 16 experts, hidden 64, ff 64): the packed
+                         experts.bin and its manifest, plus pieces.json = SHA-256 of every source tensor slice
+                         (layer, expert, piece) the repacker read.
 * ``sweep_plan.npz``  -- engine/sweep.py:34-58 (``plan_sweep``): row order and groups for empty, all-resident,
                          none-resident, mixed and Zipf-skewed rows at group sizes 1, 7 and 32.
 
@@ -26,6 +30,7 @@ fixture stores a SHA-256 of its inputs to catch generator drift.
 """
 import argparse
 import hashlib
+import json
 import sys
 from pathlib import Path
 
@@ -239,6 +244,30 @@ def make_sweep_plan(ref):
     np.savez_compressed(HERE / "sweep_plan.npz", **out)
 
 
+def make_experts_bin(ref):
+    import shutil
+    import subprocess
+    import tempfile
+    refp = ref["path"]
+    sys.path.insert(0, str(refp / "tests" / "t0"))
+    from synth_ckpt import write_synth_checkpoint  # noqa: E402
+    dst = HERE / "experts_bin"
+    dst.mkdir(exist_ok=True)
+    with tempfile.TemporaryDirectory() as td:
+        model, out = Path(td) / "model", Path(td) / "out"
+        exp = write_synth_checkpoint(model, layers=2, experts=16, hidden=64, ff=64)
+        subprocess.run([sys.executable, str(refp / "tools" / "repack_experts.py"), "--model", str(model), "--out",
+                        str(out), "--allow-buffered", "--expect-record", "0", "--max-mbps", "0"], check=True,
+                       capture_output=True)
+        shutil.copy(out / "experts.bin", dst / "experts.bin")
+        shutil.copy(out / "experts.manifest.json", dst / "experts.manifest.json")
+    names = [f"{p}.{k}" for p in ("gate_proj", "up_proj", "down_proj") for k in ("weight", "scales", "biases")]
+    t = exp["tensors"]
+    pieces = [[[hashlib.sha256(np.ascontiguousarray(t[f"language_model.model.layers.{L}.mlp.switch_mlp.{n}"][e])
+                               .tobytes()).hexdigest() for n in names] for e in range(16)] for L in range(2)]
+    (dst / "pieces.json").write_text(json.dumps({"hidden": 64, "inter": 64, "gs": 64, "sha256": pieces}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of a slotstream-spark checkout")
@@ -256,10 +285,10 @@ def main():
     import test_moe_gemv_affine  # noqa: E402
     import test_fused_moe_affine  # noqa: E402
     ref = dict(affine_ref=affine_ref, moe_align=moe_align, fm=fm, reference_torch=reference_torch,
-               test_topk=test_topk_stable, test_moe=test_moe_gemv_affine, test_fused=test_fused_moe_affine, sweep=sweep)
+               test_topk=test_topk_stable, test_moe=test_moe_gemv_affine, test_fused=test_fused_moe_affine, sweep=sweep, path=refp)
     torch.set_num_threads(8)
     makers = (make_affine, make_topk, make_align, make_combine, make_moe_ref, make_decode_ref, make_fused_ref,
-              make_sweep_plan)
+              make_sweep_plan, make_experts_bin)
     only = None if a.only is None else set(a.only.split(","))
     for f in makers:
         if only is not None and f.__name__ not in only:
