@@ -12,9 +12,10 @@
 // major, so concurrent CTAs share activation rows and expert weights in L2). TMEM holds two accumulator pairs,
 // so the epilogue of tile i overlaps the MMAs of tile i+1, and the operand pipelines run across tile borders.
 // Warp roles (16 warps):
-//  * warp 0      loads the tile's activation rows with TMA: one 2-D box of 256 rows when the rows are
-//                contiguous (permuted into expert order beforehand), else lane l gathers rows 4l..4l+3 and
-//                128+4l.. with two tile::gather4 copies; the tensor map applies the 128-byte swizzle;
+//  * warp 0      loads the tile's activation rows with TMA: one 2-D box of 128 rows per half when the rows
+//                are contiguous (permuted into expert order beforehand), else lane l gathers rows 4l..4l+3 and
+//                128+4l.. with two tile::gather4 copies; the tensor map applies the 128-byte swizzle. A second
+//                half that holds only padding rows is skipped by every role (not loaded, multiplied or stored);
 //  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma (M128 N128 K16, eight per 64-wide k-block);
 //  * warps 4..7  epilogue: TMEM -> registers -> global, one accumulator row per thread;
 //  * warps 8..15 weight producers, two threads per B-row (one half of the k-block each): stage the packed
@@ -194,6 +195,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
     const uint8_t* b = a.group_base ? (const uint8_t*)__ldg(a.group_base + e) : a.base0;
     return ((uintptr_t)b & 15) ? nullptr : b;
   };
+  // does the second 128-row half of 256-row block mb hold any row? moe_align puts an expert's rows first and its
+  // padding after them, so the half is all padding when its first row is (identity rows: when it is past R); such a
+  // half is neither loaded (box path), multiplied nor stored
+  auto half1_of = [&](int64_t mb) -> bool {
+    const int64_t m1 = mb * TM + BM;
+    if (!a.sorted_rows) return m1 < a.R;
+    const int32_t r = __ldcg(a.sorted_rows + m1);
+    return r >= 0 && r < a.R;
+  };
 
   if (tid == 0) {
     s_fail = 0;
@@ -238,6 +248,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
     int64_t issued = 0;
     if (lane == 0) prefetch_tensormap(&tm_a);
     const bool gather = a.a_box_rows != TM;
+    int64_t h_tile = -1;
+    bool two = true, two_next = true;   // box path: the second half of this tile (of the next) is loaded
     if (gather) {
       load_rows(0);
       to_coords();
@@ -264,11 +276,19 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
         s_fail = 1;
         break;
       }
-      if (lane == 0) mbar_expect_tx(&S.full_a[s], A_STAGE);
+      if (!gather && i != h_tile && lane == 0) {   // the next tile's answer is fetched a tile ahead
+        h_tile = i;
+        two = i == 0 ? half1_of(tile_of(0) / NB) : two_next;
+        if (i + 1 < my_tiles) two_next = half1_of(tile_of(i + 1) / NB);
+      }
+      if (lane == 0) mbar_expect_tx(&S.full_a[s], gather || two ? A_STAGE : A_HALF);
       __syncwarp();
-      if (!gather) {   // rows tile*256 .. +255 of the activation matrix in one copy
-        if (lane == 0)
-          tma_load_2d(smem_u32(S.a + s * A_STAGE), &tm_a, kb * BK, (int32_t)((tile_of(i) / NB) * TM), &S.full_a[s]);
+      if (!gather) {   // rows tile*256 .. +255 (or +127) of the activation matrix, one 128-row box per half
+        if (lane == 0) {
+          const int32_t r0 = (int32_t)((tile_of(i) / NB) * TM);
+          tma_load_2d(smem_u32(S.a + s * A_STAGE), &tm_a, kb * BK, r0, &S.full_a[s]);
+          if (two) tma_load_2d(smem_u32(S.a + s * A_STAGE + A_HALF), &tm_a, kb * BK, r0 + BM, &S.full_a[s]);
+        }
       } else {
         tma_gather4(smem_u32(S.a + s * A_STAGE + lane * 512), &tm_a, kb * BK, rc[0], rc[1], rc[2], rc[3],
                     &S.full_a[s]);
@@ -287,7 +307,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(BM, BN);
       int64_t j = 0;
+      int nh_next = half1_of(tile_of(0) / NB) ? MT : 1;
       for (int i = 0; i < my_tiles && !s_fail; ++i) {
+        const int nh = nh_next;   // halves of this tile; the next tile's count is fetched a tile ahead
+        if (i + 1 < my_tiles) nh_next = half1_of(tile_of(i + 1) / NB) ? MT : 1;
         const int acc = i & 1;
         if (!mbar_wait_ns(&S.tmem_empty[acc], ((i >> 1) & 1) ^ 1, SSB_WAIT_NS)) {
           s_fail = 1;
@@ -307,6 +330,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
           const uint64_t db = umma_desc_sw128(smem_u32(S.b + s * B_STAGE));
 #pragma unroll
           for (int h = 0; h < MT; ++h) {
+            if (h >= nh) break;
             const uint64_t da = umma_desc_sw128(smem_u32(S.a + s * A_STAGE + h * A_HALF));
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
@@ -330,6 +354,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       const int64_t t = tile_of(i), mb = t / NB;
       const int nb = (int)(t % NB);
       const bool shared_e = a.shared_local >= 0 && expert_of(mb) == a.shared_local;
+      const int nh = half1_of(mb) ? MT : 1;
       int64_t rows[MT];
       float wts[MT];
 #pragma unroll
@@ -346,7 +371,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
         break;
       }
 #pragma unroll 1
-      for (int h = 0; h < MT; ++h) {
+      for (int h = 0; h < nh; ++h) {
         const int64_t m = mb * TM + h * BM + 32 * q + lane;
         const int64_t row = rows[h];
         const bool valid = row >= 0 && row < a.R;
@@ -754,7 +779,8 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// 2-D tensor map over the activation rows: K elements x a_rows rows, box 64 x 1, 128-byte swizzle.
+// 2-D tensor map over the activation rows: K elements x a_rows rows, box 64 x 1 (gathered rows) or 64 x 128 (one
+// half of a 256-row block), 128-byte swizzle.
 int encode_a_map(CUtensorMap* map, const GemmArgs& a) {
   if (((uintptr_t)a.a & 15) || (a.lda * 2) % 16 || a.a_rows < 1 || a.a_rows > 0x7fffffffLL) return SSB_EINVAL;
   if (a.a_box_rows != 1 && a.a_box_rows != TM) return SSB_EINVAL;
@@ -762,7 +788,7 @@ int encode_a_map(CUtensorMap* map, const GemmArgs& a) {
   if (!encode) return SSB_ENODEVICE;
   cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.a_rows};
   cuuint64_t strides[1] = {(cuuint64_t)a.lda * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)a.a_box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)(a.a_box_rows == TM ? BM : 1)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)a.a, dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -88,3 +88,31 @@ def test_sweep_repeats_and_reuses_its_buffers(layer):
                      bias=layer["bias"])
         torch.cuda.synchronize()
         assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+
+
+def test_sweep_reads_resident_records_from_a_slot_pool(layer):
+    """Resident records where a SlotPool put them (resident_from_pool), the rest staged: still bit-equal."""
+    from slotstream_b200.slot_pool import SlotPool, host_table
+    from slotstream_b200.sweep import resident_from_pool
+    lay = layer["lay"]
+    rb = lay.record_bytes
+    pool = SlotPool(rb, 1, max_slots=200)
+    try:
+        table = host_table(layer["host"].data_ptr(), rb, 1, E)
+        want = np.sort(np.random.default_rng(9).choice(E, 150, replace=False)).astype(np.int32)
+        pool.ensure(0, want, table)
+        torch.cuda.synchronize()
+        res_ptr = resident_from_pool(pool, 0)
+        assert sorted(res_ptr) == want.tolist()
+        x = bf16_tensor(synth.activations(903, 1024, lay.hidden))
+        y_ref, _ = _resident_layer(layer, x)
+        sw = PrefillSweep(lay.hidden, lay.inter, K, 1024, rb)
+        host_base, dev_base = layer["host"].data_ptr(), layer["dev"].data_ptr()
+        y = sw.layer(x, layer["rw"], layer["sg"], dev_base + E * rb, res_ptr, lambda e: host_base + e * rb,
+                     bias=layer["bias"])
+        pool.release()
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+        assert sw.stats.resident_rows > 0 and sw.stats.staged_rows > 0
+    finally:
+        pool.close()
