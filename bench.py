@@ -701,7 +701,8 @@ def bench_sweep(args, world, rank):
     torch.cuda.synchronize()
     full_ms = max_over_ranks(sum(timed_steps(resident_step, args.steps, flush, world)) / args.steps, world)
     counts = torch.bincount(full.ids.reshape(-1).long(), minlength=E).cpu().numpy()
-    n_res = int(round(args.resident_fraction * E))
+    n_used = int((counts > 0).sum())               # experts the chunk routes to (Zipf routing leaves many idle)
+    n_res = int(round(args.resident_fraction * n_used))
     hottest = np.lexsort((np.arange(E), -counts))[:n_res]
     res_ptr = {int(e): recs.data_ptr() + int(e) * rb for e in hottest}
     shared_ptr = recs.data_ptr() + E * rb
@@ -756,8 +757,8 @@ def bench_sweep(args, world, rank):
         "metric": METRIC, "value": round(world * T / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"prefill_sweep_{T}tok_resident{n_res}of{E}", "tokens_per_gpu": T,
-                   "resident_records": n_res, "staged_per_step": per["records_staged"],
+        "config": {"workload": f"prefill_sweep_{T}tok_resident{n_res}of{n_used}used", "tokens_per_gpu": T,
+                   "resident_records": n_res, "experts_with_rows": n_used, "staged_per_step": per["records_staged"],
                    "resident_choice": "the hottest experts of the chunk's routing", "routing": args.routing,
                    "group_size": sw.group_size, "staging_groups": sw.staging_groups, "inflight": sw.inflight,
                    "l2": "flushed before every step (256 MiB write); inputs > L2", "cuda_graph": False},
@@ -775,7 +776,7 @@ def bench_sweep(args, world, rank):
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x.numel() * 2 + staged_bytes), "d2h_bytes_per_step": int(y_host.numel() * 2),
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": (3 + 5 * groups + 1) * args.steps,
+        "gpu_launches": (3 + 1 + 1 + 2 * groups + 1) * args.steps,   # route, align, permute, 2 per group, combine
         "clocks": clocks.summary(),
         "device_errors": int(sw.bufs.err.item()) + int(full.err.item()),
     }
@@ -973,7 +974,8 @@ def main():
                     help="slotpool: share of the layers x 512 records the HBM pool holds")
     ap.add_argument("--no-slotpool", action="store_true", help="skip the slot-pool sub-measurement at N=1")
     ap.add_argument("--resident-fraction", type=float, default=0.5,
-                    help="sweep: share of the layer's 512 records resident in HBM (the rest staged from host)")
+                    help="sweep: share of the experts the chunk routes to whose records are resident in HBM (the "
+                         "hottest; the rest are staged from pinned host memory)")
     ap.add_argument("--no-sweep", action="store_true", help="skip the partly resident sweep sub-measurement at N=1")
     ap.add_argument("--tokens", type=int, default=32768, help="prefill tokens per GPU")
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")

@@ -60,6 +60,13 @@ int ssb_kernel_smem(const char* name);
  * No counterpart in the reference (it runs on one GPU with no collective to overlap). */
 int ssb_set_gemm_sm_reserve(int32_t sms);
 
+/* B-rows per tile of the sorted gate_up GEMM (ssb_sorted_gate_up, ssb_prefill_experts): 256 (default: 128 gate +
+ * 128 up rows, M128 x N256 tensor-core instructions, one accumulator set that the epilogue hands back half by half)
+ * or 128 (64 + 64 rows, M128 x N128 instructions, double-buffered accumulators). Both give the same bits. A
+ * process-wide setting read at each launch; SSB_EINVAL for other values. No counterpart in the reference (a
+ * Triton autotuning choice there, kernels/tuning.py). */
+int ssb_set_gate_up_tile(int32_t b_rows);
+
 /* Bound, in nanoseconds, of the grid-barrier waits of the cooperative kernels (ssb_moe_decode_fused; default 250 ms):
  * a barrier that does not complete in time gives up, the kernel sets SSB_ERR_TIMEOUT in the caller's error word
  * and returns (its outputs are then not valid, and its sync word must be zeroed before the next call). A

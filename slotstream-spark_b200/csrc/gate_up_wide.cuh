@@ -1,0 +1,308 @@
+// Wide-tile gate_up GEMM of the sorted prefill path (included by grouped_gemm.cu inside its namespace; uses its
+// dequant8_perm / cvt_bf16x2 / silu_fast helpers and GemmArgs).
+//
+// The 256 x 128 tile of k_moe_gemm issues M128 x N128 MMAs, and an N128 tcgen05.mma occupies the tensor pipe as
+// long as an N256 one, so that kernel cannot pass half of the tensor peak. This kernel's tile is 256 activation
+// rows x 256 B-rows -- the gate rows and the up rows of the same 128 intermediate columns -- and every k-block
+// issues M128 x N256 x K16 MMAs for each 128-row half, so the dequantised B tile still feeds both halves and
+// the tensor pipe runs at its full per-instruction width.
+//
+// The two halves' accumulators (2 x 256 fp32 columns) fill the 512 TMEM columns, so there is one accumulator
+// set: the epilogue drains half 0, hands it back (tmem_empty[0]), then drains half 1 (tmem_empty[1]); the next
+// tile's first MMAs into half 0 wait only for the first hand-back, so they overlap the drain of half 1.
+//
+// Warp roles (16 warps):
+//  * warp 0      activation rows: one 2-D TMA box of 128 rows per half from the permuted rows (x_sorted); a
+//                second half that holds only padding rows is neither loaded, multiplied nor stored;
+//  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma from one thread;
+//  * warps 4..7  epilogue: TMEM -> registers, h = silu(g) * u -> bf16 rows of h_sorted (one row per thread);
+//  * warps 8..15 weight producers, one thread per B-row: the row's codes, scales and biases of four k-blocks
+//                are loaded into registers one super-step ahead (and the super-step after that is prefetched
+//                into L2), then dequantised q*s + b -> bf16 in the K order (0,4,1,5,2,6,3,7) into the 128-byte
+//                swizzled B tile.
+// Every wait is bounded and ends with SSB_ERR_TIMEOUT; a row's result depends only on the row and its
+// expert's bytes (fixed k order), as in k_moe_gemm.
+
+constexpr int WG_BN = 256;                            // B-rows per tile: 128 gate + 128 up
+constexpr int WG_STAGES = 3;
+constexpr int WG_SS = 4;                              // k-blocks per producer super-step
+constexpr uint32_t WG_A_STAGE = TM * 128;             // 32 KB: two 128-row halves
+constexpr uint32_t WG_B_STAGE = WG_BN * 128;          // 32 KB
+constexpr uint32_t WG_TMEM_COLS = 512;                // half h's accumulator at column 256 h
+constexpr size_t WG_SMEM_BYTES = 1024 + WG_STAGES * (WG_A_STAGE + WG_B_STAGE) + 8 * (3 * WG_STAGES + 3) + 16;
+
+__global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_constant__ CUtensorMap tm_a, GemmArgs a) {
+  extern __shared__ uint8_t smraw[];
+  __shared__ int s_fail;
+  uint8_t* base = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sa = base;
+  uint8_t* sb = sa + WG_STAGES * WG_A_STAGE;
+  uint64_t* full_a = (uint64_t*)(sb + WG_STAGES * WG_B_STAGE);
+  uint64_t* full_b = full_a + WG_STAGES;
+  uint64_t* empty = full_b + WG_STAGES;
+  uint64_t* tmem_full = empty + WG_STAGES;   // [1]
+  uint64_t* tmem_empty = tmem_full + 1;      // [2]: one per half
+  uint32_t* tmem_slot = (uint32_t*)(tmem_empty + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_wait();
+  pdl_trigger();
+  const int NB = a.n_nblocks;   // inter / 128
+  const int64_t n_mb = (int64_t)__ldcg(a.num_padded) / TM;
+  const int64_t n_tiles = n_mb * NB;
+  if ((int64_t)blockIdx.x >= n_tiles) return;
+  const int my_tiles = (int)((n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x);
+  const int KB = a.K / BK;
+  const int64_t steps = (int64_t)my_tiles * KB;
+  auto tile_of = [&](int i) -> int64_t { return (int64_t)blockIdx.x + (int64_t)i * gridDim.x; };
+  auto half1_of = [&](int64_t mb) -> bool {
+    const int32_t r = __ldcg(a.sorted_rows + mb * TM + BM);
+    return r >= 0 && r < a.R;
+  };
+
+  if (tid == 0) {
+    s_fail = 0;
+    for (int s = 0; s < WG_STAGES; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_b[s], N_PROD);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(&tmem_empty[0], 4);
+    mbar_init(&tmem_empty[1], 4);
+    fence_mbar_init();
+  }
+  if (warp == MMA_WARP) tmem_alloc(tmem_slot, WG_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  int commits = 0;   // MMA thread: tmem_full commits issued
+
+  if (warp == A_WARP) {
+    if (lane == 0) {
+      prefetch_tensormap(&tm_a);
+      int64_t issued = 0;
+      bool two = half1_of(tile_of(0) / NB), two_next = true;
+      for (int64_t j = 0; j < steps; ++j) {
+        const int kb = (int)(j % KB);
+        const int i = (int)(j / KB);
+        if (kb == 0) {
+          if (i > 0) two = two_next;
+          if (i + 1 < my_tiles) two_next = half1_of(tile_of(i + 1) / NB);   // a tile ahead
+        }
+        const int s = (int)(j % WG_STAGES);
+        if (!mbar_wait_ns(&empty[s], (uint32_t)((j / WG_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
+          s_fail = 1;
+          break;
+        }
+        mbar_expect_tx(&full_a[s], two ? WG_A_STAGE : A_HALF);
+        const int32_t r0 = (int32_t)((tile_of(i) / NB) * TM);
+        tma_load_2d(smem_u32(sa + s * WG_A_STAGE), &tm_a, kb * BK, r0, &full_a[s]);
+        if (two) tma_load_2d(smem_u32(sa + s * WG_A_STAGE + A_HALF), &tm_a, kb * BK, r0 + BM, &full_a[s]);
+        ++issued;
+      }
+      // no copy may still be writing shared memory when the CTA exits
+      for (int64_t j = issued > WG_STAGES ? issued - WG_STAGES : 0; j < issued; ++j)
+        mbar_wait_ns(&full_a[j % WG_STAGES], (uint32_t)((j / WG_STAGES) & 1), SSB_WAIT_NS);
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(BM, WG_BN);
+      int64_t j = 0;
+      int nh_next = half1_of(tile_of(0) / NB) ? MT : 1;
+      for (int i = 0; i < my_tiles && !s_fail; ++i) {
+        const int nh = nh_next;
+        if (i + 1 < my_tiles) nh_next = half1_of(tile_of(i + 1) / NB) ? MT : 1;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++j) {
+          const int s = (int)(j % WG_STAGES);
+          const uint32_t ph = (uint32_t)((j / WG_STAGES) & 1);
+          if (!mbar_wait_ns(&full_a[s], ph, SSB_WAIT_NS) || !mbar_wait_ns(&full_b[s], ph, SSB_WAIT_NS)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t db = umma_desc_sw128(smem_u32(sb + s * WG_B_STAGE));
+#pragma unroll
+          for (int h = 0; h < MT; ++h) {
+            if (h >= nh) break;
+            if (kb == 0) {   // the epilogue has drained this half of the previous tile
+              if (!mbar_wait_ns(&tmem_empty[h], (uint32_t)(i & 1) ^ 1, SSB_WAIT_NS)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint64_t da = umma_desc_sw128(smem_u32(sa + s * WG_A_STAGE + h * A_HALF));
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_bf16(tmem + (uint32_t)(h * WG_BN), da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                        (kb | k) != 0);
+          }
+          umma_commit(&empty[s]);
+          if (!ok) break;
+        }
+        umma_commit(tmem_full);
+        ++commits;
+        if (!ok) {
+          s_fail = 1;
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
+    const int q = warp & 3;
+    uint16_t* out = (uint16_t*)a.out;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int64_t t = tile_of(i), mb = t / NB;
+      const int nb = (int)(t % NB);
+      const bool shared_e = a.shared_local >= 0 && __ldcg(a.block_expert + mb) == a.shared_local;
+      const int nh = half1_of(mb) ? MT : 1;
+      bool valid[MT];
+#pragma unroll
+      for (int h = 0; h < MT; ++h) {
+        const int32_t r = __ldcg(a.sorted_rows + mb * TM + h * BM + 32 * q + lane);
+        valid[h] = r >= 0 && r < a.R;
+      }
+      const bool ok = mbar_wait_ns(tmem_full, (uint32_t)(i & 1), SSB_WAIT_NS);
+      tc_fence_after();
+      if (!ok) {
+        s_fail = 1;
+        break;
+      }
+#pragma unroll 1
+      for (int h = 0; h < MT; ++h) {
+        if (h < nh) {
+          const int64_t m = mb * TM + h * BM + 32 * q + lane;
+          const uint32_t taddr = tmem + (uint32_t)(h * WG_BN) + ((uint32_t)(32 * q) << 16);
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            float g[32], u[32];
+            tmem_ld32(taddr + 32 * cc, g);
+            tmem_ld32(taddr + 128 + 32 * cc, u);
+            if (valid[h]) {
+              uint4* dst = reinterpret_cast<uint4*>(out + m * a.ldo + (int64_t)nb * 128 + 32 * cc);
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                float hv[8];
+#pragma unroll
+                for (int tt = 0; tt < 8; ++tt) {
+                  const float gg = g[8 * jj + tt], uu = u[8 * jj + tt];
+                  if (shared_e) {   // shared expert: bf16(silu(bf16 g)) * bf16 u (model/moe_sweep.py:37-43)
+                    const float gb = round_bf16(gg);
+                    hv[tt] = round_bf16(gb / (1.f + expf(-gb))) * round_bf16(uu);
+                  } else {
+                    hv[tt] = silu_fast(gg) * uu;   // accg / (1 + exp(-accg)) * accu, kernels/fused_moe_affine.py:80
+                  }
+                }
+                dst[jj] = make_uint4(cvt_bf16x2(hv[0], hv[4]), cvt_bf16x2(hv[1], hv[5]), cvt_bf16x2(hv[2], hv[6]),
+                                     cvt_bf16x2(hv[3], hv[7]));
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tmem_empty[h]);   // this half may be overwritten by the next tile now
+      }
+    }
+  } else if (warp >= PROD_WARP0) {
+    // ---------------- weight producers: thread p owns B-row p (p < 128: gate row, else up row of column p % 128)
+    const int p = tid - PROD_WARP0 * 32;
+    const int piece = p >> 7;
+    const int ng = a.K / a.gs;
+    const int n_ss = (int)(steps / WG_SS);
+    int my_fail = 0;
+    // the row's codes (4 k-blocks x 32 B), scales and biases (4 bf16 each) of super-step n; zeros for an unusable
+    // record (its error bit is set once per tile)
+    struct Rows {
+      uint4 w[WG_SS][2];
+      uint2 s, b;
+    };
+    auto row_src = [&](int n, const uint8_t*& codes, const uint16_t*& sc, const uint16_t*& bi) -> bool {
+      const int64_t j0 = (int64_t)n * WG_SS;
+      const int64_t t = tile_of((int)(j0 / KB));
+      const int64_t mb = t / NB;
+      const int nb = (int)(t % NB);
+      const int e = __ldcg(a.block_expert + mb);
+      const uint8_t* rb = (e >= 0 && e < a.n_groups) ? (const uint8_t*)__ldg(a.group_base + e) : nullptr;
+      if (!rb || ((uintptr_t)rb & 15)) return false;
+      const int64_t nrow = (int64_t)nb * 128 + (p & 127);
+      const int kb0 = (int)(j0 % KB);
+      codes = rb + a.off_w[piece] + nrow * (a.K / 2) + kb0 * 32;
+      sc = (const uint16_t*)(rb + a.off_s[piece]) + nrow * ng + kb0;
+      bi = (const uint16_t*)(rb + a.off_b[piece]) + nrow * ng + kb0;
+      return true;
+    };
+    auto load = [&](int n, Rows& r) -> bool {
+      const uint8_t* c;
+      const uint16_t *sc, *bi;
+      if (!row_src(n, c, sc, bi)) {
+#pragma unroll
+        for (int u = 0; u < WG_SS; ++u) r.w[u][0] = r.w[u][1] = make_uint4(0, 0, 0, 0);
+        r.s = r.b = make_uint2(0, 0);
+        return false;
+      }
+#pragma unroll
+      for (int u = 0; u < WG_SS; ++u) {
+        r.w[u][0] = __ldg(reinterpret_cast<const uint4*>(c + 32 * u));
+        r.w[u][1] = __ldg(reinterpret_cast<const uint4*>(c + 32 * u + 16));
+      }
+      r.s = __ldg(reinterpret_cast<const uint2*>(sc));
+      r.b = __ldg(reinterpret_cast<const uint2*>(bi));
+      return true;
+    };
+    auto prefetch = [&](int n) {
+      const uint8_t* c;
+      const uint16_t *sc, *bi;
+      if (row_src(n, c, sc, bi)) prefetch_line_l2(c);   // the row's 128 B of codes for that super-step
+    };
+    Rows cur, nxt;
+    bool cur_ok = n_ss > 0 ? load(0, cur) : true;
+    if (n_ss > 1) prefetch(1);
+    for (int n = 0; n < n_ss; ++n) {
+      bool nxt_ok = true;
+      if (n + 1 < n_ss) nxt_ok = load(n + 1, nxt);
+      if (n + 2 < n_ss) prefetch(n + 2);
+      if (!cur_ok && p == 0 && (((int64_t)n * WG_SS) % KB) == 0) set_err(a.err, SSB_ERR_MISALIGNED);
+#pragma unroll
+      for (int u = 0; u < WG_SS; ++u) {
+        const int64_t j = (int64_t)n * WG_SS + u;
+        const int s = (int)(j % WG_STAGES);
+        if (my_fail || !mbar_wait_ns(&empty[s], (uint32_t)((j / WG_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
+          my_fail = 1;
+          s_fail = 1;
+          continue;
+        }
+        const uint32_t sw = (u >> 1) ? cur.s.y : cur.s.x, bw = (u >> 1) ? cur.b.y : cur.b.x;
+        const uint32_t s2 = __byte_perm(sw, 0, (u & 1) ? 0x3232 : 0x1010);
+        const uint32_t b2 = __byte_perm(bw, 0, (u & 1) ? 0x3232 : 0x1010);
+        uint8_t* bt = sb + s * WG_B_STAGE;
+        const uint32_t ws[8] = {cur.w[u][0].x, cur.w[u][0].y, cur.w[u][0].z, cur.w[u][0].w,
+                                cur.w[u][1].x, cur.w[u][1].y, cur.w[u][1].z, cur.w[u][1].w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c)   // 16-byte chunk c = elements 8c .. 8c+7 of the k-block = code word c
+          *reinterpret_cast<uint4*>(bt + swz128(p, c)) = dequant8_perm(ws[c], s2, b2);
+        fence_proxy_async_smem();
+        mbar_arrive(&full_b[s]);
+      }
+      if (my_fail) break;
+      cur = nxt;
+      cur_ok = nxt_ok;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    if (s_fail) {   // every committed MMA group finishes before TMEM is released (the last commit's phase)
+      if (lane == 0 && commits > 0) mbar_wait_ns(tmem_full, (uint32_t)((commits - 1) & 1), SSB_WAIT_NS);
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, WG_TMEM_COLS);
+  }
+  if (tid == 0 && s_fail) set_err(a.err, SSB_ERR_TIMEOUT);
+}

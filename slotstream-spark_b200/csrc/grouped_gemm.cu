@@ -650,6 +650,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
   if (tid == 0 && s_fail) set_err(a.err, SSB_ERR_TIMEOUT);
 }
 
+#include "gate_up_wide.cuh"
+
 // x_sorted[m, :] = x[row_token[sorted_rows[m]], :] for m < num_padded (zero rows for padding), one warp per row:
 // the activation rows in expert order, so the grouped GEMM reads its A tiles as whole 2-D boxes, with every group
 // of 8 columns in the K order (0,4,1,5,2,6,3,7) in which the sorted GEMMs dequantise their weights.
@@ -754,6 +756,7 @@ __global__ void __launch_bounds__(256) k_permute_by_row(const uint4* __restrict_
 // SMs the persistent GEMM leaves free for kernels that run beside it (collectives on another stream); set by
 // ssb_set_gemm_sm_reserve, read at each launch.
 int g_sm_reserve = 0;
+int g_gate_up_tile = 256;   // B-rows per tile of the sorted gate_up: 256 (k_gate_up_wide) or 128 (k_moe_gemm)
 
 int num_sms() {
   static int sms = 0;
@@ -821,6 +824,31 @@ int launch(int epi, GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t s
   return ssb_launch(k, dim3(grid), dim3(THREADS), SMEM_BYTES, st, true, tm, a);
 }
 
+// k_gate_up_wide over the sorted rows (x permuted into expert order, gs 64): tiles of 256 rows x 128 h columns.
+int launch_gate_up_wide(GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t st) {
+  if (n_mblocks <= 0) return SSB_OK;
+  if (a.gs != 64 || !a.kperm || !a.out_sorted || a.a_box_rows != TM || !a.sorted_rows || !a.num_padded ||
+      !a.block_expert || !a.group_base)
+    return SSB_EINVAL;
+  CUtensorMap tm;
+  int rc = encode_a_map(&tm, a);
+  if (rc) return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_gate_up_wide, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WG_SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    attr_set = true;
+  }
+  ssb_note_smem("fused_moe_gate_up_wide", k_gate_up_wide, WG_SMEM_BYTES);
+  a.n_mblocks = n_mblocks;
+  a.n_nblocks = n_nblocks;
+  const int64_t tiles = n_mblocks * n_nblocks;
+  int ctas = num_sms() - g_sm_reserve;
+  if (ctas < 1) ctas = 1;
+  const int grid = (int)(tiles < ctas ? tiles : ctas);
+  return ssb_launch(k_gate_up_wide, dim3(grid), dim3(THREADS), WG_SMEM_BYTES, st, true, tm, a);
+}
+
 void set_record_offsets(GemmArgs& g, int hidden, int inter, bool gate_up) {
   RecOffs o = rec_offsets(hidden, inter, 64);
   if (gate_up) {
@@ -868,6 +896,8 @@ int gate_up_impl(const uint16_t* x, int64_t tokens, int32_t hidden, int32_t inte
   g.out = h_buf;
   g.ldo = inter;
   g.err = err;
+  if (sorted && g_gate_up_tile == WG_BN && hidden % (WG_SS * BK) == 0 && inter % 128 == 0)
+    return launch_gate_up_wide(g, padded_len / TM, inter / 128, (cudaStream_t)stream);
   return launch(EPI_SWIGLU, g, padded_len / TM, inter / (BN / 2), (cudaStream_t)stream);
 }
 
@@ -1054,6 +1084,12 @@ extern "C" int ssb_gemm_dense(const uint16_t* x, int64_t m, int32_t k, const uin
   g.out_vec = (ldo % 4 == 0) && ((uintptr_t)out & 15) == 0;
   g.err = nullptr;
   return launch(EPI_PLAIN, g, (m + TM - 1) / TM, (n + BN - 1) / BN, (cudaStream_t)stream);
+}
+
+extern "C" int ssb_set_gate_up_tile(int32_t b_rows) {
+  SSB_CHECK_ARG(b_rows == 128 || b_rows == 256);
+  g_gate_up_tile = b_rows;
+  return SSB_OK;
 }
 
 extern "C" int ssb_set_gemm_sm_reserve(int32_t sms) {

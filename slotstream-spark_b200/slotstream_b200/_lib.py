@@ -28,6 +28,7 @@ SIGNATURES = {
     "ssb_device_check": [],
     "ssb_kernel_smem": [ctypes.c_char_p],
     "ssb_set_gemm_sm_reserve": [_I32],
+    "ssb_set_gate_up_tile": [_I32],
     "ssb_set_wait_limit_ns": [_I64],
     "ssb_topk_stable": [_P, _P, _I64, _I32, _I32, _P, _P, _P],
     "ssb_router_logits": [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P],

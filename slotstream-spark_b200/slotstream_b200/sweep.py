@@ -1,15 +1,19 @@
 """Prefill MoE sweep over partially resident experts -- the B200 side of slotstream_spark/model/moe_sweep.py:80-176 and
 the group planner of engine/sweep.py:34-58.
 
-A layer's (token, rank) rows are sorted stably by (resident first, expert id) and cut into groups of at most
-``group_size`` experts that never mix resident and staged experts (``plan_sweep``). A resident group reads its
-records where they already sit in HBM (pool slots). A staged group is copied from pinned host records into one of
-``staging_groups`` device staging buffers on a copy stream, ``inflight`` groups ahead of the group being computed;
-events order every reuse of a buffer after the kernels that read it. Each group is one align (its expert map selects
-its rows) and one ``ssb_prefill_experts`` launch (row permute, tcgen05 gate_up, tcgen05 down) writing its rows of
-``out_rows``; the shared expert is one more group, and ``ssb_combine_layer`` sums every token's rows in router rank
-order and adds the shared expert. A row's result depends only on that row and its expert's bytes, so the layer equals
-the all-resident ``moe_layer_prefill`` bit for bit whatever the residency, the grouping or the staging buffer.
+A layer's (token, rank) rows are grouped as the reference plans them: resident experts first, then staged ones,
+at most ``group_size`` experts per group, never mixing the two (``plan_sweep`` restates that planner over the rows;
+``plan_groups`` gives the same groups from the per-expert row counts, which is all the device path needs). A
+resident group reads its records where they already sit in HBM (pool slots). A staged group is copied from pinned
+host records into one of ``staging_groups`` device staging buffers on a copy stream, ``inflight`` groups ahead of
+the group being computed; events order every reuse of a buffer after the kernels that read it.
+
+On the device the layer is one router, one align whose expert map numbers the experts in plan order (so each
+group's rows are a contiguous run of 256-row blocks), one permute of the activation rows into that order, then per
+group the tcgen05 gate_up and down launches over the group's blocks, the shared expert's blocks last, and one
+rank-order combine with the shared add. A row's result depends only on that row and its expert's bytes, so the
+layer equals the all-resident ``moe_layer_prefill`` bit for bit whatever the residency, the grouping or the staging
+buffer.
 """
 from dataclasses import dataclass
 
@@ -69,6 +73,26 @@ def plan_sweep(expert_ids: np.ndarray, resident: np.ndarray, group_size: int = G
     return SweepPlan(order, groups)
 
 
+def plan_groups(counts: np.ndarray, resident: np.ndarray, group_size: int = GROUP_SIZE) -> SweepPlan:
+    """The groups of ``plan_sweep`` from per-expert row counts alone (int [512]): the same experts, residency and
+    row ranges, without ordering the rows on the host (the device align orders them). ``order`` is None."""
+    c = np.asarray(counts, dtype=np.int64)
+    res = np.asarray(resident, dtype=bool)
+    if c.shape != (EXPERTS,) or res.shape != (EXPERTS,) or (c < 0).any():
+        raise ValueError(f"counts and resident: want [{EXPERTS}] arrays, counts >= 0")
+    if group_size <= 0:
+        raise ValueError("group_size: want at least 1")
+    groups, pos = [], 0
+    for is_res in (True, False):
+        present = np.flatnonzero((c > 0) & (res == is_res))
+        for a in range(0, present.size, group_size):
+            ex = present[a:a + group_size]
+            n = int(c[ex].sum())
+            groups.append(Group(ex.astype(np.int32), is_res, pos, pos + n))
+            pos += n
+    return SweepPlan(None, groups)
+
+
 class SweepStats:
     def __init__(self):
         self.groups = self.staged_groups = self.records_staged = self.bytes_staged = 0
@@ -79,8 +103,15 @@ class SweepStats:
 
 
 class PrefillSweep:
-    """Buffers and streams for sweeping layers of up to ``max_tokens`` tokens (every output and workspace allocated
-    here, once)."""
+    """Buffers and streams for sweeping layers of ``max_tokens`` tokens (every output and workspace allocated here,
+    once).
+
+    Per layer: the router on the device, the per-expert row counts read back (2 KB, one host sync), the plan of
+    ``plan_groups``; then ONE align over all rows with local expert ids in plan order (so every group's rows form
+    a contiguous run of 256-row blocks), ONE permute of the activation rows into that order, and per group the
+    tcgen05 gate_up and down launches over the group's block range, reading its records where they are (HBM for
+    resident experts, a staging buffer for staged ones); the shared expert's blocks come last; one rank-order
+    combine."""
 
     def __init__(self, hidden: int, inter: int, k: int, max_tokens: int, record_bytes: int, *, experts: int = EXPERTS,
                  group_size: int = GROUP_SIZE, staging_groups: int = STAGING_GROUPS, inflight: int = INFLIGHT,
@@ -88,26 +119,25 @@ class PrefillSweep:
         from .kernels.moe_layer import PrefillLayerBuffers
         if inflight < 1 or inflight > staging_groups:
             raise ValueError("need 1 <= inflight <= staging_groups")
+        if experts != EXPERTS:
+            raise ValueError(f"the sweep plans {EXPERTS} experts per layer")
         self.hidden, self.inter, self.k, self.experts = hidden, inter, k, experts
         self.group_size, self.staging_groups, self.inflight = group_size, staging_groups, inflight
         self.record_bytes = record_bytes
         self.bufs = PrefillLayerBuffers(max_tokens, k, hidden, inter, experts, device)
-        rows = self.bufs.rows
-        p = padded_rows(rows, group_size, BLOCK_M)
-        self.sorted_rows = torch.empty(p, dtype=torch.int32, device=device)
-        self.block_expert = torch.empty(p // BLOCK_M, dtype=torch.int32, device=device)
-        self.num_padded = torch.empty(1, dtype=torch.int32, device=device)
-        self.x_sorted = torch.empty(p, hidden, dtype=torch.bfloat16, device=device)
-        self.h_sorted = torch.empty(p, inter, dtype=torch.bfloat16, device=device)
         self.staging = torch.empty((staging_groups, group_size, record_bytes), dtype=torch.uint8, device=device)
         self.copy_stream = torch.cuda.Stream(device=device)
-        self.ids_host = torch.empty((max_tokens, k), dtype=torch.int32).pin_memory()
-        # per-group expert maps and record pointers go through pinned host buffers (no pageable copies)
+        self.counts = torch.empty(experts, dtype=torch.int64, device=device)
+        self.counts_host = torch.empty(experts, dtype=torch.int64).pin_memory()
         n_max = 2 * ((experts + group_size - 1) // group_size) + 1   # groups of a layer, then the shared expert
-        self._emap_host = torch.empty((n_max, experts + 1), dtype=torch.int32).pin_memory()
-        self._ptr_host = torch.empty((n_max, group_size), dtype=torch.int64).pin_memory()
-        self._emap_dev = torch.empty((n_max, experts + 1), dtype=torch.int32, device=device)
-        self._ptr_dev = torch.empty((n_max, group_size), dtype=torch.int64, device=device)
+        # per layer: the expert map (global -> local id in plan order), record bases per local id, and per group
+        # its padded row count, through pinned host buffers
+        self._emap_host = torch.empty(experts + 1, dtype=torch.int32).pin_memory()
+        self._ptr_host = torch.empty(experts + 1, dtype=torch.int64).pin_memory()
+        self._npad_host = torch.empty(n_max, dtype=torch.int32).pin_memory()
+        self._emap_dev = torch.empty(experts + 1, dtype=torch.int32, device=device)
+        self._ptr_dev = torch.empty(experts + 1, dtype=torch.int64, device=device)
+        self._npad_dev = torch.empty(n_max, dtype=torch.int32, device=device)
         self.stats = SweepStats()
         self.last_plan = None
 
@@ -116,28 +146,52 @@ class PrefillSweep:
         of the layer's resident records; ``host_record_ptr(e)``: address of expert e's pinned host record (staged
         experts); ``shared_ptr``: device address of the shared expert's record."""
         from .kernels.moe_layer import _route_into
-        t, h = x.shape
         b = self.bufs
-        k, E = self.k, self.experts
-        if h != self.hidden or t > b.tokens or x.dtype != torch.bfloat16 or not x.is_contiguous():
-            raise ValueError("x must be contiguous bf16 [T <= max_tokens, hidden]")
-        if t != b.tokens:
-            raise ValueError("this sweep's buffers hold exactly max_tokens tokens per layer")
+        t, h = x.shape
+        k, E, H, I = self.k, self.experts, self.hidden, self.inter
+        if h != H or t != b.tokens or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise ValueError("x must be contiguous bf16 [max_tokens, hidden]")
         st = _lib.stream()
         comp = torch.cuda.current_stream()
         L = _lib.lib()
         _route_into(x, w_router, sh_gate_w, k, b, bias=bias)             # ids, weights, shared gate on the device
-        self.ids_host[:t].copy_(b.ids, non_blocking=True)
-        comp.synchronize()                                              # the router's ids, on the host
-        flat = np.ascontiguousarray(self.ids_host[:t].numpy().reshape(-1), dtype=np.int32)
+        self.counts.copy_(torch.bincount(b.ids.reshape(-1), minlength=E))
+        self.counts_host.copy_(self.counts, non_blocking=True)
+        comp.synchronize()                                              # the per-expert row counts, on the host
+        counts = self.counts_host.numpy()
         resident = np.zeros(E, dtype=bool)
         for e in resident_ptr:
             resident[int(e)] = True
-        plan = plan_sweep(flat, resident, self.group_size)
+        plan = plan_groups(counts, resident, self.group_size)
         self.last_plan = plan
         groups = plan.groups
         staged = [gi for gi, g in enumerate(groups) if not g.resident]
         buf_of = {gi: j % self.staging_groups for j, gi in enumerate(staged)}
+
+        # local ids in plan order, the shared expert last; each local expert's rows padded to 256-row blocks
+        emap = self._emap_host.numpy()
+        ptrs = self._ptr_host.numpy()
+        emap[:] = -1
+        blk = [0]
+        loc = 0
+        for gi, g in enumerate(groups):
+            for j, e in enumerate(g.experts):
+                emap[int(e)] = loc
+                ptrs[loc] = (int(resident_ptr[int(e)]) if g.resident else self.staging[buf_of[gi], j].data_ptr())
+                loc += 1
+            blk.append(blk[-1] + int(((counts[g.experts] + BLOCK_M - 1) // BLOCK_M).sum()))
+        emap[E] = loc
+        ptrs[loc] = int(shared_ptr)
+        n_local = loc + 1
+        blk.append(blk[-1] + (t + BLOCK_M - 1) // BLOCK_M)
+        npad = self._npad_host.numpy()
+        for gi in range(len(groups) + 1):
+            npad[gi] = (blk[gi + 1] - blk[gi]) * BLOCK_M
+        self._emap_dev.copy_(self._emap_host, non_blocking=True)
+        self._ptr_dev[:n_local].copy_(self._ptr_host[:n_local], non_blocking=True)
+        self._npad_dev[:len(groups) + 1].copy_(self._npad_host[:len(groups) + 1], non_blocking=True)
+
+        # the staging copies start now, beside the align, the permute and the resident groups
         copy_done, buf_free = {}, [None] * self.staging_groups
         s = self.stats
 
@@ -145,71 +199,60 @@ class PrefillSweep:
             bi = buf_of[gi]
             if buf_free[bi] is not None:
                 self.copy_stream.wait_event(buf_free[bi])
-            with torch.cuda.stream(self.copy_stream):
-                for j, e in enumerate(groups[gi].experts):
-                    _copy_async(self.staging[bi, j].data_ptr(), host_record_ptr(int(e)), self.record_bytes,
-                                self.copy_stream)
-                ev = torch.cuda.Event()
-                ev.record(self.copy_stream)
+            for j, e in enumerate(groups[gi].experts):
+                _copy_async(self.staging[bi, j].data_ptr(), host_record_ptr(int(e)), self.record_bytes,
+                            self.copy_stream)
+            ev = torch.cuda.Event()
+            ev.record(self.copy_stream)
             copy_done[gi] = ev
             s.staged_groups += 1
             s.records_staged += int(groups[gi].experts.size)
             s.bytes_staged += int(groups[gi].experts.size) * self.record_bytes
 
+        self.copy_stream.wait_stream(comp)   # the staging buffers' previous readers (the last layer) are done
         for gi in staged[:self.inflight]:
             issue(gi)
         pending = staged[self.inflight:]
-        for gi, g in enumerate(groups):
+
+        p_len = padded_rows(b.rows, n_local, BLOCK_M)
+        sr, be, npd = moe_align(b.row_expert, n_local, BLOCK_M, expert_map=self._emap_dev,
+                                out=(b.sorted_rows[:p_len], b.block_expert[:p_len // BLOCK_M], b.num_padded))
+        _lib.check(L.ssb_permute_rows(_lib.ptr(x), t, H, _lib.ptr(b.row_token), b.rows, _lib.ptr(sr), _lib.ptr(npd),
+                                      p_len, _lib.ptr(b.x_sorted), st), "sweep permute")
+        for gi in range(len(groups) + 1):
             s.groups += 1
-            n = int(g.experts.size)
-            emap = self._emap_host[gi]
-            emap.fill_(-1)
-            emap[torch.from_numpy(g.experts.astype(np.int64))] = torch.arange(n, dtype=torch.int32)
-            ptrs = self._ptr_host[gi]
-            if g.resident:
-                for j, e in enumerate(g.experts):
-                    ptrs[j] = int(resident_ptr[int(e)])
+            g = groups[gi] if gi < len(groups) else None
+            if g is not None and g.resident:
                 s.resident_rows += g.row_hi - g.row_lo
-            else:
-                bi = buf_of[gi]
-                for j in range(n):
-                    ptrs[j] = self.staging[bi, j].data_ptr()
+            elif g is not None:
                 comp.wait_event(copy_done.pop(gi))
                 s.staged_rows += g.row_hi - g.row_lo
-            self._emap_dev[gi].copy_(emap, non_blocking=True)
-            self._ptr_dev[gi, :n].copy_(ptrs[:n], non_blocking=True)
-            self._experts(x, self._emap_dev[gi], self._ptr_dev[gi, :n], n, -1, st)
-            if not g.resident:
+            self._blocks(blk[gi], blk[gi + 1], gi, n_local, n_local - 1, st)
+            if g is not None and not g.resident:
                 ev = torch.cuda.Event()
                 ev.record(comp)
                 buf_free[buf_of[gi]] = ev
                 if pending:
                     issue(pending.pop(0))   # keep `inflight` staged groups ahead of the compute
-        # the shared expert: one more group (local expert 0, the reference's bf16 rounding between its ops)
-        gi = len(groups)
-        emap = self._emap_host[gi]
-        emap.fill_(-1)
-        emap[E] = 0
-        self._emap_dev[gi].copy_(emap, non_blocking=True)
-        self._ptr_host[gi, 0] = int(shared_ptr)
-        self._ptr_dev[gi, :1].copy_(self._ptr_host[gi, :1], non_blocking=True)
-        self._experts(x, self._emap_dev[gi], self._ptr_dev[gi, :1], 1, 0, st)
-        r = t * k
-        _lib.check(L.ssb_combine_layer(_lib.ptr(b.out_rows), t, k, h, b.out_rows.data_ptr() + 4 * r * h, None,
+        _lib.check(L.ssb_combine_layer(_lib.ptr(b.out_rows), t, k, H, b.out_rows.data_ptr() + 4 * t * k * H, None,
                                        _lib.ptr(b.y), st), "combine")
         return b.y
 
-    def _experts(self, x, emap, gptr, n, shared_local, st):
-        """One group: align the layer's rows through the group's expert map, then the grouped GEMMs over them."""
+    def _blocks(self, lo, hi, gi, n_local, shared_local, st):
+        """gate_up and down over 256-row blocks [lo, hi) of the layer's aligned rows (one group)."""
         b = self.bufs
-        sr, be, npd = moe_align(b.row_expert, n, BLOCK_M, expert_map=emap,
-                                out=(self.sorted_rows[:padded_rows(b.rows, n, BLOCK_M)],
-                                     self.block_expert[:padded_rows(b.rows, n, BLOCK_M) // BLOCK_M], self.num_padded))
-        _lib.check(_lib.lib().ssb_prefill_experts(
-            _lib.ptr(x), x.shape[0], self.hidden, self.inter, _lib.ptr(b.row_token), _lib.ptr(b.row_weight), b.rows,
-            _lib.ptr(sr), _lib.ptr(be), _lib.ptr(npd), sr.numel(), _lib.ptr(gptr), n, shared_local,
-            _lib.ptr(self.x_sorted), _lib.ptr(self.h_sorted), _lib.ptr(b.out_rows), _lib.ptr(b.err), st),
-            "prefill experts (sweep group)")
+        H, I = self.hidden, self.inter
+        L = _lib.lib()
+        n = (hi - lo) * BLOCK_M
+        sr = b.sorted_rows.data_ptr() + 4 * lo * BLOCK_M
+        be = b.block_expert.data_ptr() + 4 * lo
+        npd = self._npad_dev.data_ptr() + 4 * gi
+        hs = b.h.data_ptr() + 2 * lo * BLOCK_M * I
+        _lib.check(L.ssb_sorted_gate_up(b.x_sorted.data_ptr() + 2 * lo * BLOCK_M * H, H, I, _lib.ptr(b.row_token),
+                                        b.rows, sr, be, npd, n, _lib.ptr(self._ptr_dev), n_local, shared_local, hs,
+                                        _lib.ptr(b.err), st), "sweep gate_up")
+        _lib.check(L.ssb_sorted_down(hs, b.rows, H, I, _lib.ptr(b.row_weight), sr, be, npd, n, _lib.ptr(self._ptr_dev),
+                                     n_local, shared_local, _lib.ptr(b.out_rows), _lib.ptr(b.err), st), "sweep down")
 
 
 def _copy_async(dst: int, src: int, nbytes: int, stream):

@@ -98,6 +98,7 @@ def test_sweep_reads_resident_records_from_a_slot_pool(layer):
     rb = lay.record_bytes
     pool = SlotPool(rb, 1, max_slots=200)
     try:
+        pool.resize(200)
         table = host_table(layer["host"].data_ptr(), rb, 1, E)
         want = np.sort(np.random.default_rng(9).choice(E, 150, replace=False)).astype(np.int32)
         pool.ensure(0, want, table)

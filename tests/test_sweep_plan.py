@@ -54,3 +54,20 @@ def test_plan_rejects_bad_inputs():
     with pytest.raises(ValueError):
         plan_sweep(np.zeros(3, np.int32), res, 0)
     assert plan_sweep(np.zeros(0, np.int32), res).groups == []
+
+
+def test_count_planner_gives_the_row_planner_groups():
+    """plan_groups (per-expert counts, what the device path reads back) == plan_sweep's groups."""
+    from slotstream_b200.sweep import plan_groups
+    rng = np.random.default_rng(3)
+    for trial in range(100):
+        n = int(rng.integers(0, 5000))
+        ids = ((rng.zipf(1.2, n) % EXPERTS) if trial % 2 else rng.integers(0, EXPERTS, n)).astype(np.int32)
+        res = rng.random(EXPERTS) < rng.random()
+        gs = int(rng.integers(1, 40))
+        a = plan_sweep(ids, res, gs).groups
+        b = plan_groups(np.bincount(ids, minlength=EXPERTS), res, gs).groups
+        assert len(a) == len(b)
+        for x, y in zip(a, b):
+            assert np.array_equal(x.experts, y.experts) and (x.resident, x.row_lo, x.row_hi) == (
+                y.resident, y.row_lo, y.row_hi)
