@@ -12,8 +12,8 @@
 // tile's first MMAs into half 0 wait only for the first hand-back, so they overlap the drain of half 1.
 //
 // Warp roles (16 warps):
-//  * warp 0      activation rows: one 2-D TMA box of 128 rows per half from the permuted rows (x_sorted); a
-//                second half that holds only padding rows is neither loaded, multiplied nor stored;
+//  * warp 0      activation rows: one 2-D TMA box of 256 rows from the permuted rows (x_sorted), or of the
+//                first 128 when the second half holds only padding rows (then neither loaded, multiplied nor stored);
 //  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma from one thread;
 //  * warps 4..7  epilogue: TMEM -> registers, h = silu(g) * u -> bf16 rows of h_sorted (one row per thread);
 //  * warps 8..15 weight producers, one thread per B-row: the row's codes, scales and biases of four k-blocks
@@ -24,23 +24,27 @@
 // expert's bytes (fixed k order), as in k_moe_gemm.
 
 constexpr int WG_BN = 256;                            // B-rows per tile: 128 gate + 128 up
-constexpr int WG_STAGES = 3;
+constexpr int WG_A_STAGES = 3;                        // activation stages
+constexpr int WG_B_STAGES = 3;                        // dequantised weight stages (fewer measured slower)
 constexpr int WG_SS = 4;                              // k-blocks per producer super-step
 constexpr uint32_t WG_A_STAGE = TM * 128;             // 32 KB: two 128-row halves
 constexpr uint32_t WG_B_STAGE = WG_BN * 128;          // 32 KB
 constexpr uint32_t WG_TMEM_COLS = 512;                // half h's accumulator at column 256 h
-constexpr size_t WG_SMEM_BYTES = 1024 + WG_STAGES * (WG_A_STAGE + WG_B_STAGE) + 8 * (3 * WG_STAGES + 3) + 16;
+constexpr size_t WG_SMEM_BYTES =
+    1024 + WG_A_STAGES * WG_A_STAGE + WG_B_STAGES * WG_B_STAGE + 8 * (2 * WG_A_STAGES + 2 * WG_B_STAGES + 3) + 16;
 
-__global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_constant__ CUtensorMap tm_a, GemmArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_constant__ CUtensorMap tm_a,
+                                                              const __grid_constant__ CUtensorMap tm_h, GemmArgs a) {
   extern __shared__ uint8_t smraw[];
   __shared__ int s_fail;
   uint8_t* base = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
   uint8_t* sa = base;
-  uint8_t* sb = sa + WG_STAGES * WG_A_STAGE;
-  uint64_t* full_a = (uint64_t*)(sb + WG_STAGES * WG_B_STAGE);
-  uint64_t* full_b = full_a + WG_STAGES;
-  uint64_t* empty = full_b + WG_STAGES;
-  uint64_t* tmem_full = empty + WG_STAGES;   // [1]
+  uint8_t* sb = sa + WG_A_STAGES * WG_A_STAGE;
+  uint64_t* full_a = (uint64_t*)(sb + WG_B_STAGES * WG_B_STAGE);
+  uint64_t* empty_a = full_a + WG_A_STAGES;
+  uint64_t* full_b = empty_a + WG_A_STAGES;
+  uint64_t* empty_b = full_b + WG_B_STAGES;
+  uint64_t* tmem_full = empty_b + WG_B_STAGES;   // [1]
   uint64_t* tmem_empty = tmem_full + 1;      // [2]: one per half
   uint32_t* tmem_slot = (uint32_t*)(tmem_empty + 2);
 
@@ -55,17 +59,21 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
   const int KB = a.K / BK;
   const int64_t steps = (int64_t)my_tiles * KB;
   auto tile_of = [&](int i) -> int64_t { return (int64_t)blockIdx.x + (int64_t)i * gridDim.x; };
-  auto half1_of = [&](int64_t mb) -> bool {
-    const int32_t r = __ldcg(a.sorted_rows + mb * TM + BM);
-    return r >= 0 && r < a.R;
-  };
+  // the A and MMA threads fetch the next tile's answer a tile ahead as a raw row id and test it when that tile
+  // starts, so the load's latency never stalls them
+  auto half1_row = [&](int64_t mb) -> int32_t { return __ldcg(a.sorted_rows + mb * TM + BM); };
+  auto half1_ok = [&](int32_t r) -> bool { return r >= 0 && r < a.R; };
+  auto half1_of = [&](int64_t mb) -> bool { return half1_ok(half1_row(mb)); };
 
   if (tid == 0) {
     s_fail = 0;
-    for (int s = 0; s < WG_STAGES; ++s) {
+    for (int s = 0; s < WG_A_STAGES; ++s) {
       mbar_init(&full_a[s], 1);
+      mbar_init(&empty_a[s], 1);
+    }
+    for (int s = 0; s < WG_B_STAGES; ++s) {
       mbar_init(&full_b[s], N_PROD);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty_b[s], 1);
     }
     mbar_init(tmem_full, 1);
     mbar_init(&tmem_empty[0], 4);
@@ -82,49 +90,50 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
   if (warp == A_WARP) {
     if (lane == 0) {
       prefetch_tensormap(&tm_a);
+      prefetch_tensormap(&tm_h);
       int64_t issued = 0;
-      bool two = half1_of(tile_of(0) / NB), two_next = true;
+      bool two = half1_of(tile_of(0) / NB);
+      int32_t r_next = 0;
       for (int64_t j = 0; j < steps; ++j) {
         const int kb = (int)(j % KB);
         const int i = (int)(j / KB);
         if (kb == 0) {
-          if (i > 0) two = two_next;
-          if (i + 1 < my_tiles) two_next = half1_of(tile_of(i + 1) / NB);   // a tile ahead
+          if (i > 0) two = half1_ok(r_next);
+          if (i + 1 < my_tiles) r_next = half1_row(tile_of(i + 1) / NB);
         }
-        const int s = (int)(j % WG_STAGES);
-        if (!mbar_wait_ns(&empty[s], (uint32_t)((j / WG_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
+        const int s = (int)(j % WG_A_STAGES);
+        if (!mbar_wait_ns(&empty_a[s], (uint32_t)((j / WG_A_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
           s_fail = 1;
           break;
         }
         mbar_expect_tx(&full_a[s], two ? WG_A_STAGE : A_HALF);
         const int32_t r0 = (int32_t)((tile_of(i) / NB) * TM);
-        tma_load_2d(smem_u32(sa + s * WG_A_STAGE), &tm_a, kb * BK, r0, &full_a[s]);
-        if (two) tma_load_2d(smem_u32(sa + s * WG_A_STAGE + A_HALF), &tm_a, kb * BK, r0 + BM, &full_a[s]);
+        tma_load_2d(smem_u32(sa + s * WG_A_STAGE), two ? &tm_a : &tm_h, kb * BK, r0, &full_a[s]);   // 256 or 128 rows
         ++issued;
       }
       // no copy may still be writing shared memory when the CTA exits
-      for (int64_t j = issued > WG_STAGES ? issued - WG_STAGES : 0; j < issued; ++j)
-        mbar_wait_ns(&full_a[j % WG_STAGES], (uint32_t)((j / WG_STAGES) & 1), SSB_WAIT_NS);
+      for (int64_t j = issued > WG_A_STAGES ? issued - WG_A_STAGES : 0; j < issued; ++j)
+        mbar_wait_ns(&full_a[j % WG_A_STAGES], (uint32_t)((j / WG_A_STAGES) & 1), SSB_WAIT_NS);
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(BM, WG_BN);
       int64_t j = 0;
-      int nh_next = half1_of(tile_of(0) / NB) ? MT : 1;
+      int32_t r_next = half1_row(tile_of(0) / NB);
       for (int i = 0; i < my_tiles && !s_fail; ++i) {
-        const int nh = nh_next;
-        if (i + 1 < my_tiles) nh_next = half1_of(tile_of(i + 1) / NB) ? MT : 1;
+        const int nh = half1_ok(r_next) ? MT : 1;
+        if (i + 1 < my_tiles) r_next = half1_row(tile_of(i + 1) / NB);
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++j) {
-          const int s = (int)(j % WG_STAGES);
-          const uint32_t ph = (uint32_t)((j / WG_STAGES) & 1);
-          if (!mbar_wait_ns(&full_a[s], ph, SSB_WAIT_NS) || !mbar_wait_ns(&full_b[s], ph, SSB_WAIT_NS)) {
+          const int s = (int)(j % WG_A_STAGES), t = (int)(j % WG_B_STAGES);
+          if (!mbar_wait_ns(&full_a[s], (uint32_t)((j / WG_A_STAGES) & 1), SSB_WAIT_NS) ||
+              !mbar_wait_ns(&full_b[t], (uint32_t)((j / WG_B_STAGES) & 1), SSB_WAIT_NS)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t db = umma_desc_sw128(smem_u32(sb + s * WG_B_STAGE));
+          const uint64_t db = umma_desc_sw128(smem_u32(sb + t * WG_B_STAGE));
 #pragma unroll
           for (int h = 0; h < MT; ++h) {
             if (h >= nh) break;
@@ -141,7 +150,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
               umma_bf16(tmem + (uint32_t)(h * WG_BN), da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
                         (kb | k) != 0);
           }
-          umma_commit(&empty[s]);
+          umma_commit(&empty_a[s]);
+          umma_commit(&empty_b[t]);
           if (!ok) break;
         }
         umma_commit(tmem_full);
@@ -222,30 +232,46 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
       uint4 w[WG_SS][2];
       uint2 s, b;
     };
-    auto row_src = [&](int n, const uint8_t*& codes, const uint16_t*& sc, const uint16_t*& bi) -> bool {
+    // Record base per tile, fetched ahead so that no load of a super-step waits on a dependent chain: the expert
+    // of tile T+1 is read when tile T's loads start, its base in the middle of tile T, and it is checked when
+    // tile T+1 starts. (A tile's super-steps are SPT consecutive super-steps; KB is a multiple of WG_SS.)
+    const int SPT = KB / WG_SS, MID = SPT / 2;
+    auto expert_at = [&](int i) -> int32_t { return __ldcg(a.block_expert + tile_of(i) / NB); };
+    auto base_raw = [&](int32_t e) -> const uint8_t* {
+      return (e >= 0 && e < a.n_groups) ? (const uint8_t*)__ldg(a.group_base + e) : nullptr;
+    };
+    auto usable = [](const uint8_t* rb) -> const uint8_t* { return ((uintptr_t)rb & 15) ? nullptr : rb; };
+    const uint8_t* base_cur = nullptr;   // checked base of the tile whose super-step was loaded last
+    const uint8_t* base_nxt = nullptr;   // raw base of the tile after it (from the middle of the current tile)
+    int32_t e_nxt = -1;
+    auto advance = [&](int n) {          // before loading super-step n; n = 0, 1, 2, ... in order
+      const int T = n / SPT, sub = n % SPT;
+      if (sub == 0) {
+        base_cur = T == 0 ? usable(base_raw(expert_at(0))) : usable(base_nxt);
+        if (T + 1 < my_tiles) e_nxt = expert_at(T + 1);
+      }
+      if (sub == MID && T + 1 < my_tiles) base_nxt = base_raw(e_nxt);
+    };
+    auto row_src = [&](const uint8_t* rb, int n, const uint8_t*& codes, const uint16_t*& sc, const uint16_t*& bi) {
       const int64_t j0 = (int64_t)n * WG_SS;
-      const int64_t t = tile_of((int)(j0 / KB));
-      const int64_t mb = t / NB;
-      const int nb = (int)(t % NB);
-      const int e = __ldcg(a.block_expert + mb);
-      const uint8_t* rb = (e >= 0 && e < a.n_groups) ? (const uint8_t*)__ldg(a.group_base + e) : nullptr;
-      if (!rb || ((uintptr_t)rb & 15)) return false;
+      const int nb = (int)(tile_of((int)(j0 / KB)) % NB);
       const int64_t nrow = (int64_t)nb * 128 + (p & 127);
       const int kb0 = (int)(j0 % KB);
       codes = rb + a.off_w[piece] + nrow * (a.K / 2) + kb0 * 32;
       sc = (const uint16_t*)(rb + a.off_s[piece]) + nrow * ng + kb0;
       bi = (const uint16_t*)(rb + a.off_b[piece]) + nrow * ng + kb0;
-      return true;
     };
     auto load = [&](int n, Rows& r) -> bool {
-      const uint8_t* c;
-      const uint16_t *sc, *bi;
-      if (!row_src(n, c, sc, bi)) {
+      advance(n);
+      if (!base_cur) {
 #pragma unroll
         for (int u = 0; u < WG_SS; ++u) r.w[u][0] = r.w[u][1] = make_uint4(0, 0, 0, 0);
         r.s = r.b = make_uint2(0, 0);
         return false;
       }
+      const uint8_t* c;
+      const uint16_t *sc, *bi;
+      row_src(base_cur, n, c, sc, bi);
 #pragma unroll
       for (int u = 0; u < WG_SS; ++u) {
         r.w[u][0] = __ldg(reinterpret_cast<const uint4*>(c + 32 * u));
@@ -255,10 +281,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
       r.b = __ldg(reinterpret_cast<const uint2*>(bi));
       return true;
     };
+    // L2 prefetch of super-step n's 128 B of codes, called right after load(n - 1): within the same tile it uses
+    // that tile's base, in the next tile the next base once it has had a super-step to arrive
     auto prefetch = [&](int n) {
+      const int T = n / SPT, Tl = (n - 1) / SPT, sub_l = (n - 1) % SPT;
+      const uint8_t* rb = T == Tl ? base_cur : (sub_l > MID ? usable(base_nxt) : nullptr);
+      if (!rb) return;
       const uint8_t* c;
       const uint16_t *sc, *bi;
-      if (row_src(n, c, sc, bi)) prefetch_line_l2(c);   // the row's 128 B of codes for that super-step
+      row_src(rb, n, c, sc, bi);
+      prefetch_line_l2(c);
     };
     Rows cur, nxt;
     bool cur_ok = n_ss > 0 ? load(0, cur) : true;
@@ -271,8 +303,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
 #pragma unroll
       for (int u = 0; u < WG_SS; ++u) {
         const int64_t j = (int64_t)n * WG_SS + u;
-        const int s = (int)(j % WG_STAGES);
-        if (my_fail || !mbar_wait_ns(&empty[s], (uint32_t)((j / WG_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
+        const int s = (int)(j % WG_B_STAGES);
+        if (my_fail || !mbar_wait_ns(&empty_b[s], (uint32_t)((j / WG_B_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
           my_fail = 1;
           s_fail = 1;
           continue;

@@ -12,10 +12,11 @@
 // major, so concurrent CTAs share activation rows and expert weights in L2). TMEM holds two accumulator pairs,
 // so the epilogue of tile i overlaps the MMAs of tile i+1, and the operand pipelines run across tile borders.
 // Warp roles (16 warps):
-//  * warp 0      loads the tile's activation rows with TMA: one 2-D box of 128 rows per half when the rows
-//                are contiguous (permuted into expert order beforehand), else lane l gathers rows 4l..4l+3 and
-//                128+4l.. with two tile::gather4 copies; the tensor map applies the 128-byte swizzle. A second
-//                half that holds only padding rows is skipped by every role (not loaded, multiplied or stored);
+//  * warp 0      loads the tile's activation rows with TMA: one 2-D box of 256 rows (128 when the second half
+//                holds only padding rows) when the rows are contiguous (permuted into expert order beforehand),
+//                else lane l gathers rows 4l..4l+3 and 128+4l.. with two tile::gather4 copies; the tensor map
+//                applies the 128-byte swizzle. A second half of only padding rows is skipped by every role (not
+//                loaded on the box path, not multiplied, not stored);
 //  * warp 1      owns TMEM (512 columns) and issues tcgen05.mma (M128 N128 K16, eight per 64-wide k-block);
 //  * warps 4..7  epilogue: TMEM -> registers -> global, one accumulator row per thread;
 //  * warps 8..15 weight producers, two threads per B-row (one half of the k-block each): stage the packed
@@ -172,8 +173,11 @@ SSB_DEV void scales2(float s, float2* sc2) {
 
 SSB_DEV float silu_fast(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
+SSB_DEV bool gather_path(const GemmArgs& a) { return a.a_box_rows != TM; }
+
 template <int EPI>
-__global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__ CUtensorMap tm_a, GemmArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__ CUtensorMap tm_a,
+                                                          const __grid_constant__ CUtensorMap tm_h, GemmArgs a) {
   extern __shared__ uint8_t smraw[];
   Smem S = carve(smraw);
   __shared__ int s_fail;
@@ -198,12 +202,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
   // does the second 128-row half of 256-row block mb hold any row? moe_align puts an expert's rows first and its
   // padding after them, so the half is all padding when its first row is (identity rows: when it is past R); such a
   // half is neither loaded (box path), multiplied nor stored
-  auto half1_of = [&](int64_t mb) -> bool {
+  // (the single MMA thread fetches the next tile's answer a tile ahead as a raw row id and tests it only when that
+  // tile starts, so the load's latency never stalls the issue of MMAs)
+  auto half1_row = [&](int64_t mb) -> int64_t {
     const int64_t m1 = mb * TM + BM;
-    if (!a.sorted_rows) return m1 < a.R;
-    const int32_t r = __ldcg(a.sorted_rows + m1);
-    return r >= 0 && r < a.R;
+    return a.sorted_rows ? (int64_t)__ldcg(a.sorted_rows + m1) : m1;
   };
+  auto half1_ok = [&](int64_t r) -> bool { return r >= 0 && r < a.R; };
+  auto half1_of = [&](int64_t mb) -> bool { return half1_ok(half1_row(mb)); };
 
   if (tid == 0) {
     s_fail = 0;
@@ -246,10 +252,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       }
     };
     int64_t issued = 0;
-    if (lane == 0) prefetch_tensormap(&tm_a);
+    if (lane == 0) {
+      prefetch_tensormap(&tm_a);
+      if (!gather_path(a)) prefetch_tensormap(&tm_h);
+    }
     const bool gather = a.a_box_rows != TM;
     int64_t h_tile = -1;
-    bool two = true, two_next = true;   // box path: the second half of this tile (of the next) is loaded
+    bool two = true;                    // box path: the second half of this tile is loaded
+    int64_t r_next = 0;                 // first row of the next tile's second half
     if (gather) {
       load_rows(0);
       to_coords();
@@ -278,16 +288,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       }
       if (!gather && i != h_tile && lane == 0) {   // the next tile's answer is fetched a tile ahead
         h_tile = i;
-        two = i == 0 ? half1_of(tile_of(0) / NB) : two_next;
-        if (i + 1 < my_tiles) two_next = half1_of(tile_of(i + 1) / NB);
+        two = i == 0 ? half1_of(tile_of(0) / NB) : half1_ok(r_next);
+        if (i + 1 < my_tiles) r_next = half1_row(tile_of(i + 1) / NB);
       }
       if (lane == 0) mbar_expect_tx(&S.full_a[s], gather || two ? A_STAGE : A_HALF);
       __syncwarp();
       if (!gather) {   // rows tile*256 .. +255 (or +127) of the activation matrix, one 128-row box per half
         if (lane == 0) {
           const int32_t r0 = (int32_t)((tile_of(i) / NB) * TM);
-          tma_load_2d(smem_u32(S.a + s * A_STAGE), &tm_a, kb * BK, r0, &S.full_a[s]);
-          if (two) tma_load_2d(smem_u32(S.a + s * A_STAGE + A_HALF), &tm_a, kb * BK, r0 + BM, &S.full_a[s]);
+          // both halves in one 256-row box (measurably faster than two 128-row boxes), else the first half alone
+          tma_load_2d(smem_u32(S.a + s * A_STAGE), two ? &tm_a : &tm_h, kb * BK, r0, &S.full_a[s]);
         }
       } else {
         tma_gather4(smem_u32(S.a + s * A_STAGE + lane * 512), &tm_a, kb * BK, rc[0], rc[1], rc[2], rc[3],
@@ -307,10 +317,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(BM, BN);
       int64_t j = 0;
-      int nh_next = half1_of(tile_of(0) / NB) ? MT : 1;
+      int64_t r_next = half1_row(tile_of(0) / NB);
       for (int i = 0; i < my_tiles && !s_fail; ++i) {
-        const int nh = nh_next;   // halves of this tile; the next tile's count is fetched a tile ahead
-        if (i + 1 < my_tiles) nh_next = half1_of(tile_of(i + 1) / NB) ? MT : 1;
+        const int nh = half1_ok(r_next) ? MT : 1;   // halves of this tile (its row fetched a tile ahead)
+        if (i + 1 < my_tiles) r_next = half1_row(tile_of(i + 1) / NB);
         const int acc = i & 1;
         if (!mbar_wait_ns(&S.tmem_empty[acc], ((i >> 1) & 1) ^ 1, SSB_WAIT_NS)) {
           s_fail = 1;
@@ -782,16 +792,16 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
-// 2-D tensor map over the activation rows: K elements x a_rows rows, box 64 x 1 (gathered rows) or 64 x 128 (one
-// half of a 256-row block), 128-byte swizzle.
-int encode_a_map(CUtensorMap* map, const GemmArgs& a) {
+// 2-D tensor map over the activation rows: K elements x a_rows rows, box 64 x box_rows, 128-byte swizzle: box_rows 1
+// (gathered rows), TM (a 256-row block) or BM (its first half alone, when the second holds only padding).
+int encode_a_map(CUtensorMap* map, const GemmArgs& a, int box_rows) {
   if (((uintptr_t)a.a & 15) || (a.lda * 2) % 16 || a.a_rows < 1 || a.a_rows > 0x7fffffffLL) return SSB_EINVAL;
   if (a.a_box_rows != 1 && a.a_box_rows != TM) return SSB_EINVAL;
   EncodeTiledFn encode = encode_tiled_fn();
   if (!encode) return SSB_ENODEVICE;
   cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.a_rows};
   cuuint64_t strides[1] = {(cuuint64_t)a.lda * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)(a.a_box_rows == TM ? BM : 1)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)a.a, dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -800,12 +810,13 @@ int encode_a_map(CUtensorMap* map, const GemmArgs& a) {
 }
 
 int launch(int epi, GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t st) {
-  void (*k)(CUtensorMap, GemmArgs) = epi == EPI_SWIGLU ? k_moe_gemm<EPI_SWIGLU>
+  void (*k)(CUtensorMap, CUtensorMap, GemmArgs) = epi == EPI_SWIGLU ? k_moe_gemm<EPI_SWIGLU>
                                      : epi == EPI_SCALE ? k_moe_gemm<EPI_SCALE>
                                                         : k_moe_gemm<EPI_PLAIN>;
   if (n_mblocks <= 0) return SSB_OK;
-  CUtensorMap tm;
-  int rc = encode_a_map(&tm, a);
+  CUtensorMap tm, tmh;
+  int rc = encode_a_map(&tm, a, a.a_box_rows);
+  if (!rc) rc = encode_a_map(&tmh, a, a.a_box_rows == TM ? BM : 1);
   if (rc) return rc;
   static bool attr_set[3] = {false, false, false};
   if (!attr_set[epi]) {
@@ -821,7 +832,7 @@ int launch(int epi, GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream_t s
   int ctas = num_sms() - g_sm_reserve;
   if (ctas < 1) ctas = 1;
   const int grid = (int)(tiles < ctas ? tiles : ctas);
-  return ssb_launch(k, dim3(grid), dim3(THREADS), SMEM_BYTES, st, true, tm, a);
+  return ssb_launch(k, dim3(grid), dim3(THREADS), SMEM_BYTES, st, true, tm, tmh, a);
 }
 
 // k_gate_up_wide over the sorted rows (x permuted into expert order, gs 64): tiles of 256 rows x 128 h columns.
@@ -830,8 +841,9 @@ int launch_gate_up_wide(GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream
   if (a.gs != 64 || !a.kperm || !a.out_sorted || a.a_box_rows != TM || !a.sorted_rows || !a.num_padded ||
       !a.block_expert || !a.group_base)
     return SSB_EINVAL;
-  CUtensorMap tm;
-  int rc = encode_a_map(&tm, a);
+  CUtensorMap tm, tmh;
+  int rc = encode_a_map(&tm, a, TM);
+  if (!rc) rc = encode_a_map(&tmh, a, BM);
   if (rc) return rc;
   static bool attr_set = false;
   if (!attr_set) {
@@ -846,7 +858,7 @@ int launch_gate_up_wide(GemmArgs a, int64_t n_mblocks, int n_nblocks, cudaStream
   int ctas = num_sms() - g_sm_reserve;
   if (ctas < 1) ctas = 1;
   const int grid = (int)(tiles < ctas ? tiles : ctas);
-  return ssb_launch(k_gate_up_wide, dim3(grid), dim3(THREADS), WG_SMEM_BYTES, st, true, tm, a);
+  return ssb_launch(k_gate_up_wide, dim3(grid), dim3(THREADS), WG_SMEM_BYTES, st, true, tm, tmh, a);
 }
 
 void set_record_offsets(GemmArgs& g, int hidden, int inter, bool gate_up) {

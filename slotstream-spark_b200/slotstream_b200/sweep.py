@@ -26,8 +26,12 @@ from .kernels.moe_align import moe_align, padded_rows
 
 EXPERTS = 512
 GROUP_SIZE = 32       # experts per group (engine/sweep.py:18)
-STAGING_GROUPS = 4    # staging buffers of GROUP_SIZE records (model/moe_sweep.py:25)
-INFLIGHT = 2          # staged groups issued ahead of the one being computed (model/moe_sweep.py:26)
+# Staging: the reference keeps 4 buffers of 32 records with 2 groups in flight (model/moe_sweep.py:25-26) for its
+# unified memory. On a B200 eight buffers are 453 MB of the 180 GB (2048/512 records), enough for every staged
+# record of a layer whose hottest half is resident, so all of a layer's copies are issued at once and the copy
+# engine streams them back to back while the resident groups compute.
+STAGING_GROUPS = 8    # staging buffers of GROUP_SIZE records
+INFLIGHT = 8          # staged groups issued ahead of the one being computed
 
 
 @dataclass(frozen=True)
