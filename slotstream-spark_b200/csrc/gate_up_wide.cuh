@@ -195,22 +195,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
             tmem_ld32(taddr + 128 + 32 * cc, u);
             if (valid[h]) {
               uint4* dst = reinterpret_cast<uint4*>(out + m * a.ldo + (int64_t)nb * 128 + 32 * cc);
+              uint4 pk[4];
+              if (shared_e) swiglu32<true>(g, u, true, pk);
+              else swiglu32<false>(g, u, true, pk);
 #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                float hv[8];
-#pragma unroll
-                for (int tt = 0; tt < 8; ++tt) {
-                  const float gg = g[8 * jj + tt], uu = u[8 * jj + tt];
-                  if (shared_e) {   // shared expert: bf16(silu(bf16 g)) * bf16 u (model/moe_sweep.py:37-43)
-                    const float gb = round_bf16(gg);
-                    hv[tt] = round_bf16(gb / (1.f + expf(-gb))) * round_bf16(uu);
-                  } else {
-                    hv[tt] = silu_fast(gg) * uu;   // accg / (1 + exp(-accg)) * accu, kernels/fused_moe_affine.py:80
-                  }
-                }
-                dst[jj] = make_uint4(cvt_bf16x2(hv[0], hv[4]), cvt_bf16x2(hv[1], hv[5]), cvt_bf16x2(hv[2], hv[6]),
-                                     cvt_bf16x2(hv[3], hv[7]));
-              }
+              for (int jj = 0; jj < 4; ++jj) dst[jj] = pk[jj];
             }
           }
         }

@@ -173,6 +173,33 @@ SSB_DEV void scales2(float s, float2* sc2) {
 
 SSB_DEV float silu_fast(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
+// h = silu(g) * u for 32 accumulator columns -> 32 bf16 in four uint4, in the K order (0,4,1,5,2,6,3,7) of every
+// 8 (KPERM) or in column order. SHARED: the shared expert's chain bf16(silu(bf16 g)) * bf16 u (model/moe_sweep.py:
+// 37-43); routed rows: accg / (1 + exp(-accg)) * accu (kernels/fused_moe_affine.py:80). The two are separate
+// instantiations so that a routed tile carries none of the shared chain's instructions (an exact expf and an IEEE
+// division per element, which a per-element select would otherwise execute for every tile).
+template <bool SHARED>
+SSB_DEV void swiglu32(const float* g, const float* u, bool kperm, uint4* out4) {
+  float hv[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (SHARED) {
+      const float gb = round_bf16(g[i]);
+      hv[i] = round_bf16(gb / (1.f + expf(-gb))) * round_bf16(u[i]);
+    } else {
+      hv[i] = silu_fast(g[i]) * u[i];
+    }
+  }
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const float* v = hv + 8 * jj;
+    out4[jj] = kperm ? make_uint4(cvt_bf16x2(v[0], v[4]), cvt_bf16x2(v[1], v[5]), cvt_bf16x2(v[2], v[6]),
+                                  cvt_bf16x2(v[3], v[7]))
+                     : make_uint4(cvt_bf16x2(v[0], v[1]), cvt_bf16x2(v[2], v[3]), cvt_bf16x2(v[4], v[5]),
+                                  cvt_bf16x2(v[6], v[7]));
+  }
+}
+
 SSB_DEV bool gather_path(const GemmArgs& a) { return a.a_box_rows != TM; }
 
 template <int EPI>
@@ -398,24 +425,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
             if (valid) {
               uint4* dst =
                   reinterpret_cast<uint4*>(out + (a.out_sorted ? m : row) * a.ldo + (int64_t)nb * (BN / 2) + col);
+              uint4 pk[4];
+              if (shared_e) swiglu32<true>(g, u, a.kperm, pk);
+              else swiglu32<false>(g, u, a.kperm, pk);
 #pragma unroll
-              for (int jj = 0; jj < 4; ++jj) {
-                float hv[8];
-#pragma unroll
-                for (int tt = 0; tt < 8; ++tt) {
-                  const float gg = g[8 * jj + tt], uu = u[8 * jj + tt];
-                  if (shared_e) {   // shared expert: bf16(silu(bf16 g)) * bf16 u (model/moe_sweep.py:37-43)
-                    const float gb = round_bf16(gg);
-                    hv[tt] = round_bf16(gb / (1.f + expf(-gb))) * round_bf16(uu);
-                  } else {
-                    hv[tt] = silu_fast(gg) * uu;   // accg / (1 + exp(-accg)) * accu, kernels/fused_moe_affine.py:80
-                  }
-                }
-                dst[jj] = a.kperm ? make_uint4(cvt_bf16x2(hv[0], hv[4]), cvt_bf16x2(hv[1], hv[5]),
-                                               cvt_bf16x2(hv[2], hv[6]), cvt_bf16x2(hv[3], hv[7]))
-                                  : make_uint4(cvt_bf16x2(hv[0], hv[1]), cvt_bf16x2(hv[2], hv[3]),
-                                               cvt_bf16x2(hv[4], hv[5]), cvt_bf16x2(hv[6], hv[7]));
-              }
+              for (int jj = 0; jj < 4; ++jj) dst[jj] = pk[jj];
             }
           }
         } else {
