@@ -91,25 +91,36 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
     if (lane == 0) {
       prefetch_tensormap(&tm_a);
       prefetch_tensormap(&tm_h);
+      // step counters kept incrementally (no 64-bit division on the issue path)
       int64_t issued = 0;
       bool two = half1_of(tile_of(0) / NB);
       int32_t r_next = 0;
+      int kb = 0, i = 0, s = 0;
+      uint32_t ph = 0;
+      int32_t r0 = (int32_t)((tile_of(0) / NB) * TM);
       for (int64_t j = 0; j < steps; ++j) {
-        const int kb = (int)(j % KB);
-        const int i = (int)(j / KB);
         if (kb == 0) {
-          if (i > 0) two = half1_ok(r_next);
+          if (i > 0) {
+            two = half1_ok(r_next);
+            r0 = (int32_t)((tile_of(i) / NB) * TM);
+          }
           if (i + 1 < my_tiles) r_next = half1_row(tile_of(i + 1) / NB);
         }
-        const int s = (int)(j % WG_A_STAGES);
-        if (!mbar_wait_ns(&empty_a[s], (uint32_t)((j / WG_A_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
+        if (!mbar_wait_ns(&empty_a[s], ph ^ 1, SSB_WAIT_NS)) {
           s_fail = 1;
           break;
         }
         mbar_expect_tx(&full_a[s], two ? WG_A_STAGE : A_HALF);
-        const int32_t r0 = (int32_t)((tile_of(i) / NB) * TM);
         tma_load_2d(smem_u32(sa + s * WG_A_STAGE), two ? &tm_a : &tm_h, kb * BK, r0, &full_a[s]);   // 256 or 128 rows
         ++issued;
+        if (++s == WG_A_STAGES) {
+          s = 0;
+          ph ^= 1;
+        }
+        if (++kb == KB) {
+          kb = 0;
+          ++i;
+        }
       }
       // no copy may still be writing shared memory when the CTA exits
       for (int64_t j = issued > WG_A_STAGES ? issued - WG_A_STAGES : 0; j < issued; ++j)
@@ -223,35 +234,40 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
     };
     // Record base per tile, fetched ahead so that no load of a super-step waits on a dependent chain: the expert
     // of tile T+1 is read when tile T's loads start, its base in the middle of tile T, and it is checked when
-    // tile T+1 starts. (A tile's super-steps are SPT consecutive super-steps; KB is a multiple of WG_SS.)
+    // tile T+1 starts. The loader walks super-steps in order with 32-bit counters (a tile is SPT consecutive
+    // super-steps; KB is a multiple of WG_SS), so no division runs per super-step.
     const int SPT = KB / WG_SS, MID = SPT / 2;
     auto expert_at = [&](int i) -> int32_t { return __ldcg(a.block_expert + tile_of(i) / NB); };
     auto base_raw = [&](int32_t e) -> const uint8_t* {
       return (e >= 0 && e < a.n_groups) ? (const uint8_t*)__ldg(a.group_base + e) : nullptr;
     };
     auto usable = [](const uint8_t* rb) -> const uint8_t* { return ((uintptr_t)rb & 15) ? nullptr : rb; };
-    const uint8_t* base_cur = nullptr;   // checked base of the tile whose super-step was loaded last
-    const uint8_t* base_nxt = nullptr;   // raw base of the tile after it (from the middle of the current tile)
+    auto nb_at = [&](int i) -> int { return (int)(((uint32_t)blockIdx.x + (uint32_t)i * gridDim.x) % (uint32_t)NB); };
+    const uint8_t* base_cur = nullptr;   // checked base of the tile being loaded
+    const uint8_t* base_nxt = nullptr;   // raw base of the next tile (from the middle of the current one)
     int32_t e_nxt = -1;
-    auto advance = [&](int n) {          // before loading super-step n; n = 0, 1, 2, ... in order
-      const int T = n / SPT, sub = n % SPT;
-      if (sub == 0) {
-        base_cur = T == 0 ? usable(base_raw(expert_at(0))) : usable(base_nxt);
-        if (T + 1 < my_tiles) e_nxt = expert_at(T + 1);
+    int ld_T = 0, ld_sub = -1, nb_cur = 0, nb_nxt = 0;
+    const int64_t piece_w = a.off_w[piece], piece_s = a.off_s[piece], piece_b = a.off_b[piece];
+    auto row_src = [&](const uint8_t* rb, int nb, int sub, const uint8_t*& codes, const uint16_t*& sc,
+                       const uint16_t*& bi) {
+      const int nrow = nb * 128 + (p & 127);
+      const int kb0 = sub * WG_SS;
+      codes = rb + piece_w + (int64_t)nrow * (a.K / 2) + kb0 * 32;
+      sc = (const uint16_t*)(rb + piece_s) + (int64_t)nrow * ng + kb0;
+      bi = (const uint16_t*)(rb + piece_b) + (int64_t)nrow * ng + kb0;
+    };
+    auto load = [&](Rows& r) -> bool {   // the next super-step in order
+      if (++ld_sub == SPT || ld_sub == 0) {
+        if (ld_sub == SPT) ++ld_T;
+        ld_sub = 0;
+        base_cur = ld_T == 0 ? usable(base_raw(expert_at(0))) : usable(base_nxt);
+        nb_cur = ld_T == 0 ? nb_at(0) : nb_nxt;
+        if (ld_T + 1 < my_tiles) {
+          e_nxt = expert_at(ld_T + 1);
+          nb_nxt = nb_at(ld_T + 1);
+        }
       }
-      if (sub == MID && T + 1 < my_tiles) base_nxt = base_raw(e_nxt);
-    };
-    auto row_src = [&](const uint8_t* rb, int n, const uint8_t*& codes, const uint16_t*& sc, const uint16_t*& bi) {
-      const int64_t j0 = (int64_t)n * WG_SS;
-      const int nb = (int)(tile_of((int)(j0 / KB)) % NB);
-      const int64_t nrow = (int64_t)nb * 128 + (p & 127);
-      const int kb0 = (int)(j0 % KB);
-      codes = rb + a.off_w[piece] + nrow * (a.K / 2) + kb0 * 32;
-      sc = (const uint16_t*)(rb + a.off_s[piece]) + nrow * ng + kb0;
-      bi = (const uint16_t*)(rb + a.off_b[piece]) + nrow * ng + kb0;
-    };
-    auto load = [&](int n, Rows& r) -> bool {
-      advance(n);
+      if (ld_sub == MID && ld_T + 1 < my_tiles) base_nxt = base_raw(e_nxt);
       if (!base_cur) {
 #pragma unroll
         for (int u = 0; u < WG_SS; ++u) r.w[u][0] = r.w[u][1] = make_uint4(0, 0, 0, 0);
@@ -260,7 +276,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
       }
       const uint8_t* c;
       const uint16_t *sc, *bi;
-      row_src(base_cur, n, c, sc, bi);
+      row_src(base_cur, nb_cur, ld_sub, c, sc, bi);
 #pragma unroll
       for (int u = 0; u < WG_SS; ++u) {
         r.w[u][0] = __ldg(reinterpret_cast<const uint4*>(c + 32 * u));
@@ -270,30 +286,44 @@ __global__ void __launch_bounds__(THREADS, 1) k_gate_up_wide(const __grid_consta
       r.b = __ldg(reinterpret_cast<const uint2*>(bi));
       return true;
     };
-    // L2 prefetch of super-step n's 128 B of codes, called right after load(n - 1): within the same tile it uses
-    // that tile's base, in the next tile the next base once it has had a super-step to arrive
-    auto prefetch = [&](int n) {
-      const int T = n / SPT, Tl = (n - 1) / SPT, sub_l = (n - 1) % SPT;
-      const uint8_t* rb = T == Tl ? base_cur : (sub_l > MID ? usable(base_nxt) : nullptr);
+    // L2 prefetch of the super-step after the one just loaded: in the same tile with that tile's base, in the
+    // next tile with the next base once it has had a super-step to arrive
+    auto prefetch = [&]() {
+      const uint8_t* rb;
+      int nb, sub;
+      if (ld_sub + 1 < SPT) {
+        rb = base_cur, nb = nb_cur, sub = ld_sub + 1;
+      } else {
+        if (ld_T + 1 >= my_tiles || ld_sub <= MID) return;
+        rb = usable(base_nxt), nb = nb_nxt, sub = 0;
+      }
       if (!rb) return;
       const uint8_t* c;
       const uint16_t *sc, *bi;
-      row_src(rb, n, c, sc, bi);
+      row_src(rb, nb, sub, c, sc, bi);
       prefetch_line_l2(c);
     };
     Rows cur, nxt;
-    bool cur_ok = n_ss > 0 ? load(0, cur) : true;
-    if (n_ss > 1) prefetch(1);
+    bool cur_ok = n_ss > 0 ? load(cur) : true;
+    if (n_ss > 1) prefetch();
+    int bs = 0;            // B stage of the next k-block, and its phase
+    uint32_t bph = 0;
     for (int n = 0; n < n_ss; ++n) {
       bool nxt_ok = true;
-      if (n + 1 < n_ss) nxt_ok = load(n + 1, nxt);
-      if (n + 2 < n_ss) prefetch(n + 2);
-      if (!cur_ok && p == 0 && (((int64_t)n * WG_SS) % KB) == 0) set_err(a.err, SSB_ERR_MISALIGNED);
+      if (n + 1 < n_ss) {
+        nxt_ok = load(nxt);
+        if (n + 2 < n_ss) prefetch();
+      }
+      if (!cur_ok && p == 0 && n % SPT == 0) set_err(a.err, SSB_ERR_MISALIGNED);
 #pragma unroll
       for (int u = 0; u < WG_SS; ++u) {
-        const int64_t j = (int64_t)n * WG_SS + u;
-        const int s = (int)(j % WG_B_STAGES);
-        if (my_fail || !mbar_wait_ns(&empty_b[s], (uint32_t)((j / WG_B_STAGES) & 1) ^ 1, SSB_WAIT_NS)) {
+        const int s = bs;
+        const uint32_t cur_ph = bph;
+        if (++bs == WG_B_STAGES) {
+          bs = 0;
+          bph ^= 1;
+        }
+        if (my_fail || !mbar_wait_ns(&empty_b[s], cur_ph ^ 1, SSB_WAIT_NS)) {
           my_fail = 1;
           s_fail = 1;
           continue;

@@ -291,9 +291,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       load_rows(0);
       to_coords();
     }
+    int kb = 0, i = 0;   // k-block and tile of step j, kept incrementally (no 64-bit division per step)
+    int32_t r0 = 0;
     for (int64_t j = 0; j < steps; ++j) {
-      const int kb = (int)(j % KB);
-      const int i = (int)(j / KB);
+      if (kb == 0) r0 = (int32_t)((tile_of(i) / NB) * TM);
       if (!gather) {
       } else if (kb == 0) {
 #pragma unroll
@@ -322,7 +323,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       __syncwarp();
       if (!gather) {   // rows tile*256 .. +255 (or +127) of the activation matrix, one 128-row box per half
         if (lane == 0) {
-          const int32_t r0 = (int32_t)((tile_of(i) / NB) * TM);
           // both halves in one 256-row box (measurably faster than two 128-row boxes), else the first half alone
           tma_load_2d(smem_u32(S.a + s * A_STAGE), two ? &tm_a : &tm_h, kb * BK, r0, &S.full_a[s]);
         }
@@ -333,6 +333,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
                     &S.full_a[s]);
       }
       ++issued;
+      if (++kb == KB) {
+        kb = 0;
+        ++i;
+      }
     }
     // no copy may still be writing shared memory when the CTA exits: wait for the last stages to land
     if (lane == 0)
@@ -548,13 +552,38 @@ __global__ void __launch_bounds__(THREADS, 1) k_moe_gemm(const __grid_constant__
       const void* dummy = a.a;                // valid address for zero-byte copies (rows of an unusable expert)
       uint32_t slot_ok = 0;                   // bit (n & 1): super-step n's expert has a usable record
       int my_fail = 0;
+      // The super-steps are issued in order; their tile, k-block and n-block follow from 32-bit counters, and the
+      // next tile's record base is fetched ahead (its expert when a tile's first super-step is issued, its base in
+      // the middle of the tile), so no issue waits on a division or on the dependent block_expert -> base chain.
+      const int SPT = KB / ss, MID = SPT / 2;
+      int is_T = 0, is_sub = -1, is_nb = 0, nb_nxt = 0;
+      int32_t e_nxt = -1;
+      const uint8_t* base_nxt = nullptr;
+      auto nb_at = [&](int i) -> int { return (int)(((uint32_t)blockIdx.x + (uint32_t)i * gridDim.x) % (uint32_t)NB); };
+      auto base_raw = [&](int e) -> const uint8_t* {
+        if (e < 0 || e >= a.n_groups) return nullptr;
+        return a.group_base ? (const uint8_t*)__ldg(a.group_base + e) : a.base0;
+      };
+      auto usable = [](const uint8_t* b) -> const uint8_t* { return ((uintptr_t)b & 15) ? nullptr : b; };
+      auto advance = [&]() {
+        if (++is_sub == SPT || is_sub == 0) {
+          if (is_sub == SPT) ++is_T;
+          is_sub = 0;
+          t_base = is_T == 0 ? usable(base_raw(expert_of(tile_of(0) / NB))) : usable(base_nxt);
+          is_nb = is_T == 0 ? nb_at(0) : nb_nxt;
+          t_nrow = (EPI == EPI_SWIGLU) ? (int64_t)is_nb * (BN / 2) + (br & (BN / 2 - 1)) : (int64_t)is_nb * BN + br;
+          if (is_T + 1 < my_tiles) {
+            e_nxt = expert_of(tile_of(is_T + 1) / NB);
+            nb_nxt = nb_at(is_T + 1);
+          }
+        }
+        if (is_sub == MID && is_T + 1 < my_tiles) base_nxt = base_raw(e_nxt);
+      };
       auto issue_ss = [&](int n) {
-        const int64_t j0 = (int64_t)n * ss;
-        tile_info(j0);
-        const int kb0 = (int)(j0 % KB);
+        advance();
+        const int kb0 = is_sub * ss;
         uint8_t* st = S.stg + (n & 1) * STG;
-        const int64_t t = tile_of((int)(j0 / KB));
-        const int nb = (int)(t % NB);
+        const int nb = is_nb;
 #pragma unroll
         for (int i = 0; i < SS; ++i) {
           if (i >= ss) break;
