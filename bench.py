@@ -591,7 +591,8 @@ def bench_prefill(args, world, rank, cpu_passes=None):
     dn_flop = 2.0 * bufs.rows * LAY.inter * LAY.hidden
     pk = peaks()
     gu_tf = gu_flop / (gu_ms * 1e-3) / 1e12
-    roofline = {"bound": "tensor", "kernel": "fused_moe gate_up (tcgen05 grouped GEMM, SwiGLU epilogue)",
+    roofline = {"bound": "tensor", "kernel": "fused_moe gate_up (k_gate_up_wide: tcgen05 M128xN256 grouped GEMM, "
+                                              "256 x (128 gate + 128 up) tiles, SwiGLU epilogue)",
                 "achieved": round(gu_tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(gu_tf / pk["bf16_tflops"], 4), "peak_source": pk["source"] + " (burst)",
                 "traffic": TRAFFIC_BYTES.get(f"prefill_gate_up_{T}") if args.routing == "zipf" else None,
@@ -953,9 +954,9 @@ def bench_prefill_ep(args, world, rank):
                    "l2": "flushed before every step (256 MiB write); inputs > L2", "parallelism": f"ep{world}"},
         "tflops_per_gpu": round(tf, 1), "roofline": roofline, "phases": phases, "parity": parity,
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 4),
-                "h2d_bytes_per_step": T * LAY.hidden * 2, "d2h_bytes_per_step": T * LAY.hidden * 2,
-                "schedule": "double-buffered: each step's x H2D and y D2H on copy streams beside the neighbouring "
-                            "steps' compute (per rank)"},
+                "h2d_bytes_per_step": world * T * LAY.hidden * 2, "d2h_bytes_per_step": world * T * LAY.hidden * 2,
+                "schedule": "double-buffered on every rank: each step's x H2D and y D2H on copy streams beside the "
+                            "neighbouring steps' compute (bytes summed over the ranks)"},
         "gpu_launches": launches * args.steps, "clocks": clocks, "device_errors": errs,
     }
     if alt is not None:
