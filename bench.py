@@ -41,7 +41,7 @@ L2_FLUSH_BYTES = 256 << 20
 # dram__bytes_write.sum, one replay pass) on earlier runs of these same workloads, not in this run
 TRAFFIC_BYTES = {
     "prefill_gate_up_32768": 2_360_000_000 + 357_240_000,   # one gate_up launch of the 32,768-token layer
-    "prefill_gate_up_8192": 745_336_832 + 84_327_424,       # one gate_up launch of the 8,192-token layer
+    "prefill_gate_up_8192": 654_045_440 + 88_479_744,       # one gate_up launch of the 8,192-token layer
     "decode_fused_b1": 21_684_736,                          # one fused b = 1 decode layer launch
 }
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, measured on an earlier run of " \
