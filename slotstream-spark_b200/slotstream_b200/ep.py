@@ -308,8 +308,10 @@ class CudaOps:
                       torch.empty(n_entries, dtype=torch.int32, device=dev),
                       torch.empty(n_entries, dtype=torch.float32, device=dev),
                       torch.empty(n, dtype=torch.int64, device=dev), torch.empty(n, dtype=torch.int32, device=dev))
-        ro = torch.tensor(src_row_off, dtype=torch.int32).to(dev, non_blocking=True)
-        eo = torch.tensor(src_entry_off, dtype=torch.int64).to(dev, non_blocking=True)
+        # offsets through pinned host memory: a copy from pageable memory blocks the host until a copy engine
+        # takes it, behind whatever large transfer (the next step's activations) that engine is running
+        ro = torch.tensor(src_row_off, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        eo = torch.tensor(src_entry_off, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         P = _lib.ptr
         _lib.check(_lib.lib().ssb_ep_unpack(P(meta), n, self.k, P(ro), P(eo), self.G, n_entries, P(ent.row_expert),
                                             P(ent.row_token), P(ent.row_weight), P(ent.row_e0), P(ent.row_cnt),
@@ -335,7 +337,7 @@ class CudaOps:
         dev = ids.device
         self.routed = torch.empty((t, self.hidden), dtype=torch.float32, device=dev)
         y = torch.empty((t, self.hidden), dtype=torch.bfloat16, device=dev)
-        reo = (torch.tensor(ret_entry_off, dtype=torch.int64).to(dev, non_blocking=True)
+        reo = (torch.tensor(ret_entry_off, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
                if ret_entry_off is not None else None)
         if self._sh_ready is not None:
             torch.cuda.current_stream().wait_event(self._sh_ready)   # the shared expert's rows (side stream)
