@@ -86,6 +86,18 @@ def _check_counts(counts, k, direction):
                                     f"{ent} entries (k = {k})")
 
 
+def _host_read(t: torch.Tensor) -> list:
+    """The values of a small tensor on the host. A CUDA tensor goes through pinned memory on the current stream and
+    a wait on that stream alone: a copy into pageable memory would queue behind whatever large device-to-host
+    transfer (the previous step's output) the copy engine is running."""
+    if not t.is_cuda:
+        return t.tolist()
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+    return h.tolist()
+
+
 def ep_forward(ops, x: torch.Tensor, k: int, n_ranks: int, group=None, exact: bool = False,
                micro_batches: int = 1, partials_bf16: bool = False, phases: list | None = None):
     """One expert-parallel MoE layer over this rank's tokens x [T, H] -> y bf16 [T, H].
@@ -138,7 +150,7 @@ def _ep_forward(ops, x, k, G, group, exact, m, bf16, phases=None):
     send_counts = torch.stack([p.dest_count for p in plans], dim=1).contiguous()   # [G, m, 2]: per destination
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts.view(-1), send_counts.view(-1), group=group)
-    both = torch.cat([send_counts.view(-1), recv_counts.view(-1)]).cpu().tolist()   # the one host sync
+    both = _host_read(torch.cat([send_counts.view(-1), recv_counts.view(-1)]))   # the one host sync
     half = G * m * 2
     sc = [[both[(d * m + i) * 2:(d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
     rc = [[both[half + (d * m + i) * 2:half + (d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]

@@ -10,8 +10,9 @@ the group being computed; events order every reuse of a buffer after the kernels
 
 On the device the layer is one router, one align whose expert map numbers the experts in plan order (so each
 group's rows are a contiguous run of 256-row blocks), one permute of the activation rows into that order, then per
-group the tcgen05 gate_up and down launches over the group's blocks, the shared expert's blocks last, and one
-rank-order combine with the shared add. A row's result depends only on that row and its expert's bytes, so the
+group the tcgen05 gate_up and down launches over the group's blocks (resident groups, then the shared expert,
+whose blocks close the layout, then the staged groups as their copies land), and one rank-order combine with the
+shared add. A row's result depends only on that row and its expert's bytes, so the
 layer equals the all-resident ``moe_layer_prefill`` bit for bit whatever the residency, the grouping or the staging
 buffer.
 """
@@ -114,8 +115,8 @@ class PrefillSweep:
     ``plan_groups``; then ONE align over all rows with local expert ids in plan order (so every group's rows form
     a contiguous run of 256-row blocks), ONE permute of the activation rows into that order, and per group the
     tcgen05 gate_up and down launches over the group's block range, reading its records where they are (HBM for
-    resident experts, a staging buffer for staged ones); the shared expert's blocks come last; one rank-order
-    combine."""
+    resident experts, a staging buffer for staged ones); the shared expert's blocks close the layout and are
+    launched between the resident and the staged groups; one rank-order combine."""
 
     def __init__(self, hidden: int, inter: int, k: int, max_tokens: int, record_bytes: int, *, experts: int = EXPERTS,
                  group_size: int = GROUP_SIZE, staging_groups: int = STAGING_GROUPS, inflight: int = INFLIGHT,
@@ -223,7 +224,11 @@ class PrefillSweep:
                                 out=(b.sorted_rows[:p_len], b.block_expert[:p_len // BLOCK_M], b.num_padded))
         _lib.check(L.ssb_permute_rows(_lib.ptr(x), t, H, _lib.ptr(b.row_token), b.rows, _lib.ptr(sr), _lib.ptr(npd),
                                       p_len, _lib.ptr(b.x_sorted), st), "sweep permute")
-        for gi in range(len(groups) + 1):
+        # launch order: resident groups, the shared expert (its record is resident too), then the staged groups,
+        # so the work that needs no copy runs while the copies cross
+        n_res = sum(1 for g in groups if g.resident)
+        order = list(range(n_res)) + [len(groups)] + list(range(n_res, len(groups)))
+        for gi in order:
             s.groups += 1
             g = groups[gi] if gi < len(groups) else None
             if g is not None and g.resident:
