@@ -25,7 +25,7 @@
 
 constexpr int WG_BN = 256;                            // B-rows per tile: 128 gate + 128 up
 constexpr int WG_A_STAGES = 3;                        // activation stages
-constexpr int WG_B_STAGES = 3;                        // dequantised weight stages (fewer measured slower)
+constexpr int WG_B_STAGES = 4;                        // dequantised weight stages (3: 2% slower, fewer: slower still)
 constexpr int WG_SS = 4;                              // k-blocks per producer super-step
 constexpr uint32_t WG_A_STAGE = TM * 128;             // 32 KB: two 128-row halves
 constexpr uint32_t WG_B_STAGE = WG_BN * 128;          // 32 KB
