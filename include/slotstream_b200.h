@@ -314,6 +314,13 @@ int ssb_signal(const int32_t* ids, const float* w, int32_t n, int32_t* slot_ids,
  * Replaces: Readback.wait / slotio.wait_seq, slotstream_spark/runtime/readback.py:40-46. */
 int ssb_wait_seq(const int64_t* seq, int64_t target, int64_t timeout_ns);
 
+/* Copy `bytes` (at most 16 MiB) with the SMs' own loads and stores on `stream`, between device memory and pinned
+ * host memory (which the GPU addresses directly) or within either. For the small host reads and writes of a
+ * step (counts, offsets) that must not queue on a copy engine behind a large transfer of another stream -- the
+ * previous step's output leaving, the next step's input arriving. Pinned host memory must stay allocated until
+ * the copy has run (a wait on `stream`). No counterpart in the reference (its host reads are synchronous). */
+int ssb_copy_sm(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* Rank-order combine: out[t, :] = rows[t*k] + rows[t*k + 1] + ... sequentially in fp32.
  * rows fp32 [tokens * k, hidden], out fp32 [tokens, hidden]; hidden % 4 == 0.
  * Replaces: combine_rank_order, slotstream_spark/kernels/fused_moe_affine.py:164-172. */

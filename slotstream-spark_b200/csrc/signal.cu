@@ -39,7 +39,35 @@ __global__ void __launch_bounds__(32) k_signal(const int32_t* __restrict__ ids, 
   pdl_trigger();
 }
 
+// Byte copy by the SMs: 16-byte pieces when both ends and the size allow, else bytes; grid-stride.
+__global__ void __launch_bounds__(256) k_copy_sm(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                 int64_t bytes, int vec) {
+  pdl_wait();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (vec) {
+    const int64_t n16 = bytes >> 4;
+    for (int64_t i = i0; i < n16; i += stride)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  } else {
+    for (int64_t i = i0; i < bytes; i += stride) dst[i] = src[i];
+  }
+  pdl_trigger();
+}
+
 }  // namespace
+
+extern "C" int ssb_copy_sm(void* dst, const void* src, int64_t bytes, void* stream) {
+  SSB_CHECK_ARG(bytes >= 0 && bytes <= (int64_t(1) << 24));
+  if (bytes == 0) return SSB_OK;
+  SSB_CHECK_ARG(dst && src);
+  const int vec = ((((uintptr_t)dst | (uintptr_t)src | (uintptr_t)bytes) & 15) == 0) ? 1 : 0;
+  const int64_t units = vec ? bytes / 16 : bytes;
+  const int64_t blocks = (units + 255) / 256;
+  ssb_note_smem("copy_sm", k_copy_sm, 0);
+  return ssb_launch(k_copy_sm, dim3((unsigned)(blocks < 148 ? blocks : 148)), dim3(256), 0, (cudaStream_t)stream, false,
+                    (const uint8_t*)src, (uint8_t*)dst, bytes, vec);
+}
 
 extern "C" int ssb_signal(const int32_t* ids, const float* w, int32_t n, int32_t* slot_ids, float* slot_w, int64_t* seq,
                           const int64_t* ctrl, int32_t layer, void* stream) {

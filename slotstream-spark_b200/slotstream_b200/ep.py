@@ -87,13 +87,15 @@ def _check_counts(counts, k, direction):
 
 
 def _host_read(t: torch.Tensor) -> list:
-    """The values of a small tensor on the host. A CUDA tensor goes through pinned memory on the current stream and
-    a wait on that stream alone: a copy into pageable memory would queue behind whatever large device-to-host
-    transfer (the previous step's output) the copy engine is running."""
+    """The values of a small tensor on the host. A CUDA tensor is copied by the SMs (ssb_copy_sm) into pinned host
+    memory on the current stream, then that stream alone is waited on: a copy-engine transfer would queue behind a
+    large transfer of another stream (the previous step's output leaving), and the host would wait for it."""
     if not t.is_cuda:
         return t.tolist()
+    t = t.contiguous()
     h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-    h.copy_(t, non_blocking=True)
+    _lib.check(_lib.lib().ssb_copy_sm(h.data_ptr(), t.data_ptr(), t.numel() * t.element_size(), _lib.stream()),
+               "counts to host")
     torch.cuda.current_stream().synchronize()
     return h.tolist()
 
@@ -156,6 +158,8 @@ def _ep_forward(ops, x, k, G, group, exact, m, bf16, phases=None):
     rc = [[both[half + (d * m + i) * 2:half + (d * m + i) * 2 + 2] for d in range(G)] for i in range(m)]
     _check_counts(rc, k, "received from")
     _check_counts(sc, k, "sent to")
+    if hasattr(ops, "synced"):
+        ops.synced()   # every kernel of the previous step has run: its pinned host staging may be released
     mark("counts_exchange_and_host_read")
     if phases is not None:
         phases.append(("rows", sum(c[0] for r in rc for c in r), sum(c[1] for r in rc for c in r)))
@@ -228,6 +232,7 @@ class CudaOps:
         dev = w_router.device
         self.shared_ptr = torch.tensor([int(shared_ptr)], dtype=torch.int64, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._held = []            # pinned host staging of the current step (see _to_device)
         self._static = {}
         self._side, self._sh_ready = None, None
         self.sm_reserve = int(sm_reserve)   # SMs left to the collectives while micro-batches overlap
@@ -307,6 +312,20 @@ class CudaOps:
                                           _lib.stream()), "ep plan")
         return p   # sized for the worst case; ep_forward trims to the counts it reads back
 
+    def _to_device(self, h: torch.Tensor) -> torch.Tensor:
+        """A small host array on the device, copied by the SMs from pinned memory (ssb_copy_sm) so that it does not
+        queue on a copy engine behind the next step's activations; the pinned copy is held until the next step's
+        host sync (``synced``) proves the kernel has read it."""
+        hp = h.contiguous().pin_memory()
+        d = torch.empty(hp.shape, dtype=hp.dtype, device=self.group_ptr.device)
+        _lib.check(_lib.lib().ssb_copy_sm(d.data_ptr(), hp.data_ptr(), hp.numel() * hp.element_size(), _lib.stream()),
+                   "offsets to device")
+        self._held.append(hp)
+        return d
+
+    def synced(self):
+        self._held = []
+
     def gather(self, x, idx):
         out = x.new_empty((idx.numel(), x.shape[1]))
         P = _lib.ptr
@@ -322,8 +341,8 @@ class CudaOps:
                       torch.empty(n, dtype=torch.int64, device=dev), torch.empty(n, dtype=torch.int32, device=dev))
         # offsets through pinned host memory: a copy from pageable memory blocks the host until a copy engine
         # takes it, behind whatever large transfer (the next step's activations) that engine is running
-        ro = torch.tensor(src_row_off, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
-        eo = torch.tensor(src_entry_off, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        ro = self._to_device(torch.tensor(src_row_off, dtype=torch.int32))
+        eo = self._to_device(torch.tensor(src_entry_off, dtype=torch.int64))
         P = _lib.ptr
         _lib.check(_lib.lib().ssb_ep_unpack(P(meta), n, self.k, P(ro), P(eo), self.G, n_entries, P(ent.row_expert),
                                             P(ent.row_token), P(ent.row_weight), P(ent.row_e0), P(ent.row_cnt),
@@ -349,8 +368,7 @@ class CudaOps:
         dev = ids.device
         self.routed = torch.empty((t, self.hidden), dtype=torch.float32, device=dev)
         y = torch.empty((t, self.hidden), dtype=torch.bfloat16, device=dev)
-        reo = (torch.tensor(ret_entry_off, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
-               if ret_entry_off is not None else None)
+        reo = self._to_device(torch.tensor(ret_entry_off, dtype=torch.int64)) if ret_entry_off is not None else None
         if self._sh_ready is not None:
             torch.cuda.current_stream().wait_event(self._sh_ready)   # the shared expert's rows (side stream)
         P = _lib.ptr

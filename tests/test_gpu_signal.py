@@ -72,3 +72,24 @@ def test_host_follows_a_captured_decode_step(batch):
                      bias=bias)
     torch.cuda.synchronize()
     assert torch.equal(one.y, step.bufs[NL - 1].y) and torch.equal(one.ids, step.bufs[NL - 1].ids)
+
+
+@pytest.mark.parametrize("nbytes", [0, 7, 16, 4096 + 3, 1 << 20])
+def test_copy_sm_moves_bytes_between_device_and_pinned_host(nbytes):
+    """ssb_copy_sm (the SMs' loads and stores, no copy engine): device -> pinned host, pinned host -> device and
+    device -> device give the bytes back unchanged, aligned and odd sizes alike."""
+    from slotstream_b200 import _lib
+    L, st = _lib.lib(), _lib.stream()
+    src = torch.randint(0, 256, (max(nbytes, 1),), dtype=torch.uint8, device="cuda")[:nbytes]
+    host = torch.full((max(nbytes, 1),), 7, dtype=torch.uint8).pin_memory()[:nbytes]
+    back = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device="cuda")[:nbytes]
+    dd = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device="cuda")[:nbytes]
+    _lib.check(L.ssb_copy_sm(host.data_ptr(), src.data_ptr(), nbytes, st), "d2h")
+    torch.cuda.synchronize()
+    assert torch.equal(host, src.cpu())
+    _lib.check(L.ssb_copy_sm(back.data_ptr(), host.data_ptr(), nbytes, st), "h2d")
+    _lib.check(L.ssb_copy_sm(dd.data_ptr(), back.data_ptr(), nbytes, st), "d2d")
+    torch.cuda.synchronize()
+    assert torch.equal(back, src) and torch.equal(dd, src)
+    assert L.ssb_copy_sm(None, src.data_ptr(), 16, st) == _lib.SSB_EINVAL
+    assert L.ssb_copy_sm(back.data_ptr(), src.data_ptr(), (1 << 24) + 1, st) == _lib.SSB_EINVAL
