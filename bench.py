@@ -784,13 +784,14 @@ def bench_sweep(args, world, rank):
 
 
 # ------------------------------------------------------------------ expert-parallel prefill (configs[3], N > 1)
-def pipelined_eager(x_dev, run, x_host, k, world):
+def pipelined_eager(x_dev, run, x_host, y_host, k, world):
     """ms per step of k eager steps over two buffer sets, as ``pipelined_steps`` but with ``run(b) -> y`` (a layer
     call that may synchronise the host, like the expert-parallel exchange) instead of a graph replay: step i's x
-    H2D goes on a copy stream ahead of its compute and its y D2H on another, overlapping the neighbouring steps."""
+    H2D goes on a copy stream ahead of its compute and its y D2H on another, overlapping the neighbouring steps.
+    ``y_host``: two pinned output buffers allocated by the caller beforehand (a pinned allocation inside the timed
+    loop would cost tens of milliseconds and synchronise the device)."""
     comp = torch.cuda.current_stream()
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    y_host = [None, None]
     ev = lambda: torch.cuda.Event()  # noqa: E731
     ev_in, ev_c, ev_out = [ev() for _ in range(k + 1)], [ev() for _ in range(k)], [ev() for _ in range(k)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -813,8 +814,6 @@ def pipelined_eager(x_dev, run, x_host, k, world):
         comp.wait_event(ev_in[i])
         y = run(b)
         ev_c[i].record(comp)
-        if y_host[b] is None:
-            y_host[b] = torch.empty(y.shape, dtype=y.dtype).pin_memory()
         if i >= 2:
             d2h.wait_event(ev_out[i - 2])
         d2h.wait_event(ev_c[i])
@@ -931,8 +930,9 @@ def bench_prefill_ep(args, world, rank):
         return ep_forward(ops, (x, x2)[b], K, world, micro_batches=args.micro_batches,
                           partials_bf16=args.partials == "bf16")
 
-    pipelined_eager([x, x2], run, x_host, 2, world)   # warm-up of the two-stream schedule
-    e2e_ms = max_over_ranks(pipelined_eager([x, x2], run, x_host, args.steps, world), world)
+    y_host = [torch.empty((T, LAY.hidden), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pipelined_eager([x, x2], run, x_host, y_host, 2, world)   # warm-up of the two-stream schedule
+    e2e_ms = max_over_ranks(pipelined_eager([x, x2], run, x_host, y_host, args.steps, world), world)
     pk = peaks()
     tf = T * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12      # per GPU: each rank's share of the layer's FLOPs
     roofline = {"bound": "tensor", "kernel": "whole expert-parallel layer step per GPU (FLOPs of its tokens)",
