@@ -40,7 +40,7 @@ L2_FLUSH_BYTES = 256 << 20
 # DRAM bytes (read + write) per launch of the dominant kernel: constants measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum, one replay pass) on earlier runs of these same workloads, not in this run
 TRAFFIC_BYTES = {
-    "prefill_gate_up_32768": 2_360_000_000 + 357_240_000,   # one gate_up launch of the 32,768-token layer
+    "prefill_gate_up_32768": 1_853_983_744 + 349_953_280,   # one gate_up launch of the 32,768-token layer
     "prefill_gate_up_8192": 654_045_440 + 88_479_744,       # one gate_up launch of the 8,192-token layer
     "decode_fused_b1": 21_684_736,                          # one fused b = 1 decode layer launch
 }
