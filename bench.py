@@ -259,7 +259,7 @@ def decode_world(args, rank):
 
 
 def bench_decode(args, world, rank, batch=None, W=None, cpu_seconds=None):
-    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+    from slotstream_b200.kernels.moe_layer import DecodeLayerBuffers, decode_layers, moe_layer_decode
     from slotstream_b200.records import BASELINE_LAYOUT as LAY
     NL, E, K = args.layers, 512, 10
     b = batch or args.batch
@@ -270,10 +270,13 @@ def bench_decode(args, world, rank, batch=None, W=None, cpu_seconds=None):
     bias, map_t, slot_ptr, g = W["bias"], W["map_t"], W["slot_ptr"], W["gen"]
     x = torch.randn(NL, b, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
     bufs = [DecodeLayerBuffers(b, K, LAY.hidden, LAY.inter, E, dev) for _ in range(NL)]
+    prefetch = not args.no_decode_prefetch
+    side = torch.cuda.Stream() if prefetch else None
 
     def step():
-        for l in range(NL):
-            moe_layer_decode(x[l], router_w[l], l, map_t, slot_ptr, shared[l], sh_gate_w[l], K, bufs[l], bias=bias)
+        # every layer's MoE launch; a side stream prefetches the next layer's router weight and shared record
+        decode_layers(x, router_w, sh_gate_w, shared, map_t, slot_ptr, K, bufs, bias=bias, prefetch_next=prefetch,
+                      side=side)
 
     step()
     torch.cuda.synchronize()
@@ -367,6 +370,7 @@ def bench_decode(args, world, rank, batch=None, W=None, cpu_seconds=None):
         "config": {"workload": f"decode_step_{NL}layer_b{b}", "layers": NL, "batch": b, "hidden": LAY.hidden,
                    "inter": LAY.inter, "experts": E, "topk": K, "shared_experts": 1, "routing": "zipf_s1.1",
                    "weights": "affine4_gs64 resident in HBM (48x512 records)", "cuda_graph": True,
+                   "next_layer_l2_prefetch": prefetch,
                    "l2": "flushed before every step (256 MiB write)", "parallelism": f"replicas{world}"},
         "hbm_gbs_per_step": round(step_bytes / (ms * 1e-3) / 1e9, 1),
         "bytes_per_step": int(step_bytes), "unique_experts_per_layer_mean": round(sum(uniq) / NL, 2),
@@ -983,6 +987,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="decode batch")
     ap.add_argument("--layers", type=int, default=48, help="decode layers per step (48 = configs[1])")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement at N=1")
+    ap.add_argument("--no-decode-prefetch", action="store_true",
+                    help="decode: no side-stream L2 prefetch of the next layer's router weight and shared record")
     ap.add_argument("--no-chunks", action="store_true", help="skip the 2K / 8K-token prefill sub-measurements")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="decode CPU baseline sample length")

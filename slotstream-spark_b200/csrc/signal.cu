@@ -55,7 +55,27 @@ __global__ void __launch_bounds__(256) k_copy_sm(const uint8_t* __restrict__ src
   pdl_trigger();
 }
 
+// L2 prefetch of [p, p + bytes): each lane issues bulk prefetches of 64 KB pieces (16-byte aligned inside).
+__global__ void __launch_bounds__(32) k_prefetch_l2(const uint8_t* p, int64_t bytes) {
+  const uintptr_t lo = ((uintptr_t)p + 15) & ~(uintptr_t)15;
+  const uintptr_t hi = ((uintptr_t)p + (uintptr_t)bytes) & ~(uintptr_t)15;
+  if (hi <= lo) return;
+  constexpr uintptr_t PIECE = 64 * 1024;
+  for (uintptr_t a = lo + (uintptr_t)threadIdx.x * PIECE; a < hi; a += 32 * PIECE) {
+    const uint32_t n = (uint32_t)((hi - a) < PIECE ? (hi - a) : PIECE);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+  }
+}
+
 }  // namespace
+
+extern "C" int ssb_prefetch_l2(const void* p, int64_t bytes, void* stream) {
+  SSB_CHECK_ARG(bytes >= 0);
+  if (bytes == 0) return SSB_OK;
+  SSB_CHECK_ARG(p);
+  ssb_note_smem("prefetch_l2", k_prefetch_l2, 0);
+  return ssb_launch(k_prefetch_l2, dim3(1), dim3(32), 0, (cudaStream_t)stream, false, (const uint8_t*)p, bytes);
+}
 
 extern "C" int ssb_copy_sm(void* dst, const void* src, int64_t bytes, void* stream) {
   SSB_CHECK_ARG(bytes >= 0 && bytes <= (int64_t(1) << 24));

@@ -62,6 +62,7 @@ SIGNATURES = {
     "ssb_signal": [_P, _P, _I32, _P, _P, _P, _P, _I32, _P],
     "ssb_wait_seq": [_P, _I64, _I64],
     "ssb_copy_sm": [_P, _P, _I64, _P],
+    "ssb_prefetch_l2": [_P, _I64, _P],
     "ssb_combine_rank_order": [_P, _I64, _I32, _I32, _P, _P],
     "ssb_combine_layer": [_P, _I64, _I32, _I32, _P, _P, _P, _P],
     "ssb_gemv_affine": [_P, _I32, _I64, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P],

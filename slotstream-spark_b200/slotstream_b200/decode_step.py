@@ -8,7 +8,7 @@ routing through ``kernels.signal`` (seq = base + l), so the host can follow the 
 """
 import torch
 
-from .kernels.moe_layer import DecodeLayerBuffers, moe_layer_decode
+from .kernels.moe_layer import DecodeLayerBuffers, decode_layers
 from .kernels.signal import signal
 from .readback import Readback
 
@@ -19,7 +19,7 @@ class DecodeStep:
     ``bufs[l].y``. Router weights [layers, E, H], shared-gate rows [layers, H], shared records [layers, record]."""
 
     def __init__(self, x, router_w, sh_gate_w, shared_records, map_t, slot_ptr_t, k: int, inter: int, *, bias=None,
-                 readback: Readback | None = None, fused: bool = True):
+                 readback: Readback | None = None, fused: bool = True, prefetch_next: bool = True):
         self.x = x
         nl, b, h = x.shape
         e = router_w.shape[1]
@@ -30,6 +30,8 @@ class DecodeStep:
         self.ctrl_dev = torch.zeros(2, dtype=torch.int64, device=x.device)
         self.bufs = [DecodeLayerBuffers(b, k, h, inter, e, x.device) for _ in range(nl)]
         self._args = (router_w, sh_gate_w, shared_records, map_t, slot_ptr_t, bias, fused)
+        self.prefetch_next = prefetch_next
+        self._side = torch.cuda.Stream(device=x.device) if prefetch_next else None
         self.step()                      # eager warm-up: first-use setup happens outside the capture
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
@@ -40,12 +42,14 @@ class DecodeStep:
     def step(self):
         router_w, sh_gate_w, shared_records, map_t, slot_ptr_t, bias, fused = self._args
         rb = self.readback
-        for l in range(self.layers):
-            bf = self.bufs[l]
-            moe_layer_decode(self.x[l], router_w[l], l, map_t, slot_ptr_t, shared_records[l], sh_gate_w[l], self.k, bf,
-                             bias=bias, fused=fused)
+
+        def publish(l):
             if rb is not None:
+                bf = self.bufs[l]
                 signal(bf.ids, bf.w, rb.ids, rb.w, rb.seq, rb.ctrl, l)
+
+        decode_layers(self.x, router_w, sh_gate_w, shared_records, map_t, slot_ptr_t, self.k, self.bufs, bias=bias,
+                      fused=fused, prefetch_next=self.prefetch_next, side=self._side, after_layer=publish)
 
     def replay(self, base: int = 0, pos: int = 0):
         """Launch the captured step (asynchronously); layer l's routing is readable once seq >= base + l."""

@@ -120,6 +120,39 @@ def moe_layer_prefill(x, w_router, group_ptr, sh_gate_w, k: int, bufs: PrefillLa
     return bufs.y
 
 
+def prefetch_l2(t: torch.Tensor):
+    """Bring a device tensor's bytes into L2 on the current stream (ssb_prefetch_l2, a hint: nothing is written)."""
+    if not t.is_cuda:
+        raise ValueError("prefetch_l2 takes a CUDA tensor")
+    _lib.check(_lib.lib().ssb_prefetch_l2(t.data_ptr(), t.numel() * t.element_size(), _lib.stream()), "prefetch_l2")
+
+
+def decode_layers(x, router_w, sh_gate_w, shared_records, map_t, slot_ptr_t, k: int, bufs, *, bias=None,
+                  fused: bool = True, prefetch_next: bool = True, side=None, after_layer=None):
+    """The MoE layers of one decode step (x bf16 [layers, R, H], router weights [layers, E, H], shared-gate rows
+    [layers, H], shared records [layers, record], one DecodeLayerBuffers per layer). With ``prefetch_next`` a side
+    stream brings layer l+1's router weight and shared record -- bytes that do not depend on routing -- into L2
+    while layer l streams its experts, so the next layer's router and shared rows read from L2. The side stream
+    rejoins the current stream at the end (graph-capture safe). ``after_layer(l)`` runs after layer l's launch."""
+    main = torch.cuda.current_stream()
+    side = side if side is not None else (torch.cuda.Stream(device=x.device) if prefetch_next else None)
+    nl = x.shape[0]
+    for l in range(nl):
+        if prefetch_next and l + 1 < nl:
+            ev = torch.cuda.Event()
+            ev.record(main)
+            side.wait_event(ev)
+            with torch.cuda.stream(side):
+                prefetch_l2(router_w[l + 1])
+                prefetch_l2(shared_records[l + 1])
+        moe_layer_decode(x[l], router_w[l], l, map_t, slot_ptr_t, shared_records[l], sh_gate_w[l], k, bufs[l],
+                         bias=bias, fused=fused)
+        if after_layer is not None:
+            after_layer(l)
+    if prefetch_next:
+        main.wait_stream(side)
+
+
 def _addr(rec) -> int:
     if isinstance(rec, torch.Tensor):
         if not rec.is_cuda:

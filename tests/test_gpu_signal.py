@@ -93,3 +93,17 @@ def test_copy_sm_moves_bytes_between_device_and_pinned_host(nbytes):
     assert torch.equal(back, src) and torch.equal(dd, src)
     assert L.ssb_copy_sm(None, src.data_ptr(), 16, st) == _lib.SSB_EINVAL
     assert L.ssb_copy_sm(back.data_ptr(), src.data_ptr(), (1 << 24) + 1, st) == _lib.SSB_EINVAL
+
+
+def test_prefetch_l2_is_a_hint_that_changes_nothing():
+    """ssb_prefetch_l2 on aligned and unaligned ranges returns SSB_OK and leaves the bytes as they were."""
+    from slotstream_b200 import _lib
+    from slotstream_b200.kernels.moe_layer import prefetch_l2
+    t = torch.randint(0, 256, (3 << 20,), dtype=torch.uint8, device="cuda")
+    ref = t.clone()
+    prefetch_l2(t)
+    L, st = _lib.lib(), _lib.stream()
+    for off, n in ((1, 100), (7, (1 << 20) + 5), (0, 0), (16, 15)):
+        assert L.ssb_prefetch_l2(t.data_ptr() + off, n, st) == _lib.SSB_OK
+    torch.cuda.synchronize()
+    assert torch.equal(t, ref)
