@@ -270,11 +270,12 @@ def bench_decode(args, world, rank, batch=None, W=None, cpu_seconds=None):
     bias, map_t, slot_ptr, g = W["bias"], W["map_t"], W["slot_ptr"], W["gen"]
     x = torch.randn(NL, b, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
     bufs = [DecodeLayerBuffers(b, K, LAY.hidden, LAY.inter, E, dev) for _ in range(NL)]
-    prefetch = not args.no_decode_prefetch
+    prefetch = args.decode_prefetch
     side = torch.cuda.Stream() if prefetch else None
 
     def step():
-        # every layer's MoE launch; a side stream prefetches the next layer's router weight and shared record
+        # every layer's MoE launch (with --decode-prefetch a side stream prefetches the next layer's router weight
+        # and shared record into L2)
         decode_layers(x, router_w, sh_gate_w, shared, map_t, slot_ptr, K, bufs, bias=bias, prefetch_next=prefetch,
                       side=side)
 
@@ -833,7 +834,7 @@ def pipelined_eager(x_dev, run, x_host, y_host, k, world):
 
 def bench_prefill_ep(args, world, rank):
     from slotstream_b200 import synth
-    from slotstream_b200.ep import CudaOps, ep_forward, owned_experts
+    from slotstream_b200.ep import CudaOps, balanced_labels, ep_forward, owned_experts
     from slotstream_b200.kernels.moe_layer import PrefillLayerBuffers, moe_layer_prefill
     from slotstream_b200.records import BASELINE_LAYOUT as LAY
     E, K, T = 512, 10, args.tokens
@@ -853,7 +854,23 @@ def bench_prefill_ep(args, world, rank):
     bias = torch.from_numpy(synth.zipf_bias(E)).to(dev) if args.routing == "zipf" else None
     g.manual_seed(2100 + rank)                # each rank its own tokens
     x = torch.randn(T, LAY.hidden, device=dev, generator=g).to(torch.bfloat16)
-    ops = CudaOps(router_w, sh_gate_w, group_ptr, int(base[E]), K, LAY.inter, world, strided=True, bias=bias,
+    ep_router_w, ep_bias = router_w, bias
+    if args.placement == "balanced":
+        # expert placement from measured routing counts (summed over the ranks, so every rank derives the same
+        # labels): relabel the experts so that the strided placement of the labels evens out the ranks' rows
+        logits = x.float() @ router_w.float().t()
+        if bias is not None:
+            logits += bias
+        cnt = torch.bincount(logits.topk(K, dim=1).indices.reshape(-1), minlength=E).to(torch.int64)
+        del logits
+        if world > 1:
+            torch.distributed.all_reduce(cnt)
+        label, expert = balanced_labels(cnt.cpu().numpy(), world)
+        expert_t = torch.from_numpy(expert).to(dev)
+        ep_router_w = router_w[expert_t].contiguous()
+        ep_bias = bias[expert_t].contiguous() if bias is not None else None
+        group_ptr = base[expert_t[torch.tensor(owned, device=dev)]].contiguous()
+    ops = CudaOps(ep_router_w, sh_gate_w, group_ptr, int(base[E]), K, LAY.inter, world, strided=True, bias=ep_bias,
                   sm_reserve=args.sm_reserve)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
@@ -951,7 +968,9 @@ def bench_prefill_ep(args, world, rank):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"ep_prefill_layer_{T}tok_per_gpu", "tokens_per_gpu": T, "hidden": LAY.hidden,
-                   "inter": LAY.inter, "experts": E, "experts_per_gpu": len(owned), "placement": "strided (e % G)",
+                   "inter": LAY.inter, "experts": E, "experts_per_gpu": len(owned),
+                   "placement": ("balanced: experts relabelled from this chunk's routing counts, strided over the "
+                                 "labels" if args.placement == "balanced" else "strided (e % G)"),
                    "topk": K, "shared_experts": 1, "routing": "zipf_s1.1" if args.routing == "zipf" else "uniform",
                    "exchange": f"NCCL all-to-all-v (dispatch rows + metadata, {args.partials} partial sums back)",
                    "partials": args.partials, "micro_batches": args.micro_batches, "gemm_sm_reserve": args.sm_reserve,
@@ -987,14 +1006,17 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="decode batch")
     ap.add_argument("--layers", type=int, default=48, help="decode layers per step (48 = configs[1])")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement at N=1")
-    ap.add_argument("--no-decode-prefetch", action="store_true",
-                    help="decode: no side-stream L2 prefetch of the next layer's router weight and shared record")
+    ap.add_argument("--decode-prefetch", action="store_true",
+                    help="decode: side-stream L2 prefetch of the next layer's router weight and shared record "
+                         "(measured slower; off by default)")
     ap.add_argument("--no-chunks", action="store_true", help="skip the 2K / 8K-token prefill sub-measurements")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="decode CPU baseline sample length")
     ap.add_argument("--cpu-passes", type=int, default=2, help="prefill CPU baseline: timed passes over the chunk")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU leg (baseline and parity)")
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
+    ap.add_argument("--placement", choices=["balanced", "strided"], default="balanced",
+                    help="N > 1: expert placement (balanced from measured routing counts, or strided by id)")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="N > 1: token parts whose exchanges overlap the expert GEMMs of their neighbours")
     ap.add_argument("--partials", choices=["fp32", "bf16"], default="fp32",

@@ -322,8 +322,9 @@ int ssb_wait_seq(const int64_t* seq, int64_t target, int64_t timeout_ns);
 int ssb_copy_sm(void* dst, const void* src, int64_t bytes, void* stream);
 
 /* Hint: bring [p, p + bytes) of device memory into L2 on `stream` (bulk L2 prefetches; nothing is written). A
- * decode step issues it on a side stream for the next layer's router weight and shared-expert record, which do
- * not depend on routing, while the current layer streams its experts. No counterpart in the reference. */
+ * decode step can issue it on a side stream for the next layer's router weight and shared-expert record, which
+ * do not depend on routing, while the current layer streams its experts (opt-in: measured slower in the
+ * 48-layer graph). No counterpart in the reference. */
 int ssb_prefetch_l2(const void* p, int64_t bytes, void* stream);
 
 /* Rank-order combine: out[t, :] = rows[t*k] + rows[t*k + 1] + ... sequentially in fp32.

@@ -19,7 +19,7 @@ class DecodeStep:
     ``bufs[l].y``. Router weights [layers, E, H], shared-gate rows [layers, H], shared records [layers, record]."""
 
     def __init__(self, x, router_w, sh_gate_w, shared_records, map_t, slot_ptr_t, k: int, inter: int, *, bias=None,
-                 readback: Readback | None = None, fused: bool = True, prefetch_next: bool = True):
+                 readback: Readback | None = None, fused: bool = True, prefetch_next: bool = False):
         self.x = x
         nl, b, h = x.shape
         e = router_w.shape[1]

@@ -18,7 +18,10 @@ replicated), then:
 5. output    -- y = bf16(bf16(routed) + bf16(shared)), as the one-GPU layer.
 
 Placement: ``strided`` puts expert e on rank e % G (local index e // G), spreading the popular low ids of a
-Zipf-skewed router over all ranks; contiguous puts it on rank e // (E / G).
+Zipf-skewed router over all ranks; contiguous puts it on rank e // (E / G). ``balanced_labels`` goes further
+from measured routing counts: it relabels the experts so that the strided placement of the new labels gives
+every rank about the same expected number of rows (the kernels are unchanged; the router's weight rows and
+logit bias are permuted into label order, and each rank holds the records of the experts its labels name).
 
 The exchange runs through torch.distributed collectives only (NCCL on GPUs; the same code drives gloo on CPU
 tensors in the host-side tests), with the per-destination counts copied to the host to size the all-to-all-v
@@ -44,6 +47,34 @@ def owned_experts(rank: int, experts: int, n_ranks: int, strided: bool) -> list[
     """Global ids of the experts rank `rank` owns, in local-index order."""
     epr = experts // n_ranks
     return [rank + n_ranks * i for i in range(epr)] if strided else list(range(rank * epr, (rank + 1) * epr))
+
+
+def balanced_labels(counts, n_ranks: int):
+    """Labels that balance the ranks' expected rows under the strided placement: experts are taken in decreasing
+    order of their routing count (ties to the lower id) and each goes to the rank with the fewest rows so far that
+    still has a free slot (E / G slots per rank); the expert in slot i of rank r gets label r + G * i.
+    Returns (label int64 [E]: label of expert e, expert int64 [E]: expert of label l). Apply it by permuting the
+    router's weight rows and logit bias with ``expert`` (row l = expert[l]) and giving rank r the records of
+    ``expert[owned_experts(r, E, G, True)]``: the layer's outputs are those of the original router, except where
+    two logits tie exactly (the stable top-k breaks ties by label)."""
+    import numpy as np
+    c = np.asarray(counts, dtype=np.int64)
+    e_n = c.size
+    if n_ranks < 1 or e_n % n_ranks:
+        raise ValueError("the experts must divide evenly over the ranks")
+    epr = e_n // n_ranks
+    load = np.zeros(n_ranks, dtype=np.int64)
+    used = np.zeros(n_ranks, dtype=np.int64)
+    label = np.empty(e_n, dtype=np.int64)
+    for e in np.lexsort((np.arange(e_n), -c)):
+        free = np.flatnonzero(used < epr)
+        r = int(free[np.argmin(load[free])])
+        label[e] = r + n_ranks * used[r]
+        used[r] += 1
+        load[r] += c[e]
+    expert = np.empty(e_n, dtype=np.int64)
+    expert[label] = np.arange(e_n)
+    return label, expert
 
 
 @dataclass

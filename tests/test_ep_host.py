@@ -169,3 +169,19 @@ def test_corrupt_counts_end_every_rank_with_an_error(tmp_path):
     outcomes = [(tmp_path / f"outcome{r}").read_text() for r in range(world)]
     assert outcomes[1] == "inconsistent counts"
     assert outcomes[0] in ("inconsistent counts", "collective failed")
+
+
+def test_balanced_labels_even_out_the_ranks():
+    """balanced_labels: a permutation of the experts whose strided placement gives every rank about the same
+    routing count (Zipf-skewed counts), where the plain strided placement of the original ids does not."""
+    import numpy as np
+    from slotstream_b200.ep import balanced_labels, owned_experts
+    rng = np.random.default_rng(0)
+    counts = np.bincount((rng.zipf(1.3, 40000) - 1) % 512, minlength=512)
+    for g in (2, 4, 8):
+        label, expert = balanced_labels(counts, g)
+        assert sorted(label.tolist()) == list(range(512)) and np.array_equal(label[expert], np.arange(512))
+        per_rank = [counts[expert[owned_experts(r, 512, g, True)]].sum() for r in range(g)]
+        strided = [counts[owned_experts(r, 512, g, True)].sum() for r in range(g)]
+        assert max(per_rank) <= max(strided)
+        assert max(per_rank) - min(per_rank) <= counts.max()   # within one expert of even
