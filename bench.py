@@ -1015,8 +1015,8 @@ def main():
     ap.add_argument("--cpu-passes", type=int, default=2, help="prefill CPU baseline: timed passes over the chunk")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU leg (baseline and parity)")
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent one-GPU layers instead of EP")
-    ap.add_argument("--placement", choices=["balanced", "strided"], default="balanced",
-                    help="N > 1: expert placement (balanced from measured routing counts, or strided by id)")
+    ap.add_argument("--placement", choices=["balanced", "strided"], default="strided",
+                    help="N > 1: expert placement (strided by id, or balanced from measured routing counts)")
     ap.add_argument("--micro-batches", type=int, default=1,
                     help="N > 1: token parts whose exchanges overlap the expert GEMMs of their neighbours")
     ap.add_argument("--partials", choices=["fp32", "bf16"], default="fp32",
